@@ -1,0 +1,128 @@
+// env.hpp — vectorized surf environment over PlayerMove.
+//
+// Behaviour matches the reference batch env (src/env.c:529-644): action
+// decode, basevelocity fold, one pm tick, swept goal-box test, post-move
+// triggers, fail rules, spline progress reward and same-step autoreset with a
+// terminal observation. On top of that:
+//   * step_k fuses K physics ticks (action repeat) into one call and reduces
+//     the per-tick signals (reward sum, done/trunc/goal OR) in C++;
+//   * outputs land in caller rows of arbitrary stride, so Python can hand in
+//     one pinned host buffer and ship it to the GPU with a single async copy;
+//   * a continuous yaw action (degrees-per-tick fraction in [-1, 1]) may
+//     replace the discrete yaw bin;
+//   * a persistent thread pool replaces the per-call OpenMP team.
+#pragma once
+#include <cstdint>
+#include <memory>
+#include <vector>
+
+#include "movement.hpp"
+#include "thread_pool.hpp"
+
+namespace surf {
+
+struct EnvConfig {                 // SurfEnvConfig-compatible (128 bytes)
+  int32_t num_envs = 1;
+  int32_t max_episode_ticks = 6000;
+  int32_t lookahead_k = 8;
+  float lookahead_dt = 0.25f;
+  int32_t spawn_mode = 1;          // 0 map spawns, 1 spline curriculum, 2 spawn pool
+  float spawn_curriculum_frac = 0.99f;
+  float yaw_rate_max_deg = 10.f;
+  float yaw_jitter_deg = 5.f;
+  float kill_z = -1e38f;           // <= -1e30 -> world min z - 256
+  int32_t water_fail = 1;
+  float pitch_rate_max_deg = 10.f;
+  int32_t lidar_w = 0, lidar_h = 0;
+  float lidar_hfov_deg = 120.f, lidar_vfov_deg = 90.f, lidar_range = 2000.f;
+  Physics phys;
+  int32_t yaw_adaptive = 0;
+};
+static_assert(sizeof(EnvConfig) == 128, "EnvConfig layout");
+
+constexpr int kObsFixed = 15;
+constexpr int kActionDim = 6;
+// Per-env record written by step_k (float32 columns).
+enum RecCol : int {
+  kRecOrigin = 0, kRecYaw = 3, kRecPitch = 4, kRecDucked = 5, kRecVel = 6, kRecTick = 9,
+  kRecReward = 10, kRecDone = 11, kRecTrunc = 12, kRecGoal = 13, kRecEnded = 14, kRecOnground = 15,
+  kRecCols = 16,
+};
+// Terminal pose of the last episode that ended inside a step_k call.
+enum TermCol : int { kTermOrigin = 0, kTermYaw = 3, kTermPitch = 4, kTermDucked = 5, kTermTick = 6, kTermCols = 8 };
+
+struct RowOut {                    // a strided float32 row target (nullptr = skip)
+  float* ptr = nullptr;
+  int64_t stride = 0;              // floats between consecutive env rows
+  float* row(int i) const { return ptr + static_cast<int64_t>(i) * stride; }
+};
+
+class EnvBatch {
+ public:
+  EnvBatch(std::shared_ptr<const Map> map, const EnvConfig& cfg, int threads);
+  int obs_dim() const { return obs_dim_; }
+  int num_envs() const { return cfg_.num_envs; }
+  const EnvConfig& config() const { return cfg_; }
+  const Map& map() const { return *map_; }
+
+  int set_waypoints(const float* xyz, int count);
+  int set_spawn_pool(const PlayerState* pool, int n);
+  void set_teleport_fail(bool on) { teleport_fail_ = on; }
+  void set_goal_box(const float* mins, const float* maxs);
+  void force_fail(const uint8_t* mask);
+  const uint8_t* goal_hits() const { return goal_hit_.data(); }
+
+  void reset_all(uint64_t seed, float* obs);
+  // One tick for every env (reference-compatible contract).
+  void step(const int32_t* actions, float* obs, float* rewards, uint8_t* done, uint8_t* trunc, float* terminal_obs);
+  // K ticks of action repeat. actions: int32 [N, action_stride] (first 6 used);
+  // yaw_cont: optional float [N] in [-1, 1] replacing the yaw bin;
+  // fail_mask: optional uint8 [N] stall kills applied on the first tick.
+  void step_k(const int32_t* actions, int action_stride, const float* yaw_cont, int yaw_stride,
+              const uint8_t* fail_mask, int k, RowOut obs, RowOut term_obs, RowOut rec, RowOut term_rec);
+
+  PlayerState* states() { return st_.data(); }
+  void set_state(int env, const PlayerState& s);
+
+  // Single-player primitives (parity harness, spawn auditions, play client).
+  void pm_step_usercmd(PlayerState* st, float yaw, float pitch, float fmove, float smove, int buttons, int msec);
+  int play_step(PlayerState* st, float yaw, float pitch, float fmove, float smove, int buttons, int msec);
+  void pm_step_single(PlayerState* st, const int32_t action[6]);
+  void occupancy_grid(const float* mins, float cell, int nx, int ny, int nz, uint8_t* out);
+
+ private:
+  struct TickOut { float reward; bool done, trunc, goal; };
+  float yaw_delta(const PlayerState& s, int bin) const;
+  float spline_project(const float* p, int32_t* hint) const;
+  void spline_sample(float u, float* pos, float* tang, int* seg) const;
+  void reset_env(int i);
+  int apply_triggers(int env, PlayerState* s);
+  void write_obs(const PlayerState& s, float last_yd, float last_pd, float* o) const;
+  void write_lidar(const PlayerState& s, float* o) const;
+  TickOut tick_env(int i, float yd, float pd, float fmove, float smove, int buttons, bool forced, float* obs_row,
+                   float* term_row, float* term_rec);
+
+  std::shared_ptr<const Map> map_;
+  EnvConfig cfg_;
+  PlayerMove mover_;
+  std::unique_ptr<ThreadPool> pool_;
+  int obs_dim_ = kObsFixed;
+  float kill_z_ = 0, map_center_[3] = {0, 0, 0};
+  std::vector<float> wp_, cum_, tang_;   // progress spline
+  float total_len_ = 0;
+  std::vector<float> tele_progress_;     // teleport destination progress per trigger
+  std::vector<PlayerState> spawn_pool_;
+  bool teleport_fail_ = false;
+  bool goal_on_ = false;
+  float goal_min_[3] = {0, 0, 0}, goal_max_[3] = {0, 0, 0};
+  std::vector<PlayerState> st_;
+  std::vector<StuckMemo> memo_;
+  std::vector<float> last_yd_, last_pd_;
+  std::vector<uint64_t> rng_;
+  std::vector<uint64_t> push_used_;      // per env: bitset over triggers
+  int push_words_ = 1;
+  std::vector<uint8_t> goal_hit_, pending_fail_;
+  StuckMemo single_memo_;
+};
+
+}  // namespace surf

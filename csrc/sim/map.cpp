@@ -1,0 +1,286 @@
+// map.cpp — BSP v30 reader and entity-lump interpreter.
+//
+// Entity semantics follow the reference loader (src/bsp.c:168-298) so the same
+// file yields the same triggers/solids/volumes in both simulators: see the
+// per-class notes below. Unlike the reference there are no fixed-size tables.
+#include "map.hpp"
+
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <iterator>
+#include <map>
+#include <utility>
+
+namespace surf {
+
+const float kPlayerMins[4][3] = {{-16, -16, -36}, {-16, -16, -18}, {0, 0, 0}, {-32, -32, -32}};
+const float kPlayerMaxs[4][3] = {{16, 16, 36}, {16, 16, 18}, {0, 0, 0}, {32, 32, 32}};
+const float kHullMins[4][3] = {{0, 0, 0}, {-16, -16, -36}, {-32, -32, -32}, {-16, -16, -18}};
+const float kHullMaxs[4][3] = {{0, 0, 0}, {16, 16, 36}, {32, 32, 32}, {16, 16, 18}};
+
+namespace {
+
+template <typename T>
+bool read_lump(const uint8_t* data, size_t size, const DLump& lump, std::vector<T>* out,
+               std::string* err) {
+  if (lump.offset < 0 || lump.length < 0 ||
+      static_cast<uint64_t>(lump.offset) + static_cast<uint64_t>(lump.length) > size) {
+    *err = "lump out of file bounds";
+    return false;
+  }
+  if (lump.length % static_cast<int32_t>(sizeof(T)) != 0) {
+    *err = "lump size not a multiple of its element size";
+    return false;
+  }
+  out->resize(static_cast<size_t>(lump.length) / sizeof(T));
+  if (lump.length) std::memcpy(out->data(), data + lump.offset, static_cast<size_t>(lump.length));
+  return true;
+}
+
+// One entity: ordered key/value pairs (first occurrence of a key wins).
+struct Entity {
+  std::vector<std::pair<std::string, std::string>> kv;
+  const char* get(const char* key) const {
+    for (auto& p : kv)
+      if (p.first == key) return p.second.c_str();
+    return nullptr;
+  }
+  float number(const char* key, float fallback) const {
+    const char* v = get(key);
+    return v ? static_cast<float>(std::atof(v)) : fallback;
+  }
+  void vec3(const char* key, float out[3]) const {
+    out[0] = out[1] = out[2] = 0.f;
+    if (const char* v = get(key)) std::sscanf(v, "%f %f %f", &out[0], &out[1], &out[2]);
+  }
+  int model_index() const {               // "*N" -> N, otherwise -1
+    const char* v = get("model");
+    return (v && v[0] == '*') ? std::atoi(v + 1) : -1;
+  }
+  float yaw() const {                     // "angles" pitch/yaw/roll, else legacy "angle"
+    if (const char* a = get("angles")) {
+      float v[3] = {0, 0, 0};
+      std::sscanf(a, "%f %f %f", &v[0], &v[1], &v[2]);
+      return v[1];
+    }
+    return number("angle", 0.f);
+  }
+};
+
+// Split the entity lump into { "k" "v" ... } blocks. Keys are truncated to 39
+// and values to 519 characters, as the engine's fixed buffers do.
+std::vector<Entity> tokenize_entities(const std::string& text) {
+  std::vector<Entity> out;
+  size_t i = 0, n = text.size();
+  auto at = [&](size_t k) { return k < n ? text[k] : '\0'; };
+  while (true) {
+    while (i < n && text[i] && text[i] != '{') ++i;
+    if (i >= n || !text[i]) break;
+    ++i;
+    Entity e;
+    while (true) {
+      while (i < n && text[i] && text[i] != '"' && text[i] != '}') ++i;
+      if (i >= n || !text[i] || text[i] == '}') {
+        if (at(i) == '}') ++i;
+        break;
+      }
+      size_t ks = ++i;
+      while (i < n && text[i] && text[i] != '"') ++i;
+      std::string key = text.substr(ks, i - ks);
+      if (i < n) ++i;
+      while (i < n && text[i] && text[i] != '"') ++i;
+      if (i >= n || !text[i]) break;
+      size_t vs = ++i;
+      while (i < n && text[i] && text[i] != '"') ++i;
+      std::string val = text.substr(vs, i - vs);
+      if (i < n) ++i;
+      if (e.kv.size() < 40) {
+        if (key.size() > 39) key.resize(39);
+        if (val.size() > 519) val.resize(519);
+        e.kv.emplace_back(std::move(key), std::move(val));
+      }
+    }
+    out.push_back(std::move(e));
+  }
+  return out;
+}
+
+// SetMovedir: the two "up"/"down" angle codes, otherwise the forward vector
+// of the entity angles (computed in double, stored as float).
+void movedir_from_angles(const float ang[3], float out[3]) {
+  if (ang[0] == 0 && ang[1] == -1 && ang[2] == 0) { out[0] = 0; out[1] = 0; out[2] = 1; return; }
+  if (ang[0] == 0 && ang[1] == -2 && ang[2] == 0) { out[0] = 0; out[1] = 0; out[2] = -1; return; }
+  const double deg = 3.14159265358979323846 * 2 / 360;
+  double p = ang[0] * deg, y = ang[1] * deg;
+  out[0] = static_cast<float>(std::cos(p) * std::cos(y));
+  out[1] = static_cast<float>(std::cos(p) * std::sin(y));
+  out[2] = static_cast<float>(-std::sin(p));
+}
+
+bool is_solid_class(const char* c) {
+  static const char* kClasses[] = {"func_wall", "func_breakable", "func_pushable",
+                                   "func_button", "func_train", "func_conveyor",
+                                   "func_wall_toggle", "func_rotating",
+                                   "func_door_rotating", "func_door"};
+  for (const char* k : kClasses)
+    if (!std::strcmp(c, k)) return true;
+  return false;
+}
+
+}  // namespace
+
+bool Map::load_file(const std::string& path, std::string* err) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) { *err = "cannot open bsp file"; return false; }
+  std::vector<uint8_t> buf((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+  return load_memory(buf.data(), buf.size(), err);
+}
+
+bool Map::load_memory(const uint8_t* data, size_t size, std::string* err) {
+  if (size < sizeof(DHeader)) { *err = "file too small"; return false; }
+  DHeader h;
+  std::memcpy(&h, data, sizeof h);
+  if (h.version != kBspVersion) { *err = "not a BSP v30 file"; return false; }
+  std::vector<DNode> nodes;
+  std::vector<DLeaf> leafs;
+  std::vector<char> ents;
+  if (!read_lump(data, size, h.lumps[kLumpPlanes], &planes, err) ||
+      !read_lump(data, size, h.lumps[kLumpClipnodes], &clipnodes, err) ||
+      !read_lump(data, size, h.lumps[kLumpNodes], &nodes, err) ||
+      !read_lump(data, size, h.lumps[kLumpLeafs], &leafs, err) ||
+      !read_lump(data, size, h.lumps[kLumpModels], &models, err) ||
+      !read_lump(data, size, h.lumps[kLumpEntities], &ents, err))
+    return false;
+  entities.assign(ents.begin(), ents.end());
+  // Hull 0: render nodes become clipnodes, leaf children become leaf contents.
+  hull0.resize(nodes.size());
+  for (size_t i = 0; i < nodes.size(); ++i) {
+    hull0[i].plane = nodes[i].plane;
+    for (int s = 0; s < 2; ++s) {
+      int c = nodes[i].child[s];
+      if (c >= 0) { hull0[i].child[s] = static_cast<int16_t>(c); continue; }
+      int leaf = -1 - c;
+      if (leaf < 0 || leaf >= static_cast<int>(leafs.size())) { *err = "bad leaf ref"; return false; }
+      hull0[i].child[s] = static_cast<int16_t>(leafs[leaf].contents);
+    }
+  }
+  if (models.empty()) { *err = "no models"; return false; }
+  for (int k = 0; k < 3; ++k) { world_mins[k] = models[0].mins[k]; world_maxs[k] = models[0].maxs[k]; }
+  return parse_entities();
+}
+
+HullView Map::hull(int model, int bsp_hull) const {
+  HullView v;
+  v.planes = planes.data();
+  const DModel& m = models[static_cast<size_t>(model)];
+  if (bsp_hull == 0) {
+    v.nodes = hull0.data();
+    v.last = static_cast<int>(hull0.size()) - 1;
+  } else {
+    v.nodes = clipnodes.data();
+    v.last = static_cast<int>(clipnodes.size()) - 1;
+  }
+  v.first = m.headnode[bsp_hull];
+  for (int k = 0; k < 3; ++k) { v.clip_mins[k] = kHullMins[bsp_hull][k]; v.clip_maxs[k] = kHullMaxs[bsp_hull][k]; }
+  return v;
+}
+
+bool Map::parse_entities() {
+  auto ents = tokenize_entities(entities);
+  struct Target { std::string name; float origin[3]; float yaw; };
+  std::vector<Target> targets;
+  std::vector<std::pair<size_t, std::string>> pending;     // trigger index -> target name
+  solids.clear(); volumes.clear(); triggers.clear(); spawns.clear();
+
+  auto bounds = [&](int model, const float org[3], float lo[3], float hi[3]) {
+    const DModel& m = models[static_cast<size_t>(model)];
+    for (int k = 0; k < 3; ++k) { lo[k] = m.mins[k] + org[k] - 1.f; hi[k] = m.maxs[k] + org[k] + 1.f; }
+  };
+
+  for (const Entity& e : ents) {
+    const char* cls = e.get("classname");
+    if (!cls) continue;
+    int model = e.model_index();
+    if (model >= static_cast<int>(models.size())) continue;        // malformed "*N"
+    float origin[3];
+    e.vec3("origin", origin);
+
+    if (!std::strncmp(cls, "info_player_start", 17) || !std::strncmp(cls, "info_player_deathmatch", 22)) {
+      SpawnPoint sp{{origin[0], origin[1], origin[2]}, e.yaw()};
+      spawns.push_back(sp);
+    } else if (model >= 0 && !std::strcmp(cls, "trigger_teleport")) {
+      Trigger t;
+      t.kind = TriggerKind::kTeleport; t.model = model;
+      for (int k = 0; k < 3; ++k) t.origin[k] = origin[k];
+      bounds(model, origin, t.absmin, t.absmax);
+      if (const char* tgt = e.get("target")) pending.emplace_back(triggers.size(), std::string(tgt).substr(0, 63));
+      triggers.push_back(t);
+    } else if (model >= 0 && !std::strcmp(cls, "trigger_hurt")) {
+      Trigger t;
+      t.kind = TriggerKind::kHurt; t.model = model;
+      for (int k = 0; k < 3; ++k) t.origin[k] = origin[k];
+      bounds(model, origin, t.absmin, t.absmax);
+      t.damage = e.number("dmg", 10.f);
+      triggers.push_back(t);
+    } else if (model >= 0 && !std::strcmp(cls, "trigger_push")) {
+      Trigger t;
+      t.kind = TriggerKind::kPush; t.model = model;
+      for (int k = 0; k < 3; ++k) t.origin[k] = origin[k];
+      bounds(model, origin, t.absmin, t.absmax);
+      float ang[3];
+      e.vec3("angles", ang);
+      if (!e.get("angles") && e.get("angle")) { ang[0] = ang[2] = 0; ang[1] = e.number("angle", 0.f); }
+      if (ang[0] == 0 && ang[1] == 0 && ang[2] == 0) ang[1] = 360.f;   // CTriggerPush::Spawn
+      float dir[3];
+      movedir_from_angles(ang, dir);
+      float speed = e.number("speed", 0.f);
+      if (speed == 0.f) speed = 100.f;
+      for (int k = 0; k < 3; ++k) t.push_velocity[k] = dir[k] * speed;
+      t.push_once = (static_cast<int>(e.number("spawnflags", 0)) & 1) != 0;
+      triggers.push_back(t);
+    } else if (model >= 0 &&
+               (!std::strcmp(cls, "func_water") || !std::strcmp(cls, "func_ladder") ||
+                (!std::strcmp(cls, "func_illusionary") && e.number("skin", -1.f) < -1.f) ||
+                (!std::strcmp(cls, "func_door") && e.number("skin", 0.f) < -1.f))) {
+      // Non-solid contents volumes: the brush carries its skin as contents.
+      BrushEntity v;
+      v.model = model;
+      for (int k = 0; k < 3; ++k) v.origin[k] = origin[k];
+      v.contents = !std::strcmp(cls, "func_ladder") ? kLadder : static_cast<int32_t>(e.number("skin", -3.f));
+      bounds(model, origin, v.absmin, v.absmax);
+      volumes.push_back(v);
+    } else if (model >= 0) {
+      bool solid = is_solid_class(cls);
+      // SF_CONVEYOR_NOTSOLID (2) turns a func_conveyor into decoration.
+      if (solid && !std::strcmp(cls, "func_conveyor") && (static_cast<int>(e.number("spawnflags", 0)) & 2))
+        solid = false;
+      if (solid) {
+        BrushEntity s;
+        s.model = model;
+        for (int k = 0; k < 3; ++k) s.origin[k] = origin[k];
+        bounds(model, origin, s.absmin, s.absmax);
+        solids.push_back(s);
+      }
+    } else if (const char* tn = e.get("targetname")) {
+      Target t{std::string(tn).substr(0, 63), {origin[0], origin[1], origin[2]}, e.yaw()};
+      targets.push_back(t);
+    }
+  }
+  for (auto& p : pending) {
+    for (auto& t : targets) {
+      if (t.name == p.second) {
+        Trigger& tr = triggers[p.first];
+        tr.has_dest = true;
+        for (int k = 0; k < 3; ++k) tr.dest[k] = t.origin[k];
+        tr.dest_yaw = t.yaw;
+        break;
+      }
+    }
+  }
+  return true;
+}
+
+}  // namespace surf

@@ -1,0 +1,40 @@
+"""Loading of the in-tree native libraries (``_lib/*.so``).
+
+CUDA libraries are required whenever a CUDA device is used: a missing or
+stale library raises instead of silently falling back to PyTorch, so a GPU
+run always executes the hand-written kernels.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_DIR = Path(__file__).resolve().parent / "_lib"
+_lock = threading.Lock()
+_cache: dict[str, ctypes.CDLL] = {}
+
+
+class NativeLibraryMissing(RuntimeError):
+    pass
+
+
+def load(name: str, build_if_missing: bool = True) -> ctypes.CDLL:
+    """Load ``_lib/<name>`` (building it first if it is absent)."""
+    with _lock:
+        if name in _cache:
+            return _cache[name]
+        path = LIB_DIR / name
+        if not path.exists() and build_if_missing:
+            from . import _build
+            _build.build(only=[name], verbose=False)
+        if not path.exists():
+            raise NativeLibraryMissing(
+                f"{path} is not built; run `python -c 'import __graft_entry__ as g; g.build()'`")
+        lib = ctypes.CDLL(str(path))
+        _cache[name] = lib
+        return lib
+
+
+def loaded_paths() -> list[str]:
+    return [str(LIB_DIR / n) for n in _cache]
