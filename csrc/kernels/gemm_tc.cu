@@ -1,0 +1,582 @@
+// gemm_tc.cu — bf16 GEMM on Blackwell 5th-generation tensor cores (sm_100a).
+//
+//   D[M, N] = A[M, K] * B[N, K]^T      (fp32 accumulation in tensor memory)
+//
+// Each operand is read either K-major (row-major [rows, K]) or MN-major
+// (row-major [K, rows]); the MN-major form is what lets the backward pass
+// (dX = dY W, dW = dY^T X) run on the forward activations without a
+// transpose. The kernel is persistent (grid = SMs x resident CTAs, static
+// round-robin over 128 x BN output tiles and K splits) with 6 warps:
+//
+//   warp 0, one thread : TMA producer — cp.async.bulk.tensor 2-D tiles (128 B
+//                        swizzle, no multicast) into a STAGES-deep smem ring
+//                        shared by consecutive tiles, per-stage mbarriers;
+//   warp 1, one thread : tcgen05.mma issuer — 4 MMAs (K = 16 each) per 64-wide
+//                        k-tile into one of two TMEM accumulators;
+//                        tcgen05.commit releases each smem stage and signals
+//                        the epilogue when a tile's accumulator is complete;
+//   warps 2-5          : epilogue — tcgen05.ld of the warp's 32 TMEM lanes,
+//                        fused bias / activation / activation-derivative,
+//                        stores as fp32 or bf16, optionally also transposed,
+//                        or fp32 atomic accumulation for split-K; then hand
+//                        the accumulator back, so tile i's epilogue overlaps
+//                        tile i+1's loads and MMAs.
+//
+// Every wait on an mbarrier is bounded by %globaltimer (2 s); on expiry the
+// kernel records an error code in a device flag, skips the remaining work,
+// releases its tensor memory and returns, so a fault in the pipeline shows
+// up as an error status on the host instead of a hung GPU.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "surf_cuda.cuh"
+
+namespace {
+
+constexpr int BM = 128, BK = 64;
+constexpr uint64_t kWaitNs = 2000000000ull;    // 2 s bound per barrier wait
+
+enum Act : int { kNone = 0, kRelu = 1, kTanh = 2, kReluGrad = 3, kTanhGrad = 4 };
+enum CMode : int { kStore = 0, kAtomic = 1 };
+
+struct Epilogue {
+  void* c;            // [M, N] output (or null)
+  int64_t ldc;
+  int c_dtype;        // 0 fp32, 1 bf16
+  int c_mode;         // 0 store, 1 fp32 atomic add
+  void* ct;           // optional transposed output [N, M]
+  int64_t ldct;
+  int ct_dtype;
+  const float* bias;  // [N] or null
+  int act;            // activation for columns < act_split
+  int act2;           // activation for columns >= act_split
+  int act_split;
+  const uint16_t* aux;   // bf16 [M, N] saved activation for the derivative modes
+  int64_t ld_aux;
+  int* err;           // device error flag (0 = ok)
+  int dbg;            // diagnostics: bit 0 skip epilogue stores, bit 1 skip MMAs (timing studies only)
+};
+
+// ---- PTX wrappers --------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; returns false (and records `code`) on timeout or when another
+// role already gave up (*abort set).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code, volatile int* abort) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 255) == 0) {
+      if (*abort) return false;
+      if (globaltimer() - t0 > kWaitNs) {
+        if (err) atomicCAS(err, 0, code);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor (sm100 UMMA): start, LBO, SBO (>> 4),
+// descriptor version 1, 128-byte swizzle (layout type 2).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accum), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr + 16));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(src)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ float apply_act(int act, float x, float aux) {
+  switch (act) {
+    case kRelu: return fmaxf(x, 0.0f);
+    case kTanh: return tanhf(x);
+    case kReluGrad: return aux > 0.0f ? x : 0.0f;
+    case kTanhGrad: return x * (1.0f - aux * aux);
+    default: return x;
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int STAGES>
+struct Cfg {
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kAcc = BN <= 64 ? 4 : 2;           // accumulator buffers in TMEM
+  static constexpr int kTmemCols = kAcc * BN;
+  // per epilogue warp: two 32x32 fp32 staging tiles for TMA stores (4 KB each)
+  static constexpr int kStageOutBytes = 4 * 2 * 4096;
+  // alignment slack + operand stages + barrier block (1 KB) + output staging
+  static constexpr size_t kSmem = 1024 + STAGES * static_cast<size_t>(kStageBytes) + 1024 + kStageOutBytes;
+  // instruction descriptor: D fp32, A/B bf16, majorness, N >> 3, M >> 4
+  static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((A_MN ? 1u : 0u) << 15) |
+                                     ((B_MN ? 1u : 0u) << 16) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                                     (static_cast<uint32_t>(BM >> 4) << 24);
+};
+
+struct Sched {             // static persistent schedule over (m block, n block, k split)
+  int mt, nt, splits, per, kt_total, group;
+  // Grouped rasterisation: runs of `group` m blocks sweep all n blocks, so the
+  // CTAs of one wave share A and B tiles through L2.
+  __device__ void tile(int t, int* m0, int* n0, int* kt0, int* nkt) const {
+    const int per_split = mt * nt;
+    const int sp = t / per_split;
+    const int r = t - sp * per_split;
+    const int span = group * nt;
+    const int g = r / span;
+    const int first = g * group;
+    const int gsz = min(group, mt - first);
+    const int local = r - g * span;
+    const int mb = first + local % gsz;
+    const int nb = local / gsz;
+    *m0 = mb * BM;
+    *n0 = nb;
+    *kt0 = sp * per;
+    *nkt = min(kt_total, *kt0 + per) - *kt0;
+  }
+  __device__ int count() const { return mt * nt * splits; }
+};
+
+__device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, float* v, int row, bool row_ok, int col0, int N) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int col = col0 + i;
+    if (col >= N) break;
+    float x = v[i];
+    if (ep.bias) x += ep.bias[col];
+    const int act = col < ep.act_split ? ep.act : ep.act2;
+    float aux = 0.0f;
+    if ((act == kReluGrad || act == kTanhGrad) && row_ok) aux = surfk::bf16_to_f32(ep.aux[row * ep.ld_aux + col]);
+    v[i] = apply_act(act, x, aux);
+  }
+  if (ep.ct && row_ok) {
+    // transposed store: for a fixed column the warp's 32 lanes write 32 consecutive rows
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int col = col0 + i;
+      if (col < N) {
+        if (ep.ct_dtype == 1) static_cast<uint16_t*>(ep.ct)[col * ep.ldct + row] = surfk::f32_to_bf16(v[i]);
+        else static_cast<float*>(ep.ct)[col * ep.ldct + row] = v[i];
+      }
+    }
+  }
+  if (!ep.c || !row_ok) return;
+  const int ncol = min(16, N - col0);
+  if (ep.c_mode == kAtomic) {
+    float* dst = static_cast<float*>(ep.c) + row * ep.ldc + col0;
+    for (int i = 0; i < ncol; ++i) atomicAdd(dst + i, v[i]);
+  } else if (ep.c_dtype == 1) {
+    uint16_t* dst = static_cast<uint16_t*>(ep.c) + row * ep.ldc + col0;
+    if (ncol == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+      uint32_t w[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        w[i] = static_cast<uint32_t>(surfk::f32_to_bf16(v[2 * i])) |
+               (static_cast<uint32_t>(surfk::f32_to_bf16(v[2 * i + 1])) << 16);
+      reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    } else {
+      for (int i = 0; i < ncol; ++i) dst[i] = surfk::f32_to_bf16(v[i]);
+    }
+  } else {
+    float* dst = static_cast<float*>(ep.c) + row * ep.ldc + col0;
+    if (ncol == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+      for (int i = 0; i < ncol; ++i) dst[i] = v[i];
+    }
+  }
+}
+
+// Persistent warp-specialised kernel: 6 warps = producer, MMA, 4 epilogue.
+template <int BN, bool A_MN, bool B_MN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                const __grid_constant__ CUtensorMap tma_c, int use_tma_c, int M, int N, Sched sc, Epilogue ep) {
+  using C = Cfg<BN, A_MN, B_MN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::kStageBytes);
+  // bars: [0,S) full, [S,2S) empty, then kAcc accumulator-full and kAcc accumulator-empty
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* acc_empty = bars + 2 * STAGES + C::kAcc;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2 * C::kAcc);
+  // output staging after the barrier block, 1024-aligned (swizzle atoms)
+  uint8_t* stage_out = smem + STAGES * C::kStageBytes + 1024;
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&bars[s]), 1);
+      mbar_init(smem_u32(&bars[STAGES + s]), 1);
+    }
+    for (int b = 0; b < C::kAcc; ++b) {
+      mbar_init(smem_u32(&acc_full[b]), 1);
+      mbar_init(smem_u32(&acc_empty[b]), 4);     // one arrival per epilogue warp
+    }
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int ntiles = sc.count();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer
+      int it = 0;
+      for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
+        int m0, nb, kt0, nkt;
+        sc.tile(t, &m0, &nb, &kt0, &nkt);
+        const int n0 = nb * BN;
+        for (int i = 0; i < nkt; ++i, ++it) {
+          const int s = it % STAGES;
+          if (it >= STAGES && !mbar_wait(smem_u32(&bars[STAGES + s]), ((it / STAGES) & 1) ^ 1, ep.err, 1, abort)) break;
+          const uint32_t full = smem_u32(&bars[s]);
+          mbar_expect_tx(full, C::kStageBytes);
+          const uint32_t a_dst = smem_u32(tiles + s * C::kStageBytes);
+          const uint32_t b_dst = a_dst + C::kABytes;
+          const int k = (kt0 + i) * BK;
+          if (A_MN) {
+            tma_load_2d(a_dst, &tma_a, m0, k, full);
+            tma_load_2d(a_dst + BK * 128, &tma_a, m0 + 64, k, full);
+          } else {
+            tma_load_2d(a_dst, &tma_a, k, m0, full);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * BK * 128, &tma_b, n0 + 64 * j, k, full);
+          } else {
+            tma_load_2d(b_dst, &tma_b, k, n0, full);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer
+      int it = 0, tc = 0;
+      for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, ++tc) {
+        int m0, nb, kt0, nkt;
+        sc.tile(t, &m0, &nb, &kt0, &nkt);
+        const int buf = tc % C::kAcc, use = tc / C::kAcc;
+        if (use > 0 && !mbar_wait(smem_u32(&acc_empty[buf]), (use & 1) ^ 1, ep.err, 4, abort)) break;
+        fence_after();
+        const uint32_t dtm = tmem + buf * BN;
+        bool ok = true;
+        for (int i = 0; i < nkt; ++i, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(smem_u32(&bars[s]), (it / STAGES) & 1, ep.err, 2, abort)) { ok = false; break; }
+          fence_after();
+          const uint32_t a_base = smem_u32(tiles + s * C::kStageBytes);
+          const uint32_t b_base = a_base + C::kABytes;
+#pragma unroll
+          for (int j = 0; j < BK / 16; ++j) {
+            // K-major: +32 B per 16-element k step inside the 128 B swizzled row;
+            // MN-major: +2 k-groups (2 x 1024 B) per step; MN blocks BK*128 B apart.
+            const uint64_t da = A_MN ? smem_desc(a_base + j * 2048, BK * 128, 1024) : smem_desc(a_base + j * 32, 16, 1024);
+            const uint64_t db = B_MN ? smem_desc(b_base + j * 2048, BK * 128, 1024) : smem_desc(b_base + j * 32, 16, 1024);
+            if (!(ep.dbg & 2)) mma_bf16(dtm, da, db, C::kIdesc, (i > 0 || j > 0) ? 1u : 0u);
+          }
+          mma_commit(smem_u32(&bars[STAGES + s]));      // frees the stage when these MMAs finish
+        }
+        if (!ok) break;
+        mma_commit(smem_u32(&acc_full[buf]));          // accumulator of this tile complete
+      }
+    }
+  } else {
+    // ---- epilogue warps 2..5 (TMEM lane quadrant = warp % 4)
+    const int quad = warp & 3;
+    int tc = 0;
+    int stage_ctr = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
+      int m0, nb, kt0, nkt;
+      sc.tile(t, &m0, &nb, &kt0, &nkt);
+      const int n0 = nb * BN;
+      const int buf = tc % C::kAcc, use = tc / C::kAcc;
+      if (!mbar_wait(smem_u32(&acc_full[buf]), use & 1, ep.err, 3, abort)) break;
+      fence_after();
+      const int row = m0 + quad * 32 + lane;
+      const bool row_ok = row < M;
+      if (ep.dbg & 1) {
+        float v[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN, v);
+        if (v[0] == 12345.0f && row < 0) ep.err[0] = 1;      // keep the load alive
+      } else if (use_tma_c) {
+        // bias/activation in registers, then the warp's 32 x 32 chunk goes to a
+        // swizzled smem tile and out with one asynchronous TMA store
+        const bool bf = ep.c_dtype == 1;
+        uint8_t* my_stage = stage_out + quad * 8192;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          if (n0 + c0 >= N) break;
+          float v[32];
+          tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + c0, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = n0 + c0 + i;
+            float x = v[i];
+            if (ep.bias && col < N) x += ep.bias[col];
+            const int act = col < ep.act_split ? ep.act : ep.act2;
+            float aux = 0.0f;
+            if ((act == kReluGrad || act == kTanhGrad) && row_ok && col < N)
+              aux = surfk::bf16_to_f32(ep.aux[row * ep.ld_aux + col]);
+            v[i] = apply_act(act, x, aux);
+          }
+          const int sb = stage_ctr & 1;
+          if (lane == 0 && stage_ctr >= 2) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          __syncwarp();
+          uint8_t* tile = my_stage + sb * 4096;
+          if (bf) {
+            // 64-byte rows, 64 B swizzle: 16 B chunk c of row r lands at chunk c ^ ((r >> 1) & 3)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              uint32_t w[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                w[k] = static_cast<uint32_t>(surfk::f32_to_bf16(v[8 * c + 2 * k])) |
+                       (static_cast<uint32_t>(surfk::f32_to_bf16(v[8 * c + 2 * k + 1])) << 16);
+              const int pc = c ^ ((lane >> 1) & 3);
+              *reinterpret_cast<uint4*>(tile + lane * 64 + pc * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          } else {
+            // 128-byte rows, 128 B swizzle: chunk c of row r lands at chunk c ^ (r & 7)
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const int pc = c ^ (lane & 7);
+              *reinterpret_cast<float4*>(tile + lane * 128 + pc * 16) =
+                  make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+            }
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) tma_store_2d(&tma_c, smem_u32(tile), n0 + c0, m0 + quad * 32);
+          ++stage_ctr;
+        }
+      } else {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + c0, v);
+          if (n0 + c0 < N) epilogue_chunk(ep, v, row, row_ok, n0 + c0, N);
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_empty[buf])) : "memory");
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols));
+}
+
+// ---- host side ---------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map: `rows` x `inner` elements, row stride `ld` elements,
+// box of box_inner x box_rows, 128-byte swizzle, zero fill out of bounds.
+bool make_map(CUtensorMap* m, const void* base, int64_t inner, int64_t rows, int64_t ld, int box_inner, int box_rows,
+              bool fp32 = false, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const int esize = fp32 ? 4 : 2;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * esize)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+int launch(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const Epilogue& ep, int splits,
+           cudaStream_t s) {
+  constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 6 : 4);
+  using C = Cfg<BN, A_MN, B_MN, STAGES>;
+  auto kern = gemm_kernel<BN, A_MN, B_MN, STAGES>;
+  CUtensorMap ta, tb;
+  const bool okA = A_MN ? make_map(&ta, A, M, K, lda, 64, BK) : make_map(&ta, A, K, M, lda, BK, BM);
+  const bool okB = B_MN ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, BN);
+  if (!okA || !okB) return static_cast<int>(cudaErrorInvalidValue);
+  // TMA-store epilogue for plain stores with 16-byte aligned rows
+  CUtensorMap tc;
+  std::memset(&tc, 0, sizeof tc);
+  const int esize = ep.c_dtype == 1 ? 2 : 4;
+  int use_tma_c = ep.c && ep.c_mode == kStore && !ep.ct && ((reinterpret_cast<uintptr_t>(ep.c) & 15) == 0) &&
+                  ((ep.ldc * esize) % 16 == 0);
+  if (use_tma_c)
+    use_tma_c = make_map(&tc, ep.c, N, M, ep.ldc, 32, 32, ep.c_dtype != 1,
+                         ep.c_dtype == 1 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)
+                    ? 1
+                    : 0;
+  static int resident = 0;          // CTAs per SM for this instantiation
+  static int sms = 0;
+  if (!resident) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmem));
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, 192, C::kSmem);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (resident < 1) resident = 1;
+    if (resident * C::kTmemCols > 512) resident = 512 / C::kTmemCols;
+  }
+  Sched sc;
+  sc.kt_total = (K + BK - 1) / BK;
+  if (splits < 1) splits = 1;
+  if (splits > sc.kt_total) splits = sc.kt_total;
+  sc.per = (sc.kt_total + splits - 1) / splits;
+  sc.splits = (sc.kt_total + sc.per - 1) / sc.per;
+  sc.mt = (M + BM - 1) / BM;
+  sc.nt = (N + BN - 1) / BN;
+  sc.group = 8;
+  const int64_t ntiles = static_cast<int64_t>(sc.mt) * sc.nt * sc.splits;
+  const int grid = static_cast<int>(ntiles < static_cast<int64_t>(sms) * resident ? ntiles : static_cast<int64_t>(sms) * resident);
+  kern<<<grid, 192, C::kSmem, s>>>(ta, tb, tc, use_tma_c, M, N, sc, ep);
+  SURF_RETURN_LAUNCH();
+}
+
+template <int BN>
+int dispatch_major(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn, int M, int N, int K,
+                   const Epilogue& ep, int splits, cudaStream_t s) {
+  if (a_mn && b_mn) return launch<BN, true, true>(A, lda, B, ldb, M, N, K, ep, splits, s);
+  if (a_mn) return launch<BN, true, false>(A, lda, B, ldb, M, N, K, ep, splits, s);
+  if (b_mn) return launch<BN, false, true>(A, lda, B, ldb, M, N, K, ep, splits, s);
+  return launch<BN, false, false>(A, lda, B, ldb, M, N, K, ep, splits, s);
+}
+
+}  // namespace
+
+// D = A * B^T with a fused epilogue. a_mn / b_mn select MN-major operands
+// (row-major [K, M] / [K, N]); otherwise operands are row-major [M, K] / [N, K].
+// Leading dimensions in elements (multiples of 8). bn: tile width 32/64/128/256
+// (MN-major B needs bn >= 64). splits > 1 partitions K over grid.z and
+// requires the atomic fp32 output mode.
+SURF_EXPORT int surf_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn, int M,
+                               int N, int K, const Epilogue* ep, int bn, int splits, void* stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if ((lda & 7) || (ldb & 7)) return static_cast<int>(cudaErrorInvalidValue);
+  if (splits > 1 && ep->c_mode != kAtomic) return static_cast<int>(cudaErrorInvalidValue);
+  if (b_mn && bn < 64) return static_cast<int>(cudaErrorInvalidValue);
+  auto s = static_cast<cudaStream_t>(stream);
+  switch (bn) {
+    case 32: return dispatch_major<32>(A, lda, a_mn, B, ldb, b_mn, M, N, K, *ep, splits, s);
+    case 64: return dispatch_major<64>(A, lda, a_mn, B, ldb, b_mn, M, N, K, *ep, splits, s);
+    case 128: return dispatch_major<128>(A, lda, a_mn, B, ldb, b_mn, M, N, K, *ep, splits, s);
+    case 256: return dispatch_major<256>(A, lda, a_mn, B, ldb, b_mn, M, N, K, *ep, splits, s);
+    default: return static_cast<int>(cudaErrorInvalidValue);
+  }
+}
+
+SURF_EXPORT int surf_gemm_epilogue_size() { return static_cast<int>(sizeof(Epilogue)); }

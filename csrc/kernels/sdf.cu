@@ -1,0 +1,211 @@
+// sdf.cu — GPU bake of the vision/goal occupancy grid and its Euclidean
+// distance field (sm_100a).
+//
+// Occupancy (reference: src/env.c:673-698 plus python/surfgym/vision.py:
+// 346-406): a voxel is solid when its centre is SOLID or SKY in the world's
+// point hull (hull 0) or inside a solid brush entity. "Slab" sampling ORs in
+// samples shifted by k*cell/4 (k = +-1, +-2) along each axis so that geometry
+// thinner than a voxel cannot slip between centres. The reference samples the
+// C tracer on CPU threads (13 full-grid passes); here one thread walks the
+// clip tree for all samples of its voxel.
+//
+// Distance (reference: scipy.ndimage.distance_transform_edt on the padded
+// occupancy, python/surfgym/vision.py:409-439): exact Euclidean distance from
+// each free voxel centre to the nearest solid voxel centre, outside the grid
+// counting as solid. Computed with the separable lower-envelope-of-parabolas
+// transform of Felzenszwalb & Huttenlocher ("Distance Transforms of Sampled
+// Functions", Theory of Computing 8, 2012): three 1-D passes (x, y, z), one
+// thread per grid line.
+#include <cuda_fp16.h>
+
+#include "surf_cuda.cuh"
+
+namespace {
+
+constexpr int kSolid = -2, kSky = -6, kEmpty = -1;
+
+struct TreeView {
+  const float4* planes;   // normal xyz, dist
+  const int* ptype;       // 0..2 axial, 3..5 general
+  const int3* nodes;      // plane, child0, child1
+};
+
+__device__ __forceinline__ int tree_contents(const TreeView& t, int num, float x, float y, float z) {
+  int guard = 0;
+  while (num >= 0 && guard++ < 4096) {
+    const int3 nd = t.nodes[num];
+    const float4 pl = t.planes[nd.x];
+    const int ty = t.ptype[nd.x];
+    const float d = ty == 0 ? x - pl.w : ty == 1 ? y - pl.w : ty == 2 ? z - pl.w : (x * pl.x + y * pl.y + z * pl.z) - pl.w;
+    num = d >= 0.0f ? nd.y : nd.z;
+  }
+  return num < 0 ? num : kEmpty;
+}
+
+struct SolidEnt { int head; float ox, oy, oz; float lo[3], hi[3]; };
+
+__global__ void occupancy_kernel(TreeView t, int world_head, const SolidEnt* ents, int n_ents, float mnx, float mny,
+                                 float mnz, float cell, int nx, int ny, int nz, int slab, uint8_t* out) {
+  const int64_t total = static_cast<int64_t>(nx) * ny * nz;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int ix = static_cast<int>(i % nx);
+    const int iy = static_cast<int>((i / nx) % ny);
+    const int iz = static_cast<int>(i / (static_cast<int64_t>(nx) * ny));
+    const float cx = mnx + (ix + 0.5f) * cell, cy = mny + (iy + 0.5f) * cell, cz = mnz + (iz + 0.5f) * cell;
+    const int nsamp = slab ? 13 : 1;
+    bool solid = false;
+    for (int s = 0; s < nsamp && !solid; ++s) {
+      float x = cx, y = cy, z = cz;
+      if (s > 0) {
+        const int axis = (s - 1) >> 2, which = (s - 1) & 3;
+        const float off = (which < 2 ? which - 2 : which - 1) * 0.25f * cell;   // -2,-1,+1,+2 quarters
+        if (axis == 0) x += off; else if (axis == 1) y += off; else z += off;
+      }
+      const int c = tree_contents(t, world_head, x, y, z);
+      if (c == kSolid || c == kSky) { solid = true; break; }
+      for (int e = 0; e < n_ents; ++e) {
+        const SolidEnt& se = ents[e];
+        if (x < se.lo[0] || x > se.hi[0] || y < se.lo[1] || y > se.hi[1] || z < se.lo[2] || z > se.hi[2]) continue;
+        if (tree_contents(t, se.head, x - se.ox, y - se.oy, z - se.oz) == kSolid) { solid = true; break; }
+      }
+    }
+    out[i] = solid ? 1 : 0;
+  }
+}
+
+constexpr int kMaxLine = 8192;
+constexpr float kInf = 1e20f;
+constexpr int kEdtBlocks = 148 * 4, kEdtThreads = 64;   // fixed grid: workspace is per thread
+
+// Per-thread workspace of one line transform.
+struct LineWs { int* v; float* zb; float* tmp; };
+
+__device__ __forceinline__ LineWs line_ws(int* base, int maxn) {
+  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  int* p = base + tid * static_cast<int64_t>(3 * maxn + 8);
+  return LineWs{p, reinterpret_cast<float*>(p + maxn + 2), reinterpret_cast<float*>(p + 2 * maxn + 5)};
+}
+
+// 1-D squared distance transform of one line: f[q] (squared distances in
+// voxel units, 0 = solid site, kInf = no site) -> out[q * stride], with a
+// solid site just outside each end of the line.
+template <typename F, typename Out>
+__device__ void edt_line(F fval_in, Out* out, int64_t stride, int n, LineWs ws) {
+  int* v = ws.v;
+  float* zb = ws.zb;
+  auto fval = [&](int q) -> float { return (q < 0 || q >= n) ? 0.0f : fval_in(q); };
+  int k = 0;
+  v[0] = -1;
+  zb[0] = -kInf;
+  zb[1] = kInf;
+  for (int q = 0; q <= n; ++q) {
+    const float fq = fval(q);
+    if (fq >= kInf) continue;
+    float s;
+    for (;;) {
+      const int p = v[k];
+      const float fp = fval(p);
+      s = ((fq + static_cast<float>(q) * q) - (fp + static_cast<float>(p) * p)) / (2.0f * static_cast<float>(q - p));
+      if (s <= zb[k] && k > 0) { --k; continue; }
+      break;
+    }
+    if (s <= zb[k]) k = -1;          // k == 0 and the new parabola dominates everywhere
+    ++k;
+    v[k] = q;
+    zb[k] = (k == 0) ? -kInf : s;
+    zb[k + 1] = kInf;
+  }
+  k = 0;
+  for (int q = 0; q < n; ++q) {
+    while (zb[k + 1] < static_cast<float>(q)) ++k;
+    const int p = v[k];
+    const float d = static_cast<float>(q - p);
+    out[q * stride] = d * d + fval(p);
+  }
+}
+
+// pass over x lines: occupancy -> squared distance along x
+__global__ void __launch_bounds__(kEdtThreads) edt_x_kernel(const uint8_t* occ, float* d2, int nx, int ny, int nz,
+                                                             int* ws, int maxn) {
+  const LineWs w = line_ws(ws, maxn);
+  const int64_t lines = static_cast<int64_t>(ny) * nz;
+  for (int64_t l = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; l < lines;
+       l += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint8_t* in = occ + l * nx;
+    for (int q = 0; q < nx; ++q) w.tmp[q] = in[q] ? 0.0f : kInf;
+    edt_line([&](int q) { return w.tmp[q]; }, d2 + l * nx, 1, nx, w);
+  }
+}
+
+// pass over y (axis=1) or z (axis=2) lines, in place
+__global__ void __launch_bounds__(kEdtThreads) edt_yz_kernel(float* d2, int nx, int ny, int nz, int axis, int* ws,
+                                                              int maxn) {
+  const LineWs w = line_ws(ws, maxn);
+  const int n = axis == 1 ? ny : nz;
+  const int64_t stride = axis == 1 ? nx : static_cast<int64_t>(nx) * ny;
+  const int64_t lines = static_cast<int64_t>(nx) * (axis == 1 ? nz : ny);
+  for (int64_t l = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; l < lines;
+       l += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int ix = static_cast<int>(l % nx);
+    const int64_t other = l / nx;
+    const int64_t base = axis == 1 ? (other * static_cast<int64_t>(ny) * nx + ix) : (other * nx + ix);
+    for (int q = 0; q < n; ++q) w.tmp[q] = d2[base + q * stride];
+    edt_line([&](int q) { return w.tmp[q]; }, d2 + base, stride, n, w);
+  }
+}
+
+__global__ void finish_kernel(const float* d2, float cell, int64_t total, float* out_f32, __half* out_f16) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float d = sqrtf(d2[i]) * cell;
+    if (out_f32) out_f32[i] = d;
+    if (out_f16) out_f16[i] = __float2half_rn(fminf(d, 65504.0f));
+  }
+}
+
+int grid_blocks(int64_t work, int threads) {
+  int64_t b = surfk::ceil_div(work, threads);
+  return static_cast<int>(b < 148 * 32 ? (b < 1 ? 1 : b) : 148 * 32);
+}
+
+}  // namespace
+
+// Occupancy of an nx*ny*nz grid of `cell` voxels starting at mins (voxel
+// centres at mins + (i + 0.5) * cell). ents: n_ents records of 10 floats
+// (head as float bits, origin xyz, absmin xyz, absmax xyz) for solid brush
+// entities. slab != 0 adds the 12 shifted samples per voxel.
+SURF_EXPORT int surf_occupancy(const float* planes4, const int* ptype, const int* nodes3, int world_head,
+                               const void* ents, int n_ents, float mnx, float mny, float mnz, float cell, int nx,
+                               int ny, int nz, int slab, uint8_t* out, void* stream) {
+  TreeView t{reinterpret_cast<const float4*>(planes4), ptype, reinterpret_cast<const int3*>(nodes3)};
+  const int64_t total = static_cast<int64_t>(nx) * ny * nz;
+  occupancy_kernel<<<grid_blocks(total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      t, world_head, static_cast<const SolidEnt*>(ents), n_ents, mnx, mny, mnz, cell, nx, ny, nz, slab, out);
+  SURF_RETURN_LAUNCH();
+}
+
+SURF_EXPORT int64_t surf_edt_workspace_bytes(int nx, int ny, int nz) {
+  int maxn = nx > ny ? nx : ny;
+  maxn = maxn > nz ? maxn : nz;
+  return static_cast<int64_t>(kEdtBlocks) * kEdtThreads * (3 * maxn + 8) * 4;
+}
+
+// Exact EDT of the free space of `occ` (uint8, [nz][ny][nx]), distances in
+// map units (voxel distance * cell). d2: float workspace of nx*ny*nz
+// elements; ws: surf_edt_workspace_bytes bytes. Outputs (either may be
+// null): float32 linear, fp16 linear.
+SURF_EXPORT int surf_edt(const uint8_t* occ, int nx, int ny, int nz, float cell, float* d2, void* ws,
+                         float* out_f32, void* out_f16, void* stream) {
+  if (nx > kMaxLine || ny > kMaxLine || nz > kMaxLine) return static_cast<int>(cudaErrorInvalidValue);
+  int maxn = nx > ny ? nx : ny;
+  maxn = maxn > nz ? maxn : nz;
+  auto s = static_cast<cudaStream_t>(stream);
+  int* w = static_cast<int*>(ws);
+  edt_x_kernel<<<kEdtBlocks, kEdtThreads, 0, s>>>(occ, d2, nx, ny, nz, w, maxn);
+  edt_yz_kernel<<<kEdtBlocks, kEdtThreads, 0, s>>>(d2, nx, ny, nz, 1, w, maxn);
+  edt_yz_kernel<<<kEdtBlocks, kEdtThreads, 0, s>>>(d2, nx, ny, nz, 2, w, maxn);
+  const int64_t total = static_cast<int64_t>(nx) * ny * nz;
+  finish_kernel<<<grid_blocks(total, 256), 256, 0, s>>>(d2, cell, total, out_f32, static_cast<__half*>(out_f16));
+  SURF_RETURN_LAUNCH();
+}

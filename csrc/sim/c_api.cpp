@@ -82,11 +82,11 @@ SURFSIM_API void surfsim_step(void* h, const int32_t* actions, float* obs, float
   ENV(h)->step(actions, obs, rewards, done, trunc, terminal_obs);
 }
 // Fused K-tick step; every output is a strided float row target (ptr may be null).
-SURFSIM_API void surfsim_step_k(void* h, const int32_t* actions, int32_t action_stride, const float* yaw_cont,
-                                int32_t yaw_stride, const uint8_t* fail_mask, int32_t k, float* obs, int64_t obs_stride,
-                                float* term_obs, int64_t term_obs_stride, float* rec, int64_t rec_stride, float* term_rec,
+SURFSIM_API void surfsim_step_k(void* h, const int32_t* actions, int32_t action_stride, int32_t yaw_slot,
+                                int32_t fail_slot, int32_t k, float* obs, int64_t obs_stride, float* term_obs,
+                                int64_t term_obs_stride, float* rec, int64_t rec_stride, float* term_rec,
                                 int64_t term_rec_stride) {
-  ENV(h)->step_k(actions, action_stride, yaw_cont, yaw_stride, fail_mask, k, RowOut{obs, obs_stride},
+  ENV(h)->step_k(actions, action_stride, yaw_slot, fail_slot, k, RowOut{obs, obs_stride},
                  RowOut{term_obs, term_obs_stride}, RowOut{rec, rec_stride}, RowOut{term_rec, term_rec_stride});
 }
 SURFSIM_API PlayerState* surfsim_states_ptr(void* h) { return ENV(h)->states(); }
@@ -171,6 +171,21 @@ SURFSIM_API void surfsim_export_hull0(void* h, float* planes4, int32_t* ptype, i
     nodes3[3 * i + 2] = m.hull0[i].child[1];
   }
   *headnode = m.models[0].headnode[0];
+}
+// Solid brush entities for GPU occupancy: per entity 10 floats = hull-0 head
+// node (int32 bits), origin xyz, absmin xyz, absmax xyz. Returns the count.
+SURFSIM_API int32_t surfsim_solid_entities(void* h, float* out10, int32_t cap) {
+  const Map& m = MAP(h);
+  int32_t n = static_cast<int32_t>(m.solids.size());
+  for (int32_t i = 0; i < n && i < cap; ++i) {
+    const BrushEntity& s = m.solids[static_cast<size_t>(i)];
+    int32_t head = m.models[static_cast<size_t>(s.model)].headnode[0];
+    std::memcpy(out10 + 10 * i, &head, 4);
+    std::memcpy(out10 + 10 * i + 1, s.origin, 12);
+    std::memcpy(out10 + 10 * i + 4, s.absmin, 12);
+    std::memcpy(out10 + 10 * i + 7, s.absmax, 12);
+  }
+  return n;
 }
 // Trigger list: kind, model, has_dest, and bounds (for kill-zone masking).
 SURFSIM_API int32_t surfsim_triggers(void* h, int32_t* kinds, float* bounds6, float* damage, int32_t cap) {

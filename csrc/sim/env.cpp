@@ -472,8 +472,8 @@ void EnvBatch::step(const int32_t* actions, float* obs, float* rewards, uint8_t*
   });
 }
 
-void EnvBatch::step_k(const int32_t* actions, int action_stride, const float* yaw_cont, int yaw_stride,
-                      const uint8_t* fail_mask, int k, RowOut obs, RowOut term_obs, RowOut rec, RowOut term_rec) {
+void EnvBatch::step_k(const int32_t* actions, int action_stride, int yaw_slot, int fail_slot, int k, RowOut obs,
+                      RowOut term_obs, RowOut rec, RowOut term_rec) {
   if (k < 1) k = 1;
   pool_->run(cfg_.num_envs, [&](int b, int e) {
     for (int i = b; i < e; ++i) {
@@ -485,16 +485,16 @@ void EnvBatch::step_k(const int32_t* actions, int action_stride, const float* ya
       int buttons = (a[4] ? kInJump : 0) | (a[5] ? kInDuck : 0);
       int yb = a[0] < 0 ? 0 : (a[0] > 14 ? 14 : a[0]);
       float yc = 0.f;
-      if (yaw_cont) {
-        yc = yaw_cont[static_cast<size_t>(i) * static_cast<size_t>(yaw_stride)];
+      if (yaw_slot >= 0) {
+        std::memcpy(&yc, &a[yaw_slot], sizeof yc);
         yc = yc > 1.f ? 1.f : (yc < -1.f ? -1.f : yc);
         if (yc != yc) yc = 0.f;
       }
-      bool forced = fail_mask && fail_mask[i];
+      bool forced = fail_slot >= 0 && a[fail_slot] != 0;
       float rsum = 0;
       bool done = false, trunc = false, goal = false;
       for (int j = 0; j < k; ++j) {
-        float yd = yaw_cont ? yc * cfg_.yaw_rate_max_deg : yaw_delta(st_[static_cast<size_t>(i)], yb);
+        float yd = yaw_slot >= 0 ? yc * cfg_.yaw_rate_max_deg : yaw_delta(st_[static_cast<size_t>(i)], yb);
         float* orow = (j == k - 1 && obs.ptr) ? obs.row(i) : nullptr;
         TickOut t = tick_env(i, yd, pd, fm, sm, buttons, forced && j == 0, orow,
                              term_obs.ptr ? term_obs.row(i) : nullptr, term_rec.ptr ? term_rec.row(i) : nullptr);

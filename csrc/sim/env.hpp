@@ -75,11 +75,12 @@ class EnvBatch {
   void reset_all(uint64_t seed, float* obs);
   // One tick for every env (reference-compatible contract).
   void step(const int32_t* actions, float* obs, float* rewards, uint8_t* done, uint8_t* trunc, float* terminal_obs);
-  // K ticks of action repeat. actions: int32 [N, action_stride] (first 6 used);
-  // yaw_cont: optional float [N] in [-1, 1] replacing the yaw bin;
-  // fail_mask: optional uint8 [N] stall kills applied on the first tick.
-  void step_k(const int32_t* actions, int action_stride, const float* yaw_cont, int yaw_stride,
-              const uint8_t* fail_mask, int k, RowOut obs, RowOut term_obs, RowOut rec, RowOut term_rec);
+  // K ticks of action repeat. actions: int32 rows of `action_stride` (slots
+  // 0..5 the discrete action); yaw_slot >= 0: that slot holds a float in
+  // [-1, 1] (bit pattern) replacing the yaw bin; fail_slot >= 0: a non-zero
+  // value there force-fails the env on the first tick (stall kill).
+  void step_k(const int32_t* actions, int action_stride, int yaw_slot, int fail_slot, int k, RowOut obs,
+              RowOut term_obs, RowOut rec, RowOut term_rec);
 
   PlayerState* states() { return st_.data(); }
   void set_state(int env, const PlayerState& s);

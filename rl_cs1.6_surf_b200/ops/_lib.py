@@ -1,0 +1,75 @@
+"""ctypes bindings of the CUDA kernel libraries.
+
+Every entry point takes raw device pointers and the CUDA stream to launch on
+(the caller's current torch stream), so the kernels compose with torch
+tensors and can be captured in CUDA graphs. A non-zero return value is a CUDA
+error code and raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_float, c_int, c_int64, c_void_p
+
+import torch
+
+from .._native import load
+
+_V = c_void_p
+_I = c_int
+_L = c_int64
+_F = c_float
+
+_SIGS = {
+    "libsurf_vision.so": {
+        "surf_march": (_I, [_V, _L, _I, _I, _I, _V, _I, _I, _I, _F, _F, _F, _F, _V, _V, _F, _F, _I, _I, _V, _L, _I,
+                            _I, _V, _V, _I, _V]),
+        "surf_brick_size": (_L, [_I, _I, _I]),
+        "surf_brick_sdf": (_I, [_V, _I, _V, _I, _I, _I, _V]),
+        "surf_brick_i8": (_I, [_V, _V, _I, _I, _I, _V]),
+        "surf_occupancy": (_I, [_V, _V, _V, _I, _V, _I, _F, _F, _F, _F, _I, _I, _I, _I, _V, _V]),
+        "surf_edt_workspace_bytes": (_L, [_I, _I, _I]),
+        "surf_edt": (_I, [_V, _I, _I, _I, _F, _V, _V, _V, _V, _V]),
+    },
+}
+
+
+class KernelError(RuntimeError):
+    pass
+
+
+_bound: dict = {}
+
+
+def lib(name: str) -> ctypes.CDLL:
+    if name in _bound:
+        return _bound[name]
+    l = load(name)
+    for fn, (res, args) in _SIGS.get(name, {}).items():
+        f = getattr(l, fn)
+        f.restype = res
+        f.argtypes = args
+    _bound[name] = l
+    return l
+
+
+def register(name: str, sigs: dict) -> None:
+    _SIGS.setdefault(name, {}).update(sigs)
+    _bound.pop(name, None)
+
+
+def stream_ptr(device=None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t) -> int:
+    return 0 if t is None else int(t.data_ptr())
+
+
+def check(code: int, what: str) -> None:
+    if code != 0:
+        raise KernelError(f"{what} failed with CUDA error {code}")
+
+
+def require_cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise KernelError(f"{what}: the CUDA kernel needs CUDA tensors (use the *_reference CPU oracle on CPU)")

@@ -176,7 +176,7 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
         "surfsim_force_fail": (None, [c_void_p, _P_U8]),
         "surfsim_reset_all": (None, [c_void_p, c_uint64, _P_F]),
         "surfsim_step": (None, [c_void_p, _P_I, _P_F, _P_F, _P_U8, _P_U8, _P_F]),
-        "surfsim_step_k": (None, [c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_void_p, c_int32,
+        "surfsim_step_k": (None, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
                                   c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64]),
         "surfsim_states_ptr": (c_void_p, [c_void_p]),
         "surfsim_get_states": (None, [c_void_p, c_void_p]),
@@ -193,6 +193,7 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
         "surfsim_map_bounds": (None, [c_void_p, _P_F, _P_F]),
         "surfsim_map_counts": (None, [c_void_p, _P_I]),
         "surfsim_export_hull0": (None, [c_void_p, c_void_p, c_void_p, c_void_p, _P_I]),
+        "surfsim_solid_entities": (c_int32, [c_void_p, c_void_p, c_int32]),
         "surfsim_triggers": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32]),
         "surfsim_trigger_contains": (None, [c_void_p, c_int32, c_void_p, c_int64, c_int32, c_void_p]),
         "surfsim_compile_bsp": (c_int64, [c_void_p, c_int64, c_char_p, c_void_p, c_int64, c_char_p, c_int32]),
@@ -311,14 +312,16 @@ class SimCore:
                               self._done.ctypes.data_as(_P_U8), self._trunc.ctypes.data_as(_P_U8), _fptr(self._term))
         return self._obs, self._rew, self._done, self._trunc, self._term
 
-    def step_k(self, actions_ptr: int, action_stride: int, k: int, *, yaw_ptr: int = 0, yaw_stride: int = 1,
-               fail_ptr: int = 0, obs: tuple = (0, 0), term_obs: tuple = (0, 0), rec: tuple = (0, 0),
-               term_rec: tuple = (0, 0)) -> None:
+    def step_k(self, actions_ptr: int, action_stride: int, k: int, *, yaw_slot: int = -1, fail_slot: int = -1,
+               obs: tuple = (0, 0), term_obs: tuple = (0, 0), rec: tuple = (0, 0), term_rec: tuple = (0, 0)) -> None:
         """K ticks of action repeat over raw host pointers (int addresses, e.g.
-        ``tensor.data_ptr()`` of pinned tensors). ``obs``/``term_obs``/``rec``/
-        ``term_rec`` are (pointer, row stride in floats) pairs; 0 skips one."""
-        self.lib.surfsim_step_k(self._h, c_void_p(actions_ptr), int(action_stride), c_void_p(yaw_ptr or None),
-                                int(yaw_stride), c_void_p(fail_ptr or None), int(k),
+        ``tensor.data_ptr()`` of pinned tensors). Action rows are int32 of
+        ``action_stride``; ``yaw_slot`` names a slot holding a continuous yaw
+        (float bits in [-1, 1]) and ``fail_slot`` one holding a force-fail
+        flag (-1 = unused). ``obs``/``term_obs``/``rec``/``term_rec`` are
+        (pointer, row stride in floats) pairs; 0 skips one."""
+        self.lib.surfsim_step_k(self._h, c_void_p(actions_ptr), int(action_stride), int(yaw_slot), int(fail_slot),
+                                int(k),
                                 c_void_p(obs[0] or None), int(obs[1]), c_void_p(term_obs[0] or None), int(term_obs[1]),
                                 c_void_p(rec[0] or None), int(rec[1]), c_void_p(term_rec[0] or None), int(term_rec[1]))
 
@@ -326,15 +329,18 @@ class SimCore:
                      fail: Optional[np.ndarray] = None):
         """Convenience step_k on numpy arrays: returns (obs, term_obs, rec, term_rec)."""
         n = self.num_envs
-        actions = np.ascontiguousarray(actions, np.int32)
+        rows = np.zeros((n, 8), np.int32)
+        rows[:, :6] = np.asarray(actions, np.int32)[:, :6]
+        if yaw is not None:
+            rows[:, 6] = np.ascontiguousarray(yaw, np.float32).view(np.int32)
+        if fail is not None:
+            rows[:, 7] = np.asarray(fail, np.int32)
         obs = np.zeros((n, self.obs_dim), np.float32)
         tob = np.zeros((n, self.obs_dim), np.float32)
         rec = np.zeros((n, REC_COLS), np.float32)
         trec = np.zeros((n, TERM_COLS), np.float32)
-        y = None if yaw is None else np.ascontiguousarray(yaw, np.float32)
-        f = None if fail is None else np.ascontiguousarray(fail, np.uint8)
-        self.step_k(actions.ctypes.data, actions.shape[1], k, yaw_ptr=0 if y is None else y.ctypes.data,
-                    fail_ptr=0 if f is None else f.ctypes.data, obs=(obs.ctypes.data, self.obs_dim),
+        self.step_k(rows.ctypes.data, 8, k, yaw_slot=6 if yaw is not None else -1,
+                    fail_slot=7 if fail is not None else -1, obs=(obs.ctypes.data, self.obs_dim),
                     term_obs=(tob.ctypes.data, self.obs_dim), rec=(rec.ctypes.data, REC_COLS),
                     term_rec=(trec.ctypes.data, TERM_COLS))
         return obs, tob, rec, trec
@@ -439,6 +445,14 @@ class SimCore:
         self.lib.surfsim_export_hull0(self._h, c_void_p(planes.ctypes.data), c_void_p(types.ctypes.data),
                                       c_void_p(nodes.ctypes.data), ctypes.byref(head))
         return planes, types, nodes, int(head.value)
+
+    def solid_entities(self) -> np.ndarray:
+        """(n, 10) float32 rows: hull-0 head node (int32 bits), origin, absmin, absmax."""
+        n = self.map_counts()["solids"]
+        out = np.zeros((n, 10), np.float32)
+        if n:
+            self.lib.surfsim_solid_entities(self._h, c_void_p(out.ctypes.data), n)
+        return out
 
     def triggers(self):
         n = self.map_counts()["triggers"]
