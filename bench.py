@@ -1,0 +1,181 @@
+"""Headline benchmark: end-to-end vision-PPO throughput (physics ticks / s).
+
+One step = one PPO iteration of the benchmark configuration (per GPU: 2048
+envs x 128 decisions x 3 ticks = 786,432 physics ticks of rollout, GAE, and
+4 epochs x 8 minibatches of updates). Weak scaling: every rank runs 2048
+envs, data parallel over NVLink. The value is the whole-job aggregate.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 launch with torchrun (one rank per GPU). Timing: W untimed
+iterations, then exactly K iterations bracketed by a barrier and a device
+synchronize on both sides, measured with CUDA events on the training stream;
+the job time is the max over ranks. Rollout buffers (~4.3 GB of depth
+images per GPU) exceed L2, so no flush is needed between iterations.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+BASELINE_TICKS_PER_S = 281482.0          # reference, 1x RTX 5090 (BASELINE.md main table)
+METRIC = "vision-PPO env-steps/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--envs", type=int, default=2048)
+    ap.add_argument("--comm", choices=["p2p", "nccl"], default="p2p")
+    ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--json", default=None)
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def start(self):
+        def run():
+            q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap")
+            while not self._stop.is_set():
+                try:
+                    out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                         timeout=5).stdout.strip()
+                    if out:
+                        self.samples.append([x.strip() for x in out.split(",")])
+                except Exception:
+                    pass
+                self._stop.wait(0.2)
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+
+    def stop(self) -> dict:
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=6)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit())
+        mx = max(float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[4 + i].strip().lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def run_ours(args) -> None:
+    import torch
+    import surfb200  # noqa: F401
+    from surfb200.trainer.config import bench_config
+    from surfb200.trainer.ppo import Trainer
+    from surfb200.ops import _lib as L
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    comm = None
+    if world > 1:
+        from surfb200.parallel.dist import init_process_group, make_comm
+        init_process_group()
+        comm = make_comm(args.comm)
+    cfg = bench_config(args.envs)
+    cfg.graphs = not args.no_graphs
+    cfg.seed = 0
+    tr = Trainer(cfg, rank=rank, world=world, comm=comm, verbose=(rank == 0))
+    for _ in range(args.warmup):
+        tr.train_iteration()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    if comm is not None:
+        comm.barrier()
+    torch.cuda.synchronize()
+    launches0 = L.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    e0.record()
+    for _ in range(args.steps):
+        stats = tr.train_iteration()
+    e1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - w0
+    if comm is not None:
+        comm.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    launches = L.launch_count() - launches0
+    if comm is not None:
+        ms = comm.max_scalar(ms)
+        wall = comm.max_scalar(wall)
+    ticks_per_iter = cfg.envs * cfg.n_steps * cfg.act_every * world
+    value = ticks_per_iter * args.steps / (ms / 1e3)
+    # end-to-end through the public API: the same iterations, wall clock incl.
+    # every host<->device copy of the step (env records in, actions out, stats out)
+    h2d = (cfg.n_steps + 1) * cfg.envs * 64 * 4
+    d2h = cfg.n_steps * cfg.envs * 8 * 4 + 6 * 4 + 8 * 4
+    e2e = ticks_per_iter * args.steps / wall
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": round(value, 1), "unit": "ticks/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": round(value / BASELINE_TICKS_PER_S, 3), "dtype": "bf16",
+            "data": "synthetic (seeded procedural BSP map, random-init weights)",
+            "config": {"model": "nature-cnn-128x64+proprio256 vision PPO", "global_batch": cfg.envs * world,
+                       "seq_len": cfg.n_steps, "parallelism": f"dp{world}", "envs_per_gpu": cfg.envs,
+                       "act_every": cfg.act_every, "epochs": cfg.epochs, "minibatches": cfg.minibatches,
+                       "map": "procedural random field, 512 brushes, 16u SDF 1024x1024x256",
+                       "comm": args.comm if world > 1 else "none", "cuda_graphs": cfg.graphs,
+                       "l2": "inputs larger than L2 (4.3 GB rollout images per GPU)"},
+            "clocks": clocks,
+            "e2e": {"value": round(e2e, 1), "unit": "ticks/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches,
+            "last_iteration": {k: v for k, v in stats.items() if k != "timing"},
+        }
+        line = json.dumps(out)
+        print(line, flush=True)
+        if args.json:
+            Path(args.json).write_text(line)
+    if comm is not None:
+        comm.close()
+
+
+def run_reference(args) -> None:
+    from surfb200.baseline_ref import run_reference_bench
+    run_reference_bench(args)
+
+
+if __name__ == "__main__":
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)

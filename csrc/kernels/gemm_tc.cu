@@ -175,13 +175,74 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 
-__device__ __forceinline__ float apply_act(int act, float x, float aux) {
-  switch (act) {
-    case kRelu: return fmaxf(x, 0.0f);
-    case kTanh: return tanhf(x);
-    case kReluGrad: return aux > 0.0f ? x : 0.0f;
-    case kTanhGrad: return x * (1.0f - aux * aux);
-    default: return x;
+// tanh(x) = 1 - 2 / (exp(2x) + 1), with exp from the fast intrinsic; |x| > 9
+// saturates (the bf16 outputs cannot tell the difference).
+__device__ __forceinline__ float tanh_fast(float x) {
+  const float c = fminf(fmaxf(x, -9.0f), 9.0f);
+  return 1.0f - 2.0f / (__expf(2.0f * c) + 1.0f);
+}
+
+// Bias + activation (or activation derivative) for a 32-column chunk of one
+// row. The activation is chosen once per chunk (act_split is a multiple of
+// 32), bias and the saved activation are loaded with vector loads, and each
+// activation has its own tight loop.
+__device__ __forceinline__ void process_chunk32(const Epilogue& ep, float* v, int row, bool row_ok, int col0, int N) {
+  const bool full = col0 + 32 <= N;
+  if (ep.bias) {
+    if (full) {
+      const float4* b4 = reinterpret_cast<const float4*>(ep.bias + col0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 b = __ldg(b4 + i);
+        v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < N) v[i] += __ldg(ep.bias + col0 + i);
+    }
+  }
+  const int act = col0 < ep.act_split ? ep.act : ep.act2;
+  if (act == kNone) return;
+  if (act == kRelu) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.0f);
+    return;
+  }
+  if (act == kTanh) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = tanh_fast(v[i]);
+    return;
+  }
+  // derivative modes: aux = saved bf16 activation of this row
+  float a[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) a[i] = 0.0f;
+  if (row_ok) {
+    const uint16_t* src = ep.aux + row * ep.ld_aux + col0;
+    if (full && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 w = *reinterpret_cast<const uint4*>(src + 8 * q);
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          a[8 * q + 2 * k] = __uint_as_float(ww[k] << 16);
+          a[8 * q + 2 * k + 1] = __uint_as_float(ww[k] & 0xFFFF0000u);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < N) a[i] = surfk::bf16_to_f32(src[i]);
+    }
+  }
+  if (act == kReluGrad) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = a[i] > 0.0f ? v[i] : 0.0f;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = v[i] * (1.0f - a[i] * a[i]);
   }
 }
 
@@ -225,52 +286,42 @@ struct Sched {             // static persistent schedule over (m block, n block,
   __device__ int count() const { return mt * nt * splits; }
 };
 
-__device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, float* v, int row, bool row_ok, int col0, int N) {
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int col = col0 + i;
-    if (col >= N) break;
-    float x = v[i];
-    if (ep.bias) x += ep.bias[col];
-    const int act = col < ep.act_split ? ep.act : ep.act2;
-    float aux = 0.0f;
-    if ((act == kReluGrad || act == kTanhGrad) && row_ok) aux = surfk::bf16_to_f32(ep.aux[row * ep.ld_aux + col]);
-    v[i] = apply_act(act, x, aux);
-  }
-  if (ep.ct && row_ok) {
-    // transposed store: for a fixed column the warp's 32 lanes write 32 consecutive rows
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int col = col0 + i;
-      if (col < N) {
-        if (ep.ct_dtype == 1) static_cast<uint16_t*>(ep.ct)[col * ep.ldct + row] = surfk::f32_to_bf16(v[i]);
-        else static_cast<float*>(ep.ct)[col * ep.ldct + row] = v[i];
-      }
+// Register-path stores of a processed 32-column chunk (transposed output,
+// fp32 atomics, or rows that TMA cannot address).
+__device__ __forceinline__ void store_chunk32(const Epilogue& ep, const float* v, int row, bool row_ok, int col0, int N) {
+  if (!row_ok) return;
+  const int ncol = min(32, N - col0);
+  if (ep.ct) {
+    // for a fixed column the warp's 32 lanes write 32 consecutive rows
+    for (int i = 0; i < ncol; ++i) {
+      if (ep.ct_dtype == 1) static_cast<uint16_t*>(ep.ct)[(col0 + i) * ep.ldct + row] = surfk::f32_to_bf16(v[i]);
+      else static_cast<float*>(ep.ct)[(col0 + i) * ep.ldct + row] = v[i];
     }
   }
-  if (!ep.c || !row_ok) return;
-  const int ncol = min(16, N - col0);
+  if (!ep.c) return;
   if (ep.c_mode == kAtomic) {
     float* dst = static_cast<float*>(ep.c) + row * ep.ldc + col0;
     for (int i = 0; i < ncol; ++i) atomicAdd(dst + i, v[i]);
   } else if (ep.c_dtype == 1) {
     uint16_t* dst = static_cast<uint16_t*>(ep.c) + row * ep.ldc + col0;
-    if (ncol == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-      uint32_t w[8];
+    if (ncol == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        w[i] = static_cast<uint32_t>(surfk::f32_to_bf16(v[2 * i])) |
-               (static_cast<uint32_t>(surfk::f32_to_bf16(v[2 * i + 1])) << 16);
-      reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-      reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      for (int q = 0; q < 4; ++q) {
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          w[k] = static_cast<uint32_t>(surfk::f32_to_bf16(v[8 * q + 2 * k])) |
+                 (static_cast<uint32_t>(surfk::f32_to_bf16(v[8 * q + 2 * k + 1])) << 16);
+        reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
     } else {
       for (int i = 0; i < ncol; ++i) dst[i] = surfk::f32_to_bf16(v[i]);
     }
   } else {
     float* dst = static_cast<float*>(ep.c) + row * ep.ldc + col0;
-    if (ncol == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    if (ncol == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      for (int i = 0; i < 8; ++i) reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     } else {
       for (int i = 0; i < ncol; ++i) dst[i] = v[i];
     }
@@ -409,17 +460,7 @@ __global__ void __launch_bounds__(192, 1)
           if (n0 + c0 >= N) break;
           float v[32];
           tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + c0, v);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = n0 + c0 + i;
-            float x = v[i];
-            if (ep.bias && col < N) x += ep.bias[col];
-            const int act = col < ep.act_split ? ep.act : ep.act2;
-            float aux = 0.0f;
-            if ((act == kReluGrad || act == kTanhGrad) && row_ok && col < N)
-              aux = surfk::bf16_to_f32(ep.aux[row * ep.ld_aux + col]);
-            v[i] = apply_act(act, x, aux);
-          }
+          process_chunk32(ep, v, row, row_ok, n0 + c0, N);
           const int sb = stage_ctr & 1;
           if (lane == 0 && stage_ctr >= 2) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
           __syncwarp();
@@ -452,10 +493,12 @@ __global__ void __launch_bounds__(192, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          float v[16];
-          tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + c0, v);
-          if (n0 + c0 < N) epilogue_chunk(ep, v, row, row_ok, n0 + c0, N);
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          if (n0 + c0 >= N) break;
+          float v[32];
+          tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + c0, v);
+          process_chunk32(ep, v, row, row_ok, n0 + c0, N);
+          store_chunk32(ep, v, row, row_ok, n0 + c0, N);
         }
       }
       fence_before();
@@ -569,6 +612,7 @@ SURF_EXPORT int surf_gemm_bf16(const void* A, int64_t lda, int a_mn, const void*
   if ((lda & 7) || (ldb & 7)) return static_cast<int>(cudaErrorInvalidValue);
   if (splits > 1 && ep->c_mode != kAtomic) return static_cast<int>(cudaErrorInvalidValue);
   if (b_mn && bn < 64) return static_cast<int>(cudaErrorInvalidValue);
+  if (ep->act_split < N && (ep->act_split & 31)) return static_cast<int>(cudaErrorInvalidValue);
   auto s = static_cast<cudaStream_t>(stream);
   switch (bn) {
     case 32: return dispatch_major<32>(A, lda, a_mn, B, ldb, b_mn, M, N, K, *ep, splits, s);

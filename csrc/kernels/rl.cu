@@ -70,11 +70,15 @@ __device__ __forceinline__ float warp_sum(float v) {
 // ---- sampling ----------------------------------------------------------------
 template <typename T>
 __global__ void sample_kernel(const T* logits, int64_t ld_logits, HeadSpec hs, const float* log_std, int n,
-                              uint64_t seed, uint64_t counter, int greedy, int32_t* act, int64_t ld_act, float* logp_out,
-                              float* value_src, int64_t ld_value, float* value_out, const uint8_t* fail_src) {
+                              uint64_t seed, uint64_t counter0, const int64_t* counter_ptr, int greedy, int32_t* act,
+                              int64_t ld_act, float* logp_out, float* value_src, int64_t ld_value, float* value_out,
+                              const uint8_t* fail_src) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= n) return;
+  // decision counter: a device value (advanced by the trainer, so captured
+  // graphs draw fresh noise on every replay) plus this launch's offset
+  const uint64_t counter = counter0 + (counter_ptr ? static_cast<uint64_t>(*counter_ptr) : 0ull);
   const T* row = logits + warp * ld_logits;
   int32_t* out = act + warp * ld_act;
   float logp = 0.0f;
@@ -304,7 +308,8 @@ HeadSpec make_spec(const int* sizes, int n_heads, const int* slots, int cont, co
 // neutral[6]: value for each sim slot no head drives (-1 = a head drives it).
 SURF_EXPORT int surf_sample_heads(const void* logits, int logits_bf16, int64_t ld_logits, const int* sizes, int n_heads,
                                   const int* slots, int cont, const int* neutral, const float* log_std, int n,
-                                  uint64_t seed, uint64_t counter, int greedy, int32_t* act, int64_t ld_act,
+                                  uint64_t seed, uint64_t counter, const int64_t* counter_ptr, int greedy,
+                                  int32_t* act, int64_t ld_act,
                                   float* logp, const float* value_src, int64_t ld_value, float* value_out,
                                   const uint8_t* fail_src, void* stream) {
   if (n_heads > kMaxHeads) return static_cast<int>(cudaErrorInvalidValue);
@@ -315,11 +320,12 @@ SURF_EXPORT int surf_sample_heads(const void* logits, int logits_bf16, int64_t l
   auto s = static_cast<cudaStream_t>(stream);
   if (logits_bf16)
     sample_kernel<uint16_t><<<blocks, threads, 0, s>>>(static_cast<const uint16_t*>(logits), ld_logits, hs, log_std, n,
-                                                       seed, counter, greedy, act, ld_act, logp,
+                                                       seed, counter, counter_ptr, greedy, act, ld_act, logp,
                                                        const_cast<float*>(value_src), ld_value, value_out, fail_src);
   else
     sample_kernel<float><<<blocks, threads, 0, s>>>(static_cast<const float*>(logits), ld_logits, hs, log_std, n, seed,
-                                                    counter, greedy, act, ld_act, logp, const_cast<float*>(value_src),
+                                                    counter, counter_ptr, greedy, act, ld_act, logp,
+                                                    const_cast<float*>(value_src),
                                                     ld_value, value_out, fail_src);
   SURF_RETURN_LAUNCH();
 }
@@ -359,5 +365,13 @@ SURF_EXPORT int surf_ppo_loss(const void* logits, int logits_bf16, int64_t ld_lo
     ppo_loss_kernel<float><<<blocks, threads, 0, s>>>(static_cast<const float*>(logits), ld_logits, value, ld_value,
                                                       act, ld_act, old_logp, adv, ret, idx, moments, hs, log_std, la,
                                                       n, dlogits, ld_dlogits, dvalue, ld_dvalue, dlog_std, stats);
+  SURF_RETURN_LAUNCH();
+}
+
+__global__ void counter_add_kernel(int64_t* c, int64_t inc) { *c += inc; }
+
+// *counter += inc (stream-ordered; used to advance the sampling counter once per rollout)
+SURF_EXPORT int surf_counter_add(int64_t* counter, int64_t inc, void* stream) {
+  counter_add_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(counter, inc);
   SURF_RETURN_LAUNCH();
 }

@@ -65,9 +65,28 @@ def ptr(t) -> int:
     return 0 if t is None else int(t.data_ptr())
 
 
+# Kernel launches issued by each entry point (for launch accounting; entry
+# points not listed launch exactly one kernel).
+_KERNELS_PER_CALL = {"surf_reward": 2, "surf_permutation": 2, "surf_edt": 4, "surf_geodesic_pass": 3,
+                     "surf_geodesic_init": 3, "surf_geodesic_finish": 2}
+_launches = [0]
+
+
 def check(code: int, what: str) -> None:
+    """Raise on a non-zero CUDA status; count the entry point's launches."""
+    _launches[0] += _KERNELS_PER_CALL.get(what, 1)
     if code != 0:
         raise KernelError(f"{what} failed with CUDA error {code}")
+
+
+def launch_count() -> int:
+    """Kernels launched through this package so far (graph replays included
+    via ``add_launches``)."""
+    return _launches[0]
+
+
+def add_launches(n: int) -> None:
+    _launches[0] += int(n)
 
 
 def require_cuda(t: torch.Tensor, what: str) -> None:

@@ -26,8 +26,9 @@ RLIB = "libsurf_rl.so"
 NLIB = "libsurf_nn.so"
 _lib.register(RLIB, {
     "surf_sample_heads": (c_int, [c_void_p, c_int, c_int64, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
-                                  c_int, c_uint64, c_uint64, c_int, c_void_p, c_int64, c_void_p, c_void_p, c_int64,
-                                  c_void_p, c_void_p, c_void_p]),
+                                  c_int, c_uint64, c_uint64, c_void_p, c_int, c_void_p, c_int64, c_void_p, c_void_p,
+                                  c_int64, c_void_p, c_void_p, c_void_p]),
+    "surf_counter_add": (c_int, [c_void_p, c_int64, c_void_p]),
     "surf_gae": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_float, c_void_p, c_void_p,
                          c_void_p, c_void_p]),
     "surf_adv_moments": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p]),
@@ -59,15 +60,20 @@ class HeadArgs:
 def sample_heads(logits: torch.Tensor, heads: HeadArgs, log_std: torch.Tensor, act_out: torch.Tensor,
                  logp_out: Optional[torch.Tensor], seed: int, counter: int, greedy: bool = False,
                  value_src: Optional[torch.Tensor] = None, value_out: Optional[torch.Tensor] = None,
-                 fail_src: Optional[torch.Tensor] = None) -> None:
+                 fail_src: Optional[torch.Tensor] = None, counter_ptr: Optional[torch.Tensor] = None,
+                 counter_offset: int = 0) -> None:
     """Sample every head for each row of ``logits`` ([N, >=n_logits] fp32);
     writes the int32 action rows (``act_out`` [N, 8]) and summed log-probs;
-    optionally copies a strided value column to ``value_out``."""
+    optionally copies a strided value column to ``value_out`` and the stall
+    flags ``fail_src`` into action slot 7. The Philox counter is
+    ``counter + counter_offset`` (+ ``*counter_ptr`` when given, a device
+    int64 the trainer advances, so graph replays draw fresh noise)."""
     n = logits.shape[0]
     check(_lib.lib(RLIB).surf_sample_heads(
         ptr(logits), 1 if logits.dtype == torch.bfloat16 else 0, logits.stride(0), heads.host_ptr(heads.sizes),
         heads.n_heads, heads.host_ptr(heads.slots), heads.cont, heads.host_ptr(heads.neutral), ptr(log_std), n,
-        int(seed) & (2 ** 64 - 1), int(counter) & (2 ** 64 - 1), 1 if greedy else 0, ptr(act_out), act_out.stride(0),
+        int(seed) & (2 ** 64 - 1), (int(counter) + int(counter_offset)) & (2 ** 64 - 1), ptr(counter_ptr),
+        1 if greedy else 0, ptr(act_out), act_out.stride(0),
         ptr(logp_out), ptr(value_src), value_src.stride(0) if value_src is not None else 0, ptr(value_out),
         ptr(fail_src), stream_ptr(logits.device)), "surf_sample_heads")
 
@@ -116,6 +122,10 @@ def sample_reference(logits: torch.Tensor, layout, log_std: torch.Tensor, genera
     logp, _ = log_prob_reference(logits, act, layout, log_std)
     del NEUTRAL
     return act, logp
+
+
+def bump_counter(counter: torch.Tensor, inc: int) -> None:
+    check(_lib.lib(RLIB).surf_counter_add(ptr(counter), int(inc), stream_ptr(counter.device)), "surf_counter_add")
 
 
 # ---- GAE ----------------------------------------------------------------------------

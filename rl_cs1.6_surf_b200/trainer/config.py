@@ -1,0 +1,120 @@
+"""Run configuration (the self-describing part of every checkpoint).
+
+Mirrors the reference trainer's flag set (python/train_fast.py:694-993) for
+the features this framework implements; ``RUN_DEFINING`` lists the keys a
+bare ``--ckpt`` resume restores from the checkpoint unless the flag is given
+again on the command line (reference restore logic: train_fast.py:1009-1211).
+"""
+from __future__ import annotations
+
+from dataclasses import asdict, dataclass, field, fields
+from typing import Optional
+
+from ..rewards.spec import RewardSpec
+
+# keys restored from a checkpoint unless given on the command line
+RUN_DEFINING = (
+    "map", "map_seed", "ep_ticks", "n_steps", "act_every", "epochs", "minibatches", "lr", "gamma", "gae", "clip",
+    "ent", "ent_final", "vf", "max_grad_norm", "spawn", "teleport_fail", "yaw_jitter", "maxvel", "airaccelerate",
+    "vision", "lidar_w", "lidar_h", "lidar_range", "lidar_near", "lidar_cell", "pinhole", "march_steps",
+    "continuous_yaw", "gps", "heads", "hidden", "fc", "proprio", "mlp", "reward", "pitch_rate", "yaw_adaptive",
+    "respawn_frac", "respawn_margin", "respawn_reservoir", "train_stride",
+)
+
+
+@dataclass
+class TrainConfig:
+    # map / environment
+    map: str = "field"                 # procedural kind (ramps | field | race) or a .bsp path
+    map_seed: int = 0
+    envs: int = 2048                   # per rank
+    ep_ticks: int = 6000               # truncation (ticks)
+    spawn: str = "pool"                # pool (map's drop/start pool) | map (map spawn points)
+    teleport_fail: bool = True
+    yaw_jitter: float = 8.0
+    maxvel: float = 3500.0             # sv_maxvelocity (surf servers)
+    airaccelerate: float = 100.0
+    pitch_rate: float = 10.0
+    yaw_adaptive: bool = False
+    # PPO
+    steps: float = 1e9                 # physics ticks (all ranks)
+    n_steps: int = 128                 # decisions per rollout
+    act_every: int = 3                 # physics ticks per decision
+    epochs: int = 4
+    minibatches: int = 8
+    train_stride: int = 1
+    lr: float = 3e-4
+    gamma: float = 0.9995              # per tick; GAE uses gamma ** act_every
+    gae: float = 0.95
+    clip: float = 0.2
+    ent: float = 0.005
+    ent_final: Optional[float] = None
+    vf: float = 0.5
+    max_grad_norm: float = 0.5
+    # vision
+    vision: bool = True
+    lidar_w: int = 128
+    lidar_h: int = 64
+    lidar_range: float = 2000.0
+    lidar_near: Optional[float] = None
+    lidar_cell: float = 16.0
+    pinhole: bool = False
+    march_steps: int = 64
+    # network
+    continuous_yaw: bool = False
+    gps: bool = False
+    heads: tuple = ("yaw", "pitch", "fwd", "side", "jump", "duck")
+    fc: int = 512
+    proprio: int = 256
+    hidden: int = 512
+    mlp: tuple = (256, 256)
+    # reward
+    reward: RewardSpec = field(default_factory=RewardSpec)
+    # respawn reservoir (Go-Explore restarts)
+    respawn_frac: float = 0.0
+    respawn_margin: float = 10.0
+    respawn_reservoir: int = 100_000
+    # run
+    seed: int = 0
+    device: str = "cuda"
+    graphs: bool = True
+    comm: str = "p2p"                  # p2p (fused NVLink kernels) | nccl (library baseline)
+    threads: Optional[int] = None
+    run: str = "runs/default"
+    ckpt_every: float = 50e6
+    record_every: float = 0.0
+    eval_eps: int = 3
+    timing: bool = False
+
+    def to_dict(self) -> dict:
+        d = asdict(self)
+        d["reward"] = self.reward.to_dict()
+        d["heads"] = list(self.heads)
+        d["mlp"] = list(self.mlp)
+        return d
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "TrainConfig":
+        kw = {}
+        names = {f.name for f in fields(cls)}
+        for k, v in d.items():
+            if k not in names:
+                continue
+            if k == "reward":
+                v = RewardSpec.from_dict(v)
+            elif k in ("heads", "mlp"):
+                v = tuple(v)
+            kw[k] = v
+        return cls(**kw)
+
+
+def bench_config(n_envs: int = 2048) -> TrainConfig:
+    """The vision-PPO benchmark configuration: 2048 envs per GPU on the
+    512-brush procedural map, ramp drop spawns 400-800u with random
+    velocity / yaw / gaze, 128x64 depth + proprioception, Nature-CNN policy,
+    PPO gamma 0.9995 / lambda 0.95 / 4 epochs / 8 minibatches / clip 0.2,
+    curiosity 0.25 keyed on position x speed x gaze."""
+    return TrainConfig(
+        map="field", envs=n_envs, ep_ticks=6000, n_steps=128, act_every=3, epochs=4, minibatches=8,
+        gamma=0.9995, gae=0.95, clip=0.2,
+        reward=RewardSpec(mode="coverage", int_coef=0.25, int_cell=256.0, int_view=8, int_speed=8))

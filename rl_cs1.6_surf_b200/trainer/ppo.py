@@ -1,0 +1,519 @@
+"""GPU-resident PPO trainer (reference: python/train_fast.py main loop).
+
+Per iteration: a rollout of T decisions x K physics ticks for every env, GAE,
+then E epochs x M minibatches of clipped-PPO updates. On a CUDA device:
+
+* the simulator steps on CPU threads and writes one record row per env into
+  a pinned host buffer; one async copy ships it to the GPU;
+* each decision t replays a captured CUDA graph: copy in, reward of decision
+  t-1 (reward kernel), depth render straight into the rollout buffer slot,
+  proprio features, policy forward on the tcgen05 kernels, fused sampling,
+  and the async copy of the action rows back to pinned memory;
+* truncated episodes get gamma * V(s_T) from an eager render + forward of
+  their terminal poses (added by the next reward kernel);
+* the update replays one captured graph per epoch: permutation (keyed
+  Feistel), per-minibatch advantage moments, then per minibatch the row
+  gathers, forward, fused PPO loss/gradient, explicit backward, gradient
+  synchronisation across ranks (data parallel) and fused clip + Adam.
+
+On CPU the same components run through their PyTorch/numpy oracles (the
+eyeless configuration trains on CPU).
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+import time
+from pathlib import Path
+from typing import Optional
+
+import numpy as np
+import torch
+
+from ..models.policy import HeadLayout, NetConfig, PolicyNet, Workspace, backward_gpu, forward_gpu
+from ..ops import rl as R
+from ..rewards.spec import CpuReward, GpuReward, RewardSpec
+from ..sim import mapgen
+from ..sim.core import REC_COLS, STATE_DTYPE, TERM_COLS, SimCore, default_config
+from ..utils.timer import PhaseTimer
+from .config import TrainConfig
+
+# column layout of the per-env host record (float32)
+C_OBS, C_TOBS, C_REC, C_TREC, H_COLS = 0, 16, 32, 48, 64
+NOGPS = (0, 1, 2, 3, 4, 5, 6, 9, 10, 11)      # honest proprioception (no heading, no position)
+
+
+class Trainer:
+    def __init__(self, cfg: TrainConfig, rank: int = 0, world: int = 1, comm=None, verbose: bool = True):
+        self.cfg = cfg
+        self.rank, self.world, self.comm = rank, world, comm
+        self.verbose = verbose and rank == 0
+        self.device = torch.device(cfg.device)
+        self.gpu = self.device.type == "cuda"
+        torch.manual_seed(cfg.seed + 1000 * rank)
+        self._setup_env()
+        self._setup_net()
+        self._setup_buffers()
+        self.global_step = 0
+        self.iteration = 0
+        self.timer = PhaseTimer(cfg.timing, self.gpu)
+        self.last_stats: dict = {}
+
+    # ---- setup ------------------------------------------------------------------------
+    def _log(self, msg: str) -> None:
+        if self.verbose:
+            print(msg, flush=True)
+
+    def _setup_env(self) -> None:
+        cfg = self.cfg
+        if cfg.map in mapgen.MAP_KINDS:
+            self.procmap = mapgen.generate(cfg.map, cfg.map_seed)
+            image = self.procmap.image
+            self.zones = self.procmap.zones
+            pool = self.procmap.spawn_pool
+        else:
+            self.procmap = None
+            image = Path(cfg.map).read_bytes()
+            zp = Path(cfg.map).with_suffix("").as_posix() + ".zones.json"
+            self.zones = json.loads(Path(zp).read_text()) if Path(zp).exists() else {}
+            pool = None
+        self.map_image = image
+        spawn_mode = 2 if (cfg.spawn == "pool" and pool is not None) else 0
+        env_cfg = default_config(cfg.envs, max_episode_ticks=cfg.ep_ticks, spawn_mode=spawn_mode,
+                                 yaw_jitter_deg=cfg.yaw_jitter, sv_maxvelocity=cfg.maxvel,
+                                 sv_airaccelerate=cfg.airaccelerate, pitch_rate_max_deg=cfg.pitch_rate,
+                                 yaw_adaptive=int(cfg.yaw_adaptive))
+        self.core = SimCore.from_bytes(image, env_cfg, threads=cfg.threads)
+        if spawn_mode == 2:
+            self.core.set_spawn_pool(pool)
+        self.spawn_pool = pool
+        self.core.set_teleport_fail(cfg.teleport_fail)
+        end = self.zones.get("end") if self.zones else None
+        if end:
+            self.core.set_goal_box(end["mins"], end["maxs"])
+        self.bounds = self.core.map_bounds()
+        self.field = None
+        self.d0 = None
+        if cfg.reward.mode == "race":
+            from ..ops.geodesic import bake_goal_field
+            self.field = bake_goal_field(self.core, end, cell=max(cfg.lidar_cell, 16.0),
+                                         device=self.device if self.gpu else "cpu")
+            start = pool["origin"] if pool is not None else np.array([s[0] for s in self.core.spawns()])
+            self.d0 = float(np.median(self.field.sample(start)))
+            self._log(f"goal field: reach_max {self.field.reach_max:.0f}u, start distance {self.d0:.0f}u")
+
+    def _setup_net(self) -> None:
+        cfg = self.cfg
+        heads = tuple(h for h in cfg.heads if not (cfg.continuous_yaw and h == "yaw"))
+        if not cfg.vision:
+            heads = tuple(h for h in heads if h != "pitch")
+        self.layout = HeadLayout(heads, cfg.continuous_yaw)
+        self.feat_idx = tuple(range(15)) if cfg.gps else NOGPS
+        ncfg = NetConfig(vision=cfg.vision, img_h=cfg.lidar_h, img_w=cfg.lidar_w, n_scalar=len(self.feat_idx),
+                         scalar_pad=16, fc=cfg.fc, proprio=cfg.proprio, hidden=cfg.hidden, mlp=tuple(cfg.mlp),
+                         heads=self.layout)
+        self.net = PolicyNet(ncfg, self.device, seed=cfg.seed)
+        if self.comm is not None:
+            self.comm.broadcast_params(self.net)
+        self.opt = R.Adam(self.net, lr=cfg.lr, eps=1e-5, max_norm=cfg.max_grad_norm)
+        self.heads = R.HeadArgs(self.layout, self.device)
+        if cfg.vision:
+            from ..ops.vision import DepthCamera, SdfVolume
+            if self.procmap is not None and "grid_mins" in self.procmap.meta:
+                m = self.procmap.meta
+                self.volume = SdfVolume.build(self.core, cell=m["cell"], mins=np.array(m["grid_mins"]),
+                                              dims=tuple(m["dims"]), device=self.device)
+            else:
+                self.volume = SdfVolume.build(self.core, cell=cfg.lidar_cell, device=self.device)
+            self.camera = DepthCamera(self.volume, cfg.lidar_w, cfg.lidar_h, range_units=cfg.lidar_range,
+                                      near_range=cfg.lidar_near, max_steps=cfg.march_steps, pinhole=cfg.pinhole,
+                                      dtype=torch.bfloat16)
+        self._log(f"policy: {self.net.n_params:,} parameters, heads {self.layout.heads}"
+                  f"{' + continuous yaw' if self.layout.continuous_yaw else ''}")
+
+    def _setup_buffers(self) -> None:
+        cfg, dev = self.cfg, self.device
+        N, T = cfg.envs, cfg.n_steps
+        self.N, self.T, self.K = N, T, cfg.act_every
+        self.frame = cfg.lidar_w * cfg.lidar_h if cfg.vision else 0
+        pin = self.gpu
+        self.hrec = torch.zeros((N, H_COLS), dtype=torch.float32, pin_memory=pin)
+        self.act_pin = torch.zeros((N, 8), dtype=torch.int32, pin_memory=pin)
+        self.hdev = torch.zeros((N, H_COLS), dtype=torch.float32, device=dev)
+        bf = torch.bfloat16 if self.gpu else torch.float32
+        self.b_img = torch.zeros((T + 1, N, max(self.frame, 8)), dtype=bf, device=dev) if cfg.vision else None
+        self.b_scal = torch.zeros((T + 1, N, 16), dtype=bf, device=dev)
+        self.b_act = torch.zeros((T, N, 8), dtype=torch.int32, device=dev)
+        self.b_logp = torch.zeros((T, N), device=dev)
+        self.b_val = torch.zeros((T, N), device=dev)
+        self.b_rew = torch.zeros((T, N), device=dev)
+        self.b_done = torch.zeros((T, N), device=dev)
+        self.adv = torch.zeros((T, N), device=dev)
+        self.ret = torch.zeros((T, N), device=dev)
+        self.last_val = torch.zeros(N, device=dev)
+        self.moments = torch.zeros(2, dtype=torch.float64, device=dev)
+        self.feat_idx_t = torch.tensor(list(self.feat_idx) + [0] * (16 - len(self.feat_idx)), dtype=torch.int32,
+                                       device=dev)
+        self.mb = T * N // cfg.minibatches
+        if self.gpu:
+            self.ws_roll = Workspace(self.net, N)
+            self.ws_upd = Workspace(self.net, self.mb)
+            self.perm = torch.zeros(T * N, dtype=torch.int64, device=dev)
+            self.perm_key = torch.tensor([cfg.seed * 7919 + self.rank], dtype=torch.int64, device=dev)
+            self.mom_mb = torch.zeros((cfg.minibatches, 2), dtype=torch.float64, device=dev)
+            self.img_mb = torch.zeros((self.mb, max(self.frame, 8)), dtype=torch.bfloat16, device=dev)
+            self.scal_mb = torch.zeros((self.mb, 16), dtype=torch.bfloat16, device=dev)
+            self.coef = torch.tensor([cfg.clip, cfg.vf, cfg.ent], dtype=torch.float32, device=dev)
+            self.loss_stats = torch.zeros(6, dtype=torch.float32, device=dev)
+            self.sample_counter = torch.zeros(1, dtype=torch.int64, device=dev)
+            self.reward = GpuReward(cfg.reward, N, self.K, self.bounds, dev, self.field, self.d0)
+            self.rew_graphs: list = []
+            self.upd_graph = None
+            self.act_event = torch.cuda.Event()
+        else:
+            self.reward = CpuReward(cfg.reward, N, self.K, self.bounds, self.field, self.d0)
+        self.seed_base = (self.cfg.seed * 1_000_003 + self.rank * 7_777_777) & 0xFFFFFFFFFFFF
+
+    # ---- environment plumbing -------------------------------------------------------------
+    def _env_step(self) -> None:
+        h = self.hrec
+        base, stride = h.data_ptr(), H_COLS
+        self.core.step_k(self.act_pin.data_ptr(), 8, self.K, yaw_slot=6 if self.layout.continuous_yaw else -1,
+                         fail_slot=7, obs=(base + 4 * C_OBS, stride), term_obs=(base + 4 * C_TOBS, stride),
+                         rec=(base + 4 * C_REC, stride), term_rec=(base + 4 * C_TREC, stride))
+
+    def reset(self) -> None:
+        """Reset every env and write the spawn records (first decision)."""
+        obs = self.core.reset(self.cfg.seed * 1009 + self.rank * 100_003)
+        st = self.core.states_view
+        h = self.hrec.numpy()
+        h[:] = 0
+        h[:, C_OBS:C_OBS + 15] = obs[:, :15]
+        h[:, C_REC:C_REC + 3] = st["origin"]
+        h[:, C_REC + 3] = st["yaw"]
+        h[:, C_REC + 4] = st["pitch"]
+        h[:, C_REC + 5] = st["ducked"]
+        h[:, C_REC + 6:C_REC + 9] = st["velocity"]
+        if self.gpu:
+            self.hdev.copy_(self.hrec, non_blocking=True)
+            self.reward.init(self.hdev[:, C_REC:C_REC + REC_COLS])
+        else:
+            self.reward.init(h[:, C_REC:C_REC + REC_COLS].copy())
+
+    # ---- GPU rollout ------------------------------------------------------------------------
+    def _features(self, obs: torch.Tensor, out: torch.Tensor) -> None:
+        from ..ops import _lib
+        from ..ops._lib import check, ptr, stream_ptr
+        check(_lib.lib("libsurf_rl.so").surf_obs_features(ptr(obs), obs.stride(0), ptr(self.feat_idx_t),
+                                                          len(self.feat_idx), 16, ptr(out), out.stride(0),
+                                                          obs.shape[0], None, 0, stream_ptr(obs.device)),
+              "surf_obs_features")
+
+    def _observe(self, t: int) -> None:
+        """Render + features of the current records into rollout slot t."""
+        if self.cfg.vision:
+            self.camera.render(self.hdev[:, C_REC:C_REC + 6], out=self.b_img[t])
+        self._features(self.hdev[:, C_OBS:C_OBS + 15], self.b_scal[t])
+
+    def _decide(self, t: int) -> None:
+        img = self.b_img[t] if self.cfg.vision else None
+        out = forward_gpu(self.net, self.ws_roll, self.b_scal[t], img)
+        R.sample_heads(out, self.heads, self.net.p("log_std"), self.b_act[t], self.b_logp[t], self.seed_base,
+                       0, value_src=out[:, self.layout.value_col], value_out=self.b_val[t],
+                       fail_src=self.reward.stall, counter_ptr=self.sample_counter, counter_offset=t)
+
+    def _decision_body(self, t: int) -> None:
+        self.hdev.copy_(self.hrec, non_blocking=True)
+        if t > 0:
+            self.reward(self.hdev[:, C_REC:C_REC + REC_COLS], self.b_rew[t - 1], self.b_done[t - 1])
+        self._observe(t)
+        self._decide(t)
+        self.act_pin.copy_(self.b_act[t], non_blocking=True)
+
+    def _tail_body(self) -> None:
+        T = self.T
+        self.hdev.copy_(self.hrec, non_blocking=True)
+        self.reward(self.hdev[:, C_REC:C_REC + REC_COLS], self.b_rew[T - 1], self.b_done[T - 1])
+        self._observe(T)
+        img = self.b_img[T] if self.cfg.vision else None
+        out = forward_gpu(self.net, self.ws_roll, self.b_scal[T], img)
+        self.last_val.copy_(out[:, self.layout.value_col])
+        R.bump_counter(self.sample_counter, T)
+
+    def _capture(self) -> None:
+        """One CUDA graph per decision slot plus the rollout tail."""
+        T = self.T
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for t in range(min(T, 2)):                 # warm-up (kernel attributes, lazy inits)
+                self._decision_body(t)
+            self._tail_body()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.sample_counter.zero_()
+        from ..ops import _lib
+        self.rew_graphs = []
+        self.graph_launches = []
+        for t in range(T):
+            g = torch.cuda.CUDAGraph()
+            c0 = _lib.launch_count()
+            with torch.cuda.graph(g, stream=s):
+                self._decision_body(t)
+            self.graph_launches.append(_lib.launch_count() - c0)
+            self.rew_graphs.append(g)
+        self.tail_graph = torch.cuda.CUDAGraph()
+        c0 = _lib.launch_count()
+        with torch.cuda.graph(self.tail_graph, stream=s):
+            self._tail_body()
+        self.tail_launches = _lib.launch_count() - c0
+        torch.cuda.synchronize()
+        self.reset()                      # the warm-up touched env-facing reward state
+        self._log(f"captured {T + 1} rollout graphs")
+
+    def _bootstrap_truncations(self) -> None:
+        """gamma * V(s_T) for envs whose episode was truncated this decision
+        (their states are already the next episode's): render the terminal
+        poses, run the value head, stage the bonus for the next reward kernel."""
+        h = self.hrec.numpy()
+        trunc = np.flatnonzero(h[:, C_REC + 12] != 0)
+        if len(trunc) == 0:
+            return
+        idx = torch.as_tensor(trunc, device=self.device)
+        self.hdev.copy_(self.hrec, non_blocking=True)
+        rows = self.hdev[idx]                                    # [M, 64]
+        M = len(trunc)
+        scal = torch.zeros((M, 16), dtype=torch.bfloat16, device=self.device)
+        self._features(rows[:, C_TOBS:C_TOBS + 15].contiguous(), scal)
+        img = None
+        if self.cfg.vision:
+            pose = rows[:, C_TREC:C_TREC + 6].contiguous()
+            img = self.camera.render(pose)
+        out = forward_gpu(self.net, self.ws_roll, scal, img, B=M)
+        self.reward.boot.index_copy_(0, idx, self.cfg.gamma * out[:, self.layout.value_col])
+
+    def rollout_gpu(self) -> None:
+        from ..ops import _lib
+        T = self.T
+        tm = self.timer
+        if self.cfg.graphs and not self.rew_graphs:
+            self._capture()
+        for t in range(T):
+            ev = tm.gpu_start("rollout_gpu")
+            if self.cfg.graphs:
+                self.rew_graphs[t].replay()
+                _lib.add_launches(self.graph_launches[t])
+            else:
+                self._decision_body(t)
+            tm.gpu_end(ev)
+            self.act_event.record()
+            t0 = tm.now()
+            self.act_event.synchronize()
+            tm.add("wait_gpu", t0)
+            t0 = tm.now()
+            self._env_step()
+            tm.add("env", t0)
+            if self.cfg.ep_ticks and (self.hrec[:, C_REC + 12] != 0).any():
+                self._bootstrap_truncations()
+            self.global_step += self.N * self.K * self.world
+        if self.cfg.graphs:
+            self.tail_graph.replay()
+            _lib.add_launches(self.tail_launches)
+        else:
+            self._tail_body()
+
+    # ---- GPU update ---------------------------------------------------------------------------
+    def _epoch_body(self) -> None:
+        from ..ops import gemm as G
+        from ..ops import _lib
+        from ..ops._lib import check, ptr, stream_ptr
+        T, N, mb, nmb = self.T, self.N, self.mb, self.cfg.minibatches
+        lib = _lib.lib("libsurf_rl.so")
+        check(lib.surf_permutation(ptr(self.perm), T * N, ptr(self.perm_key), stream_ptr(self.device)),
+              "surf_permutation")
+        self.mom_mb.zero_()
+        R.adv_moments(self.adv.view(-1), self.perm, mb, nmb, self.mom_mb)
+        if self.comm is not None:
+            self.comm.allreduce_moments(self.mom_mb)
+        f_img = self.b_img[:T].view(T * N, -1) if self.cfg.vision else None
+        f_scal = self.b_scal[:T].view(T * N, 16)
+        for m in range(nmb):
+            idx = self.perm[m * mb:(m + 1) * mb]
+            if self.cfg.vision:
+                G.gather_rows(f_img, idx, self.img_mb)
+            G.gather_rows(f_scal, idx, self.scal_mb)
+            out = forward_gpu(self.net, self.ws_upd, self.scal_mb, self.img_mb if self.cfg.vision else None)
+            R.ppo_loss(out, self.layout.value_col, self.b_act.view(T * N, 8), self.b_logp.view(-1),
+                       self.adv.view(-1), self.ret.view(-1), idx, self.mom_mb[m], self.heads, self.net.p("log_std"),
+                       self.coef, float(mb * self.world), self.ws_upd.dout, self.net.g("log_std"), self.loss_stats)
+            G.to_bf16(self.ws_upd.dout, self.ws_upd.dout16)
+            backward_gpu(self.net, self.ws_upd, self.scal_mb)
+            if self.comm is not None:
+                self.comm.step(self.net, self.opt)          # fused all-reduce + clip + Adam
+            else:
+                self.opt.step()
+
+    def update_gpu(self) -> None:
+        from ..ops import _lib
+        cfg = self.cfg
+        frac = min(1.0, self.global_step / max(1.0, cfg.steps))
+        ent = cfg.ent if cfg.ent_final is None else cfg.ent + (cfg.ent_final - cfg.ent) * frac
+        self.coef[2] = ent
+        self.moments.zero_()
+        R.gae(self.b_rew, self.b_val, self.b_done, self.last_val, cfg.gamma ** self.K, cfg.gae, self.adv, self.ret,
+              self.moments)
+        self.loss_stats.zero_()
+        if cfg.graphs:
+            if self.upd_graph is None:
+                s = torch.cuda.Stream()
+                s.wait_stream(torch.cuda.current_stream())
+                snap = (self.net.flat.clone(), self.opt.m.clone(), self.opt.v.clone(), self.opt.hyper.clone())
+                with torch.cuda.stream(s):
+                    self._epoch_body()                         # warm-up outside capture
+                torch.cuda.current_stream().wait_stream(s)
+                torch.cuda.synchronize()
+                # undo the warm-up step so the first real update starts from the same weights
+                self.net.flat.copy_(snap[0]); self.opt.m.copy_(snap[1]); self.opt.v.copy_(snap[2])
+                self.opt.hyper.copy_(snap[3]); self.net.sync_bf16(); self.net.grad.zero_()
+                self.loss_stats.zero_()
+                self.upd_graph = torch.cuda.CUDAGraph()
+                c0 = _lib.launch_count()
+                with torch.cuda.graph(self.upd_graph, stream=s):
+                    self._epoch_body()
+                self.upd_launches = _lib.launch_count() - c0
+                torch.cuda.synchronize()
+                self._log("captured the update graph (one epoch)")
+            for _ in range(cfg.epochs):
+                self.upd_graph.replay()
+                _lib.add_launches(self.upd_launches)
+        else:
+            for _ in range(cfg.epochs):
+                self._epoch_body()
+
+    # ---- CPU path -------------------------------------------------------------------------------
+    def _cpu_obs(self, t: int) -> None:
+        h = self.hrec.numpy()
+        feats = np.zeros((self.N, 16), np.float32)
+        feats[:, :len(self.feat_idx)] = h[:, [C_OBS + i for i in self.feat_idx]]
+        self.b_scal[t].copy_(torch.from_numpy(feats))
+        if self.cfg.vision:
+            raise RuntimeError("the vision policy needs a CUDA device (the depth camera is a GPU kernel)")
+
+    def rollout_cpu(self) -> None:
+        T = self.T
+        gen = torch.Generator().manual_seed(self.cfg.seed * 31 + self.iteration)
+        for t in range(T):
+            self._cpu_obs(t)
+            with torch.no_grad():
+                out = self.net.forward_reference(self.b_scal[t], None)
+                act, logp = R.sample_reference(out, self.layout, self.net.p("log_std"), gen)
+            stall = getattr(self, "_stall", None)
+            if stall is not None:
+                act[:, 7] = torch.from_numpy(stall.astype(np.int32))
+            self.b_act[t].copy_(act)
+            self.b_logp[t].copy_(logp)
+            self.b_val[t].copy_(out[:, self.layout.value_col])
+            self.act_pin.copy_(act)
+            self._env_step()
+            h = self.hrec.numpy()
+            boot = None
+            trunc = np.flatnonzero(h[:, C_REC + 12] != 0)
+            if len(trunc):
+                feats = np.zeros((len(trunc), 16), np.float32)
+                feats[:, :len(self.feat_idx)] = h[trunc][:, [C_TOBS + i for i in self.feat_idx]]
+                with torch.no_grad():
+                    v = self.net.forward_reference(torch.from_numpy(feats), None)[:, self.layout.value_col]
+                boot = np.zeros(self.N, np.float32)
+                boot[trunc] = self.cfg.gamma * v.numpy()
+            r, d, self._stall = self.reward(h[:, C_REC:C_REC + REC_COLS].copy(), boot)
+            self.b_rew[t].copy_(torch.from_numpy(r))
+            self.b_done[t].copy_(torch.from_numpy(d))
+            self.global_step += self.N * self.K * self.world
+        self._cpu_obs(T)
+        with torch.no_grad():
+            self.last_val.copy_(self.net.forward_reference(self.b_scal[T], None)[:, self.layout.value_col])
+
+    def update_cpu(self) -> dict:
+        cfg = self.cfg
+        adv, ret = R.gae_reference(self.b_rew, self.b_val, self.b_done, self.last_val, cfg.gamma ** self.K, cfg.gae)
+        self.adv.copy_(adv)
+        self.ret.copy_(ret)
+        T, N, mb = self.T, self.N, self.mb
+        frac = min(1.0, self.global_step / max(1.0, cfg.steps))
+        ent = cfg.ent if cfg.ent_final is None else cfg.ent + (cfg.ent_final - cfg.ent) * frac
+        stats = np.zeros(4)
+        for _ in range(cfg.epochs):
+            perm = torch.randperm(T * N)
+            for m in range(cfg.minibatches):
+                idx = perm[m * mb:(m + 1) * mb]
+                params = self.net.autograd_params()
+                out = self.net.forward_reference(self.b_scal[:T].reshape(T * N, 16)[idx], None, params)
+                loss, pg, vl, en = R.ppo_loss_reference(out, self.layout.value_col, self.b_act.view(T * N, 8)[idx],
+                                                        self.b_logp.view(-1)[idx], self.adv.view(-1)[idx],
+                                                        self.ret.view(-1)[idx], self.layout, params["log_std"],
+                                                        cfg.clip, cfg.vf, ent)
+                loss.backward()
+                self.net.collect_grads(params)
+                self.opt.step_reference()
+                stats += [pg.item(), vl.item(), en.item(), 1.0]
+        return {"policy_loss": stats[0] / stats[3], "value_loss": stats[1] / stats[3], "entropy": stats[2] / stats[3]}
+
+    # ---- iteration ------------------------------------------------------------------------------
+    def train_iteration(self) -> dict:
+        tm = self.timer
+        tm.start_iter()
+        if self.iteration == 0 and self.global_step == 0:
+            self.reset()
+        self.iteration += 1
+        t0 = tm.now()
+        if self.gpu:
+            self.rollout_gpu()
+        else:
+            self.rollout_cpu()
+        tm.add("rollout", t0)
+        t0 = tm.now()
+        if self.gpu:
+            ev = tm.gpu_start("update_gpu")
+            self.update_gpu()
+            tm.gpu_end(ev)
+            if self.comm is not None:
+                self.comm.merge_counts(self.reward)
+            ls = self.loss_stats.tolist()
+            n = max(ls[5], 1.0)
+            loss = {"policy_loss": ls[0] / n, "value_loss": ls[1] / n, "entropy": ls[2] / n, "approx_kl": ls[3] / n,
+                    "clip_frac": ls[4] / n}
+        else:
+            loss = self.update_cpu()
+        tm.add("update", t0)
+        stats = dict(self.reward.pop_stats(), **loss)
+        stats["global_step"] = self.global_step
+        stats["iteration"] = self.iteration
+        stats["timing"] = tm.flush(self.iteration)
+        self.last_stats = stats
+        return stats
+
+    # ---- checkpoints ----------------------------------------------------------------------------
+    def state_dict(self) -> dict:
+        counts = None
+        if self.cfg.reward.int_coef > 0:
+            c = self.reward.counts
+            counts = (c.cpu().numpy() if torch.is_tensor(c) else c).astype(np.uint32)
+        return {"format": "surfb200-ckpt-1", "policy": self.net.state_dict(), "optimizer": self.opt.state_dict(),
+                "global_step": self.global_step, "iteration": self.iteration, "config": self.cfg.to_dict(),
+                "int_counts": counts}
+
+    def load_state_dict(self, sd: dict, reset_steps: bool = False, reset_counts: bool = False) -> None:
+        self.net.load_state_dict(sd["policy"])
+        self.opt.load_state_dict(sd["optimizer"])
+        if not reset_steps:
+            self.global_step = int(sd["global_step"])
+            self.iteration = int(sd.get("iteration", 0))
+        c = sd.get("int_counts")
+        if c is not None and not reset_counts and self.cfg.reward.int_coef > 0:
+            if len(c) == len(self.reward.counts):
+                src = torch.as_tensor(np.asarray(c).astype(np.int64))
+                if torch.is_tensor(self.reward.counts):
+                    self.reward.counts.copy_(src.to(torch.int32).to(self.reward.counts.device))
+                else:
+                    self.reward.counts[:] = np.asarray(c)
