@@ -41,6 +41,7 @@ def parse():
     ap.add_argument("--comm", choices=["p2p", "nccl"], default="p2p")
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--json", default=None)
+    ap.add_argument("--timing", action="store_true", help="print per-phase times of each timed iteration to stderr")
     return ap.parse_args()
 
 
@@ -109,6 +110,7 @@ def run_ours(args) -> None:
     cfg = bench_config(args.envs)
     cfg.graphs = not args.no_graphs
     cfg.seed = 0
+    cfg.timing = args.timing
     tr = Trainer(cfg, rank=rank, world=world, comm=comm, verbose=(rank == 0))
     for _ in range(args.warmup):
         tr.train_iteration()
@@ -124,6 +126,9 @@ def run_ours(args) -> None:
     e0.record()
     for _ in range(args.steps):
         stats = tr.train_iteration()
+        if args.timing and rank == 0:
+            from surfb200.utils.timer import PhaseTimer
+            print(PhaseTimer.format(tr.iteration, stats.get("timing", {})), file=sys.stderr, flush=True)
     e1.record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - w0
@@ -164,6 +169,7 @@ def run_ours(args) -> None:
         print(line, flush=True)
         if args.json:
             Path(args.json).write_text(line)
+    tr.release_graphs()
     if comm is not None:
         comm.close()
 

@@ -1,0 +1,130 @@
+"""Per-op device times of one PPO minibatch update (forward, loss, backward, Adam).
+
+The reference's isolated minibatch bench is tools/bench_update.py; this one
+runs the framework's own kernels eagerly at the benchmark minibatch (32,768
+rows = 2048 envs x 128 decisions / 8 minibatches), wraps every entry point of
+ops.gemm / ops.rl in CUDA-event pairs on the launching stream, and prints the
+time of each call after warm-up, with the FLOPs of the GEMMs and the achieved
+TFLOP/s.
+
+    python bench/bench_update.py [--rows 32768] [--iters 5] [--json out.json]
+"""
+from __future__ import annotations
+
+import argparse
+import collections
+import json
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--rows", type=int, default=32768)
+    ap.add_argument("--iters", type=int, default=5)
+    ap.add_argument("--json", default=None)
+    args = ap.parse_args()
+    import torch
+    import surfb200  # noqa: F401
+    from surfb200.models.policy import HeadLayout, NetConfig, PolicyNet, Workspace, backward_gpu, forward_gpu
+    from surfb200.ops import gemm as G
+    from surfb200.ops import rl as R
+
+    dev = torch.device("cuda")
+    layout = HeadLayout(("yaw", "pitch", "fwd", "side", "jump", "duck"), False)
+    net = PolicyNet(NetConfig(vision=True, img_h=64, img_w=128, n_scalar=10, scalar_pad=16, heads=layout), dev)
+    B = args.rows
+    ws = Workspace(net, B)
+    opt = R.Adam(net)
+    heads = R.HeadArgs(layout, dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    img = torch.rand(B, 64 * 128, device=dev, generator=g).to(torch.bfloat16)
+    scal = torch.randn(B, 16, device=dev, generator=g).to(torch.bfloat16)
+    act = torch.zeros(B, 8, dtype=torch.int32, device=dev)
+    old_logp = torch.zeros(B, device=dev)
+    adv = torch.randn(B, device=dev, generator=g)
+    ret = torch.randn(B, device=dev, generator=g)
+    idx = torch.arange(B, device=dev)
+    mom = torch.tensor([float(adv.sum()), float((adv * adv).sum())], dtype=torch.float64, device=dev)
+    coef = torch.tensor([0.2, 0.5, 0.005], device=dev)
+    stats = torch.zeros(6, device=dev)
+
+    records = []
+    active = [False]
+
+    def wrap(mod, name):
+        fn = getattr(mod, name)
+
+        def inner(*a, **k):
+            if not active[0]:
+                return fn(*a, **k)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            r = fn(*a, **k)
+            e1.record()
+            desc = ""
+            if name == "gemm":
+                A, Bm = a[0], a[1]
+                M = k.get("M") or (A.shape[1] if k.get("a_mn") else A.shape[0])
+                Kd = k.get("K") or (A.shape[0] if k.get("a_mn") else A.shape[1])
+                N = (Bm.shape[1] if k.get("b_mn") else Bm.shape[0])
+                desc = f"{M}x{N}x{Kd}{' mnA' if k.get('a_mn') else ''}{' mnB' if k.get('b_mn') else ''}"
+                flops = 2.0 * M * N * Kd
+            else:
+                flops = 0.0
+            records.append((name, desc, flops, e0, e1))
+            return r
+        setattr(mod, name, inner)
+
+    for n in ("gemm", "im2col", "col2im", "colsum", "gather_rows", "to_bf16"):
+        wrap(G, n)
+    for n in ("ppo_loss",):
+        wrap(R, n)
+
+    def step():
+        out = forward_gpu(net, ws, scal, img)
+        R.ppo_loss(out, layout.value_col, act, old_logp, adv, ret, idx, mom, heads, net.p("log_std"), coef, float(B),
+                   ws.dout, net.g("log_std"), stats)
+        G.to_bf16(ws.dout, ws.dout16)
+        backward_gpu(net, ws, scal)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        opt.step()
+        e1.record()
+        records.append(("adam", f"{net.numel}", 0.0, e0, e1))
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    active[0] = True
+    t0.record()
+    for _ in range(args.iters):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    per_iter = len(records) // args.iters
+    agg = collections.OrderedDict()
+    for i, (name, desc, flops, e0, e1) in enumerate(records):
+        key = (i % per_iter, name, desc)
+        ms = e0.elapsed_time(e1)
+        a = agg.setdefault(key, [0.0, flops])
+        a[0] += ms / args.iters
+    total = sum(v[0] for v in agg.values())
+    rows = []
+    print(f"{'#':>3} {'op':<12} {'shape':<28} {'ms':>8} {'%':>6} {'TFLOP/s':>8}")
+    for (i, name, desc), (ms, flops) in agg.items():
+        tf = flops / (ms * 1e-3) / 1e12 if flops and ms > 0 else 0.0
+        rows.append({"i": i, "op": name, "shape": desc, "ms": round(ms, 4), "tflops": round(tf, 1)})
+        print(f"{i:>3} {name:<12} {desc:<28} {ms:8.3f} {100 * ms / total:6.1f} {tf:8.1f}")
+    wall = t0.elapsed_time(t1) / args.iters
+    print(f"sum of ops {total:.3f} ms; minibatch step (events around the whole step, incl. gaps) {wall:.3f} ms")
+    if args.json:
+        Path(args.json).write_text(json.dumps({"rows": B, "ops": rows, "sum_ms": total, "step_ms": wall}, indent=1))
+
+
+if __name__ == "__main__":
+    main()

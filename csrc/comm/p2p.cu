@@ -1,0 +1,547 @@
+// p2p.cu — data-parallel collectives over NVLink peer memory (sm_100a).
+//
+// One process per GPU. Every rank shares a few of its device buffers with
+// the others through CUDA IPC (the gradient, the fp32 master parameters,
+// their bf16 copy, the curiosity-count increments and a small sync block);
+// the kernels below then read and write the peers' memory directly with
+// plain loads/stores over NVLink/NVSwitch. No TMA, no multicast.
+//
+// Gradient step (three kernels on the training stream, graph-capturable):
+//   grad_rs_kernel    barrier-in: tell every peer "my gradient is final",
+//                     wait until every peer said so; then reduce-scatter:
+//                     rank r sums shard r of all W gradients (fixed rank
+//                     order, fp32) into its own gradient buffer and the sum
+//                     of squares of the shard (fp64, deterministic block
+//                     order) is published to every peer's norm slot.
+//   grad_adam_kernel  wait for all W shard norms, global-norm clip
+//                     coefficient (identical on every rank: same values,
+//                     same order), Adam on the owned shard (m, v local),
+//                     then push the new fp32 and bf16 parameters of the
+//                     shard into every peer's parameter buffers; the last
+//                     block raises "done" on every peer.
+//   grad_done_kernel  wait for every peer's "done" (all parameters pushed
+//                     here and every peer finished reading my gradient),
+//                     zero the local gradient for the next backward and
+//                     advance the local sequence number.
+// Moments: one block, all-gather of a few doubles + ordered local sum.
+// Counts: increments of the curiosity table summed over peers into the
+//   local table, then the local increments are zeroed.
+//
+// Every wait polls a flag with ld.acquire.sys and gives up after a bounded
+// time (%globaltimer): the kernel then records an error code in the local
+// sync block and returns, so a dead or stalled peer never hangs a GPU. Once
+// an error is recorded every later collective kernel returns at once; the
+// host reads the code after the step and raises.
+//
+// Semantics follow the data-parallel design of the reference
+// (docs/ddp-plan.md:404-434 gradient sum after backward, before the clip;
+// :133-147 global advantage moments; :174-225 count increments), realised
+// here as fused peer-memory kernels instead of library all-reduces.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+
+#include "surf_cuda.cuh"
+
+namespace {
+
+constexpr int kMaxW = 8;
+constexpr int kMaxBlocks = 1024;
+constexpr int kMaxMom = 256;
+
+// Sync block layout (uint64 words, one block per rank, zeroed at start).
+enum : int {
+  kSeqGrad = 0, kSeqMom = 1, kSeqCnt = 2, kErr = 3, kErrTarget = 4,
+  kArrive = 8,                       // 8 counters
+  kFlags = 16,                       // [6][kMaxW]
+  kNormSlots = 64,                   // [2][kMaxW] doubles
+  kPartial = 128,                    // [kMaxBlocks] doubles
+  kMomSlots = kPartial + kMaxBlocks, // [2][kMaxW][kMaxMom] doubles
+  kSyncWords = kMomSlots + 2 * kMaxW * kMaxMom,
+};
+enum : int { kFReady = 0, kFNorm = 1, kFDone = 2, kFMom = 3, kFCntReady = 4, kFCntDone = 5 };
+enum : int { kArrRs = 0, kArrAdam = 1, kArrDone = 2, kArrCnt = 3, kArrCntDone = 4 };
+
+__host__ __device__ constexpr int flag_word(int f, int rank) { return kFlags + f * kMaxW + rank; }
+
+struct Hyper { float lr, beta1, beta2, eps, max_norm, step; };
+
+struct Plan {
+  int rank = 0, world = 1;
+  uint64_t timeout_ns = 0;
+  uint64_t* sync = nullptr;                 // local sync block
+  uint64_t* sync_peer[kMaxW] = {};          // every rank's sync block (peer[rank] = local)
+  // gradient step
+  int64_t n = 0, shard = 0;
+  float* grad_peer[kMaxW] = {};
+  float* p_peer[kMaxW] = {};
+  uint16_t* p16_peer[kMaxW] = {};
+  float* m = nullptr;
+  float* v = nullptr;
+  float* hyper = nullptr;
+  // counts merge
+  int64_t cn = 0;
+  int* counts = nullptr;
+  int* delta_peer[kMaxW] = {};
+};
+
+// ---- memory-model helpers (inline PTX) -----------------------------------------------------
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys(double* p, double v) {
+  asm volatile("st.relaxed.sys.global.f64 [%0], %1;" ::"l"(p), "d"(v) : "memory");
+}
+__device__ __forceinline__ double ld_relaxed_sys(const double* p) {
+  double v;
+  asm volatile("ld.relaxed.sys.global.f64 %0, [%1];" : "=d"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Record the first error (code, and the sequence number it happened at).
+__device__ void set_error(uint64_t* sync, uint64_t code, uint64_t target) {
+  if (atomicCAS(reinterpret_cast<unsigned long long*>(sync + kErr), 0ull, static_cast<unsigned long long>(code)) == 0ull)
+    sync[kErrTarget] = target;
+}
+
+// Poll until *flag >= target; false (error recorded) after timeout_ns or when
+// another block of this rank already recorded an error.
+__device__ bool wait_flag(const uint64_t* flag, uint64_t target, uint64_t* sync, uint64_t timeout_ns, uint64_t code) {
+  if (ld_acquire_sys(flag) >= target) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(128);
+    if (ld_acquire_sys(flag) >= target) return true;
+    if ((it & 31u) == 0u) {
+      if (ld_relaxed_sys_u64(sync + kErr) != 0ull) return false;
+      if (globaltimer() - t0 > timeout_ns || it > 0x7fffffffu) {
+        set_error(sync, code, target);
+        return false;
+      }
+    }
+  }
+}
+
+// Every thread t < world waits for flag f of rank t; the block agrees on the
+// result. Returns false if any wait failed (or an error is already recorded).
+__device__ bool block_wait_all(const Plan& P, int f, uint64_t target, uint64_t code) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = ld_relaxed_sys_u64(P.sync + kErr) == 0ull;
+  __syncthreads();
+  if (ok && static_cast<int>(threadIdx.x) < P.world) {
+    if (!wait_flag(P.sync + flag_word(f, threadIdx.x), target, P.sync, P.timeout_ns, code + threadIdx.x)) ok = 0;
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+// Last-block election: after every block called this once, exactly one block
+// (the last to arrive) gets true. The counter is reset by that block.
+__device__ bool last_block(uint64_t* counter) {
+  __shared__ int last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned long long prev = atomicAdd(reinterpret_cast<unsigned long long*>(counter), 1ull);
+    last = prev == gridDim.x - 1;
+    if (last) *counter = 0;
+  }
+  __syncthreads();
+  if (last) __threadfence();
+  return last != 0;
+}
+
+__device__ __forceinline__ double block_sum(double s) {
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  __shared__ double red[32];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[w] = s;
+  __syncthreads();
+  double t = 0.0;
+  if (threadIdx.x == 0)
+    for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) t += red[i];
+  __syncthreads();
+  return t;   // valid in thread 0
+}
+
+// ---- gradient step ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) grad_rs_kernel(Plan P) {
+  uint64_t* sync = P.sync;
+  if (ld_relaxed_sys_u64(sync + kErr) != 0ull) return;
+  const uint64_t target = sync[kSeqGrad] + 1;
+  if (blockIdx.x == 0 && static_cast<int>(threadIdx.x) < P.world) {
+    __threadfence_system();
+    st_release_sys(P.sync_peer[threadIdx.x] + flag_word(kFReady, P.rank), target);
+  }
+  if (!block_wait_all(P, kFReady, target, 0x100)) return;
+
+  const int64_t lo = static_cast<int64_t>(P.rank) * P.shard;
+  const int64_t hi = lo + P.shard < P.n ? lo + P.shard : P.n;
+  const int64_t cnt = hi > lo ? hi - lo : 0;
+  const int64_t nv = cnt >> 2;                          // float4 groups (shard start is 16-byte aligned)
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  float* mine = P.grad_peer[P.rank];
+  double ss = 0.0;
+  for (int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; j < nv; j += stride) {
+    const int64_t i = lo + 4 * j;
+    float4 v[kMaxW];
+#pragma unroll
+    for (int q = 0; q < kMaxW; ++q)
+      if (q < P.world) v[q] = *reinterpret_cast<const float4*>(P.grad_peer[q] + i);
+    float4 a = v[0];
+#pragma unroll
+    for (int q = 1; q < kMaxW; ++q)
+      if (q < P.world) { a.x += v[q].x; a.y += v[q].y; a.z += v[q].z; a.w += v[q].w; }
+    *reinterpret_cast<float4*>(mine + i) = a;
+    ss += static_cast<double>(a.x) * a.x + static_cast<double>(a.y) * a.y + static_cast<double>(a.z) * a.z +
+          static_cast<double>(a.w) * a.w;
+  }
+  for (int64_t i = lo + 4 * nv + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < hi; i += stride) {
+    float a = P.grad_peer[0][i];
+    for (int q = 1; q < P.world; ++q) a += P.grad_peer[q][i];
+    mine[i] = a;
+    ss += static_cast<double>(a) * a;
+  }
+  const double bs = block_sum(ss);
+  double* partial = reinterpret_cast<double*>(sync + kPartial);
+  if (threadIdx.x == 0) partial[blockIdx.x] = bs;
+  if (last_block(sync + kArrive + kArrRs)) {
+    if (threadIdx.x == 0) {
+      double tot = 0.0;
+      for (unsigned b = 0; b < gridDim.x; ++b) tot += partial[b];   // fixed order: deterministic
+      reinterpret_cast<Hyper*>(P.hyper)->step += 1.0f;
+      const int par = static_cast<int>(target & 1);
+      for (int q = 0; q < P.world; ++q)
+        st_relaxed_sys(reinterpret_cast<double*>(P.sync_peer[q] + kNormSlots) + par * kMaxW + P.rank, tot);
+      __threadfence_system();
+      for (int q = 0; q < P.world; ++q) st_release_sys(P.sync_peer[q] + flag_word(kFNorm, P.rank), target);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) grad_adam_kernel(Plan P) {
+  uint64_t* sync = P.sync;
+  if (ld_relaxed_sys_u64(sync + kErr) != 0ull) return;
+  const uint64_t target = sync[kSeqGrad] + 1;
+  if (!block_wait_all(P, kFNorm, target, 0x200)) return;
+  __shared__ float s_coef;
+  if (threadIdx.x == 0) {
+    const int par = static_cast<int>(target & 1);
+    const double* slots = reinterpret_cast<const double*>(sync + kNormSlots) + par * kMaxW;
+    double tot = 0.0;
+    for (int q = 0; q < P.world; ++q) tot += ld_relaxed_sys(slots + q);
+    const Hyper* h = reinterpret_cast<const Hyper*>(P.hyper);
+    const float norm = static_cast<float>(sqrt(tot));
+    s_coef = h->max_norm > 0.0f ? fminf(1.0f, h->max_norm / (norm + 1e-6f)) : 1.0f;
+  }
+  __syncthreads();
+  const Hyper* h = reinterpret_cast<const Hyper*>(P.hyper);
+  const float coef = s_coef, b1 = h->beta1, b2 = h->beta2, t = h->step, eps = h->eps;
+  const float bc1 = 1.0f - powf(b1, t), bc2 = 1.0f - powf(b2, t);
+  const float lr_t = h->lr / bc1, rbc2 = rsqrtf(bc2);
+
+  const int64_t lo = static_cast<int64_t>(P.rank) * P.shard;
+  const int64_t hi = lo + P.shard < P.n ? lo + P.shard : P.n;
+  const int64_t cnt = hi > lo ? hi - lo : 0;
+  const int64_t nv = cnt >> 2;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const float* g = P.grad_peer[P.rank];
+  const float* pl = P.p_peer[P.rank];
+  auto adam1 = [&](float gi, float& mi, float& vi, float pi) {
+    gi *= coef;
+    mi = b1 * mi + (1.0f - b1) * gi;
+    vi = b2 * vi + (1.0f - b2) * gi * gi;
+    return pi - lr_t * mi / (sqrtf(vi) * rbc2 + eps);
+  };
+  for (int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; j < nv; j += stride) {
+    const int64_t i = lo + 4 * j;
+    const float4 gg = *reinterpret_cast<const float4*>(g + i);
+    float4 mm = *reinterpret_cast<const float4*>(P.m + i);
+    float4 vv = *reinterpret_cast<const float4*>(P.v + i);
+    float4 pp = *reinterpret_cast<const float4*>(pl + i);
+    pp.x = adam1(gg.x, mm.x, vv.x, pp.x);
+    pp.y = adam1(gg.y, mm.y, vv.y, pp.y);
+    pp.z = adam1(gg.z, mm.z, vv.z, pp.z);
+    pp.w = adam1(gg.w, mm.w, vv.w, pp.w);
+    *reinterpret_cast<float4*>(P.m + i) = mm;
+    *reinterpret_cast<float4*>(P.v + i) = vv;
+    uint2 b;
+    b.x = static_cast<uint32_t>(surfk::f32_to_bf16(pp.x)) | (static_cast<uint32_t>(surfk::f32_to_bf16(pp.y)) << 16);
+    b.y = static_cast<uint32_t>(surfk::f32_to_bf16(pp.z)) | (static_cast<uint32_t>(surfk::f32_to_bf16(pp.w)) << 16);
+#pragma unroll
+    for (int q = 0; q < kMaxW; ++q) {
+      if (q < P.world) {
+        *reinterpret_cast<float4*>(P.p_peer[q] + i) = pp;
+        *reinterpret_cast<uint2*>(P.p16_peer[q] + i) = b;
+      }
+    }
+  }
+  for (int64_t i = lo + 4 * nv + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < hi; i += stride) {
+    float mi = P.m[i], vi = P.v[i];
+    const float pi = adam1(g[i], mi, vi, pl[i]);
+    P.m[i] = mi;
+    P.v[i] = vi;
+    const uint16_t b = surfk::f32_to_bf16(pi);
+    for (int q = 0; q < P.world; ++q) {
+      P.p_peer[q][i] = pi;
+      P.p16_peer[q][i] = b;
+    }
+  }
+  if (last_block(sync + kArrive + kArrAdam)) {
+    if (static_cast<int>(threadIdx.x) < P.world)
+      st_release_sys(P.sync_peer[threadIdx.x] + flag_word(kFDone, P.rank), target);
+  }
+}
+
+__global__ void __launch_bounds__(256) grad_done_kernel(Plan P) {
+  uint64_t* sync = P.sync;
+  if (ld_relaxed_sys_u64(sync + kErr) != 0ull) return;
+  const uint64_t target = sync[kSeqGrad] + 1;
+  if (!block_wait_all(P, kFDone, target, 0x300)) return;
+  float* g = P.grad_peer[P.rank];
+  const int64_t nv = P.n >> 2;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; j < nv; j += stride)
+    reinterpret_cast<float4*>(g)[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t i = 4 * nv + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < P.n; i += stride)
+    g[i] = 0.0f;
+  if (last_block(sync + kArrive + kArrDone)) {
+    if (threadIdx.x == 0) sync[kSeqGrad] = target;
+  }
+}
+
+// ---- moments (tiny all-reduce, one block) ---------------------------------------------------
+__global__ void __launch_bounds__(256) moments_kernel(Plan P, double* mom, int cnt) {
+  uint64_t* sync = P.sync;
+  if (ld_relaxed_sys_u64(sync + kErr) != 0ull) return;
+  const uint64_t target = sync[kSeqMom] + 1;
+  const int par = static_cast<int>(target & 1);
+  for (int i = threadIdx.x; i < P.world * cnt; i += blockDim.x) {
+    const int q = i / cnt, k = i % cnt;
+    double* dst = reinterpret_cast<double*>(P.sync_peer[q] + kMomSlots) + (par * kMaxW + P.rank) * kMaxMom + k;
+    st_relaxed_sys(dst, mom[k]);
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (static_cast<int>(threadIdx.x) < P.world)
+    st_release_sys(P.sync_peer[threadIdx.x] + flag_word(kFMom, P.rank), target);
+  if (!block_wait_all(P, kFMom, target, 0x400)) return;
+  const double* slots = reinterpret_cast<const double*>(sync + kMomSlots) + par * kMaxW * kMaxMom;
+  for (int k = threadIdx.x; k < cnt; k += blockDim.x) {
+    double s = 0.0;
+    for (int q = 0; q < P.world; ++q) s += ld_relaxed_sys(slots + q * kMaxMom + k);
+    mom[k] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) sync[kSeqMom] = target;
+}
+
+// ---- curiosity count merge -----------------------------------------------------------------
+__global__ void __launch_bounds__(256) counts_add_kernel(Plan P) {
+  uint64_t* sync = P.sync;
+  if (ld_relaxed_sys_u64(sync + kErr) != 0ull) return;
+  const uint64_t target = sync[kSeqCnt] + 1;
+  if (blockIdx.x == 0 && static_cast<int>(threadIdx.x) < P.world) {
+    __threadfence_system();
+    st_release_sys(P.sync_peer[threadIdx.x] + flag_word(kFCntReady, P.rank), target);
+  }
+  if (!block_wait_all(P, kFCntReady, target, 0x500)) return;
+  const int64_t nv = P.cn >> 2;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; j < nv; j += stride) {
+    int4 acc = reinterpret_cast<const int4*>(P.counts)[j];
+#pragma unroll
+    for (int q = 0; q < kMaxW; ++q) {
+      if (q < P.world && q != P.rank) {
+        const int4 d = reinterpret_cast<const int4*>(P.delta_peer[q])[j];
+        acc.x += d.x; acc.y += d.y; acc.z += d.z; acc.w += d.w;
+      }
+    }
+    reinterpret_cast<int4*>(P.counts)[j] = acc;
+  }
+  for (int64_t i = 4 * nv + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < P.cn; i += stride) {
+    int acc = P.counts[i];
+    for (int q = 0; q < P.world; ++q)
+      if (q != P.rank) acc += P.delta_peer[q][i];
+    P.counts[i] = acc;
+  }
+  if (last_block(sync + kArrive + kArrCnt)) {
+    if (static_cast<int>(threadIdx.x) < P.world)
+      st_release_sys(P.sync_peer[threadIdx.x] + flag_word(kFCntDone, P.rank), target);
+  }
+}
+
+__global__ void __launch_bounds__(256) counts_done_kernel(Plan P) {
+  uint64_t* sync = P.sync;
+  if (ld_relaxed_sys_u64(sync + kErr) != 0ull) return;
+  const uint64_t target = sync[kSeqCnt] + 1;
+  if (!block_wait_all(P, kFCntDone, target, 0x600)) return;
+  int* d = P.delta_peer[P.rank];
+  const int64_t nv = P.cn >> 2;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; j < nv; j += stride)
+    reinterpret_cast<int4*>(d)[j] = make_int4(0, 0, 0, 0);
+  for (int64_t i = 4 * nv + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < P.cn; i += stride)
+    d[i] = 0;
+  if (last_block(sync + kArrive + kArrCntDone)) {
+    if (threadIdx.x == 0) sync[kSeqCnt] = target;
+  }
+}
+
+int grid_for(int64_t items) {
+  const int64_t b = surfk::ceil_div(items, 256);
+  return static_cast<int>(b < 1 ? 1 : (b > 148 * 2 ? 148 * 2 : b));
+}
+
+// ---- IPC bookkeeping -----------------------------------------------------------------------
+std::mutex g_mu;
+std::map<std::string, void*> g_opened;    // handle bytes -> mapped base (one mapping per allocation)
+
+}  // namespace
+
+SURF_EXPORT int surf_p2p_sync_words() { return kSyncWords; }
+SURF_EXPORT int surf_p2p_max_world() { return kMaxW; }
+SURF_EXPORT int surf_p2p_max_moments() { return kMaxMom; }
+
+// Handle of the allocation containing p (64 bytes) and p's offset in it.
+SURF_EXPORT int surf_ipc_handle(const void* p, void* handle_out, int64_t* offset_out) {
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  CUresult r = cuMemGetAddressRange(&base, &size, reinterpret_cast<CUdeviceptr>(p));
+  if (r != CUDA_SUCCESS) return 1000 + static_cast<int>(r);
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return static_cast<int>(e);
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = static_cast<int64_t>(reinterpret_cast<uintptr_t>(p) - static_cast<uintptr_t>(base));
+  return 0;
+}
+
+// Map a peer's allocation (once per allocation) and return base + offset.
+SURF_EXPORT int surf_ipc_open(const void* handle, int64_t offset, void** ptr_out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  const std::string key(static_cast<const char*>(handle), sizeof(cudaIpcMemHandle_t));
+  auto it = g_opened.find(key);
+  void* base = nullptr;
+  if (it != g_opened.end()) {
+    base = it->second;
+  } else {
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    g_opened[key] = base;
+  }
+  *ptr_out = static_cast<char*>(base) + offset;
+  return 0;
+}
+
+// Unmap every peer allocation opened by this process.
+SURF_EXPORT int surf_ipc_close_all() {
+  std::lock_guard<std::mutex> lk(g_mu);
+  int rc = 0;
+  for (auto& kv : g_opened) {
+    cudaError_t e = cudaIpcCloseMemHandle(kv.second);
+    if (e != cudaSuccess && rc == 0) rc = static_cast<int>(e);
+  }
+  g_opened.clear();
+  return rc;
+}
+
+// Host-side plan (no device memory is allocated here).
+SURF_EXPORT void* surf_p2p_create(int rank, int world, void* const* sync_peers, double timeout_s) {
+  if (world < 1 || world > kMaxW || rank < 0 || rank >= world) return nullptr;
+  Plan* p = new Plan();
+  p->rank = rank;
+  p->world = world;
+  p->timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
+  for (int q = 0; q < world; ++q) p->sync_peer[q] = static_cast<uint64_t*>(sync_peers[q]);
+  p->sync = p->sync_peer[rank];
+  return p;
+}
+
+SURF_EXPORT void surf_p2p_destroy(void* plan) { delete static_cast<Plan*>(plan); }
+
+// Shard = ceil(n / world) rounded up to 4 elements; every buffer must be
+// 16-byte aligned (torch allocations are).
+SURF_EXPORT int surf_p2p_set_grad(void* plan, int64_t n, void* const* grad_peers, void* const* p_peers,
+                                  void* const* p16_peers, float* m, float* v, float* hyper) {
+  Plan* P = static_cast<Plan*>(plan);
+  P->n = n;
+  P->shard = surfk::ceil_div(surfk::ceil_div(n, P->world), 4) * 4;
+  for (int q = 0; q < P->world; ++q) {
+    P->grad_peer[q] = static_cast<float*>(grad_peers[q]);
+    P->p_peer[q] = static_cast<float*>(p_peers[q]);
+    P->p16_peer[q] = static_cast<uint16_t*>(p16_peers[q]);
+    if ((reinterpret_cast<uintptr_t>(grad_peers[q]) | reinterpret_cast<uintptr_t>(p_peers[q])) & 15u)
+      return static_cast<int>(cudaErrorMisalignedAddress);
+    if (reinterpret_cast<uintptr_t>(p16_peers[q]) & 7u) return static_cast<int>(cudaErrorMisalignedAddress);
+  }
+  P->m = m;
+  P->v = v;
+  P->hyper = hyper;
+  if ((reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v)) & 15u)
+    return static_cast<int>(cudaErrorMisalignedAddress);
+  return 0;
+}
+
+SURF_EXPORT int64_t surf_p2p_shard(void* plan) { return static_cast<Plan*>(plan)->shard; }
+
+SURF_EXPORT int surf_p2p_set_counts(void* plan, int64_t n, int* counts, void* const* delta_peers) {
+  Plan* P = static_cast<Plan*>(plan);
+  P->cn = n;
+  P->counts = counts;
+  for (int q = 0; q < P->world; ++q) {
+    P->delta_peer[q] = static_cast<int*>(delta_peers[q]);
+    if (reinterpret_cast<uintptr_t>(delta_peers[q]) & 15u) return static_cast<int>(cudaErrorMisalignedAddress);
+  }
+  return reinterpret_cast<uintptr_t>(counts) & 15u ? static_cast<int>(cudaErrorMisalignedAddress) : 0;
+}
+
+SURF_EXPORT int surf_p2p_grad_step(void* plan, void* stream) {
+  const Plan& P = *static_cast<const Plan*>(plan);
+  if (!P.n) return static_cast<int>(cudaErrorInvalidValue);
+  auto s = static_cast<cudaStream_t>(stream);
+  const int g = grid_for(surfk::ceil_div(P.shard, 4));
+  grad_rs_kernel<<<g, 256, 0, s>>>(P);
+  grad_adam_kernel<<<g, 256, 0, s>>>(P);
+  grad_done_kernel<<<grid_for(surfk::ceil_div(P.n, 4)), 256, 0, s>>>(P);
+  SURF_RETURN_LAUNCH();
+}
+
+SURF_EXPORT int surf_p2p_moments(void* plan, double* mom, int cnt, void* stream) {
+  const Plan& P = *static_cast<const Plan*>(plan);
+  if (cnt < 1 || cnt > kMaxMom) return static_cast<int>(cudaErrorInvalidValue);
+  moments_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(P, mom, cnt);
+  SURF_RETURN_LAUNCH();
+}
+
+SURF_EXPORT int surf_p2p_merge_counts(void* plan, void* stream) {
+  const Plan& P = *static_cast<const Plan*>(plan);
+  if (!P.cn) return static_cast<int>(cudaErrorInvalidValue);
+  auto s = static_cast<cudaStream_t>(stream);
+  const int g = grid_for(surfk::ceil_div(P.cn, 4));
+  counts_add_kernel<<<g, 256, 0, s>>>(P);
+  counts_done_kernel<<<g, 256, 0, s>>>(P);
+  SURF_RETURN_LAUNCH();
+}

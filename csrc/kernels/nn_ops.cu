@@ -2,8 +2,9 @@
 //
 //   * im2col: NHWC bf16 activations -> convolution patch rows (kh, kw, c order)
 //     so that a convolution is one tensor-core GEMM;
-//   * col2im_relu: the transposed scatter, written as a gather (no atomics),
-//     fused with the ReLU derivative of the layer below;
+//   * col2im_relu: the transposed scatter, written as a gather (no atomics,
+//     8 channels per thread, only the stride-congruent taps visited), fused
+//     with the ReLU derivative of the layer below;
 //   * colsum: bias gradients (sum of dY over rows), fp32 accumulation;
 //   * gather_rows: minibatch rows of the rollout buffers (any element size);
 //   * cast kernels between fp32 and bf16.
@@ -19,68 +20,131 @@ struct ConvGeom {
   int OH, OW;
 };
 
-// one thread per (output row, kh, 8-element chunk of the kw*C run)
+// One thread per (output pixel, kh, 8-element chunk of the kw*C run) of ONE
+// image: blockIdx.y is the image, so all index math is 32-bit.
 __global__ void im2col_kernel(const uint16_t* x, uint16_t* col, int64_t ldcol, ConvGeom g) {
   const int run = g.KW * g.C;                 // contiguous elements per kh
   const int chunks = (run + 7) / 8;
-  const int64_t total = static_cast<int64_t>(g.B) * g.OH * g.OW * g.KH * chunks;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int ch = static_cast<int>(i % chunks);
-    int64_t r = i / chunks;
-    const int kh = static_cast<int>(r % g.KH);
-    const int64_t row = r / g.KH;
-    const int ow = static_cast<int>(row % g.OW);
-    const int64_t t = row / g.OW;
-    const int oh = static_cast<int>(t % g.OH);
-    const int b = static_cast<int>(t / g.OH);
-    const int ih = oh * g.S + kh, iw = ow * g.S;
-    const uint16_t* src = x + ((static_cast<int64_t>(b) * g.H + ih) * g.W + iw) * g.C;
-    uint16_t* dst = col + row * ldcol + kh * run;
-    const int e0 = ch * 8;
-    const int n = min(8, run - e0);
-    if (n == 8 && ((reinterpret_cast<uintptr_t>(src + e0) | reinterpret_cast<uintptr_t>(dst + e0)) & 15) == 0) {
-      *reinterpret_cast<uint4*>(dst + e0) = *reinterpret_cast<const uint4*>(src + e0);
-    } else if (n == 8 && ((reinterpret_cast<uintptr_t>(src + e0) | reinterpret_cast<uintptr_t>(dst + e0)) & 3) == 0) {
-      const uint32_t* s4 = reinterpret_cast<const uint32_t*>(src + e0);
-      uint32_t* d4 = reinterpret_cast<uint32_t*>(dst + e0);
-      d4[0] = s4[0]; d4[1] = s4[1]; d4[2] = s4[2]; d4[3] = s4[3];
-    } else {
-      for (int e = 0; e < n; ++e) dst[e0 + e] = src[e0 + e];
+  const int per_image = g.OH * g.OW * g.KH * chunks;
+  for (int b = blockIdx.y; b < g.B; b += gridDim.y) {
+    const uint16_t* xb = x + static_cast<int64_t>(b) * g.H * g.W * g.C;
+    uint16_t* cb = col + static_cast<int64_t>(b) * g.OH * g.OW * ldcol;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < per_image; i += gridDim.x * blockDim.x) {
+      const int ch = i % chunks;
+      const int r = i / chunks;
+      const int kh = r % g.KH;
+      const int pix = r / g.KH;               // oh * OW + ow
+      const int ow = pix % g.OW, oh = pix / g.OW;
+      const uint16_t* src = xb + ((oh * g.S + kh) * g.W + ow * g.S) * g.C;
+      uint16_t* dst = cb + pix * ldcol + kh * run;
+      const int e0 = ch * 8;
+      const int n = min(8, run - e0);
+      const uintptr_t al = reinterpret_cast<uintptr_t>(src + e0) | reinterpret_cast<uintptr_t>(dst + e0);
+      if (n == 8 && (al & 15) == 0) {
+        *reinterpret_cast<uint4*>(dst + e0) = __ldg(reinterpret_cast<const uint4*>(src + e0));
+      } else if (n == 8 && (al & 7) == 0) {
+        const uint2* s2 = reinterpret_cast<const uint2*>(src + e0);
+        uint2* d2 = reinterpret_cast<uint2*>(dst + e0);
+        d2[0] = __ldg(s2);
+        d2[1] = __ldg(s2 + 1);
+      } else {
+        for (int e = 0; e < n; ++e) dst[e0 + e] = src[e0 + e];
+      }
     }
   }
 }
 
-// dX[b, ih, iw, c] = relu'(X) * sum over the (kh, kw) taps that read it of dcol
+// dX[b, ih, iw, c..c+7] = relu'(X) * sum over the taps (kh, kw) that read the
+// pixel of dcol[row(oh, ow), (kh, kw, c..c+7)], 8 channels per thread (C % 8 == 0).
+// Only the taps congruent to the pixel modulo the stride are visited.
 __global__ void col2im_kernel(const uint16_t* dcol, int64_t ldcol, const uint16_t* x_act, uint16_t* dx, ConvGeom g,
                               int relu) {
-  const int64_t total = static_cast<int64_t>(g.B) * g.H * g.W * g.C;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int c = static_cast<int>(i % g.C);
-    int64_t t = i / g.C;
-    const int iw = static_cast<int>(t % g.W);
-    t /= g.W;
-    const int ih = static_cast<int>(t % g.H);
-    const int b = static_cast<int>(t / g.H);
-    float acc = 0.0f;
-    if (!relu || surfk::bf16_to_f32(x_act[i]) > 0.0f) {
-      for (int kh = 0; kh < g.KH; ++kh) {
-        const int oh_s = ih - kh;
-        if (oh_s < 0 || oh_s % g.S) continue;
-        const int oh = oh_s / g.S;
-        if (oh >= g.OH) continue;
-        for (int kw = 0; kw < g.KW; ++kw) {
-          const int ow_s = iw - kw;
-          if (ow_s < 0 || ow_s % g.S) continue;
-          const int ow = ow_s / g.S;
-          if (ow >= g.OW) continue;
-          const int64_t row = (static_cast<int64_t>(b) * g.OH + oh) * g.OW + ow;
-          acc += surfk::bf16_to_f32(dcol[row * ldcol + (kh * g.KW + kw) * g.C + c]);
+  const int cv = g.C / 8;
+  const int per_image = g.H * g.W * cv;
+  for (int b = blockIdx.y; b < g.B; b += gridDim.y) {
+    const int64_t img = static_cast<int64_t>(b) * g.H * g.W * g.C;
+    const uint16_t* db = dcol + static_cast<int64_t>(b) * g.OH * g.OW * ldcol;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < per_image; i += gridDim.x * blockDim.x) {
+      const int v = i % cv;
+      const int pix = i / cv;
+      const int iw = pix % g.W, ih = pix / g.W;
+      const int64_t off = img + static_cast<int64_t>(pix) * g.C + v * 8;
+      uint4 mask = make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
+      if (relu) {
+        const uint4 xa = __ldg(reinterpret_cast<const uint4*>(x_act + off));
+        const uint32_t w4[4] = {xa.x, xa.y, xa.z, xa.w};
+        uint32_t m4[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          // bf16 > 0: sign clear and non-zero magnitude, per half-word
+          const uint32_t lo = (w4[q] & 0x8000u) == 0 && (w4[q] & 0x7fffu) != 0 ? 0x0000ffffu : 0u;
+          const uint32_t hi = (w4[q] & 0x80000000u) == 0 && (w4[q] & 0x7fff0000u) != 0 ? 0xffff0000u : 0u;
+          m4[q] = lo | hi;
+        }
+        mask = make_uint4(m4[0], m4[1], m4[2], m4[3]);
+      }
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (mask.x | mask.y | mask.z | mask.w) {
+        for (int kh = ih % g.S; kh < g.KH; kh += g.S) {
+          const int oh = (ih - kh) / g.S;
+          if (oh < 0) break;
+          if (oh >= g.OH) continue;
+          for (int kw = iw % g.S; kw < g.KW; kw += g.S) {
+            const int ow = (iw - kw) / g.S;
+            if (ow < 0) break;
+            if (ow >= g.OW) continue;
+            const uint4 d = __ldg(reinterpret_cast<const uint4*>(db + static_cast<int64_t>(oh * g.OW + ow) * ldcol +
+                                                                 (kh * g.KW + kw) * g.C + v * 8));
+            const uint32_t w4[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              acc[2 * q] += __uint_as_float(w4[q] << 16);
+              acc[2 * q + 1] += __uint_as_float(w4[q] & 0xffff0000u);
+            }
+          }
         }
       }
+      uint4 o;
+      uint32_t* o4 = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        o4[q] = static_cast<uint32_t>(surfk::f32_to_bf16(acc[2 * q])) |
+                (static_cast<uint32_t>(surfk::f32_to_bf16(acc[2 * q + 1])) << 16);
+      o.x &= mask.x; o.y &= mask.y; o.z &= mask.z; o.w &= mask.w;
+      *reinterpret_cast<uint4*>(dx + off) = o;
     }
-    dx[i] = surfk::f32_to_bf16(acc);
+  }
+}
+
+// out[n] += sum_m X[m, n] for bf16 X with N % 8 == 0 and 16-byte aligned rows:
+// each thread owns one 8-column chunk of a row slot and accumulates in fp32.
+__global__ void __launch_bounds__(256) colsum_vec_kernel(const uint16_t* x, int64_t ldx, int64_t M, int N,
+                                                         float* out) {
+  const int chunks = N / 8;
+  const int slots = blockDim.x / chunks;          // rows in flight per block
+  const int c = threadIdx.x % chunks, slot = threadIdx.x / chunks;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (slot < slots) {
+    for (int64_t m = static_cast<int64_t>(blockIdx.x) * slots + slot; m < M;
+         m += static_cast<int64_t>(gridDim.x) * slots) {
+      const uint4 d = __ldg(reinterpret_cast<const uint4*>(x + m * ldx + c * 8));
+      const uint32_t w4[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] += __uint_as_float(w4[q] << 16);
+        acc[2 * q + 1] += __uint_as_float(w4[q] & 0xffff0000u);
+      }
+    }
+  }
+  extern __shared__ float red[];                  // [blockDim.x][8]
+#pragma unroll
+  for (int e = 0; e < 8; ++e) red[threadIdx.x * 8 + e] = slot < slots ? acc[e] : 0.0f;
+  __syncthreads();
+  for (int j = threadIdx.x; j < N; j += blockDim.x) {
+    const int cc = j / 8, e = j % 8;
+    float s = 0.0f;
+    for (int sl = 0; sl < slots; ++sl) s += red[(sl * chunks + cc) * 8 + e];
+    atomicAdd(out + j, s);
   }
 }
 
@@ -140,17 +204,22 @@ int blocks_for(int64_t work, int threads) {
 SURF_EXPORT int surf_im2col(const void* x, int B, int H, int W, int C, int KH, int KW, int S, void* col, int64_t ldcol,
                             void* stream) {
   ConvGeom g{B, H, W, C, KH, KW, S, (H - KH) / S + 1, (W - KW) / S + 1};
-  const int64_t work = static_cast<int64_t>(B) * g.OH * g.OW * KH * ((KW * C + 7) / 8);
-  im2col_kernel<<<blocks_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t*>(x), static_cast<uint16_t*>(col), ldcol, g);
+  const int per_image = g.OH * g.OW * KH * ((KW * C + 7) / 8);
+  dim3 grid(static_cast<unsigned>(surfk::ceil_div(per_image, 256)), static_cast<unsigned>(B < 65535 ? B : 65535));
+  im2col_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const uint16_t*>(x),
+                                                                      static_cast<uint16_t*>(col), ldcol, g);
   SURF_RETURN_LAUNCH();
 }
 
 SURF_EXPORT int surf_col2im(const void* dcol, int64_t ldcol, const void* x_act, void* dx, int B, int H, int W, int C,
                             int KH, int KW, int S, int relu, void* stream) {
   ConvGeom g{B, H, W, C, KH, KW, S, (H - KH) / S + 1, (W - KW) / S + 1};
-  const int64_t work = static_cast<int64_t>(B) * H * W * C;
-  col2im_kernel<<<blocks_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  if ((C & 7) || (ldcol & 7) || ((reinterpret_cast<uintptr_t>(dcol) | reinterpret_cast<uintptr_t>(dx) |
+                                  reinterpret_cast<uintptr_t>(x_act)) & 15))
+    return static_cast<int>(cudaErrorInvalidValue);     // 8-channel vectors need C % 8 == 0 and aligned rows
+  const int per_image = H * W * (C / 8);
+  dim3 grid(static_cast<unsigned>(surfk::ceil_div(per_image, 256)), static_cast<unsigned>(B < 65535 ? B : 65535));
+  col2im_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(dcol), ldcol, static_cast<const uint16_t*>(x_act), static_cast<uint16_t*>(dx), g,
       relu);
   SURF_RETURN_LAUNCH();
@@ -158,8 +227,17 @@ SURF_EXPORT int surf_col2im(const void* dcol, int64_t ldcol, const void* x_act, 
 
 // out (fp32 [N]) += column sums of X ([M, N], bf16 if bf16 != 0 else fp32)
 SURF_EXPORT int surf_colsum(const void* x, int bf16, int64_t ldx, int64_t M, int N, float* out, void* stream) {
-  dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>(M / 64 > 256 ? 256 : (M / 64 < 1 ? 1 : M / 64)));
   auto s = static_cast<cudaStream_t>(stream);
+  if (bf16 && N % 8 == 0 && N <= 2048 && ldx % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const int slots = 256 / (N / 8) > 0 ? 256 / (N / 8) : 1;
+    const int threads = N / 8 > 256 ? N / 8 : 256;
+    const int64_t want = surfk::ceil_div(M, static_cast<int64_t>(slots) * 16);
+    const int blocks = static_cast<int>(want < 1 ? 1 : (want > 148 * 4 ? 148 * 4 : want));
+    colsum_vec_kernel<<<blocks, threads, threads * 8 * sizeof(float), s>>>(static_cast<const uint16_t*>(x), ldx, M, N,
+                                                                          out);
+    SURF_RETURN_LAUNCH();
+  }
+  dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>(M / 64 > 256 ? 256 : (M / 64 < 1 ? 1 : M / 64)));
   if (bf16) colsum_kernel<uint16_t><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(x), ldx, M, N, out);
   else colsum_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(x), ldx, M, N, out);
   SURF_RETURN_LAUNCH();

@@ -12,6 +12,7 @@
 
 #include "bspwrite.hpp"
 #include "env.hpp"
+#include "mesh.hpp"
 
 using namespace surf;
 
@@ -171,6 +172,24 @@ SURFSIM_API void surfsim_export_hull0(void* h, float* planes4, int32_t* ptype, i
     nodes3[3 * i + 2] = m.hull0[i].child[1];
   }
   *headnode = m.models[0].headnode[0];
+}
+// Triangle mesh of the solid geometry (world + solid brush entities):
+// float32 xyz vertices and int32 triangle indices. n_out = {vertices,
+// triangles}; buffers are filled only when their capacity suffices (call
+// once with zero capacities for the sizes).
+SURFSIM_API int32_t surfsim_export_mesh(void* h, float* verts, int32_t cap_verts, int32_t* tris, int32_t cap_tris,
+                                        int32_t* n_out) {
+  const Map& m = MAP(h);
+  std::vector<float> v;
+  std::vector<int32_t> t;
+  const float zero[3] = {0.0f, 0.0f, 0.0f};
+  solid_mesh(m, 0, zero, 1.0f, v, t);
+  for (const BrushEntity& s : m.solids) solid_mesh(m, s.model, s.origin, 1.0f, v, t);
+  n_out[0] = static_cast<int32_t>(v.size() / 3);
+  n_out[1] = static_cast<int32_t>(t.size() / 3);
+  if (verts && cap_verts >= n_out[0]) std::memcpy(verts, v.data(), v.size() * sizeof(float));
+  if (tris && cap_tris >= n_out[1]) std::memcpy(tris, t.data(), t.size() * sizeof(int32_t));
+  return 0;
 }
 // Solid brush entities for GPU occupancy: per entity 10 floats = hull-0 head
 // node (int32 bits), origin xyz, absmin xyz, absmax xyz. Returns the count.

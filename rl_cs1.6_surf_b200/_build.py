@@ -65,7 +65,7 @@ def _targets():
     for name, srcs in groups.items():
         srcs = [s for s in srcs if Path(s).exists()]
         if srcs:
-            t[name] = ("nvcc", srcs, [], ["-lcuda"] if name in ("libsurf_nn.so",) else [])
+            t[name] = ("nvcc", srcs, [], ["-lcuda"] if name in ("libsurf_nn.so", "libsurf_comm.so") else [])
     return t
 
 

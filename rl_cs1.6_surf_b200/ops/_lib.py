@@ -40,16 +40,34 @@ class KernelError(RuntimeError):
 _bound: dict = {}
 
 
-def lib(name: str) -> ctypes.CDLL:
+class _Bound:
+    """A loaded library exposing only its registered entry points.
+
+    ctypes would call an entry point without a signature by converting every
+    Python int to a C int, silently truncating 64-bit device pointers; an
+    unregistered name therefore raises instead."""
+
+    def __init__(self, name: str, cdll: ctypes.CDLL):
+        self._name = name
+        self._cdll = cdll
+        for fn, (res, args) in _SIGS.get(name, {}).items():
+            f = getattr(cdll, fn)
+            f.restype = res
+            f.argtypes = args
+            setattr(self, fn, f)
+
+    def __getattr__(self, fn: str):
+        if fn.startswith("surf_"):
+            raise AttributeError(f"{self._name}: entry point {fn} has no registered signature")
+        raise AttributeError(fn)
+
+
+def lib(name: str) -> _Bound:
     if name in _bound:
         return _bound[name]
-    l = load(name)
-    for fn, (res, args) in _SIGS.get(name, {}).items():
-        f = getattr(l, fn)
-        f.restype = res
-        f.argtypes = args
-    _bound[name] = l
-    return l
+    b = _Bound(name, load(name))
+    _bound[name] = b
+    return b
 
 
 def register(name: str, sigs: dict) -> None:

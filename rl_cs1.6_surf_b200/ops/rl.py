@@ -20,6 +20,7 @@ from typing import Optional
 import torch
 
 from . import _lib
+from . import gemm as _gemm  # noqa: F401  (registers the libsurf_nn.so signatures the optimizer uses)
 from ._lib import check, ptr, stream_ptr
 
 RLIB = "libsurf_rl.so"
@@ -172,15 +173,22 @@ def ppo_loss(out: torch.Tensor, value_col: int, act: torch.Tensor, old_logp, adv
 
 
 def ppo_loss_reference(logits_value, value_col: int, act, old_logp, adv, ret, layout, log_std, clip: float,
-                       vf_coef: float, ent_coef: float, norm_adv: bool = True):
+                       vf_coef: float, ent_coef: float, norm_adv: bool = True, moments=None):
     """Scalar loss in autograd form (reference mb_step, python/train_fast.py:1846-1864):
-    returns (loss, pg, vl, entropy)."""
+    returns (loss, pg, vl, entropy). ``moments`` = (sum, sum of squares, count)
+    of the advantages over the whole (multi-rank) minibatch; by default the
+    local minibatch's mean and std (ddof=1) normalise them."""
     logits = logits_value[:, :value_col]
     value = logits_value[:, value_col]
     logp, ent = log_prob_reference(logits, act, layout, log_std)
     ratio = torch.exp(logp - old_logp)
     a = adv
-    if norm_adv:
+    if norm_adv and moments is not None:
+        s, ss, n = (float(x) for x in moments)
+        mean = s / n
+        std = max((ss - s * mean) / max(n - 1.0, 1.0), 0.0) ** 0.5
+        a = (a - mean) / (std + 1e-8)
+    elif norm_adv:
         a = (a - a.mean()) / (a.std() + 1e-8)
     pg = torch.max(-a * ratio, -a * torch.clamp(ratio, 1 - clip, 1 + clip)).mean()
     vl = 0.5 * (value - ret).pow(2).mean()

@@ -107,6 +107,15 @@ class GoalFieldData:
     def valid_max(self) -> float:
         return self.reach_max + 0.5 * self.cell
 
+    def save(self, path) -> None:
+        np.savez_compressed(path, grid=self.grid, mins=self.mins, cell=self.cell, quant=self.quant,
+                            reach_max=self.reach_max)
+
+    @classmethod
+    def load(cls, path) -> "GoalFieldData":
+        z = np.load(path)
+        return cls(z["grid"], z["mins"].astype(np.float64), float(z["cell"]), float(z["quant"]), float(z["reach_max"]))
+
     def sample(self, pos: np.ndarray) -> np.ndarray:
         """Honest-corner trilinear sample (numpy), float32."""
         g = (np.atleast_2d(np.asarray(pos, np.float64)) - self.mins) / self.cell - 0.5

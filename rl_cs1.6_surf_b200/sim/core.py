@@ -193,6 +193,7 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
         "surfsim_map_bounds": (None, [c_void_p, _P_F, _P_F]),
         "surfsim_map_counts": (None, [c_void_p, _P_I]),
         "surfsim_export_hull0": (None, [c_void_p, c_void_p, c_void_p, c_void_p, _P_I]),
+        "surfsim_export_mesh": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_int32, _P_I]),
         "surfsim_solid_entities": (c_int32, [c_void_p, c_void_p, c_int32]),
         "surfsim_triggers": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32]),
         "surfsim_trigger_contains": (None, [c_void_p, c_int32, c_void_p, c_int64, c_int32, c_void_p]),
@@ -231,7 +232,8 @@ class TraceResult:
 
 
 def default_threads() -> int:
-    """Env worker threads: the CPUs this process may use, minus one for the
+    """Env worker threads: this process's share of the CPUs it may use (the
+    node's ranks, LOCAL_WORLD_SIZE, split them evenly), minus one for the
     Python/GPU-driving thread, capped at 64 (overridable via SURF_THREADS)."""
     env = os.environ.get("SURF_THREADS")
     if env:
@@ -240,7 +242,8 @@ def default_threads() -> int:
         n = len(os.sched_getaffinity(0))
     except AttributeError:   # pragma: no cover
         n = os.cpu_count() or 4
-    return max(1, min(64, n - 1))
+    local = max(1, int(os.environ.get("LOCAL_WORLD_SIZE", "1")))
+    return max(1, min(64, n // local - 1))
 
 
 class SimCore:
@@ -445,6 +448,15 @@ class SimCore:
         self.lib.surfsim_export_hull0(self._h, c_void_p(planes.ctypes.data), c_void_p(types.ctypes.data),
                                       c_void_p(nodes.ctypes.data), ctypes.byref(head))
         return planes, types, nodes, int(head.value)
+
+    def export_mesh(self):
+        """(vertices float32 [V, 3], triangles int32 [T, 3]) of the solid geometry."""
+        n = (c_int32 * 2)()
+        self.lib.surfsim_export_mesh(self._h, None, 0, None, 0, n)
+        v = np.zeros((n[0], 3), np.float32)
+        t = np.zeros((n[1], 3), np.int32)
+        self.lib.surfsim_export_mesh(self._h, c_void_p(v.ctypes.data), n[0], c_void_p(t.ctypes.data), n[1], n)
+        return v, t
 
     def solid_entities(self) -> np.ndarray:
         """(n, 10) float32 rows: hull-0 head node (int32 bits), origin, absmin, absmax."""

@@ -266,6 +266,13 @@ def random_field_map(seed: int = 0, n_brushes: int = 512, cell: float = 16.0,
     _kill_net(b, (lo[0], lo[1], 0), (hi[0], hi[1], 64), (0.0, 0.0, hi[2] - 200))
     for r in ramps[:16]:
         b.point("info_player_start", r.face_point(0.0, 1.0, 0.0) + np.array([0, 0, 400.0]), angle=f"{r.yaw:g}")
+    # a start platform whose -y edge drops onto a 50-degree face (the timed-map
+    # convention; fixed geometry, so the seeded brushes above are unchanged)
+    start = Ramp(cx=0.0, cy=0.0, z0=1600.0, yaw=0.0, length=2400.0, width=800.0, angle=50.0)
+    b.world(start.planes())
+    top = start.z0 + start.height + 64.0
+    b.world(box_planes((-128.0, 250.0, top - 32.0), (128.0, 506.0, top)))
+    b.point("info_player_start", (0.0, 378.0, top + 37.0), angle="270")
     image = b.compile()
     core = _probe_core(image)
     pool = drop_spawns(core, ramps, rng, spawns, zmax=hi[2])

@@ -18,7 +18,8 @@ RUN_DEFINING = (
     "ent", "ent_final", "vf", "max_grad_norm", "spawn", "teleport_fail", "yaw_jitter", "maxvel", "airaccelerate",
     "vision", "lidar_w", "lidar_h", "lidar_range", "lidar_near", "lidar_cell", "pinhole", "march_steps",
     "continuous_yaw", "gps", "heads", "hidden", "fc", "proprio", "mlp", "reward", "pitch_rate", "yaw_adaptive",
-    "respawn_frac", "respawn_margin", "respawn_reservoir", "train_stride",
+    "respawn_frac", "respawn_margin", "respawn_reservoir", "train_stride", "drop_frac", "drop_min", "drop_max",
+    "punch_min", "punch_max",
 )
 
 
@@ -29,7 +30,12 @@ class TrainConfig:
     map_seed: int = 0
     envs: int = 2048                   # per rank
     ep_ticks: int = 6000               # truncation (ticks)
-    spawn: str = "pool"                # pool (map's drop/start pool) | map (map spawn points)
+    spawn: str = "pool"                # pool (procedural drop pool) | drop | platform | mixed | ramp | map
+    drop_frac: float = 0.5             # mixed: fraction of drop starts
+    drop_min: float = 400.0            # drop height above the face (units)
+    drop_max: float = 800.0
+    punch_min: float = 100.0           # drop horizontal speed (u/s)
+    punch_max: float = 400.0
     teleport_fail: bool = True
     yaw_jitter: float = 8.0
     maxvel: float = 3500.0             # sv_maxvelocity (surf servers)

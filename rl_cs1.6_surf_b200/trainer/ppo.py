@@ -44,6 +44,27 @@ C_OBS, C_TOBS, C_REC, C_TREC, H_COLS = 0, 16, 32, 48, 64
 NOGPS = (0, 1, 2, 3, 4, 5, 6, 9, 10, 11)      # honest proprioception (no heading, no position)
 
 
+def build_spawn_pool(core, kind: str, cfg, procedural=None):
+    """The start-state pool of a spawn mode (reference --spawn, python/train_fast.py:1391-1426):
+    pool (the procedural map's drop pool, else a drop scan) | drop | platform | mixed | ramp | map."""
+    from ..sim import spawns
+    drops = lambda: spawns.drop_pool(core, h_range=(cfg.drop_min, cfg.drop_max),
+                                     speed_range=(cfg.punch_min, cfg.punch_max), seed=cfg.map_seed + 17)
+    if kind == "pool":
+        return procedural if procedural is not None else drops()
+    if kind == "drop":
+        return drops()
+    if kind == "platform":
+        return spawns.platform_pool(core)
+    if kind == "mixed":
+        return spawns.mixed_pool(spawns.platform_pool(core), drops(), cfg.drop_frac)
+    if kind == "ramp":
+        return spawns.ramp_pool(core)
+    if kind == "map":
+        return None
+    raise ValueError(f"unknown spawn mode {kind!r}")
+
+
 class Trainer:
     def __init__(self, cfg: TrainConfig, rank: int = 0, world: int = 1, comm=None, verbose: bool = True):
         self.cfg = cfg
@@ -57,6 +78,7 @@ class Trainer:
         self._setup_buffers()
         self.global_step = 0
         self.iteration = 0
+        self._env_ready = False
         self.timer = PhaseTimer(cfg.timing, self.gpu)
         self.last_stats: dict = {}
 
@@ -79,7 +101,12 @@ class Trainer:
             self.zones = json.loads(Path(zp).read_text()) if Path(zp).exists() else {}
             pool = None
         self.map_image = image
-        spawn_mode = 2 if (cfg.spawn == "pool" and pool is not None) else 0
+        probe = None
+        if cfg.spawn not in ("pool", "map") or (cfg.spawn == "pool" and pool is None):
+            probe = SimCore.from_bytes(image, default_config(1), threads=1)
+            pool = build_spawn_pool(probe, cfg.spawn, cfg, procedural=pool)
+            probe.close()
+        spawn_mode = 2 if (cfg.spawn != "map" and pool is not None) else 0
         env_cfg = default_config(cfg.envs, max_episode_ticks=cfg.ep_ticks, spawn_mode=spawn_mode,
                                  yaw_jitter_deg=cfg.yaw_jitter, sv_maxvelocity=cfg.maxvel,
                                  sv_airaccelerate=cfg.airaccelerate, pitch_rate_max_deg=cfg.pitch_rate,
@@ -168,6 +195,8 @@ class Trainer:
             self.loss_stats = torch.zeros(6, dtype=torch.float32, device=dev)
             self.sample_counter = torch.zeros(1, dtype=torch.int64, device=dev)
             self.reward = GpuReward(cfg.reward, N, self.K, self.bounds, dev, self.field, self.d0)
+            if self.comm is not None and hasattr(self.comm, "attach"):
+                self.comm.attach(self.net, self.opt, self.reward)
             self.rew_graphs: list = []
             self.upd_graph = None
             self.act_event = torch.cuda.Event()
@@ -402,7 +431,7 @@ class Trainer:
 
     def rollout_cpu(self) -> None:
         T = self.T
-        gen = torch.Generator().manual_seed(self.cfg.seed * 31 + self.iteration)
+        gen = torch.Generator().manual_seed(self.cfg.seed * 31 + self.iteration * 1_000_003 + self.rank * 7919)
         for t in range(T):
             self._cpu_obs(t)
             with torch.no_grad():
@@ -443,19 +472,29 @@ class Trainer:
         frac = min(1.0, self.global_step / max(1.0, cfg.steps))
         ent = cfg.ent if cfg.ent_final is None else cfg.ent + (cfg.ent_final - cfg.ent) * frac
         stats = np.zeros(4)
+        gen = torch.Generator().manual_seed(self.cfg.seed * 7919 + self.rank * 104729 + self.iteration)
         for _ in range(cfg.epochs):
-            perm = torch.randperm(T * N)
+            perm = torch.randperm(T * N, generator=gen)
             for m in range(cfg.minibatches):
                 idx = perm[m * mb:(m + 1) * mb]
+                a = self.adv.view(-1)[idx]
+                moments = None
+                if self.comm is not None:      # global advantage moments (sum, sum of squares, count)
+                    mom = torch.stack([a.double().sum(), (a.double() ** 2).sum(), torch.tensor(float(mb)).double()])
+                    self.comm.allreduce_moments(mom)
+                    moments = mom
                 params = self.net.autograd_params()
                 out = self.net.forward_reference(self.b_scal[:T].reshape(T * N, 16)[idx], None, params)
                 loss, pg, vl, en = R.ppo_loss_reference(out, self.layout.value_col, self.b_act.view(T * N, 8)[idx],
-                                                        self.b_logp.view(-1)[idx], self.adv.view(-1)[idx],
-                                                        self.ret.view(-1)[idx], self.layout, params["log_std"],
-                                                        cfg.clip, cfg.vf, ent)
-                loss.backward()
+                                                        self.b_logp.view(-1)[idx], a, self.ret.view(-1)[idx],
+                                                        self.layout, params["log_std"], cfg.clip, cfg.vf, ent,
+                                                        moments=moments)
+                (loss / self.world).backward()          # the summed gradient is the global-mean gradient
                 self.net.collect_grads(params)
-                self.opt.step_reference()
+                if self.comm is not None:
+                    self.comm.step(self.net, self.opt)
+                else:
+                    self.opt.step_reference()
                 stats += [pg.item(), vl.item(), en.item(), 1.0]
         return {"policy_loss": stats[0] / stats[3], "value_loss": stats[1] / stats[3], "entropy": stats[2] / stats[3]}
 
@@ -463,8 +502,9 @@ class Trainer:
     def train_iteration(self) -> dict:
         tm = self.timer
         tm.start_iter()
-        if self.iteration == 0 and self.global_step == 0:
+        if not self._env_ready:              # first iteration of this process (fresh or resumed run)
             self.reset()
+            self._env_ready = True
         self.iteration += 1
         t0 = tm.now()
         if self.gpu:
@@ -480,6 +520,8 @@ class Trainer:
             if self.comm is not None:
                 self.comm.merge_counts(self.reward)
             ls = self.loss_stats.tolist()
+            if self.comm is not None and hasattr(self.comm, "check"):
+                self.comm.check()
             n = max(ls[5], 1.0)
             loss = {"policy_loss": ls[0] / n, "value_loss": ls[1] / n, "entropy": ls[2] / n, "approx_kl": ls[3] / n,
                     "clip_frac": ls[4] / n}
@@ -493,13 +535,28 @@ class Trainer:
         self.last_stats = stats
         return stats
 
+    def release_graphs(self) -> None:
+        """Drop every captured CUDA graph (graphs holding NCCL calls must be
+        released before the process group is destroyed)."""
+        if self.gpu:
+            torch.cuda.synchronize()
+            self.rew_graphs = []
+            self.tail_graph = None
+            self.upd_graph = None
+            import gc
+            gc.collect()
+            torch.cuda.synchronize()
+
     # ---- checkpoints ----------------------------------------------------------------------------
     def state_dict(self) -> dict:
         counts = None
         if self.cfg.reward.int_coef > 0:
             c = self.reward.counts
             counts = (c.cpu().numpy() if torch.is_tensor(c) else c).astype(np.uint32)
-        return {"format": "surfb200-ckpt-1", "policy": self.net.state_dict(), "optimizer": self.opt.state_dict(),
+        opt = self.opt.state_dict()
+        if self.comm is not None and hasattr(self.comm, "full_optimizer_state"):
+            opt.update({k: v.cpu() for k, v in self.comm.full_optimizer_state(self.opt).items()})
+        return {"format": "surfb200-ckpt-1", "policy": self.net.state_dict(), "optimizer": opt,
                 "global_step": self.global_step, "iteration": self.iteration, "config": self.cfg.to_dict(),
                 "int_counts": counts}
 

@@ -14,3 +14,7 @@ _spec = _ilu.spec_from_file_location("surfb200", _os.path.join(_dir, "__init__.p
 _mod = _ilu.module_from_spec(_spec)
 _sys.modules["surfb200"] = _mod
 _spec.loader.exec_module(_mod)
+
+if __name__ == "__main__":      # python -m surfb200 <command> ...
+    from surfb200.cli import main as _main
+    _sys.exit(_main())
