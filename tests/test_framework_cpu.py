@@ -1,0 +1,174 @@
+"""CPU tests of the framework plumbing: spawn pools, scripted policies,
+adapters, mesh export, checkpoints / resume rules, run logs, the CLI."""
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+@pytest.fixture(scope="module")
+def field_core():
+    from surfb200.sim import mapgen
+    from surfb200.sim.core import SimCore, default_config
+    m = mapgen.generate("field", 0)
+    c = SimCore.from_bytes(m.image, default_config(4), threads=2)
+    yield c
+    c.close()
+
+
+def test_spawn_pools(field_core):
+    from surfb200.sim import spawns
+    p = spawns.platform_pool(field_core)
+    assert len(p) >= 1
+    faces = spawns.scan_faces(field_core)
+    assert len(faces[0]) > 100
+    assert np.all((faces[1][:, 2] > 0.35) & (faces[1][:, 2] < 0.68))
+    d = spawns.drop_pool(field_core, faces=faces)
+    speed = np.hypot(d["velocity"][:, 0], d["velocity"][:, 1])
+    assert len(d) > 100 and speed.min() >= 99.9 and speed.max() <= 400.1
+    # every drop start is free for the player hull
+    tr = field_core.trace_batch(d["origin"], d["origin"], hull=0)
+    assert not tr[:, 7].any()
+    r = spawns.ramp_pool(field_core, faces=faces)
+    assert len(r) > 10
+    mixed = spawns.mixed_pool(p, d, 0.5)
+    assert abs((len(mixed) - len(d)) / len(mixed) - 0.5) < 0.1
+    assert len(spawns.map_pool(field_core)) == len(field_core.spawns())
+
+
+def test_scripted_strafer_gains_speed_in_air():
+    """Air-strafe sync on a ramp: horizontal speed grows (air acceleration works)."""
+    from surfb200.sim import mapgen
+    from surfb200.sim.core import SimCore, default_config
+    from surfb200.sim.policies import RandomPolicy, ScriptedStrafer
+    m = mapgen.generate("ramps", 0)
+    core = SimCore.from_bytes(m.image, default_config(8, spawn_mode=2, max_episode_ticks=5000), threads=2)
+    core.set_spawn_pool(m.spawn_pool[:8])
+    core.reset(3)
+    pol = ScriptedStrafer(core, period_ticks=60)
+    v0 = np.hypot(core.states_view["velocity"][:, 0], core.states_view["velocity"][:, 1]).copy()
+    peak = v0.copy()
+    for _ in range(300):
+        core.step(pol.act(None))
+        v = np.hypot(core.states_view["velocity"][:, 0], core.states_view["velocity"][:, 1])
+        peak = np.maximum(peak, v)
+    assert (peak > v0 + 100).mean() >= 0.5
+    a = RandomPolicy(0).act(np.zeros((5, 15)))
+    assert a.shape == (5, 6) and (a < np.array([15, 7, 3, 3, 2, 2])).all()
+    core.close()
+
+
+def test_next_step_autoreset_shim():
+    from surfb200.sim import mapgen
+    from surfb200.sim.adapters import NextStepAutoreset
+    from surfb200.sim.core import SimCore, default_config
+    m = mapgen.generate("ramps", 0)
+    core = SimCore.from_bytes(m.image, default_config(4, max_episode_ticks=20), threads=1)
+    shim = NextStepAutoreset(core)
+    shim.reset(0)
+    act = np.tile(np.array([7, 3, 1, 1, 0, 0], np.int32), (4, 1))
+    saw_end = False
+    for t in range(45):
+        obs, rew, done, trunc = shim.step(act)
+        ended = done | trunc
+        if ended.any():
+            saw_end = True
+            obs2, rew2, done2, trunc2 = shim.step(act)
+            assert not (done2[ended] | trunc2[ended]).any()
+            assert np.all(rew2[ended] == 0.0)
+    assert saw_end
+    core.close()
+
+
+def test_mesh_export(tmp_path):
+    from surfb200.sim import mapgen
+    from surfb200.sim.core import SimCore, default_config
+    from surfb200.sim.export import export_mesh
+    m = mapgen.generate("ramps", 0)
+    core = SimCore.from_bytes(m.image, default_config(1), threads=1)
+    doc = export_mesh(core, m.name)
+    v = np.asarray(doc["vertices"]).reshape(-1, 3)
+    t = np.asarray(doc["indices"]).reshape(-1, 3)
+    assert len(t) > 50 and t.max() < len(v)
+    # every triangle's centroid lies on solid geometry's boundary: nudging it
+    # along the outward normal leaves the solid
+    p0, p1, p2 = v[t[:, 0]], v[t[:, 1]], v[t[:, 2]]
+    n = np.cross(p1 - p0, p2 - p0)
+    area = np.linalg.norm(n, axis=1)
+    ok = area > 1.0
+    n = n[ok] / area[ok, None]
+    c = (p0 + p1 + p2)[ok] / 3
+    outside = np.array([core.point_contents(x) for x in c + 2.0 * n])
+    inside = np.array([core.point_contents(x) for x in c - 2.0 * n])
+    assert (inside == -2).mean() > 0.95
+    assert (outside != -2).mean() > 0.6        # coplanar faces between adjacent solid cells face solid
+
+
+def test_checkpoint_resolve_rules(tmp_path):
+    from surfb200.trainer import checkpoint as C
+    from surfb200.trainer.config import TrainConfig
+    cfg = TrainConfig(envs=32, hidden=128, lr=1e-3)
+    sd = {"format": C.FORMAT, "config": cfg.to_dict(), "policy": {"flat": torch.zeros(3)}}
+    p = C.save(tmp_path / "ckpt_0000000001.pt", sd)
+    sd2 = C.load(p)
+    new, restored, changed = C.resolve_config(sd2, {"lr": 5e-4})
+    assert new.hidden == 128 and new.lr == 5e-4 and "lr" in changed and "hidden" in restored
+    with pytest.raises(C.CheckpointError):
+        C.resolve_config(sd2, {"hidden": 256})
+    bad = dict(sd2, config=dict(sd2["config"], mystery_flag=1))
+    assert C.audit(bad) == ["mystery_flag"]
+    assert C.find_resume(tmp_path) == p
+    cad = C.Cadence(100, 60.0, start_step=250)
+    assert not cad.numbered(299) and cad.numbered(300) and not cad.numbered(350) and cad.numbered(401)
+
+
+def test_runlog_csv_migration(tmp_path):
+    from surfb200.utils.runlog import CSV_COLS, RunLogger
+    (tmp_path / "progress.csv").write_text(",".join(CSV_COLS[:8]) + "\n1,2,3,4,5,6,7,8\n")
+    log = RunLogger(tmp_path, {"a": 1})
+    log.log({"global_step": 10, "iteration": 1, "policy_loss": 0.1, "value_loss": 0.2, "entropy": 1.0})
+    rows = (tmp_path / "progress.csv").read_text().splitlines()
+    assert rows[0].split(",") == list(CSV_COLS) and len(rows) == 3
+    assert len(rows[1].split(",")) == len(CSV_COLS)
+    log.finish({"x": 1})
+    doc = json.loads((tmp_path / "run.json").read_text())
+    assert doc["config"] == {"a": 1} and "finished" in doc
+
+
+def test_perf_report_parses_timing(tmp_path):
+    from surfb200.utils.perf_report import parse, summarise
+    p = tmp_path / "log.txt"
+    p.write_text("\n".join(f"TIMING iter={i} rollout={100 + i}.0 update=50.0 total={150 + i}.0" for i in range(40)))
+    s = summarise(parse(p), last=30)
+    assert s["update"]["median"] == 50.0 and s["total"]["n"] == 30
+
+
+def test_cli_train_resume_eval(tmp_path):
+    run = tmp_path / "run"
+    base = [sys.executable, str(ROOT / "surfb200.py")]
+    common = ["--map", "ramps", "--envs", "16", "--n-steps", "8", "--epochs", "1", "--minibatches", "2",
+              "--no-vision", "--device", "cpu", "--no-graphs", "--ep-ticks", "100", "--reward", "speed",
+              "--run", str(run), "--ckpt-every", "500", "--threads", "2"]
+    r = subprocess.run(base + ["train"] + common + ["--iterations", "2"], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert (run / "ckpt_final.pt").exists() and (run / "progress.csv").exists()
+    r = subprocess.run(base + ["train", "--ckpt", str(run), "--iterations", "1", "--lr", "1e-4"], capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "resumed from" in r.stdout and "overridden lr" in r.stdout
+    from surfb200.trainer import checkpoint as C
+    sd = C.load(run / "ckpt_final.pt")
+    assert sd["global_step"] == 3 * 16 * 8 * 3 and sd["config"]["lr"] == 1e-4
+    r = subprocess.run(base + ["eval", "--ckpt", str(run / "ckpt_final.pt"), "--episodes", "2", "--max-ticks", "90",
+                               "--out", str(tmp_path / "t.jsonl")], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    from surfb200.trainer.evaluate import read_trajectory
+    eps = read_trajectory(tmp_path / "t.jsonl")
+    assert len(eps) == 2 and eps[0]["header"]["tick_ms"] == 10 and eps[0]["trailer"]["end"] in ("done", "fail", "trunc")
+    assert eps[0]["ticks"].shape[1] == 15 and eps[0]["trailer"]["ticks"] == len(eps[0]["ticks"])
