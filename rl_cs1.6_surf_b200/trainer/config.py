@@ -19,7 +19,7 @@ RUN_DEFINING = (
     "vision", "lidar_w", "lidar_h", "lidar_range", "lidar_near", "lidar_cell", "pinhole", "march_steps",
     "continuous_yaw", "gps", "heads", "hidden", "fc", "proprio", "mlp", "reward", "pitch_rate", "yaw_adaptive",
     "respawn_frac", "respawn_margin", "respawn_reservoir", "train_stride", "drop_frac", "drop_min", "drop_max",
-    "punch_min", "punch_max",
+    "punch_min", "punch_max", "respawn_speed", "respawn_binned", "respawn_pool",
 )
 
 
@@ -77,9 +77,12 @@ class TrainConfig:
     # reward
     reward: RewardSpec = field(default_factory=RewardSpec)
     # respawn reservoir (Go-Explore restarts)
-    respawn_frac: float = 0.0
-    respawn_margin: float = 10.0
+    respawn_frac: float = 0.0          # share of episodes started from the reservoir (0 = off)
+    respawn_margin: float = 10.0       # seconds before an episode's end that are still harvestable
     respawn_reservoir: int = 100_000
+    respawn_speed: tuple = (0.9, 1.1)  # spawn speed multiplier range of reservoir starts
+    respawn_binned: int = 0            # distance bins for reservoir sampling (race; 0 = uniform)
+    respawn_pool: int = 4096
     # run
     seed: int = 0
     device: str = "cuda"
@@ -97,6 +100,7 @@ class TrainConfig:
         d["reward"] = self.reward.to_dict()
         d["heads"] = list(self.heads)
         d["mlp"] = list(self.mlp)
+        d["respawn_speed"] = list(self.respawn_speed)
         return d
 
     @classmethod
@@ -108,7 +112,7 @@ class TrainConfig:
                 continue
             if k == "reward":
                 v = RewardSpec.from_dict(v)
-            elif k in ("heads", "mlp"):
+            elif k in ("heads", "mlp", "respawn_speed"):
                 v = tuple(v)
             kw[k] = v
         return cls(**kw)

@@ -106,7 +106,12 @@ class Trainer:
             probe = SimCore.from_bytes(image, default_config(1), threads=1)
             pool = build_spawn_pool(probe, cfg.spawn, cfg, procedural=pool)
             probe.close()
-        spawn_mode = 2 if (cfg.spawn != "map" and pool is not None) else 0
+        if cfg.respawn_frac > 0 and pool is None:        # the reservoir needs pool spawning
+            from ..sim import spawns
+            probe = SimCore.from_bytes(image, default_config(1), threads=1)
+            pool = spawns.map_pool(probe)
+            probe.close()
+        spawn_mode = 2 if (cfg.spawn != "map" or cfg.respawn_frac > 0) and pool is not None else 0
         env_cfg = default_config(cfg.envs, max_episode_ticks=cfg.ep_ticks, spawn_mode=spawn_mode,
                                  yaw_jitter_deg=cfg.yaw_jitter, sv_maxvelocity=cfg.maxvel,
                                  sv_airaccelerate=cfg.airaccelerate, pitch_rate_max_deg=cfg.pitch_rate,
@@ -203,6 +208,36 @@ class Trainer:
         else:
             self.reward = CpuReward(cfg.reward, N, self.K, self.bounds, self.field, self.d0)
         self.seed_base = (self.cfg.seed * 1_000_003 + self.rank * 7_777_777) & 0xFFFFFFFFFFFF
+        self.respawn = None
+        if cfg.respawn_frac > 0:
+            from .respawn import RespawnReservoir
+            binned = cfg.respawn_binned > 0 and self.field is not None
+            self.respawn = RespawnReservoir(
+                N, cfg.respawn_reservoir, margin_ticks=int(round(cfg.respawn_margin * 100)), map_id=self._map_id(),
+                seed=cfg.seed * 31 + 23, dist_fn=self.field.sample if binned else None,
+                dist_max=self.d0 if binned else None, dist_valid_max=self.field.valid_max if binned else None,
+                bins=max(cfg.respawn_binned, 1), rank=self.rank)
+            self.start_pool = self.spawn_pool
+
+    def _map_id(self) -> str:
+        import hashlib
+        return hashlib.sha1(self.map_image).hexdigest()[:16]
+
+    def _observe_respawn(self, t: int) -> None:
+        if self.respawn is None:
+            return
+        h = self.hrec.numpy()
+        ended = (h[:, C_REC + 11] != 0) | (h[:, C_REC + 12] != 0)
+        self.respawn.observe(self.core.states_view, ended, ticks=self.K, step_index=t)
+
+    def _refresh_respawn_pool(self) -> None:
+        if self.respawn is None:
+            return
+        self.respawn.commit(self.comm if self.world > 1 else None)
+        pool = self.respawn.build_pool(self.start_pool, pool_size=self.cfg.respawn_pool,
+                                       fresh_frac=1.0 - self.cfg.respawn_frac,
+                                       vel_scale=tuple(self.cfg.respawn_speed))
+        self.core.set_spawn_pool(pool)
 
     # ---- environment plumbing -------------------------------------------------------------
     def _env_step(self) -> None:
@@ -343,6 +378,7 @@ class Trainer:
             t0 = tm.now()
             self._env_step()
             tm.add("env", t0)
+            self._observe_respawn(t)
             if self.cfg.ep_ticks and (self.hrec[:, C_REC + 12] != 0).any():
                 self._bootstrap_truncations()
             self.global_step += self.N * self.K * self.world
@@ -445,6 +481,7 @@ class Trainer:
             self.b_val[t].copy_(out[:, self.layout.value_col])
             self.act_pin.copy_(act)
             self._env_step()
+            self._observe_respawn(t)
             h = self.hrec.numpy()
             boot = None
             trunc = np.flatnonzero(h[:, C_REC + 12] != 0)
@@ -513,6 +550,9 @@ class Trainer:
             self.rollout_cpu()
         tm.add("rollout", t0)
         t0 = tm.now()
+        self._refresh_respawn_pool()
+        tm.add("respawn", t0)
+        t0 = tm.now()
         if self.gpu:
             ev = tm.gpu_start("update_gpu")
             self.update_gpu()
@@ -558,7 +598,7 @@ class Trainer:
             opt.update({k: v.cpu() for k, v in self.comm.full_optimizer_state(self.opt).items()})
         return {"format": "surfb200-ckpt-1", "policy": self.net.state_dict(), "optimizer": opt,
                 "global_step": self.global_step, "iteration": self.iteration, "config": self.cfg.to_dict(),
-                "int_counts": counts}
+                "int_counts": counts, "respawn": self.respawn.state_dict() if self.respawn is not None else None}
 
     def load_state_dict(self, sd: dict, reset_steps: bool = False, reset_counts: bool = False) -> None:
         self.net.load_state_dict(sd["policy"])
@@ -566,6 +606,9 @@ class Trainer:
         if not reset_steps:
             self.global_step = int(sd["global_step"])
             self.iteration = int(sd.get("iteration", 0))
+        if self.respawn is not None and sd.get("respawn"):
+            if not self.respawn.load_state_dict(sd["respawn"]) and self.verbose:
+                print("respawn reservoir not restored (empty, or recorded on another map)")
         c = sd.get("int_counts")
         if c is not None and not reset_counts and self.cfg.reward.int_coef > 0:
             if len(c) == len(self.reward.counts):

@@ -172,3 +172,60 @@ def test_cli_train_resume_eval(tmp_path):
     eps = read_trajectory(tmp_path / "t.jsonl")
     assert len(eps) == 2 and eps[0]["header"]["tick_ms"] == 10 and eps[0]["trailer"]["end"] in ("done", "fail", "trunc")
     assert eps[0]["ticks"].shape[1] == 15 and eps[0]["trailer"]["ticks"] == len(eps[0]["ticks"])
+
+
+def test_respawn_reservoir_rules():
+    from surfb200.sim.core import STATE_DTYPE
+    from surfb200.trainer.respawn import RespawnReservoir
+    n = 4
+    r = RespawnReservoir(n, reservoir=1000, margin_ticks=300, snap_every=100, map_id="m")
+    st = np.zeros(n, STATE_DTYPE)
+    for t in range(10):                    # 10 decisions of 100 ticks: snapshots at ticks 100..1000
+        st["origin"][:, 0] = t
+        ended = np.zeros(n, bool)
+        if t == 9:
+            ended[0] = True                # env 0 ends at tick 1000: snapshots at <= 700 are harvestable
+        r.observe(st, ended, ticks=100, step_index=t)
+    assert r.commit() == 7 and r.size == 7
+    assert set(r.store["origin"][:7, 0].tolist()) == set(range(7))
+    pool = r.build_pool(np.zeros(3, STATE_DTYPE), pool_size=100, fresh_frac=0.1)
+    assert len(pool) == 100
+    sd = r.state_dict()
+    r2 = RespawnReservoir(n, map_id="other")
+    assert not r2.load_state_dict(sd) and r2.size == 0
+    r3 = RespawnReservoir(n, map_id="m")
+    assert r3.load_state_dict(sd) and r3.size == 7
+
+
+def test_respawn_binned_sampling_flattens_bins():
+    from surfb200.sim.core import STATE_DTYPE
+    from surfb200.trainer.respawn import RespawnReservoir
+    r = RespawnReservoir(1, reservoir=5000, dist_fn=lambda o: o[:, 0], dist_max=1000.0, dist_valid_max=1000.0,
+                         bins=10)
+    rows = np.zeros(1900, STATE_DTYPE)
+    rows["origin"][:1000, 0] = np.random.default_rng(0).uniform(0, 100, 1000)    # crowded first bin
+    rows["origin"][1000:, 0] = np.random.default_rng(1).uniform(100, 1000, 900)  # sparser frontier bins
+    r.new_rows = [(0, i, rows[i]) for i in range(len(rows))]
+    r.commit()
+    pick = r.binned_pick(2000)
+    d = r.d[pick]
+    first = (d < 100).mean()
+    assert 0.08 < first < 0.2                 # ~1/10 of draws instead of 10/19
+    counts = np.bincount(np.clip((d // 100).astype(int), 0, 9), minlength=10)
+    per_bin_pop = np.bincount(np.clip((r.d[:r.size] // 100).astype(int), 0, 9), minlength=10)
+    assert np.all(counts <= 4 * per_bin_pop + 1)
+
+
+def test_trainer_respawn_cpu():
+    from surfb200.rewards.spec import RewardSpec
+    from surfb200.trainer.config import TrainConfig
+    from surfb200.trainer.ppo import Trainer
+    cfg = TrainConfig(map="ramps", envs=16, n_steps=32, epochs=1, minibatches=2, vision=False, device="cpu",
+                      graphs=False, ep_ticks=150, reward=RewardSpec(mode="speed"), respawn_frac=0.5,
+                      respawn_margin=0.3, threads=2)
+    tr = Trainer(cfg, verbose=False)
+    for _ in range(3):
+        tr.train_iteration()
+    assert tr.respawn.size > 0
+    sd = tr.state_dict()
+    assert sd["respawn"]["states"] is not None
