@@ -111,6 +111,9 @@ def main():
         del g
         torch.cuda.synchronize()
     comm.check()
+    phases = comm.phase_times_us()
+    pt = [None] * world
+    dist.all_gather_object(pt, phases)
     copy_us = results.pop("copy")
     fused_us = results["fused_p2p"] - copy_us
     nccl_us = results["nccl_allreduce_adam"] - copy_us
@@ -122,7 +125,8 @@ def main():
                           "speedup_vs_nccl": round(nccl_us / fused_us, 3) if fused_us > 0 else None,
                           "nvlink_bytes_per_direction": int(bytes_dir), "roofline_us": round(roof_us, 2),
                           "frac_of_roofline": round(roof_us / fused_us, 3) if fused_us > 0 else None,
-                          "link_gbs_measured": LINK_GBS, "grad_copy_us_subtracted": round(copy_us, 2)}), flush=True)
+                          "link_gbs_measured": LINK_GBS, "grad_copy_us_subtracted": round(copy_us, 2),
+                          "last_step_phases_us": [{k: round(v, 2) for k, v in p.items()} for p in pt]}), flush=True)
     comm.close()
 
 

@@ -6,32 +6,33 @@
 // the kernels below then read and write the peers' memory directly with
 // plain loads/stores over NVLink/NVSwitch. No TMA, no multicast.
 //
-// Gradient step (three kernels on the training stream, graph-capturable):
-//   grad_rs_kernel    barrier-in: tell every peer "my gradient is final",
-//                     wait until every peer said so; then reduce-scatter:
-//                     rank r sums shard r of all W gradients (fixed rank
-//                     order, fp32) into its own gradient buffer and the sum
-//                     of squares of the shard (fp64, deterministic block
-//                     order) is published to every peer's norm slot.
-//   grad_adam_kernel  wait for all W shard norms, global-norm clip
-//                     coefficient (identical on every rank: same values,
-//                     same order), Adam on the owned shard (m, v local),
-//                     then push the new fp32 and bf16 parameters of the
-//                     shard into every peer's parameter buffers; the last
-//                     block raises "done" on every peer.
-//   grad_done_kernel  wait for every peer's "done" (all parameters pushed
-//                     here and every peer finished reading my gradient),
-//                     zero the local gradient for the next backward and
-//                     advance the local sequence number.
+// Gradient step: ONE cooperative kernel (co-residency guaranteed by the
+// cooperative launch attribute, so in-kernel grid barriers are safe; the
+// launch is graph-capturable):
+//   A  barrier-in: tell every peer "my gradient is final"; wait for all.
+//   B  reduce-scatter: rank r sums shard r of all W gradients (fixed rank
+//      order, fp32, 8 elements per thread step) into its own gradient
+//      buffer; per-block sums of squares (fp64).            -- grid barrier
+//   C  block 0 adds the block sums in block order and publishes the shard's
+//      sum of squares to every peer; every block waits for all W shard
+//      norms and forms the clip coefficient (same values, same order on
+//      every rank, so every rank clips identically).
+//   D  Adam on the owned shard (m, v local); the new bf16 parameters are
+//      pushed into every peer's buffers, the fp32 ones only for the tail
+//      region the kernels read in fp32 (biases, log-std): the fp32 master
+//      of the weight matrices stays sharded (16-byte stores). -- grid barrier
+//   E  block 0 raises "done" on every peer; every block waits for all
+//      peers' "done" (every parameter pushed here, every peer finished
+//      reading my gradient) and zeroes its part of the local gradient.
 // Moments: one block, all-gather of a few doubles + ordered local sum.
-// Counts: increments of the curiosity table summed over peers into the
-//   local table, then the local increments are zeroed.
+// Counts: one cooperative kernel: barrier-in, counts += every other rank's
+//   increments, grid barrier, "done", wait, clear the local increments.
 //
-// Every wait polls a flag with ld.acquire.sys and gives up after a bounded
-// time (%globaltimer): the kernel then records an error code in the local
-// sync block and returns, so a dead or stalled peer never hangs a GPU. Once
-// an error is recorded every later collective kernel returns at once; the
-// host reads the code after the step and raises.
+// Every wait (peer flags and grid barriers) polls with a bounded time
+// (%globaltimer): a wait that runs out records an error code in the local
+// sync block and the kernel returns, so a dead or stalled peer never hangs a
+// GPU. Once an error is recorded every later collective kernel returns at
+// once; the host reads the code after the step and raises.
 //
 // Semantics follow the data-parallel design of the reference
 // (docs/ddp-plan.md:404-434 gradient sum after backward, before the clip;
@@ -57,15 +58,16 @@ constexpr int kMaxMom = 256;
 // Sync block layout (uint64 words, one block per rank, zeroed at start).
 enum : int {
   kSeqGrad = 0, kSeqMom = 1, kSeqCnt = 2, kErr = 3, kErrTarget = 4,
-  kArrive = 8,                       // 8 counters
   kFlags = 16,                       // [6][kMaxW]
   kNormSlots = 64,                   // [2][kMaxW] doubles
+  kBar = 96,                         // 8 grid barriers x (count, generation)
+  kProf = 112,                       // phase timestamps of the last gradient step (block 0)
   kPartial = 128,                    // [kMaxBlocks] doubles
   kMomSlots = kPartial + kMaxBlocks, // [2][kMaxW][kMaxMom] doubles
   kSyncWords = kMomSlots + 2 * kMaxW * kMaxMom,
 };
 enum : int { kFReady = 0, kFNorm = 1, kFDone = 2, kFMom = 3, kFCntReady = 4, kFCntDone = 5 };
-enum : int { kArrRs = 0, kArrAdam = 1, kArrDone = 2, kArrCnt = 3, kArrCntDone = 4 };
+enum : int { kBarGrad1 = 0, kBarGrad2 = 1, kBarCnt = 2 };
 
 __host__ __device__ constexpr int flag_word(int f, int rank) { return kFlags + f * kMaxW + rank; }
 
@@ -84,6 +86,8 @@ struct Plan {
   float* m = nullptr;
   float* v = nullptr;
   float* hyper = nullptr;
+  int64_t push32_from = 0;                  // fp32 parameters pushed to peers only from this index on
+  int coop_grid = 148;                      // co-resident blocks of the cooperative kernels
   // counts merge
   int64_t cn = 0;
   int* counts = nullptr;
@@ -155,22 +159,6 @@ __device__ bool block_wait_all(const Plan& P, int f, uint64_t target, uint64_t c
   return ok != 0;
 }
 
-// Last-block election: after every block called this once, exactly one block
-// (the last to arrive) gets true. The counter is reset by that block.
-__device__ bool last_block(uint64_t* counter) {
-  __shared__ int last;
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned long long prev = atomicAdd(reinterpret_cast<unsigned long long*>(counter), 1ull);
-    last = prev == gridDim.x - 1;
-    if (last) *counter = 0;
-  }
-  __syncthreads();
-  if (last) __threadfence();
-  return last != 0;
-}
-
 __device__ __forceinline__ double block_sum(double s) {
   for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   __shared__ double red[32];
@@ -184,39 +172,97 @@ __device__ __forceinline__ double block_sum(double s) {
   return t;   // valid in thread 0
 }
 
+__device__ __forceinline__ uint64_t ld_acquire_gpu(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid-wide barrier of a cooperative launch (sense by generation counter),
+// bounded like every other wait. `fence_sys` makes this block's earlier
+// stores (peer stores included) visible system-wide before it arrives.
+__device__ bool grid_barrier(uint64_t* sync, int slot, bool fence_sys, uint64_t timeout_ns, uint64_t code,
+                             uint64_t target) {
+  __shared__ int ok;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    ok = 1;
+    unsigned long long* cnt = reinterpret_cast<unsigned long long*>(sync + kBar + 2 * slot);
+    unsigned long long* gen = cnt + 1;
+    const uint64_t g = ld_acquire_gpu(reinterpret_cast<uint64_t*>(gen));
+    if (fence_sys) __threadfence_system();
+    else __threadfence();
+    if (atomicAdd(cnt, 1ull) == gridDim.x - 1) {
+      atomicExch(cnt, 0ull);
+      __threadfence();
+      atomicAdd(gen, 1ull);
+    } else {
+      const uint64_t t0 = globaltimer();
+      for (uint32_t it = 1; ld_acquire_gpu(reinterpret_cast<uint64_t*>(gen)) == g; ++it) {
+        if ((it & 63u) == 0u) {
+          if (ld_relaxed_sys_u64(sync + kErr) != 0ull) { ok = 0; break; }
+          if (globaltimer() - t0 > timeout_ns) { set_error(sync, code, target); ok = 0; break; }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+__device__ __forceinline__ void prof_mark(const Plan& P, int k) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) P.sync[kProf + k] = globaltimer();
+}
+
+__device__ __forceinline__ void add4(float4& a, const float4& b) { a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w; }
+__device__ __forceinline__ double sq4(const float4& a) {
+  return static_cast<double>(a.x) * a.x + static_cast<double>(a.y) * a.y + static_cast<double>(a.z) * a.z +
+         static_cast<double>(a.w) * a.w;
+}
+
 // ---- gradient step ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) grad_rs_kernel(Plan P) {
+__global__ void __launch_bounds__(256) grad_step_kernel(Plan P) {
   uint64_t* sync = P.sync;
   if (ld_relaxed_sys_u64(sync + kErr) != 0ull) return;
   const uint64_t target = sync[kSeqGrad] + 1;
+  const int par = static_cast<int>(target & 1);
+  prof_mark(P, 0);
+  // A: barrier-in
   if (blockIdx.x == 0 && static_cast<int>(threadIdx.x) < P.world) {
     __threadfence_system();
     st_release_sys(P.sync_peer[threadIdx.x] + flag_word(kFReady, P.rank), target);
   }
   if (!block_wait_all(P, kFReady, target, 0x100)) return;
+  prof_mark(P, 1);
 
   const int64_t lo = static_cast<int64_t>(P.rank) * P.shard;
   const int64_t hi = lo + P.shard < P.n ? lo + P.shard : P.n;
   const int64_t cnt = hi > lo ? hi - lo : 0;
-  const int64_t nv = cnt >> 2;                          // float4 groups (shard start is 16-byte aligned)
+  const int64_t n8 = cnt >> 3;                          // 8-element groups (the shard start is 32-byte aligned)
+  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   float* mine = P.grad_peer[P.rank];
+  // B: reduce-scatter of the owned shard
   double ss = 0.0;
-  for (int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; j < nv; j += stride) {
-    const int64_t i = lo + 4 * j;
-    float4 v[kMaxW];
+  for (int64_t j = tid; j < n8; j += stride) {
+    const int64_t i = lo + 8 * j;
+    float4 v0[kMaxW], v1[kMaxW];
 #pragma unroll
-    for (int q = 0; q < kMaxW; ++q)
-      if (q < P.world) v[q] = *reinterpret_cast<const float4*>(P.grad_peer[q] + i);
-    float4 a = v[0];
+    for (int q = 0; q < kMaxW; ++q) {
+      if (q < P.world) {
+        v0[q] = *reinterpret_cast<const float4*>(P.grad_peer[q] + i);
+        v1[q] = *reinterpret_cast<const float4*>(P.grad_peer[q] + i + 4);
+      }
+    }
+    float4 a0 = v0[0], a1 = v1[0];
 #pragma unroll
     for (int q = 1; q < kMaxW; ++q)
-      if (q < P.world) { a.x += v[q].x; a.y += v[q].y; a.z += v[q].z; a.w += v[q].w; }
-    *reinterpret_cast<float4*>(mine + i) = a;
-    ss += static_cast<double>(a.x) * a.x + static_cast<double>(a.y) * a.y + static_cast<double>(a.z) * a.z +
-          static_cast<double>(a.w) * a.w;
+      if (q < P.world) { add4(a0, v0[q]); add4(a1, v1[q]); }
+    *reinterpret_cast<float4*>(mine + i) = a0;
+    *reinterpret_cast<float4*>(mine + i + 4) = a1;
+    ss += sq4(a0) + sq4(a1);
   }
-  for (int64_t i = lo + 4 * nv + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < hi; i += stride) {
+  for (int64_t i = lo + 8 * n8 + tid; i < hi; i += stride) {
     float a = P.grad_peer[0][i];
     for (int q = 1; q < P.world; ++q) a += P.grad_peer[q][i];
     mine[i] = a;
@@ -225,47 +271,38 @@ __global__ void __launch_bounds__(256) grad_rs_kernel(Plan P) {
   const double bs = block_sum(ss);
   double* partial = reinterpret_cast<double*>(sync + kPartial);
   if (threadIdx.x == 0) partial[blockIdx.x] = bs;
-  if (last_block(sync + kArrive + kArrRs)) {
+  if (!grid_barrier(sync, kBarGrad1, false, P.timeout_ns, 0x710, target)) return;
+  prof_mark(P, 2);
+  // C: shard norm out, all norms in
+  if (blockIdx.x == 0) {
+    // ordered (deterministic) sum of the block partials by the whole block:
+    // thread t adds blocks t, t+256, ... then a fixed-shape tree
+    double part = 0.0;
+    for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) part += partial[b];
+    const double tot_b = block_sum(part);
     if (threadIdx.x == 0) {
-      double tot = 0.0;
-      for (unsigned b = 0; b < gridDim.x; ++b) tot += partial[b];   // fixed order: deterministic
-      reinterpret_cast<Hyper*>(P.hyper)->step += 1.0f;
-      const int par = static_cast<int>(target & 1);
       for (int q = 0; q < P.world; ++q)
-        st_relaxed_sys(reinterpret_cast<double*>(P.sync_peer[q] + kNormSlots) + par * kMaxW + P.rank, tot);
+        st_relaxed_sys(reinterpret_cast<double*>(P.sync_peer[q] + kNormSlots) + par * kMaxW + P.rank, tot_b);
       __threadfence_system();
       for (int q = 0; q < P.world; ++q) st_release_sys(P.sync_peer[q] + flag_word(kFNorm, P.rank), target);
     }
   }
-}
-
-__global__ void __launch_bounds__(256) grad_adam_kernel(Plan P) {
-  uint64_t* sync = P.sync;
-  if (ld_relaxed_sys_u64(sync + kErr) != 0ull) return;
-  const uint64_t target = sync[kSeqGrad] + 1;
   if (!block_wait_all(P, kFNorm, target, 0x200)) return;
+  prof_mark(P, 3);
   __shared__ float s_coef;
+  const Hyper* h = reinterpret_cast<const Hyper*>(P.hyper);
   if (threadIdx.x == 0) {
-    const int par = static_cast<int>(target & 1);
     const double* slots = reinterpret_cast<const double*>(sync + kNormSlots) + par * kMaxW;
     double tot = 0.0;
     for (int q = 0; q < P.world; ++q) tot += ld_relaxed_sys(slots + q);
-    const Hyper* h = reinterpret_cast<const Hyper*>(P.hyper);
     const float norm = static_cast<float>(sqrt(tot));
     s_coef = h->max_norm > 0.0f ? fminf(1.0f, h->max_norm / (norm + 1e-6f)) : 1.0f;
   }
   __syncthreads();
-  const Hyper* h = reinterpret_cast<const Hyper*>(P.hyper);
-  const float coef = s_coef, b1 = h->beta1, b2 = h->beta2, t = h->step, eps = h->eps;
+  // D: Adam on the owned shard, push the new parameters everywhere
+  const float coef = s_coef, b1 = h->beta1, b2 = h->beta2, t = h->step + 1.0f, eps = h->eps;
   const float bc1 = 1.0f - powf(b1, t), bc2 = 1.0f - powf(b2, t);
   const float lr_t = h->lr / bc1, rbc2 = rsqrtf(bc2);
-
-  const int64_t lo = static_cast<int64_t>(P.rank) * P.shard;
-  const int64_t hi = lo + P.shard < P.n ? lo + P.shard : P.n;
-  const int64_t cnt = hi > lo ? hi - lo : 0;
-  const int64_t nv = cnt >> 2;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const float* g = P.grad_peer[P.rank];
   const float* pl = P.p_peer[P.rank];
   auto adam1 = [&](float gi, float& mi, float& vi, float pi) {
     gi *= coef;
@@ -273,61 +310,65 @@ __global__ void __launch_bounds__(256) grad_adam_kernel(Plan P) {
     vi = b2 * vi + (1.0f - b2) * gi * gi;
     return pi - lr_t * mi / (sqrtf(vi) * rbc2 + eps);
   };
-  for (int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; j < nv; j += stride) {
-    const int64_t i = lo + 4 * j;
-    const float4 gg = *reinterpret_cast<const float4*>(g + i);
-    float4 mm = *reinterpret_cast<const float4*>(P.m + i);
-    float4 vv = *reinterpret_cast<const float4*>(P.v + i);
-    float4 pp = *reinterpret_cast<const float4*>(pl + i);
-    pp.x = adam1(gg.x, mm.x, vv.x, pp.x);
-    pp.y = adam1(gg.y, mm.y, vv.y, pp.y);
-    pp.z = adam1(gg.z, mm.z, vv.z, pp.z);
-    pp.w = adam1(gg.w, mm.w, vv.w, pp.w);
-    *reinterpret_cast<float4*>(P.m + i) = mm;
-    *reinterpret_cast<float4*>(P.v + i) = vv;
-    uint2 b;
-    b.x = static_cast<uint32_t>(surfk::f32_to_bf16(pp.x)) | (static_cast<uint32_t>(surfk::f32_to_bf16(pp.y)) << 16);
-    b.y = static_cast<uint32_t>(surfk::f32_to_bf16(pp.z)) | (static_cast<uint32_t>(surfk::f32_to_bf16(pp.w)) << 16);
+  auto adam4 = [&](const float4 g4, float4& m4, float4& v4, float4 p4) {
+    p4.x = adam1(g4.x, m4.x, v4.x, p4.x);
+    p4.y = adam1(g4.y, m4.y, v4.y, p4.y);
+    p4.z = adam1(g4.z, m4.z, v4.z, p4.z);
+    p4.w = adam1(g4.w, m4.w, v4.w, p4.w);
+    return p4;
+  };
+  auto pack2 = [](float a, float b) {
+    return static_cast<uint32_t>(surfk::f32_to_bf16(a)) | (static_cast<uint32_t>(surfk::f32_to_bf16(b)) << 16);
+  };
+  for (int64_t j = tid; j < n8; j += stride) {
+    const int64_t i = lo + 8 * j;
+    float4 m0 = *reinterpret_cast<const float4*>(P.m + i), m1 = *reinterpret_cast<const float4*>(P.m + i + 4);
+    float4 w0 = *reinterpret_cast<const float4*>(P.v + i), w1 = *reinterpret_cast<const float4*>(P.v + i + 4);
+    const float4 p0 = adam4(*reinterpret_cast<const float4*>(mine + i), m0, w0, *reinterpret_cast<const float4*>(pl + i));
+    const float4 p1 = adam4(*reinterpret_cast<const float4*>(mine + i + 4), m1, w1,
+                            *reinterpret_cast<const float4*>(pl + i + 4));
+    *reinterpret_cast<float4*>(P.m + i) = m0;
+    *reinterpret_cast<float4*>(P.m + i + 4) = m1;
+    *reinterpret_cast<float4*>(P.v + i) = w0;
+    *reinterpret_cast<float4*>(P.v + i + 4) = w1;
+    const uint4 b = make_uint4(pack2(p0.x, p0.y), pack2(p0.z, p0.w), pack2(p1.x, p1.y), pack2(p1.z, p1.w));
+    const bool all32 = i >= P.push32_from;          // 64-aligned region boundary: never inside a group of 8
 #pragma unroll
     for (int q = 0; q < kMaxW; ++q) {
       if (q < P.world) {
-        *reinterpret_cast<float4*>(P.p_peer[q] + i) = pp;
-        *reinterpret_cast<uint2*>(P.p16_peer[q] + i) = b;
+        if (all32 || q == P.rank) {
+          *reinterpret_cast<float4*>(P.p_peer[q] + i) = p0;
+          *reinterpret_cast<float4*>(P.p_peer[q] + i + 4) = p1;
+        }
+        *reinterpret_cast<uint4*>(P.p16_peer[q] + i) = b;
       }
     }
   }
-  for (int64_t i = lo + 4 * nv + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < hi; i += stride) {
+  for (int64_t i = lo + 8 * n8 + tid; i < hi; i += stride) {
     float mi = P.m[i], vi = P.v[i];
-    const float pi = adam1(g[i], mi, vi, pl[i]);
+    const float pi = adam1(mine[i], mi, vi, pl[i]);
     P.m[i] = mi;
     P.v[i] = vi;
     const uint16_t b = surfk::f32_to_bf16(pi);
     for (int q = 0; q < P.world; ++q) {
-      P.p_peer[q][i] = pi;
+      if (i >= P.push32_from || q == P.rank) P.p_peer[q][i] = pi;
       P.p16_peer[q][i] = b;
     }
   }
-  if (last_block(sync + kArrive + kArrAdam)) {
-    if (static_cast<int>(threadIdx.x) < P.world)
-      st_release_sys(P.sync_peer[threadIdx.x] + flag_word(kFDone, P.rank), target);
+  if (!grid_barrier(sync, kBarGrad2, true, P.timeout_ns, 0x720, target)) return;
+  prof_mark(P, 4);
+  // E: done out, all done in, clear the local gradient
+  if (blockIdx.x == 0 && static_cast<int>(threadIdx.x) < P.world)
+    st_release_sys(P.sync_peer[threadIdx.x] + flag_word(kFDone, P.rank), target);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    reinterpret_cast<Hyper*>(P.hyper)->step = t;    // every block read the old step before the barrier
+    sync[kSeqGrad] = target;
   }
-}
-
-__global__ void __launch_bounds__(256) grad_done_kernel(Plan P) {
-  uint64_t* sync = P.sync;
-  if (ld_relaxed_sys_u64(sync + kErr) != 0ull) return;
-  const uint64_t target = sync[kSeqGrad] + 1;
   if (!block_wait_all(P, kFDone, target, 0x300)) return;
-  float* g = P.grad_peer[P.rank];
+  prof_mark(P, 5);
   const int64_t nv = P.n >> 2;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; j < nv; j += stride)
-    reinterpret_cast<float4*>(g)[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int64_t i = 4 * nv + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < P.n; i += stride)
-    g[i] = 0.0f;
-  if (last_block(sync + kArrive + kArrDone)) {
-    if (threadIdx.x == 0) sync[kSeqGrad] = target;
-  }
+  for (int64_t j = tid; j < nv; j += stride) reinterpret_cast<float4*>(mine)[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t i = 4 * nv + tid; i < P.n; i += stride) mine[i] = 0.0f;
 }
 
 // ---- moments (tiny all-reduce, one block) ---------------------------------------------------
@@ -357,7 +398,7 @@ __global__ void __launch_bounds__(256) moments_kernel(Plan P, double* mom, int c
 }
 
 // ---- curiosity count merge -----------------------------------------------------------------
-__global__ void __launch_bounds__(256) counts_add_kernel(Plan P) {
+__global__ void __launch_bounds__(256) counts_merge_kernel(Plan P) {
   uint64_t* sync = P.sync;
   if (ld_relaxed_sys_u64(sync + kErr) != 0ull) return;
   const uint64_t target = sync[kSeqCnt] + 1;
@@ -367,8 +408,9 @@ __global__ void __launch_bounds__(256) counts_add_kernel(Plan P) {
   }
   if (!block_wait_all(P, kFCntReady, target, 0x500)) return;
   const int64_t nv = P.cn >> 2;
+  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; j < nv; j += stride) {
+  for (int64_t j = tid; j < nv; j += stride) {
     int4 acc = reinterpret_cast<const int4*>(P.counts)[j];
 #pragma unroll
     for (int q = 0; q < kMaxW; ++q) {
@@ -379,39 +421,37 @@ __global__ void __launch_bounds__(256) counts_add_kernel(Plan P) {
     }
     reinterpret_cast<int4*>(P.counts)[j] = acc;
   }
-  for (int64_t i = 4 * nv + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < P.cn; i += stride) {
+  for (int64_t i = 4 * nv + tid; i < P.cn; i += stride) {
     int acc = P.counts[i];
     for (int q = 0; q < P.world; ++q)
       if (q != P.rank) acc += P.delta_peer[q][i];
     P.counts[i] = acc;
   }
-  if (last_block(sync + kArrive + kArrCnt)) {
-    if (static_cast<int>(threadIdx.x) < P.world)
-      st_release_sys(P.sync_peer[threadIdx.x] + flag_word(kFCntDone, P.rank), target);
-  }
-}
-
-__global__ void __launch_bounds__(256) counts_done_kernel(Plan P) {
-  uint64_t* sync = P.sync;
-  if (ld_relaxed_sys_u64(sync + kErr) != 0ull) return;
-  const uint64_t target = sync[kSeqCnt] + 1;
+  if (!grid_barrier(sync, kBarCnt, true, P.timeout_ns, 0x730, target)) return;
+  if (blockIdx.x == 0 && static_cast<int>(threadIdx.x) < P.world)
+    st_release_sys(P.sync_peer[threadIdx.x] + flag_word(kFCntDone, P.rank), target);
+  if (blockIdx.x == 0 && threadIdx.x == 0) sync[kSeqCnt] = target;
   if (!block_wait_all(P, kFCntDone, target, 0x600)) return;
   int* d = P.delta_peer[P.rank];
-  const int64_t nv = P.cn >> 2;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; j < nv; j += stride)
-    reinterpret_cast<int4*>(d)[j] = make_int4(0, 0, 0, 0);
-  for (int64_t i = 4 * nv + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < P.cn; i += stride)
-    d[i] = 0;
-  if (last_block(sync + kArrive + kArrCntDone)) {
-    if (threadIdx.x == 0) sync[kSeqCnt] = target;
-  }
+  for (int64_t j = tid; j < nv; j += stride) reinterpret_cast<int4*>(d)[j] = make_int4(0, 0, 0, 0);
+  for (int64_t i = 4 * nv + tid; i < P.cn; i += stride) d[i] = 0;
 }
 
-int grid_for(int64_t items) {
-  const int64_t b = surfk::ceil_div(items, 256);
-  return static_cast<int>(b < 1 ? 1 : (b > 148 * 2 ? 148 * 2 : b));
+// Cooperative launch (all blocks co-resident, so grid barriers are safe).
+template <typename K>
+int launch_coop(K kernel, int grid, cudaStream_t s, const Plan& P) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, P));
 }
+
 
 // ---- IPC bookkeeping -----------------------------------------------------------------------
 std::mutex g_mu;
@@ -477,18 +517,30 @@ SURF_EXPORT void* surf_p2p_create(int rank, int world, void* const* sync_peers, 
   p->timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
   for (int q = 0; q < world; ++q) p->sync_peer[q] = static_cast<uint64_t*>(sync_peers[q]);
   p->sync = p->sync_peer[rank];
+  int dev = 0, sms = 148, per_sm = 1, per_sm2 = 1;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, grad_step_kernel, 256, 0);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm2, counts_merge_kernel, 256, 0);
+  const int m = per_sm < per_sm2 ? per_sm : per_sm2;
+  p->coop_grid = sms * (m < 2 ? (m < 1 ? 1 : m) : 2);
+  if (p->coop_grid > kMaxBlocks) p->coop_grid = kMaxBlocks;
   return p;
 }
 
 SURF_EXPORT void surf_p2p_destroy(void* plan) { delete static_cast<Plan*>(plan); }
 
-// Shard = ceil(n / world) rounded up to 4 elements; every buffer must be
+// Shard = ceil(n / world) rounded up to 8 elements; every buffer must be
 // 16-byte aligned (torch allocations are).
+// push32_from: parameters below this index keep their fp32 master on the
+// owning rank only (peers receive the bf16 copy); from it on, every rank
+// receives fp32 too. Must be a multiple of 8 (0 = replicate everything).
 SURF_EXPORT int surf_p2p_set_grad(void* plan, int64_t n, void* const* grad_peers, void* const* p_peers,
-                                  void* const* p16_peers, float* m, float* v, float* hyper) {
+                                  void* const* p16_peers, float* m, float* v, float* hyper, int64_t push32_from) {
   Plan* P = static_cast<Plan*>(plan);
+  if (push32_from < 0 || push32_from % 8) return static_cast<int>(cudaErrorInvalidValue);
   P->n = n;
-  P->shard = surfk::ceil_div(surfk::ceil_div(n, P->world), 4) * 4;
+  P->push32_from = push32_from;
+  P->shard = surfk::ceil_div(surfk::ceil_div(n, P->world), 8) * 8;   // 32-byte aligned shard starts
   for (int q = 0; q < P->world; ++q) {
     P->grad_peer[q] = static_cast<float*>(grad_peers[q]);
     P->p_peer[q] = static_cast<float*>(p_peers[q]);
@@ -521,13 +573,12 @@ SURF_EXPORT int surf_p2p_set_counts(void* plan, int64_t n, int* counts, void* co
 SURF_EXPORT int surf_p2p_grad_step(void* plan, void* stream) {
   const Plan& P = *static_cast<const Plan*>(plan);
   if (!P.n) return static_cast<int>(cudaErrorInvalidValue);
-  auto s = static_cast<cudaStream_t>(stream);
-  const int g = grid_for(surfk::ceil_div(P.shard, 4));
-  grad_rs_kernel<<<g, 256, 0, s>>>(P);
-  grad_adam_kernel<<<g, 256, 0, s>>>(P);
-  grad_done_kernel<<<grid_for(surfk::ceil_div(P.n, 4)), 256, 0, s>>>(P);
-  SURF_RETURN_LAUNCH();
+  return launch_coop(grad_step_kernel, P.coop_grid, static_cast<cudaStream_t>(stream), P);
 }
+
+// Phase timestamps (ns, %globaltimer) of this rank's last gradient step:
+// start, peers ready, reduce-scatter done, norms in, parameters pushed, done in.
+SURF_EXPORT int surf_p2p_prof_words() { return 6; }
 
 SURF_EXPORT int surf_p2p_moments(void* plan, double* mom, int cnt, void* stream) {
   const Plan& P = *static_cast<const Plan*>(plan);
@@ -539,9 +590,5 @@ SURF_EXPORT int surf_p2p_moments(void* plan, double* mom, int cnt, void* stream)
 SURF_EXPORT int surf_p2p_merge_counts(void* plan, void* stream) {
   const Plan& P = *static_cast<const Plan*>(plan);
   if (!P.cn) return static_cast<int>(cudaErrorInvalidValue);
-  auto s = static_cast<cudaStream_t>(stream);
-  const int g = grid_for(surfk::ceil_div(P.cn, 4));
-  counts_add_kernel<<<g, 256, 0, s>>>(P);
-  counts_done_kernel<<<g, 256, 0, s>>>(P);
-  SURF_RETURN_LAUNCH();
+  return launch_coop(counts_merge_kernel, P.coop_grid, static_cast<cudaStream_t>(stream), P);
 }

@@ -15,7 +15,9 @@
 //                        k-tile into one of two TMEM accumulators;
 //                        tcgen05.commit releases each smem stage and signals
 //                        the epilogue when a tile's accumulator is complete;
-//   warps 2-5          : epilogue — tcgen05.ld of the warp's 32 TMEM lanes,
+//   warps 2-9          : epilogue — two warps per 32-lane TMEM quadrant, each
+//                        taking every other 32-column chunk: tcgen05.ld of the
+//                        warp's 32 TMEM lanes,
 //                        fused bias / activation / activation-derivative,
 //                        stores as fp32 or bf16, optionally also transposed,
 //                        or fp32 atomic accumulation for split-K; then hand
@@ -39,6 +41,8 @@
 namespace {
 
 constexpr int BM = 128, BK = 64;
+constexpr int kEpiWarps = 8;                   // epilogue warps (2 per TMEM lane quadrant)
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer warp + MMA warp + epilogue
 constexpr uint64_t kWaitNs = 2000000000ull;    // 2 s bound per barrier wait
 
 enum Act : int { kNone = 0, kRelu = 1, kTanh = 2, kReluGrad = 3, kTanhGrad = 4 };
@@ -254,7 +258,7 @@ struct Cfg {
   static constexpr int kAcc = BN <= 64 ? 4 : 2;           // accumulator buffers in TMEM
   static constexpr int kTmemCols = kAcc * BN;
   // per epilogue warp: two 32x32 fp32 staging tiles for TMA stores (4 KB each)
-  static constexpr int kStageOutBytes = 4 * 2 * 4096;
+  static constexpr int kStageOutBytes = kEpiWarps * 2 * 4096;
   // alignment slack + operand stages + barrier block (1 KB) + output staging
   static constexpr size_t kSmem = 1024 + STAGES * static_cast<size_t>(kStageBytes) + 1024 + kStageOutBytes;
   // instruction descriptor: D fp32, A/B bf16, majorness, N >> 3, M >> 4
@@ -328,9 +332,9 @@ __device__ __forceinline__ void store_chunk32(const Epilogue& ep, const float* v
   }
 }
 
-// Persistent warp-specialised kernel: 6 warps = producer, MMA, 4 epilogue.
+// Persistent warp-specialised kernel: 10 warps = producer, MMA, 8 epilogue.
 template <int BN, bool A_MN, bool B_MN, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                 const __grid_constant__ CUtensorMap tma_c, int use_tma_c, int M, int N, Sched sc, Epilogue ep) {
   using C = Cfg<BN, A_MN, B_MN, STAGES>;
@@ -354,7 +358,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < C::kAcc; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
-      mbar_init(smem_u32(&acc_empty[b]), 4);     // one arrival per epilogue warp
+      mbar_init(smem_u32(&acc_empty[b]), kEpiWarps);     // one arrival per epilogue warp
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -433,8 +437,10 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // ---- epilogue warps 2..5 (TMEM lane quadrant = warp % 4)
+    // ---- epilogue warps 2..9 (TMEM lane quadrant = warp % 4; `half` picks
+    // the even or odd 32-column chunks of the tile)
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     int tc = 0;
     int stage_ctr = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
@@ -454,9 +460,9 @@ __global__ void __launch_bounds__(192, 1)
         // bias/activation in registers, then the warp's 32 x 32 chunk goes to a
         // swizzled smem tile and out with one asynchronous TMA store
         const bool bf = ep.c_dtype == 1;
-        uint8_t* my_stage = stage_out + quad * 8192;
+        uint8_t* my_stage = stage_out + (warp - 2) * 8192;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        for (int c0 = 32 * half; c0 < BN; c0 += 64) {
           if (n0 + c0 >= N) break;
           float v[32];
           tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + c0, v);
@@ -493,7 +499,7 @@ __global__ void __launch_bounds__(192, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        for (int c0 = 32 * half; c0 < BN; c0 += 64) {
           if (n0 + c0 >= N) break;
           float v[32];
           tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + c0, v);
@@ -546,7 +552,7 @@ bool make_map(CUtensorMap* m, const void* base, int64_t inner, int64_t rows, int
 template <int BN, bool A_MN, bool B_MN>
 int launch(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const Epilogue& ep, int splits,
            cudaStream_t s) {
-  constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 6 : 4);
+  constexpr int STAGES = BN >= 256 ? 3 : 4;
   using C = Cfg<BN, A_MN, B_MN, STAGES>;
   auto kern = gemm_kernel<BN, A_MN, B_MN, STAGES>;
   CUtensorMap ta, tb;
@@ -568,7 +574,7 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N,
   static int sms = 0;
   if (!resident) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmem));
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, 192, C::kSmem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, kThreads, C::kSmem);
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -586,7 +592,7 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N,
   sc.group = 8;
   const int64_t ntiles = static_cast<int64_t>(sc.mt) * sc.nt * sc.splits;
   const int grid = static_cast<int>(ntiles < static_cast<int64_t>(sms) * resident ? ntiles : static_cast<int64_t>(sms) * resident);
-  kern<<<grid, 192, C::kSmem, s>>>(ta, tb, tc, use_tma_c, M, N, sc, ep);
+  kern<<<grid, kThreads, C::kSmem, s>>>(ta, tb, tc, use_tma_c, M, N, sc, ep);
   SURF_RETURN_LAUNCH();
 }
 

@@ -13,6 +13,10 @@
 //   maxspeed   new maxima of v_h                            (MaxSpeedReward)
 //   coverage   v_h * scale on entering an unvisited cell of this episode,
 //              -revisit_pen on re-entering one              (CoverageSpeedReward)
+//   acro       coverage + style: banked air-spin rotation paid on landing a
+//              real flight, switch (backwards) landings, backwards ramp
+//              riding                                          (AcroCoverageReward)
+//   blend      (1 - w) forward + w path, w annealed by the trainer (BlendedReward)
 //   race       scale * (d_prev - d) - time_pen on the geodesic distance field
 //              (trilinear over honest corners), success bonus (+ finish_k
 //              time bonus), fail penalty, speed-equivalent potential with
@@ -30,9 +34,10 @@
 
 namespace {
 
-enum Mode : int { kSpeed = 0, kAvgSpeed = 1, kForward = 2, kPath = 3, kMaxSpeed = 4, kCoverage = 5, kRace = 6 };
-enum RecCol : int { kOx = 0, kOy = 1, kOz = 2, kYaw = 3, kVx = 6, kVy = 7, kTick = 9, kBase = 10, kDone = 11,
-                    kTrunc = 12, kGoal = 13, kEnded = 14 };
+enum Mode : int { kSpeed = 0, kAvgSpeed = 1, kForward = 2, kPath = 3, kMaxSpeed = 4, kCoverage = 5, kRace = 6,
+                  kAcro = 7, kBlend = 8 };
+enum RecCol : int { kOx = 0, kOy = 1, kOz = 2, kYaw = 3, kVx = 6, kVy = 7, kVz = 8, kTick = 9, kBase = 10, kDone = 11,
+                    kTrunc = 12, kGoal = 13, kEnded = 14, kOnground = 15 };
 
 struct RewardParams {
   int mode, n, K;
@@ -55,11 +60,25 @@ struct RewardParams {
   int int_dim[3];
   uint32_t table_mask;            // table size - 1 (power of two)
   float gamma_boot;               // unused here (bootstraps are precomputed)
+  // acro style terms (per tick; scaled by K per decision)
+  float spin_bonus, switch_bonus, spin_rate_cap, back_bonus, gravity_tick;
+  int max_spins, min_air;         // min_air in ticks
+  // blend: weight w of path over forward, read from device memory (schedules
+  // change it without re-capturing the graphs that launch this kernel)
+  const float* blend_w;
 };
 
-// per-env state (float [n, 16])
+// per-env state (float [n, kStateFloats])
+constexpr int kStateFloats = 24;
 enum St : int { sPx = 0, sPy = 1, sPz = 2, sSpeed = 3, sBest = 4, sSince = 5, sTicks = 6, sDirX = 7, sDirY = 8,
-                sRefX = 9, sRefY = 10, sD = 11, sEpRet = 12, sEpLen = 13, sInit = 14, sCell = 15 };
+                sRefX = 9, sRefY = 10, sD = 11, sEpRet = 12, sEpLen = 13, sInit = 14, sCell = 15,
+                sYaw = 16, sVx = 17, sVy = 18, sVz = 19, sStreak = 20, sSpin = 21, sBest2 = 22 };
+
+__device__ __forceinline__ float wrap180(float a) {
+  a = fmodf(a + 180.0f, 360.0f);
+  if (a < 0.0f) a += 360.0f;
+  return a - 180.0f;
+}
 
 __device__ __forceinline__ float hspeed(const float* r) { return sqrtf(r[kVx] * r[kVx] + r[kVy] * r[kVy]); }
 
@@ -123,12 +142,13 @@ __device__ __forceinline__ int cov_cell(const RewardParams& p, const float* r) {
 }
 
 // init: per-env state from the spawn records (first decision of a run)
-__global__ void reward_init_kernel(RewardParams p, const float* rec, int64_t ld, float* st, uint32_t* visited) {
+__global__ void reward_init_kernel(RewardParams p, const float* rec, int64_t ld, float* st, uint32_t* visited,
+                                   int64_t* keys) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= p.n) return;
   const float* r = rec + i * ld;
-  float* s = st + i * 16;
-  for (int k = 0; k < 16; ++k) s[k] = 0.0f;
+  float* s = st + static_cast<int64_t>(i) * kStateFloats;
+  for (int k = 0; k < kStateFloats; ++k) s[k] = 0.0f;
   s[sPx] = r[kOx]; s[sPy] = r[kOy]; s[sPz] = r[kOz];
   s[sSpeed] = hspeed(r);
   s[sBest] = s[sSpeed];
@@ -136,26 +156,28 @@ __global__ void reward_init_kernel(RewardParams p, const float* rec, int64_t ld,
   s[sDirX] = cosf(yaw); s[sDirY] = sinf(yaw);
   s[sRefX] = r[kOx]; s[sRefY] = r[kOy];
   if (p.mode == kRace) { s[sD] = field_sample(p, r[kOx], r[kOy], r[kOz]); s[sBest] = s[sD]; }
-  if (p.mode == kCoverage) {
+  if (p.mode == kForward || p.mode == kBlend) s[sBest] = 0.0f;
+  s[sYaw] = r[kYaw]; s[sVx] = r[kVx]; s[sVy] = r[kVy]; s[sVz] = r[kVz];
+  if (p.mode == kCoverage || p.mode == kAcro) {
     uint32_t* v = visited + static_cast<int64_t>(i) * p.cov_words;
     for (int w = 0; w < p.cov_words; ++w) v[w] = 0;
     const int c = cov_cell(p, r);
     v[c >> 5] |= 1u << (c & 31);
     s[sCell] = __int_as_float(c);
   }
-  if (p.int_coef > 0) reinterpret_cast<int64_t*>(st + p.n * 16)[i] = curiosity_key(p, r);
+  if (p.int_coef > 0) keys[i] = curiosity_key(p, r);
   s[sInit] = 1.0f;
 }
 
 // phase 1: reward, state update, curiosity key; bonus read from current counts
 __global__ void reward_kernel(RewardParams p, const float* rec, int64_t ld, float* st, uint32_t* visited,
                               const int* counts, float* boot, float* rew_out, float* done_out, uint8_t* stall,
-                              int64_t* new_key, float* stats) {
+                              int64_t* new_key, int64_t* keys, float* stats) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   float rr = 0.0f, ep_done = 0.0f, ep_ret = 0.0f, ep_len = 0.0f, succ = 0.0f, fail = 0.0f, trn = 0.0f, ibonus = 0.0f;
   if (i < p.n) {
     const float* r = rec + i * ld;
-    float* s = st + i * 16;
+    float* s = st + static_cast<int64_t>(i) * kStateFloats;
     const bool ended = r[kEnded] != 0.0f, done = r[kDone] != 0.0f, goal = r[kGoal] != 0.0f;
     const float sp = hspeed(r);
     const float dx = r[kOx] - s[sPx], dy = r[kOy] - s[sPy];
@@ -176,6 +198,17 @@ __global__ void reward_kernel(RewardParams p, const float* rec, int64_t ld, floa
         s[sBest] = fmaxf(s[sBest], proj);
         break;
       }
+      case kBlend: {       // (1 - w) * forward + w * path, both anchors kept live
+        if (teleported) { s[sRefX] += dx; s[sRefY] += dy; }
+        const float proj = (r[kOx] - s[sRefX]) * s[sDirX] + (r[kOy] - s[sRefY]) * s[sDirY];
+        const float fwd = fmaxf(proj - s[sBest], 0.0f) * p.scale;
+        s[sBest] = fmaxf(s[sBest], proj);
+        const float path = teleported ? 0.0f : hstep * p.scale;
+        const float w = p.blend_w ? fminf(fmaxf(*p.blend_w, 0.0f), 1.0f) : 0.0f;
+        rr = (1.0f - w) * fwd + w * path;
+        break;
+      }
+      case kAcro:
       case kCoverage: {
         const int c = cov_cell(p, r);
         const int prev = __float_as_int(s[sCell]);
@@ -213,10 +246,33 @@ __global__ void reward_kernel(RewardParams p, const float* rec, int64_t ld, floa
         break;
       }
     }
+    if (p.mode == kAcro) {
+      // style bonuses over the K ticks of this decision: ballistic flight =
+      // velocity changed by gravity and small air-strafe increments only; a
+      // ramp catch or floor is a large velocity change (reference
+      // AcroCoverageReward, thresholds scaled from per tick to per decision)
+      const float K = static_cast<float>(p.K);
+      const float dvx = r[kVx] - s[sVx], dvy = r[kVy] - s[sVy], dvz = r[kVz] - s[sVz];
+      const bool contact = fabsf(dvx) + fabsf(dvy) > 40.0f * K || fabsf(dvz + p.gravity_tick * K) > 12.0f * K;
+      const bool grounded = r[kOnground] != 0.0f;
+      const bool ballistic = !grounded && !contact;
+      const float dyaw = fabsf(wrap180(r[kYaw] - s[sYaw]));
+      const bool flight_end = s[sStreak] * K >= static_cast<float>(p.min_air) && (contact || grounded);
+      const float spin_frac = fminf(s[sSpin], 360.0f * p.max_spins) / 360.0f;
+      float style = flight_end ? p.spin_bonus * spin_frac : 0.0f;
+      const float heading = atan2f(r[kVy], r[kVx]) * 57.29577951308232f;
+      const bool backwards = fabsf(wrap180(r[kYaw] - heading)) >= 140.0f;
+      if (flight_end && sp >= 300.0f && backwards) style += p.switch_bonus;
+      if (!grounded && contact && sp >= 500.0f && backwards) style += p.back_bonus * K;
+      s[sSpin] = ballistic ? s[sSpin] + (s[sStreak] > 0.0f ? fminf(dyaw, p.spin_rate_cap * K) : 0.0f) : 0.0f;
+      s[sStreak] = ballistic ? s[sStreak] + 1.0f : 0.0f;
+      if (!ended) rr += style;
+      else { s[sSpin] = 0.0f; s[sStreak] = 0.0f; }
+    }
+    s[sYaw] = r[kYaw]; s[sVx] = r[kVx]; s[sVy] = r[kVy]; s[sVz] = r[kVz];
     if (p.mode != kRace && ended) rr = 0.0f;
     // curiosity: bonus from the counts as they stood before this decision
     if (p.int_coef > 0) {
-      int64_t* keys = reinterpret_cast<int64_t*>(st + p.n * 16);
       const int64_t key = curiosity_key(p, r);
       int64_t nk = -1;
       if (key != keys[i] && !ended) {
@@ -247,9 +303,9 @@ __global__ void reward_kernel(RewardParams p, const float* rec, int64_t ld, floa
       const float yaw = r[kYaw] * 0.017453292519943295f;
       s[sDirX] = cosf(yaw); s[sDirY] = sinf(yaw);
       s[sRefX] = r[kOx]; s[sRefY] = r[kOy];
-      if (p.mode == kForward) s[sBest] = 0.0f;
+      if (p.mode == kForward || p.mode == kBlend) s[sBest] = 0.0f;
       if (p.mode == kRace) { s[sBest] = s[sD]; s[sSince] = 0.0f; s[sTicks] = 0.0f; }
-      if (p.mode == kCoverage) {
+      if (p.mode == kCoverage || p.mode == kAcro) {
         uint32_t* v = visited + static_cast<int64_t>(i) * p.cov_words;
         for (int w = 0; w < p.cov_words; ++w) v[w] = 0;
         const int c = cov_cell(p, r);
@@ -339,23 +395,39 @@ __global__ void bump_key_kernel(uint64_t* key) {
 }  // namespace
 
 SURF_EXPORT int surf_reward_params_size() { return static_cast<int>(sizeof(RewardParams)); }
+SURF_EXPORT int surf_reward_state_floats() { return kStateFloats; }
 
-// state: float [n*16] + int64 [n] curiosity keys (float [n*18] total).
+// state: float [n*24] per env; keys: int64 [n] curiosity keys of the last
+// decision. Every per-env pointer is indexed by the env's position in this
+// call, so a contiguous group of envs is addressed by offsetting the pointers
+// and setting p->n to the group size.
 SURF_EXPORT int surf_reward_init(const RewardParams* p, const float* rec, int64_t ld, float* state, uint32_t* visited,
-                                 void* stream) {
+                                 int64_t* keys, void* stream) {
   reward_init_kernel<<<static_cast<int>(surfk::ceil_div(p->n, 128)), 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      *p, rec, ld, state, visited);
+      *p, rec, ld, state, visited, keys);
   SURF_RETURN_LAUNCH();
 }
 
+// do_counts = 0 skips phase 2: a caller that splits the envs into groups
+// runs phase 1 for every group, then surf_reward_counts once over all envs,
+// so that every bonus of a decision reads the counts from before it.
 SURF_EXPORT int surf_reward(const RewardParams* p, const float* rec, int64_t ld, float* state, uint32_t* visited,
                             int* counts, int* delta, float* boot, float* rew_out, float* done_out, uint8_t* stall,
-                            int64_t* new_key, float* stats, void* stream) {
+                            int64_t* new_key, int64_t* keys, float* stats, int do_counts, void* stream) {
   auto s = static_cast<cudaStream_t>(stream);
   const int blocks = static_cast<int>(surfk::ceil_div(p->n, 128));
   reward_kernel<<<blocks, 128, 0, s>>>(*p, rec, ld, state, visited, counts, boot, rew_out, done_out, stall, new_key,
-                                       stats);
-  if (p->int_coef > 0) count_kernel<<<blocks, 128, 0, s>>>(*p, new_key, counts, delta);
+                                       keys, stats);
+  if (p->int_coef > 0 && do_counts) count_kernel<<<blocks, 128, 0, s>>>(*p, new_key, counts, delta);
+  SURF_RETURN_LAUNCH();
+}
+
+// phase 2 alone: count increments of the keys staged by phase 1 (p->n envs)
+SURF_EXPORT int surf_reward_counts(const RewardParams* p, const int64_t* new_key, int* counts, int* delta,
+                                   void* stream) {
+  if (p->int_coef > 0)
+    count_kernel<<<static_cast<int>(surfk::ceil_div(p->n, 128)), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        *p, new_key, counts, delta);
   SURF_RETURN_LAUNCH();
 }
 

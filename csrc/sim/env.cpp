@@ -474,9 +474,17 @@ void EnvBatch::step(const int32_t* actions, float* obs, float* rewards, uint8_t*
 
 void EnvBatch::step_k(const int32_t* actions, int action_stride, int yaw_slot, int fail_slot, int k, RowOut obs,
                       RowOut term_obs, RowOut rec, RowOut term_rec) {
+  step_k_range(0, cfg_.num_envs, actions, action_stride, yaw_slot, fail_slot, k, obs, term_obs, rec, term_rec);
+}
+
+void EnvBatch::step_k_range(int lo, int hi, const int32_t* actions, int action_stride, int yaw_slot, int fail_slot,
+                            int k, RowOut obs, RowOut term_obs, RowOut rec, RowOut term_rec) {
   if (k < 1) k = 1;
-  pool_->run(cfg_.num_envs, [&](int b, int e) {
-    for (int i = b; i < e; ++i) {
+  lo = lo < 0 ? 0 : lo;
+  hi = hi > cfg_.num_envs ? cfg_.num_envs : hi;
+  if (hi <= lo) return;
+  pool_->run(hi - lo, [&](int b, int e) {
+    for (int i = b + lo; i < e + lo; ++i) {
       const int32_t* a = &actions[static_cast<size_t>(i) * static_cast<size_t>(action_stride)];
       int pb = a[1] < 0 ? 0 : (a[1] > 6 ? 6 : a[1]);
       float pd = kPitchBins[pb] * (cfg_.pitch_rate_max_deg / 10.0f);

@@ -81,6 +81,10 @@ class EnvBatch {
   // value there force-fails the env on the first tick (stall kill).
   void step_k(const int32_t* actions, int action_stride, int yaw_slot, int fail_slot, int k, RowOut obs,
               RowOut term_obs, RowOut rec, RowOut term_rec);
+  // step_k over envs [lo, hi) only (pointers still index the whole batch), so
+  // that two halves of the batch can alternate with the GPU work of the other.
+  void step_k_range(int lo, int hi, const int32_t* actions, int action_stride, int yaw_slot, int fail_slot, int k,
+                    RowOut obs, RowOut term_obs, RowOut rec, RowOut term_rec);
 
   PlayerState* states() { return st_.data(); }
   void set_state(int env, const PlayerState& s);

@@ -55,7 +55,10 @@ def _targets():
     sim = sorted(str(p) for p in (CSRC / "sim").glob("*.cpp"))
     kern = lambda *names: [str(CSRC / "kernels" / n) for n in names]
     comm = lambda *names: [str(CSRC / "comm" / n) for n in names]
-    t = {"libsurfsim.so": ("g++", sim, [], [])}
+    t = {"libsurfsim.so": ("g++", sim, [], []),
+         # native acceptance gates of the simulator (an executable, run by tests/test_sim.py)
+         "surfsim_gates": ("g++exe", [x for x in sim if not x.endswith("c_api.cpp")] +
+                           [str(CSRC / "sim" / "tests" / "gates.cpp")], [], [])}
     groups = {
         "libsurf_vision.so": kern("march.cu", "sdf.cu", "geodesic.cu"),
         "libsurf_rl.so": kern("rl.cu", "reward.cu"),
@@ -83,11 +86,15 @@ def _digest(compiler: str, srcs: list[str], flags: list[str]) -> str:
     return h.hexdigest()
 
 
-def _compile(name: str, spec, force: bool) -> str:
+def _plan(name: str, spec):
+    """(command, content digest) of one target."""
     compiler, srcs, extra, link = spec
     out = LIB / name
-    stamp = LIB / (name + ".sha")
-    if compiler == "g++":
+    if compiler == "g++exe":
+        base = [f for f in CXX_FLAGS if f not in ("-shared", "-fPIC", "-fvisibility=hidden")]
+        cmd = ["g++"] + base + extra + srcs + ["-o", str(out)] + link
+        flags = base + extra + link
+    elif compiler == "g++":
         cmd = ["g++"] + CXX_FLAGS + extra + srcs + ["-o", str(out)] + link
         flags = CXX_FLAGS + extra + link
     else:
@@ -95,11 +102,28 @@ def _compile(name: str, spec, force: bool) -> str:
         inc = ["-I", str(CSRC / "common")] + _cutlass_include()
         cmd = [nvcc] + NVCC_FLAGS + inc + extra + srcs + ["-o", str(out)] + link
         flags = NVCC_FLAGS + extra + link
-    dig = _digest(compiler, srcs, flags)
+    return cmd, _digest(compiler, srcs, flags)
+
+
+def is_stale(name: str) -> bool:
+    """True when ``_lib/<name>`` is missing or was built from other sources or flags."""
+    spec = _targets().get(name)
+    out, stamp = LIB / name, LIB / (name + ".sha")
+    if spec is None:
+        return not out.exists()
+    if not out.exists() or not stamp.exists():
+        return True
+    return stamp.read_text() != _plan(name, spec)[1]
+
+
+def _compile(name: str, spec, force: bool) -> str:
+    out = LIB / name
+    stamp = LIB / (name + ".sha")
+    cmd, dig = _plan(name, spec)
     if not force and out.exists() and stamp.exists() and stamp.read_text() == dig:
         return f"{name}: up to date"
     LIB.mkdir(parents=True, exist_ok=True)
-    tmp = out.with_suffix(".so.tmp")
+    tmp = out.with_name(out.name + ".tmp")
     cmd[cmd.index(str(out))] = str(tmp)
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:

@@ -25,9 +25,16 @@ def load(name: str, build_if_missing: bool = True) -> ctypes.CDLL:
         if name in _cache:
             return _cache[name]
         path = LIB_DIR / name
-        if not path.exists() and build_if_missing:
+        if build_if_missing:
+            # a library built from other sources than these would be called
+            # with the wrong signatures: rebuild it first (nvcc / g++ exist
+            # wherever the framework runs)
             from . import _build
-            _build.build(only=[name], verbose=False)
+            if _build.is_stale(name):
+                try:
+                    _build.build(only=[name], verbose=False)
+                except Exception as e:                    # noqa: BLE001
+                    raise NativeLibraryMissing(f"{path} is stale and could not be rebuilt: {e}") from e
         if not path.exists():
             raise NativeLibraryMissing(
                 f"{path} is not built; run `python -c 'import __graft_entry__ as g; g.build()'`")

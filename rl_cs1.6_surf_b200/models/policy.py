@@ -152,7 +152,15 @@ class PolicyNet:
         self.specs = _param_specs(cfg)
         self.offsets = {}
         off = 0
-        for name, shape, *_ in self.specs:
+        # storage: every weight matrix first, then the biases and log_std
+        # (the parameters read in fp32 by the kernels) as one tail region
+        # starting at fp32_from; data-parallel ranks keep full fp32 replicas
+        # of the tail only and bf16 replicas of everything
+        order = [s for s in self.specs if not s[4]] + [s for s in self.specs if s[4]]
+        self.fp32_from = 0
+        for name, shape, _, _, is_bias in order:
+            if is_bias and not self.fp32_from:
+                self.fp32_from = off
             self.offsets[name] = (off, shape)
             off += (int(np.prod(shape)) + 63) // 64 * 64       # 256-byte aligned views
         self.numel = off

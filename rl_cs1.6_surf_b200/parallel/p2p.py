@@ -9,7 +9,8 @@ path:
 
 * ``step``  — reduce-scatter of the gradient over peer loads, global-norm
   clip, Adam on the owned shard, push of the updated shard to every peer
-  (three kernels, graph-capturable; replaces all-reduce + clip + Adam);
+  (one cooperative kernel with in-kernel grid barriers, graph-capturable;
+  replaces all-reduce + clip + Adam);
 * ``allreduce_moments`` — per-minibatch advantage moments (one block);
 * ``merge_counts`` — curiosity count increments summed into every rank's
   table, then cleared.
@@ -49,19 +50,20 @@ _lib.register(CLIB, {
     "surf_p2p_create": (c_void_p, [c_int, c_int, ctypes.POINTER(c_void_p), c_double]),
     "surf_p2p_destroy": (None, [c_void_p]),
     "surf_p2p_set_grad": (c_int, [c_void_p, c_int64, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p),
-                                  ctypes.POINTER(c_void_p), c_void_p, c_void_p, c_void_p]),
+                                  ctypes.POINTER(c_void_p), c_void_p, c_void_p, c_void_p, c_int64]),
     "surf_p2p_shard": (c_int64, [c_void_p]),
     "surf_p2p_set_counts": (c_int, [c_void_p, c_int64, c_void_p, ctypes.POINTER(c_void_p)]),
     "surf_p2p_grad_step": (c_int, [c_void_p, c_void_p]),
     "surf_p2p_moments": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
     "surf_p2p_merge_counts": (c_int, [c_void_p, c_void_p]),
+    "surf_p2p_prof_words": (c_int, []),
 })
-_lib._KERNELS_PER_CALL.update({"surf_p2p_grad_step": 3, "surf_p2p_merge_counts": 2})
+
 
 # sync-block words (csrc/comm/p2p.cu)
-W_SEQ_GRAD, W_SEQ_MOM, W_SEQ_CNT, W_ERR, W_ERR_TARGET = 0, 1, 2, 3, 4
+W_SEQ_GRAD, W_SEQ_MOM, W_SEQ_CNT, W_ERR, W_ERR_TARGET, W_PROF = 0, 1, 2, 3, 4, 112
 _STAGES = {1: "gradient barrier", 2: "norm exchange", 3: "parameter push", 4: "moments", 5: "count barrier",
-           6: "count drain"}
+           6: "count drain", 7: "in-kernel grid barrier"}
 
 
 class P2PError(RuntimeError):
@@ -70,6 +72,8 @@ class P2PError(RuntimeError):
 
 def describe_error(code: int, target: int) -> str:
     stage = _STAGES.get((code >> 8) & 0xF, "unknown stage")
+    if (code >> 8) & 0xF == 7:
+        return f"peer-memory collective timed out at an {stage} (call #{target})"
     return f"peer-memory collective timed out in the {stage} waiting for rank {code & 0xFF} (call #{target})"
 
 
@@ -97,6 +101,7 @@ class P2PComm(NcclComm):
         if not self.plan:
             raise P2PError("surf_p2p_create failed")
         self.shard = 0
+        self.push32_from = 0
         self._opt = None
         self._counts = False
 
@@ -133,8 +138,9 @@ class P2PComm(NcclComm):
         g = self.share(net.grad)
         p = self.share(net.flat)
         p16 = self.share(net.flat16)
+        self.push32_from = int(getattr(net, "fp32_from", 0))
         check(L.surf_p2p_set_grad(self.plan, net.numel, _ptr_array(g), _ptr_array(p), _ptr_array(p16), ptr(opt.m),
-                                  ptr(opt.v), ptr(opt.hyper)), "surf_p2p_set_grad")
+                                  ptr(opt.v), ptr(opt.hyper), self.push32_from), "surf_p2p_set_grad")
         self.shard = int(L.surf_p2p_shard(self.plan))
         self._opt = opt
         use_counts = reward is not None and reward.spec.int_coef > 0 and torch.is_tensor(reward.counts)
@@ -177,6 +183,12 @@ class P2PComm(NcclComm):
         if code:
             raise P2PError(f"rank {self.rank}: {describe_error(code, target)}")
 
+    def phase_times_us(self) -> dict:
+        """Phase durations of this rank's last gradient step (device clock)."""
+        t = [int(x) for x in self.sync[W_PROF:W_PROF + 6].tolist()]
+        names = ("barrier_in", "reduce_scatter", "norm_exchange", "adam_push", "done_wait")
+        return {k: (t[i + 1] - t[i]) / 1e3 for i, k in enumerate(names)}
+
     def sequence(self) -> tuple:
         return tuple(int(x) for x in self.sync[:3].tolist())
 
@@ -184,18 +196,34 @@ class P2PComm(NcclComm):
         lo = min(n, self.rank * self.shard)
         return lo, min(n, lo + self.shard)
 
+    def _gather_shards(self, t: torch.Tensor) -> torch.Tensor:
+        n = t.numel()
+        full = torch.zeros_like(t)
+        lo, hi = self.shard_range(n)
+        full[lo:hi] = t[lo:hi]
+        dist.all_reduce(full)
+        return full
+
+    def full_params(self, net) -> torch.Tensor:
+        """The complete fp32 master weights (collective): each rank keeps only
+        its shard of the weight matrices current in fp32."""
+        full = self._gather_shards(net.flat)
+        if self.push32_from:
+            full[self.push32_from:] = net.flat[self.push32_from:]
+        return full
+
+    def checksum(self, net) -> tuple:
+        """(min, max) over ranks of the sum of the replicated parameters (bf16
+        copy + fp32 tail): equal iff the replicas agree."""
+        s = net.flat16.double().sum() + net.flat[self.push32_from:].double().sum()
+        lo, hi = s.reshape(1).clone(), s.reshape(1).clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        return float(lo.item()), float(hi.item())
+
     def full_optimizer_state(self, opt) -> dict:
         """m and v of every shard on every rank (collective)."""
-        n = opt.m.numel()
-        out = {}
-        for name in ("m", "v"):
-            t = getattr(opt, name)
-            full = torch.zeros_like(t)
-            lo, hi = self.shard_range(n)
-            full[lo:hi] = t[lo:hi]
-            dist.all_reduce(full)
-            out[name] = full
-        return out
+        return {name: self._gather_shards(getattr(opt, name)) for name in ("m", "v")}
 
     def close(self) -> None:
         if self.plan:

@@ -21,10 +21,12 @@ import torch
 from ..ops import _lib
 from ..ops._lib import check, ptr, stream_ptr
 
-MODES = ("speed", "avgspeed", "forward", "path", "maxspeed", "coverage", "race")
+MODES = ("speed", "avgspeed", "forward", "path", "maxspeed", "coverage", "race", "acro", "blend")
 DEFAULT_SCALE = {"speed": 0.01, "avgspeed": 0.0005, "forward": 0.01, "path": 0.01, "maxspeed": 0.05,
-                 "coverage": 0.001, "race": None}
-REC_O, REC_YAW, REC_V, REC_TICK, REC_BASE, REC_DONE, REC_TRUNC, REC_GOAL, REC_ENDED = 0, 3, 6, 9, 10, 11, 12, 13, 14
+                 "coverage": 0.001, "race": None, "acro": 0.001, "blend": 0.01}
+STATE_FLOATS = 24
+REC_O, REC_YAW, REC_V, REC_TICK, REC_BASE, REC_DONE, REC_TRUNC, REC_GOAL, REC_ENDED, REC_ONGROUND = \
+    0, 3, 6, 9, 10, 11, 12, 13, 14, 15
 
 
 @dataclass
@@ -44,6 +46,16 @@ class RewardSpec:
     speed_equiv: float = 0.0
     stall_secs: float = 15.0
     stall_eps: float = 32.0
+    # acro style (per tick)
+    spin_bonus: float = 1.5
+    switch_bonus: float = 2.0
+    spin_rate_cap: float = 6.0
+    max_spins: int = 2
+    min_air: int = 30
+    back_bonus: float = 0.01
+    # blend: forward -> path between these global steps
+    blend_start: float = 100e6
+    blend_end: float = 200e6
     # curiosity
     int_coef: float = 0.0
     int_cell: float = 256.0
@@ -75,15 +87,20 @@ class RewardParams(ctypes.Structure):
                 ("fail_pen", c_float), ("speed_coef", c_float), ("speed_equiv", c_float), ("stall_ticks", c_int),
                 ("stall_eps", c_float), ("int_coef", c_float), ("int_cell", c_float), ("int_view", c_int),
                 ("int_speed", c_int), ("int_min", c_float * 3), ("int_dim", c_int * 3), ("table_mask", c_uint32),
-                ("gamma_boot", c_float)]
+                ("gamma_boot", c_float), ("spin_bonus", c_float), ("switch_bonus", c_float),
+                ("spin_rate_cap", c_float), ("back_bonus", c_float), ("gravity_tick", c_float), ("max_spins", c_int),
+                ("min_air", c_int), ("blend_w", c_void_p)]
 
 
 RLIB = "libsurf_rl.so"
 _lib.register(RLIB, {
     "surf_reward_params_size": (c_int, []),
-    "surf_reward_init": (c_int, [ctypes.POINTER(RewardParams), c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
+    "surf_reward_state_floats": (c_int, []),
+    "surf_reward_init": (c_int, [ctypes.POINTER(RewardParams), c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+                                 c_void_p]),
     "surf_reward": (c_int, [ctypes.POINTER(RewardParams), c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
-                            c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+                            c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+    "surf_reward_counts": (c_int, [ctypes.POINTER(RewardParams), c_void_p, c_void_p, c_void_p, c_void_p]),
     "surf_obs_features": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_int64, c_int, c_void_p,
                                   c_int, c_void_p]),
     "surf_permutation": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),
@@ -179,7 +196,15 @@ def build_params(spec: RewardSpec, n: int, K: int, bounds, field: Optional[GoalF
         p.int_min[a] = mins[a]
         p.int_dim[a] = idim[a]
     p.table_mask = (1 << spec.table_log2) - 1
+    p.spin_bonus, p.switch_bonus, p.spin_rate_cap = spec.spin_bonus, spec.switch_bonus, spec.spin_rate_cap
+    p.back_bonus, p.max_spins, p.min_air = spec.back_bonus, spec.max_spins, spec.min_air
+    p.gravity_tick = 800.0 * 0.01
     return p
+
+
+def blend_weight(spec: RewardSpec, global_step: float) -> float:
+    """Forward -> path curriculum weight (reference BlendedReward.weight)."""
+    return min(1.0, max(0.0, (float(global_step) - spec.blend_start) / max(spec.blend_end - spec.blend_start, 1.0)))
 
 
 class GpuReward:
@@ -191,7 +216,10 @@ class GpuReward:
         dev = torch.device(device)
         self.field_t = torch.as_tensor(field.grid.astype(np.int16).view(np.int16), device=dev) if field is not None else None
         self.params = build_params(spec, n, K, bounds, field, ptr(self.field_t), d0)
-        self.state = torch.zeros(n * 18, dtype=torch.float32, device=dev)
+        self.state = torch.zeros(n * STATE_FLOATS, dtype=torch.float32, device=dev)
+        self.blend_w = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.params.blend_w = ptr(self.blend_w)
+        self.keys = torch.zeros(n, dtype=torch.int64, device=dev)
         self.visited = torch.zeros(max(1, n * self.params.cov_words), dtype=torch.int32, device=dev)
         tsize = 1 << spec.table_log2 if spec.int_coef > 0 else 1
         self.counts = torch.zeros(tsize, dtype=torch.int32, device=dev)
@@ -201,16 +229,57 @@ class GpuReward:
         self.boot = torch.zeros(n, dtype=torch.float32, device=dev)
         self.stats = torch.zeros(8, dtype=torch.float32, device=dev)
         self.lib = _lib.lib(RLIB)
+        if int(self.lib.surf_reward_params_size()) != ctypes.sizeof(RewardParams) or \
+                int(self.lib.surf_reward_state_floats()) != STATE_FLOATS:
+            raise RuntimeError("libsurf_rl.so reward layout differs from rewards/spec.py (rebuild the library)")
+        self._group_params: dict = {}
 
-    def init(self, rec: torch.Tensor) -> None:
-        check(self.lib.surf_reward_init(ctypes.byref(self.params), ptr(rec), rec.stride(0), ptr(self.state),
-                                        ptr(self.visited), stream_ptr(rec.device)), "surf_reward_init")
+    def _params(self, lo: int, hi: int) -> RewardParams:
+        if (lo, hi) == (0, self.n):
+            return self.params
+        key = (lo, hi)
+        if key not in self._group_params:
+            p = RewardParams()
+            ctypes.memmove(ctypes.byref(p), ctypes.byref(self.params), ctypes.sizeof(RewardParams))
+            p.n = hi - lo
+            self._group_params[key] = p
+        return self._group_params[key]
 
-    def __call__(self, rec: torch.Tensor, rew_out: torch.Tensor, done_out: torch.Tensor) -> None:
-        check(self.lib.surf_reward(ctypes.byref(self.params), ptr(rec), rec.stride(0), ptr(self.state),
-                                   ptr(self.visited), ptr(self.counts), ptr(self.delta), ptr(self.boot), ptr(rew_out),
-                                   ptr(done_out), ptr(self.stall), ptr(self.new_key), ptr(self.stats),
-                                   stream_ptr(rec.device)), "surf_reward")
+    def _ptrs(self, lo: int):
+        w = self.params.cov_words
+        return (ptr(self.state) + 4 * STATE_FLOATS * lo, ptr(self.visited) + 4 * w * lo if w else ptr(self.visited),
+                ptr(self.boot) + 4 * lo, ptr(self.stall) + lo, ptr(self.new_key) + 8 * lo, ptr(self.keys) + 8 * lo)
+
+    def set_step(self, global_step: float) -> None:
+        """Schedules that live in device memory (the blend weight)."""
+        if self.spec.mode == "blend":
+            self.blend_w.fill_(blend_weight(self.spec, global_step))
+
+    def init(self, rec: torch.Tensor, lo: int = 0, hi: Optional[int] = None) -> None:
+        """Per-env state from the spawn records; ``rec`` holds rows lo..hi."""
+        hi = self.n if hi is None else hi
+        st, vis, _, _, _, keys = self._ptrs(lo)
+        check(self.lib.surf_reward_init(ctypes.byref(self._params(lo, hi)), ptr(rec), rec.stride(0), st, vis, keys,
+                                        stream_ptr(rec.device)), "surf_reward_init")
+
+    def __call__(self, rec: torch.Tensor, rew_out: torch.Tensor, done_out: torch.Tensor, lo: int = 0,
+                 hi: Optional[int] = None, counts: bool = True) -> None:
+        """Rewards of envs lo..hi (``rec``, ``rew_out``, ``done_out`` hold those
+        rows). With ``counts=False`` the curiosity increments are only staged;
+        ``count_all`` applies them for every env (env groups call it once per
+        decision after the last group, so every bonus of a decision reads the
+        counts from before it)."""
+        hi = self.n if hi is None else hi
+        st, vis, boot, stall, nk, keys = self._ptrs(lo)
+        check(self.lib.surf_reward(ctypes.byref(self._params(lo, hi)), ptr(rec), rec.stride(0), st, vis,
+                                   ptr(self.counts), ptr(self.delta), boot, ptr(rew_out), ptr(done_out), stall, nk,
+                                   keys, ptr(self.stats), 1 if counts else 0, stream_ptr(rec.device)),
+              "surf_reward" if counts and self.spec.int_coef > 0 else "surf_reward_phase1")
+
+    def count_all(self) -> None:
+        if self.spec.int_coef > 0:
+            check(self.lib.surf_reward_counts(ctypes.byref(self.params), ptr(self.new_key), ptr(self.counts),
+                                              ptr(self.delta), stream_ptr(self.counts.device)), "surf_reward_counts")
 
     def pop_stats(self) -> dict:
         s = self.stats.tolist()
@@ -248,6 +317,10 @@ class CpuReward:
         self.visited = np.zeros((n, ncell), bool)
         self.counts = np.zeros(1 << spec.table_log2 if spec.int_coef > 0 else 1, np.int64)
         self.stats = np.zeros(8, np.float64)
+        self.step = 0.0
+
+    def set_step(self, global_step: float) -> None:
+        self.step = float(global_step)
 
     def _cov_cell(self, pos):
         c = [np.clip(np.floor((pos[:, a] - self.p.cmin[a]) / self.p.cell).astype(np.int64), 0, self.p.cdim[a] - 1)
@@ -284,6 +357,12 @@ class CpuReward:
         if self.mode == "race":
             self.d = self.field.sample(rec[:, 0:3])
             self.best = self.d.copy()
+        if self.mode in ("forward", "blend"):
+            self.best[:] = 0.0
+        self.yaw = rec[:, REC_YAW].astype(np.float32).copy()
+        self.vel = rec[:, REC_V:REC_V + 3].astype(np.float32).copy()
+        self.streak = np.zeros(n, np.float32)
+        self.spin = np.zeros(n, np.float32)
         self.cell = self._cov_cell(rec[:, 0:3])
         self.visited[:] = False
         self.visited[np.arange(n), self.cell] = True
@@ -313,7 +392,15 @@ class CpuReward:
             proj = (rec[:, 0] - self.ref[:, 0]) * self.dir[:, 0] + (rec[:, 1] - self.ref[:, 1]) * self.dir[:, 1]
             r = np.maximum(proj - self.best, 0) * p.scale
             self.best = np.maximum(self.best, proj)
-        elif m == "coverage":
+        elif m == "blend":
+            self.ref[tele] += dxy[tele]
+            proj = (rec[:, 0] - self.ref[:, 0]) * self.dir[:, 0] + (rec[:, 1] - self.ref[:, 1]) * self.dir[:, 1]
+            fwd = np.maximum(proj - self.best, 0) * p.scale
+            self.best = np.maximum(self.best, proj)
+            path = np.where(tele, 0.0, hstep * p.scale)
+            w = blend_weight(self.spec, self.step)
+            r = (1.0 - w) * fwd + w * path
+        elif m in ("coverage", "acro"):
             c = self._cov_cell(rec[:, 0:3])
             moved = c != self.cell
             seen = self.visited[np.arange(n), c]
@@ -343,6 +430,29 @@ class CpuReward:
             self.since = np.where(improved, 0.0, self.since + p.K)
             self.d = d
         r = r.astype(np.float32)
+        if m == "acro":
+            K = float(p.K)
+            v = rec[:, REC_V:REC_V + 3].astype(np.float32)
+            dv = v - self.vel
+            contact = (np.abs(dv[:, 0]) + np.abs(dv[:, 1]) > 40.0 * K) | (np.abs(dv[:, 2] + p.gravity_tick * K) > 12.0 * K)
+            grounded = rec[:, REC_ONGROUND] != 0
+            ballistic = ~grounded & ~contact
+            wrap = lambda a: np.mod(a + 180.0, 360.0) - 180.0
+            dyaw = np.abs(wrap(rec[:, REC_YAW] - self.yaw))
+            flight_end = (self.streak * K >= p.min_air) & (contact | grounded)
+            style = np.where(flight_end, p.spin_bonus * np.minimum(self.spin, 360.0 * p.max_spins) / 360.0, 0.0)
+            heading = np.degrees(np.arctan2(v[:, 1], v[:, 0]))
+            back = np.abs(wrap(rec[:, REC_YAW] - heading)) >= 140.0
+            style += np.where(flight_end & (sp >= 300.0) & back, p.switch_bonus, 0.0)
+            style += np.where(~grounded & contact & (sp >= 500.0) & back, p.back_bonus * K, 0.0)
+            self.spin = np.where(ballistic, self.spin + np.where(self.streak > 0, np.minimum(dyaw, p.spin_rate_cap * K), 0),
+                                 0.0).astype(np.float32)
+            self.streak = np.where(ballistic, self.streak + 1, 0).astype(np.float32)
+            r = (r + np.where(ended, 0.0, style)).astype(np.float32)
+            self.spin[ended] = 0
+            self.streak[ended] = 0
+        self.yaw = rec[:, REC_YAW].astype(np.float32).copy()
+        self.vel = rec[:, REC_V:REC_V + 3].astype(np.float32).copy()
         if m != "race":
             r[ended] = 0.0
         if self.spec.int_coef > 0:
@@ -373,13 +483,13 @@ class CpuReward:
             yaw = np.radians(rec[e, REC_YAW])
             self.dir[e] = np.stack([np.cos(yaw), np.sin(yaw)], 1)
             self.ref[e] = rec[e, 0:2]
-            if m == "forward":
+            if m in ("forward", "blend"):
                 self.best[e] = 0.0
             if m == "race":
                 self.best[e] = self.d[e]
                 self.since[e] = 0
                 self.ticks[e] = 0
-            if m == "coverage":
+            if m in ("coverage", "acro"):
                 self.visited[e] = False
                 c = self._cov_cell(rec[e, 0:3])
                 self.visited[e, c] = True

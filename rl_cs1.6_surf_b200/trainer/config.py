@@ -19,7 +19,7 @@ RUN_DEFINING = (
     "vision", "lidar_w", "lidar_h", "lidar_range", "lidar_near", "lidar_cell", "pinhole", "march_steps",
     "continuous_yaw", "gps", "heads", "hidden", "fc", "proprio", "mlp", "reward", "pitch_rate", "yaw_adaptive",
     "respawn_frac", "respawn_margin", "respawn_reservoir", "train_stride", "drop_frac", "drop_min", "drop_max",
-    "punch_min", "punch_max", "respawn_speed", "respawn_binned", "respawn_pool",
+    "punch_min", "punch_max", "respawn_speed", "respawn_binned", "respawn_pool", "rnd_coef",
 )
 
 
@@ -83,10 +83,13 @@ class TrainConfig:
     respawn_speed: tuple = (0.9, 1.1)  # spawn speed multiplier range of reservoir starts
     respawn_binned: int = 0            # distance bins for reservoir sampling (race; 0 = uniform)
     respawn_pool: int = 4096
+    # random network distillation novelty (0 = off)
+    rnd_coef: float = 0.0
     # run
     seed: int = 0
     device: str = "cuda"
     graphs: bool = True
+    env_groups: int = 2                # rollout: env groups alternating host stepping with GPU work
     comm: str = "p2p"                  # p2p (fused NVLink kernels) | nccl (library baseline)
     threads: Optional[int] = None
     run: str = "runs/default"

@@ -96,10 +96,13 @@ class Trainer:
             pool = self.procmap.spawn_pool
         else:
             self.procmap = None
+            from ..sim.zones import load_zones
             image = Path(cfg.map).read_bytes()
-            zp = Path(cfg.map).with_suffix("").as_posix() + ".zones.json"
-            self.zones = json.loads(Path(zp).read_text()) if Path(zp).exists() else {}
+            self.zones = load_zones(cfg.map)
             pool = None
+            zp = Path(cfg.map).with_suffix(".spawns.npy")
+            if zp.exists():                                   # a procedural map saved to disk keeps its pool
+                pool = np.load(zp)
         self.map_image = image
         probe = None
         if cfg.spawn not in ("pool", "map") or (cfg.spawn == "pool" and pool is None):
@@ -189,7 +192,11 @@ class Trainer:
                                        device=dev)
         self.mb = T * N // cfg.minibatches
         if self.gpu:
-            self.ws_roll = Workspace(self.net, N)
+            G = cfg.env_groups if (cfg.env_groups > 1 and N % cfg.env_groups == 0 and N // cfg.env_groups >= 64) else 1
+            step = N // G
+            self.groups = [(g * step, (g + 1) * step) for g in range(G)]
+            self.ws_grp = [Workspace(self.net, step) for _ in range(G)]
+            self.grp_events = [torch.cuda.Event() for _ in range(G)]
             self.ws_upd = Workspace(self.net, self.mb)
             self.perm = torch.zeros(T * N, dtype=torch.int64, device=dev)
             self.perm_key = torch.tensor([cfg.seed * 7919 + self.rank], dtype=torch.int64, device=dev)
@@ -204,10 +211,14 @@ class Trainer:
                 self.comm.attach(self.net, self.opt, self.reward)
             self.rew_graphs: list = []
             self.upd_graph = None
-            self.act_event = torch.cuda.Event()
         else:
             self.reward = CpuReward(cfg.reward, N, self.K, self.bounds, self.field, self.d0)
         self.seed_base = (self.cfg.seed * 1_000_003 + self.rank * 7_777_777) & 0xFFFFFFFFFFFF
+        self.rnd = None
+        if cfg.rnd_coef > 0:
+            from .rnd import RND
+            self.rnd = RND(15, device=dev, seed=cfg.seed)
+            self.rnd_obs = torch.zeros((T + 1, N, 15), device=dev)
         self.respawn = None
         if cfg.respawn_frac > 0:
             from .respawn import RespawnReservoir
@@ -229,6 +240,19 @@ class Trainer:
         h = self.hrec.numpy()
         ended = (h[:, C_REC + 11] != 0) | (h[:, C_REC + 12] != 0)
         self.respawn.observe(self.core.states_view, ended, ticks=self.K, step_index=t)
+
+    def _train_rnd(self, steps: int = 4, batch: int = 4096) -> None:
+        """A few predictor updates on random observations of this rollout."""
+        T, N = self.T, self.N
+        if self.gpu:
+            obs = self.rnd_obs[1:].reshape(-1, 15)
+        else:
+            obs = torch.from_numpy(self.hrec.numpy()[:, C_OBS:C_OBS + 15].copy())
+        g = torch.Generator(device=obs.device).manual_seed(self.cfg.seed * 977 + self.iteration)
+        for _ in range(steps):
+            idx = torch.randint(0, obs.shape[0], (min(batch, obs.shape[0]),), device=obs.device, generator=g)
+            self.rnd.train_step(obs[idx])
+        del T, N
 
     def _refresh_respawn_pool(self) -> None:
         if self.respawn is None:
@@ -274,119 +298,135 @@ class Trainer:
                                                           obs.shape[0], None, 0, stream_ptr(obs.device)),
               "surf_obs_features")
 
-    def _observe(self, t: int) -> None:
-        """Render + features of the current records into rollout slot t."""
-        if self.cfg.vision:
-            self.camera.render(self.hdev[:, C_REC:C_REC + 6], out=self.b_img[t])
-        self._features(self.hdev[:, C_OBS:C_OBS + 15], self.b_scal[t])
-
-    def _decide(self, t: int) -> None:
-        img = self.b_img[t] if self.cfg.vision else None
-        out = forward_gpu(self.net, self.ws_roll, self.b_scal[t], img)
-        R.sample_heads(out, self.heads, self.net.p("log_std"), self.b_act[t], self.b_logp[t], self.seed_base,
-                       0, value_src=out[:, self.layout.value_col], value_out=self.b_val[t],
-                       fail_src=self.reward.stall, counter_ptr=self.sample_counter, counter_offset=t)
-
-    def _decision_body(self, t: int) -> None:
-        self.hdev.copy_(self.hrec, non_blocking=True)
-        if t > 0:
-            self.reward(self.hdev[:, C_REC:C_REC + REC_COLS], self.b_rew[t - 1], self.b_done[t - 1])
-        self._observe(t)
-        self._decide(t)
-        self.act_pin.copy_(self.b_act[t], non_blocking=True)
-
-    def _tail_body(self) -> None:
+    def _group_body(self, g: int, t: int) -> None:
+        """GPU work of env group g at decision slot t (t == T: the rollout
+        tail): upload the group's host records, reward of the previous
+        decision, depth render + features, policy forward, then sampling and
+        the async copy of the actions to pinned memory (or, at the tail, the
+        bootstrap value)."""
+        lo, hi = self.groups[g]
         T = self.T
-        self.hdev.copy_(self.hrec, non_blocking=True)
-        self.reward(self.hdev[:, C_REC:C_REC + REC_COLS], self.b_rew[T - 1], self.b_done[T - 1])
-        self._observe(T)
-        img = self.b_img[T] if self.cfg.vision else None
-        out = forward_gpu(self.net, self.ws_roll, self.b_scal[T], img)
-        self.last_val.copy_(out[:, self.layout.value_col])
-        R.bump_counter(self.sample_counter, T)
+        self.hdev[lo:hi].copy_(self.hrec[lo:hi], non_blocking=True)
+        if t > 0:
+            last = g == len(self.groups) - 1
+            self.reward(self.hdev[lo:hi, C_REC:C_REC + REC_COLS], self.b_rew[t - 1, lo:hi], self.b_done[t - 1, lo:hi],
+                        lo, hi, counts=len(self.groups) == 1)
+            if last and len(self.groups) > 1:
+                self.reward.count_all()
+            if self.rnd is not None:
+                self.rnd_obs[t, lo:hi].copy_(self.hdev[lo:hi, C_OBS:C_OBS + 15])
+                self.b_rew[t - 1, lo:hi].add_(self.cfg.rnd_coef * self.rnd.bonus(self.rnd_obs[t, lo:hi]))
+        img = None
+        if self.cfg.vision:
+            img = self.b_img[t, lo:hi]
+            self.camera.render(self.hdev[lo:hi, C_REC:C_REC + 6], out=img)
+        self._features(self.hdev[lo:hi, C_OBS:C_OBS + 15], self.b_scal[t, lo:hi])
+        out = forward_gpu(self.net, self.ws_grp[g], self.b_scal[t, lo:hi], img)
+        vc = self.layout.value_col
+        if t < T:
+            R.sample_heads(out, self.heads, self.net.p("log_std"), self.b_act[t, lo:hi], self.b_logp[t, lo:hi],
+                           self.seed_base ^ (0x9E3779B97F4A7C15 * (g + 1) & 0xFFFFFFFFFFFF), 0,
+                           value_src=out[:, vc], value_out=self.b_val[t, lo:hi], fail_src=self.reward.stall[lo:hi],
+                           counter_ptr=self.sample_counter, counter_offset=t)
+            self.act_pin[lo:hi].copy_(self.b_act[t, lo:hi], non_blocking=True)
+        else:
+            self.last_val[lo:hi].copy_(out[:, vc])
+            if g == len(self.groups) - 1:
+                R.bump_counter(self.sample_counter, T)
 
     def _capture(self) -> None:
-        """One CUDA graph per decision slot plus the rollout tail."""
+        """One CUDA graph per (env group, decision slot), the rollout tail included."""
         T = self.T
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
-            for t in range(min(T, 2)):                 # warm-up (kernel attributes, lazy inits)
-                self._decision_body(t)
-            self._tail_body()
+            for g in range(len(self.groups)):          # warm-up (kernel attributes, lazy inits)
+                for t in (0, 1, T):
+                    self._group_body(g, t)
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
         self.sample_counter.zero_()
         from ..ops import _lib
         self.rew_graphs = []
         self.graph_launches = []
-        for t in range(T):
-            g = torch.cuda.CUDAGraph()
-            c0 = _lib.launch_count()
-            with torch.cuda.graph(g, stream=s):
-                self._decision_body(t)
-            self.graph_launches.append(_lib.launch_count() - c0)
-            self.rew_graphs.append(g)
-        self.tail_graph = torch.cuda.CUDAGraph()
-        c0 = _lib.launch_count()
-        with torch.cuda.graph(self.tail_graph, stream=s):
-            self._tail_body()
-        self.tail_launches = _lib.launch_count() - c0
+        for g in range(len(self.groups)):
+            row, counts = [], []
+            for t in range(T + 1):
+                gr = torch.cuda.CUDAGraph()
+                c0 = _lib.launch_count()
+                with torch.cuda.graph(gr, stream=s):
+                    self._group_body(g, t)
+                counts.append(_lib.launch_count() - c0)
+                row.append(gr)
+            self.rew_graphs.append(row)
+            self.graph_launches.append(counts)
         torch.cuda.synchronize()
         self.reset()                      # the warm-up touched env-facing reward state
-        self._log(f"captured {T + 1} rollout graphs")
+        self._log(f"captured {len(self.groups) * (T + 1)} rollout graphs ({len(self.groups)} env groups)")
 
-    def _bootstrap_truncations(self) -> None:
-        """gamma * V(s_T) for envs whose episode was truncated this decision
-        (their states are already the next episode's): render the terminal
-        poses, run the value head, stage the bonus for the next reward kernel."""
+    def _run_group(self, g: int, t: int) -> None:
+        from ..ops import _lib
+        ev = self.timer.gpu_start("rollout_gpu")
+        if self.cfg.graphs:
+            self.rew_graphs[g][t].replay()
+            _lib.add_launches(self.graph_launches[g][t])
+        else:
+            self._group_body(g, t)
+        self.timer.gpu_end(ev)
+        self.grp_events[g].record()
+
+    def _env_step_group(self, g: int) -> None:
+        lo, hi = self.groups[g]
+        h = self.hrec
+        base, stride = h.data_ptr(), H_COLS
+        self.core.step_k_range(lo, hi, self.act_pin.data_ptr(), 8, self.K,
+                               yaw_slot=6 if self.layout.continuous_yaw else -1, fail_slot=7,
+                               obs=(base + 4 * C_OBS, stride), term_obs=(base + 4 * C_TOBS, stride),
+                               rec=(base + 4 * C_REC, stride), term_rec=(base + 4 * C_TREC, stride))
+
+    def _bootstrap_truncations(self, g: int) -> None:
+        """gamma * V(s_T) for envs of group g whose episode was truncated this
+        decision (their states are already the next episode's): render the
+        terminal poses, run the value head, stage the bonus for the group's
+        next reward kernel (stream-ordered before it)."""
+        lo, hi = self.groups[g]
         h = self.hrec.numpy()
-        trunc = np.flatnonzero(h[:, C_REC + 12] != 0)
+        trunc = lo + np.flatnonzero(h[lo:hi, C_REC + 12] != 0)
         if len(trunc) == 0:
             return
         idx = torch.as_tensor(trunc, device=self.device)
-        self.hdev.copy_(self.hrec, non_blocking=True)
-        rows = self.hdev[idx]                                    # [M, 64]
+        rows = self.hrec[torch.as_tensor(trunc)].to(self.device, non_blocking=True)      # [M, 64]
         M = len(trunc)
         scal = torch.zeros((M, 16), dtype=torch.bfloat16, device=self.device)
         self._features(rows[:, C_TOBS:C_TOBS + 15].contiguous(), scal)
         img = None
         if self.cfg.vision:
-            pose = rows[:, C_TREC:C_TREC + 6].contiguous()
-            img = self.camera.render(pose)
-        out = forward_gpu(self.net, self.ws_roll, scal, img, B=M)
+            img = self.camera.render(rows[:, C_TREC:C_TREC + 6].contiguous())
+        out = forward_gpu(self.net, self.ws_grp[g], scal, img, B=M)
         self.reward.boot.index_copy_(0, idx, self.cfg.gamma * out[:, self.layout.value_col])
 
     def rollout_gpu(self) -> None:
-        from ..ops import _lib
-        T = self.T
+        """Env groups alternate with the GPU: while the host steps group g's
+        envs, the GPU works on the other group's decision."""
+        T, G = self.T, len(self.groups)
         tm = self.timer
         if self.cfg.graphs and not self.rew_graphs:
             self._capture()
+        for g in range(G):
+            self._run_group(g, 0)
         for t in range(T):
-            ev = tm.gpu_start("rollout_gpu")
-            if self.cfg.graphs:
-                self.rew_graphs[t].replay()
-                _lib.add_launches(self.graph_launches[t])
-            else:
-                self._decision_body(t)
-            tm.gpu_end(ev)
-            self.act_event.record()
-            t0 = tm.now()
-            self.act_event.synchronize()
-            tm.add("wait_gpu", t0)
-            t0 = tm.now()
-            self._env_step()
-            tm.add("env", t0)
+            for g in range(G):
+                t0 = tm.now()
+                self.grp_events[g].synchronize()
+                tm.add("wait_gpu", t0)
+                t0 = tm.now()
+                self._env_step_group(g)
+                tm.add("env", t0)
+                if self.cfg.ep_ticks:
+                    self._bootstrap_truncations(g)
+                self._run_group(g, t + 1)
             self._observe_respawn(t)
-            if self.cfg.ep_ticks and (self.hrec[:, C_REC + 12] != 0).any():
-                self._bootstrap_truncations()
             self.global_step += self.N * self.K * self.world
-        if self.cfg.graphs:
-            self.tail_graph.replay()
-            _lib.add_launches(self.tail_launches)
-        else:
-            self._tail_body()
 
     # ---- GPU update ---------------------------------------------------------------------------
     def _epoch_body(self) -> None:
@@ -493,6 +533,8 @@ class Trainer:
                 boot = np.zeros(self.N, np.float32)
                 boot[trunc] = self.cfg.gamma * v.numpy()
             r, d, self._stall = self.reward(h[:, C_REC:C_REC + REC_COLS].copy(), boot)
+            if self.rnd is not None:
+                r = r + self.cfg.rnd_coef * self.rnd.bonus(torch.from_numpy(h[:, C_OBS:C_OBS + 15].copy())).numpy()
             self.b_rew[t].copy_(torch.from_numpy(r))
             self.b_done[t].copy_(torch.from_numpy(d))
             self.global_step += self.N * self.K * self.world
@@ -543,12 +585,17 @@ class Trainer:
             self.reset()
             self._env_ready = True
         self.iteration += 1
+        self.reward.set_step(self.global_step)
         t0 = tm.now()
         if self.gpu:
             self.rollout_gpu()
         else:
             self.rollout_cpu()
         tm.add("rollout", t0)
+        if self.rnd is not None:
+            t0 = tm.now()
+            self._train_rnd()
+            tm.add("rnd", t0)
         t0 = tm.now()
         self._refresh_respawn_pool()
         tm.add("respawn", t0)
@@ -581,7 +628,6 @@ class Trainer:
         if self.gpu:
             torch.cuda.synchronize()
             self.rew_graphs = []
-            self.tail_graph = None
             self.upd_graph = None
             import gc
             gc.collect()
@@ -594,9 +640,11 @@ class Trainer:
             c = self.reward.counts
             counts = (c.cpu().numpy() if torch.is_tensor(c) else c).astype(np.uint32)
         opt = self.opt.state_dict()
+        policy = self.net.state_dict()
         if self.comm is not None and hasattr(self.comm, "full_optimizer_state"):
             opt.update({k: v.cpu() for k, v in self.comm.full_optimizer_state(self.opt).items()})
-        return {"format": "surfb200-ckpt-1", "policy": self.net.state_dict(), "optimizer": opt,
+            policy["flat"] = self.comm.full_params(self.net).detach().cpu()
+        return {"format": "surfb200-ckpt-1", "policy": policy, "optimizer": opt,
                 "global_step": self.global_step, "iteration": self.iteration, "config": self.cfg.to_dict(),
                 "int_counts": counts, "respawn": self.respawn.state_dict() if self.respawn is not None else None}
 

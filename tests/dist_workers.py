@@ -121,6 +121,7 @@ def p2p_collectives(rank: int, world: int, port: int, q) -> None:
         gen = torch.Generator().manual_seed(0)
         net = Net()
         net.numel = n
+        net.fp32_from = 600_000          # weights below: fp32 master sharded, bf16 replicated
         net.flat = torch.randn(n, generator=gen).to(dev)
         net.grad = torch.zeros(n, device=dev)
         net.flat16 = net.flat.to(torch.bfloat16)
@@ -169,13 +170,21 @@ def p2p_collectives(rank: int, world: int, port: int, q) -> None:
                 graph.replay()
             torch.cuda.synchronize()
             comm.check()
-            err = float(((net.flat - p_ref).abs() / (p_ref.abs() + 1e-3)).max())
+            lo, hi = comm.shard_range(n)
+            own = torch.zeros(n, dtype=torch.bool, device=dev)
+            own[lo:hi] = True
+            own[net.fp32_from:] = True               # the fp32 tail is replicated
+            err = float(((net.flat - p_ref).abs() / (p_ref.abs() + 1e-3))[own].max())
             assert err < 1e-4, ("params", step, err)
-            assert torch.equal(net.flat16, net.flat.to(torch.bfloat16)), "bf16 copy out of sync"
+            e16 = float(((net.flat16.float() - p_ref).abs() / (p_ref.abs() + 1e-3)).max())
+            assert e16 < 1e-2, ("bf16 params", step, e16)
+            assert torch.equal(net.flat16[own], net.flat[own].to(torch.bfloat16)), "bf16 copy out of sync"
             assert not net.grad.any(), "gradient not cleared"
             assert int(opt.hyper[5].item()) == step
-        lo, hi = comm.checksum(net)
-        assert lo == hi, ("replicas differ", lo, hi)
+        c_lo, c_hi = comm.checksum(net)
+        assert c_lo == c_hi, ("replicas differ", c_lo, c_hi)
+        full = comm.full_params(net)
+        assert float(((full - p_ref).abs() / (p_ref.abs() + 1e-3)).max()) < 1e-4
         full = comm.full_optimizer_state(opt)
         assert float((full["m"] - m_ref).abs().max()) < 1e-6
 

