@@ -15,6 +15,12 @@ Commands (reference tools they replace in brackets):
   perf-report       medians / IQR of TIMING lines, A/B (tools/perf_report.py)
   gpu-health        HBM copy and bf16 GEMM against the measured peaks
                     (tools/gpu_health.py)
+  render-pov        depth frames along a recorded trajectory, headless
+                    (tools/render_pov.py)
+  sample-traj       synthetic trajectory file (tools/make_sample_traj.py)
+  compare-runs      runs side by side at step marks (tools/compare_runs.py)
+  serve-metrics     JSON metrics API over a runs directory (tools/dashboard.py)
+  bench-env         env step throughput per thread count (tools/bench_env.py)
 
 Train flags mirror the reference's (--envs, --n-steps, --epochs, --lr,
 --gamma, --reward, --int-coef, ...): every ``TrainConfig`` field is a flag.
@@ -289,6 +295,41 @@ def cmd_gpu_health(args) -> int:
     return health_main(args)
 
 
+def cmd_render_pov(args) -> int:
+    from .utils.tools import render_pov
+    n = render_pov(args.traj, args.map, args.out, width=args.width, height=args.height, cell=args.cell,
+                   episode=args.episode, stride=args.stride, pinhole=args.pinhole)
+    print(f"{n} frames -> {args.out}")
+    return 0
+
+
+def cmd_sample_traj(args) -> int:
+    from .utils.tools import sample_trajectory
+    print(sample_trajectory(args.out))
+    return 0
+
+
+def cmd_compare_runs(args) -> int:
+    from .utils.tools import compare_runs
+    marks = tuple(float(x) for x in args.marks.split(","))
+    print(compare_runs(args.runs, marks, args.col))
+    return 0
+
+
+def cmd_serve_metrics(args) -> int:
+    from .utils.tools import serve_metrics
+    print(f"serving {args.runs_dir} on http://{args.host}:{args.port}/api/runs", flush=True)
+    serve_metrics(args.runs_dir, args.host, args.port)
+    return 0
+
+
+def cmd_bench_env(args) -> int:
+    from .utils.tools import env_thread_sweep
+    for r in env_thread_sweep(args.map, args.envs, args.k, args.reps):
+        print(json.dumps(r))
+    return 0
+
+
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="surfb200", description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -324,6 +365,31 @@ def build_parser() -> argparse.ArgumentParser:
     pr.add_argument("logs", nargs="+")
     pr.add_argument("--last", type=int, default=30)
     pr.add_argument("--vs", default=None, help="a second log to compare against")
+    rp = sub.add_parser("render-pov", help="depth frames (PGM + npy) along a recorded trajectory")
+    rp.add_argument("--traj", required=True)
+    rp.add_argument("--map", required=True, help="a .bsp path or a procedural kind")
+    rp.add_argument("--out", required=True)
+    rp.add_argument("--width", type=int, default=128)
+    rp.add_argument("--height", type=int, default=64)
+    rp.add_argument("--cell", type=float, default=16.0)
+    rp.add_argument("--episode", type=int, default=0)
+    rp.add_argument("--stride", type=int, default=3)
+    rp.add_argument("--pinhole", action="store_true")
+    st = sub.add_parser("sample-traj", help="write a synthetic trajectory file")
+    st.add_argument("--out", required=True)
+    cr = sub.add_parser("compare-runs", help="runs side by side at step marks")
+    cr.add_argument("runs", nargs="+")
+    cr.add_argument("--marks", default="250e6,500e6,1e9")
+    cr.add_argument("--col", default="rew", choices=["rew", "len", "spd", "track", "fin"])
+    sm = sub.add_parser("serve-metrics", help="JSON metrics API over a runs directory")
+    sm.add_argument("runs_dir")
+    sm.add_argument("--host", default="127.0.0.1")
+    sm.add_argument("--port", type=int, default=8008)
+    be = sub.add_parser("bench-env", help="env ticks/s per worker thread count")
+    be.add_argument("--map", default="field")
+    be.add_argument("--envs", type=int, default=2048)
+    be.add_argument("--k", type=int, default=3)
+    be.add_argument("--reps", type=int, default=20)
     gh = sub.add_parser("gpu-health", help="HBM and bf16 GEMM health check")
     gh.add_argument("--seconds", type=float, default=2.0)
     gh.add_argument("--peaks", default=None)
@@ -334,7 +400,8 @@ def main(argv=None) -> int:
     args = build_parser().parse_args(argv)
     fn = {"train": cmd_train, "eval": cmd_eval, "mapgen": cmd_mapgen, "bake": cmd_bake,
           "export-map": cmd_export_map, "export-goalfield": cmd_export_goalfield, "perf-report": cmd_perf_report,
-          "gpu-health": cmd_gpu_health}[args.cmd]
+          "gpu-health": cmd_gpu_health, "render-pov": cmd_render_pov, "sample-traj": cmd_sample_traj,
+          "compare-runs": cmd_compare_runs, "serve-metrics": cmd_serve_metrics, "bench-env": cmd_bench_env}[args.cmd]
     return int(fn(args) or 0)
 
 

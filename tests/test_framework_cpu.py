@@ -282,3 +282,35 @@ def test_trainer_cpu_with_rnd_and_blend():
     for _ in range(2):
         s = tr.train_iteration()
     assert np.isfinite(s["policy_loss"])
+
+
+def test_operator_tools(tmp_path):
+    import threading
+    import urllib.request
+    from surfb200.trainer.evaluate import read_trajectory
+    from surfb200.utils import tools
+    from surfb200.utils.runlog import RunLogger
+    p = tools.sample_trajectory(tmp_path / "s.traj.jsonl", episodes=2, ticks=50)
+    eps = read_trajectory(p)
+    assert len(eps) == 2 and eps[1]["ticks"].shape == (50, 15) and eps[0]["trailer"]["end"] == "done"
+    for name, k in (("a", 1.0), ("b", 2.0)):
+        log = RunLogger(tmp_path / "runs" / name, {"x": 1})
+        for i in range(10):
+            log.log({"global_step": (i + 1) * 1e6, "ep_rew_mean": k * i, "iteration": i})
+    table = tools.compare_runs([tmp_path / "runs" / "a", tmp_path / "runs" / "b"], marks=(5e6,))
+    assert "a" in table and "b" in table
+    srv = tools.serve_metrics(tmp_path / "runs", port=0, once=True)
+    th = threading.Thread(target=srv.handle_request, daemon=True)
+    th.start()
+    port = srv.server_address[1]
+    runs = json.loads(urllib.request.urlopen(f"http://127.0.0.1:{port}/api/runs", timeout=10).read())
+    assert [r["run"] for r in runs] == ["a", "b"]
+    th.join(5)
+    th = threading.Thread(target=srv.handle_request, daemon=True)
+    th.start()
+    m = json.loads(urllib.request.urlopen(f"http://127.0.0.1:{port}/api/metrics?run=b", timeout=10).read())
+    assert len(m["rows"]) == 10
+    th.join(5)
+    srv.server_close()
+    sweep = tools.env_thread_sweep("ramps", envs=64, k=3, reps=2, threads=[1, 2])
+    assert len(sweep) == 2 and all(r["ticks_per_s"] > 0 for r in sweep)
