@@ -26,10 +26,12 @@ def main():
     ap.add_argument("--rows", type=int, default=32768)
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--json", default=None)
+    ap.add_argument("--explicit", action="store_true", help="im2col + GEMM for every convolution (A/B baseline)")
     args = ap.parse_args()
     import torch
     import surfb200  # noqa: F401
     from surfb200.models.policy import HeadLayout, NetConfig, PolicyNet, Workspace, backward_gpu, forward_gpu
+    from surfb200.ops import conv as CV
     from surfb200.ops import gemm as G
     from surfb200.ops import rl as R
 
@@ -37,6 +39,7 @@ def main():
     layout = HeadLayout(("yaw", "pitch", "fwd", "side", "jump", "duck"), False)
     net = PolicyNet(NetConfig(vision=True, img_h=64, img_w=128, n_scalar=10, scalar_pad=16, heads=layout), dev)
     B = args.rows
+    net.implicit_conv = not args.explicit
     ws = Workspace(net, B)
     opt = R.Adam(net)
     heads = R.HeadArgs(layout, dev)
@@ -83,6 +86,9 @@ def main():
         wrap(G, n)
     for n in ("ppo_loss",):
         wrap(R, n)
+    for n in ("conv_forward", "conv_weight_grad", "conv_input_grad", "weight_classes"):
+        wrap(CV, n)
+
 
     def step():
         out = forward_gpu(net, ws, scal, img)

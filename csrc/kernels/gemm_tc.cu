@@ -66,6 +66,53 @@ struct Epilogue {
   int dbg;            // diagnostics: bit 0 skip epilogue stores, bit 1 skip MMAs (timing studies only)
 };
 
+// Implicit-GEMM convolution operands. An operand with mode != 0 is read
+// through a 4-D tensor map over an NHWC activation (dims C, W, H, B; the map's
+// element strides implement the convolution stride) instead of a 2-D matrix:
+//   mode 1 (K-major, forward / input-gradient A): the 128 rows of an M tile
+//          are a tw x th x tb box of output-grid positions; k-block kb is
+//          tap kb / per_tap (kh = tap / kw_n, kw = tap % kw_n), channel
+//          chunk kb % per_tap; the box starts at
+//          (chunk * 64, w0 * sw + sign * kw, h0 * sh + sign * kh, b0);
+//   mode 2 (MN-major, weight-gradient operands): the 64 rows of a k-block are
+//          a tw x th x tb box of output positions (k-block = position tile),
+//          the MN coordinate picks the channels: for A the output channel
+//          chunk (m0), for B the tap of each 64-wide n sub-block.
+// Out-of-range coordinates (negative ones included) load zeros, which is
+// what makes the padded tile edges and the transposed-convolution halo free.
+struct Geo {
+  int mode;
+  int tw, th, tb;          // box extent in output-grid units (tw * th * tb = rows of the tile)
+  int tiles_w, tiles_h;    // tiles along w / h of the output grid
+  int sw, sh;              // input coordinate per output unit (the conv stride)
+  int kw_n;                // taps along w
+  int sign;                // +1: input = output * stride + tap; -1: input = output - tap
+  int per_tap;             // 64-channel chunks per tap (mode 1)
+};
+// Convolution-grid output: row r of an M tile is position (b, h, w) of the
+// same box decomposition as geometry A; it is stored at
+// ((b * out_h + h * ys + yo) * out_w + w * xs + xo) * ldc when h < gh, w < gw
+// and b < gb (the input-gradient parity classes use ys = xs = 2).
+// With cls_cols > 0 the N columns are (ys * xs) parity classes of cls_cols
+// channels each: class (py, px) = column / cls_cols goes to input position
+// (h * ys + py, w * xs + px) — the whole stride-s input gradient in one GEMM,
+// whose A operand (the output gradient) is the same for every class.
+struct OutGeo {
+  int on;
+  int gw, gh, gb;
+  int out_w, out_h, ys, xs, yo, xo;
+  int cls_cols;
+};
+struct ConvCfg { Geo a, b; OutGeo o; };
+
+__device__ __forceinline__ void tile_origin(const Geo& g, int t, int* b0, int* h0, int* w0) {
+  const int wt = t % g.tiles_w;
+  const int r = t / g.tiles_w;
+  *w0 = wt * g.tw;
+  *h0 = (r % g.tiles_h) * g.th;
+  *b0 = (r / g.tiles_h) * g.tb;
+}
+
 // ---- PTX wrappers --------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
@@ -117,6 +164,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c, int w, int h, int b,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c), "r"(w), "r"(h), "r"(b), "r"(bar)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor (sm100 UMMA): start, LBO, SBO (>> 4),
 // descriptor version 1, 128-byte swizzle (layout type 2).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -141,18 +196,6 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   uint32_t r[32];
@@ -190,7 +233,8 @@ __device__ __forceinline__ float tanh_fast(float x) {
 // row. The activation is chosen once per chunk (act_split is a multiple of
 // 32), bias and the saved activation are loaded with vector loads, and each
 // activation has its own tight loop.
-__device__ __forceinline__ void process_chunk32(const Epilogue& ep, float* v, int row, bool row_ok, int col0, int N) {
+__device__ __forceinline__ void process_chunk32(const Epilogue& ep, float* v, int64_t row, bool row_ok, int col0,
+                                                int N) {
   const bool full = col0 + 32 <= N;
   if (ep.bias) {
     if (full) {
@@ -292,7 +336,8 @@ struct Sched {             // static persistent schedule over (m block, n block,
 
 // Register-path stores of a processed 32-column chunk (transposed output,
 // fp32 atomics, or rows that TMA cannot address).
-__device__ __forceinline__ void store_chunk32(const Epilogue& ep, const float* v, int row, bool row_ok, int col0, int N) {
+__device__ __forceinline__ void store_chunk32(const Epilogue& ep, const float* v, int64_t row, bool row_ok, int col0,
+                                              int N) {
   if (!row_ok) return;
   const int ncol = min(32, N - col0);
   if (ep.ct) {
@@ -336,7 +381,8 @@ __device__ __forceinline__ void store_chunk32(const Epilogue& ep, const float* v
 template <int BN, bool A_MN, bool B_MN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                const __grid_constant__ CUtensorMap tma_c, int use_tma_c, int M, int N, Sched sc, Epilogue ep) {
+                const __grid_constant__ CUtensorMap tma_c, int use_tma_c, int M, int N, Sched sc, Epilogue ep,
+                const ConvCfg cc) {
   using C = Cfg<BN, A_MN, B_MN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -388,14 +434,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_expect_tx(full, C::kStageBytes);
           const uint32_t a_dst = smem_u32(tiles + s * C::kStageBytes);
           const uint32_t b_dst = a_dst + C::kABytes;
-          const int k = (kt0 + i) * BK;
-          if (A_MN) {
+          const int kb = kt0 + i;
+          const int k = kb * BK;
+          if (cc.a.mode == 1) {
+            int b0, h0, w0;
+            tile_origin(cc.a, m0 / BM, &b0, &h0, &w0);
+            const int tap = kb / cc.a.per_tap, ch = (kb - tap * cc.a.per_tap) * 64;
+            const int kh = tap / cc.a.kw_n, kw = tap - kh * cc.a.kw_n;
+            tma_load_4d(a_dst, &tma_a, ch, w0 * cc.a.sw + cc.a.sign * kw, h0 * cc.a.sh + cc.a.sign * kh, b0, full);
+          } else if (cc.a.mode == 2) {
+            int b0, h0, w0;
+            tile_origin(cc.a, kb, &b0, &h0, &w0);
+            tma_load_4d(a_dst, &tma_a, m0, w0, h0, b0, full);
+            tma_load_4d(a_dst + BK * 128, &tma_a, m0 + 64, w0, h0, b0, full);
+          } else if (A_MN) {
             tma_load_2d(a_dst, &tma_a, m0, k, full);
             tma_load_2d(a_dst + BK * 128, &tma_a, m0 + 64, k, full);
           } else {
             tma_load_2d(a_dst, &tma_a, k, m0, full);
           }
-          if (B_MN) {
+          if (cc.b.mode == 2) {
+            int b0, h0, w0;
+            tile_origin(cc.b, kb, &b0, &h0, &w0);
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) {
+              const int tap = n0 / 64 + j;
+              const int kh = tap / cc.b.kw_n, kw = tap - kh * cc.b.kw_n;
+              tma_load_4d(b_dst + j * BK * 128, &tma_b, 0, w0 * cc.b.sw + kw, h0 * cc.b.sh + kh, b0, full);
+            }
+          } else if (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * BK * 128, &tma_b, n0 + 64 * j, k, full);
           } else {
@@ -450,8 +517,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int buf = tc % C::kAcc, use = tc / C::kAcc;
       if (!mbar_wait(smem_u32(&acc_full[buf]), use & 1, ep.err, 3, abort)) break;
       fence_after();
-      const int row = m0 + quad * 32 + lane;
-      const bool row_ok = row < M;
+      int row = m0 + quad * 32 + lane;
+      bool row_ok = row < M;
+      int64_t roff = static_cast<int64_t>(row);         // row index in units of ldc / ld_aux
+      int gpos_b = 0, gpos_h = 0, gpos_w = 0;
+      if (cc.o.on) {
+        int b0, h0, w0;
+        tile_origin(cc.a, m0 / BM, &b0, &h0, &w0);
+        const int r = quad * 32 + lane;
+        const int wi = r % cc.a.tw, hi = (r / cc.a.tw) % cc.a.th, bi = r / (cc.a.tw * cc.a.th);
+        gpos_w = w0 + wi;
+        gpos_h = h0 + hi;
+        gpos_b = b0 + bi;
+        row_ok = gpos_w < cc.o.gw && gpos_h < cc.o.gh && gpos_b < cc.o.gb;
+        roff = (static_cast<int64_t>(gpos_b) * cc.o.out_h + gpos_h * cc.o.ys + cc.o.yo) * cc.o.out_w +
+               gpos_w * cc.o.xs + cc.o.xo;
+      }
       if (ep.dbg & 1) {
         float v[32];
         tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN, v);
@@ -466,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (n0 + c0 >= N) break;
           float v[32];
           tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + c0, v);
-          process_chunk32(ep, v, row, row_ok, n0 + c0, N);
+          process_chunk32(ep, v, roff, row_ok, n0 + c0, N);
           const int sb = stage_ctr & 1;
           if (lane == 0 && stage_ctr >= 2) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
           __syncwarp();
@@ -503,8 +584,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (n0 + c0 >= N) break;
           float v[32];
           tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + c0, v);
-          process_chunk32(ep, v, row, row_ok, n0 + c0, N);
-          store_chunk32(ep, v, row, row_ok, n0 + c0, N);
+          if (cc.o.cls_cols) {
+            const int cls = (n0 + c0) / cc.o.cls_cols;
+            const int col = n0 + c0 - cls * cc.o.cls_cols;
+            const int hh = gpos_h * cc.o.ys + cls / cc.o.xs, ww = gpos_w * cc.o.xs + cls % cc.o.xs;
+            const bool ok = row_ok && hh < cc.o.out_h && ww < cc.o.out_w;
+            const int64_t off = (static_cast<int64_t>(gpos_b) * cc.o.out_h + hh) * cc.o.out_w + ww;
+            process_chunk32(ep, v, off, ok, col, cc.o.cls_cols);
+            store_chunk32(ep, v, off, ok, col, cc.o.cls_cols);
+          } else {
+            process_chunk32(ep, v, roff, row_ok, n0 + c0, N);
+            store_chunk32(ep, v, roff, row_ok, n0 + c0, N);
+          }
         }
       }
       fence_before();
@@ -549,22 +640,58 @@ bool make_map(CUtensorMap* m, const void* base, int64_t inner, int64_t rows, int
   return r == CUDA_SUCCESS;
 }
 
+// A 4-D bf16 NHWC activation view for an implicit-convolution operand.
+struct MapDesc {
+  const void* base;
+  int64_t dims[4];          // C, W, H, B (elements)
+  int64_t strides[3];       // bytes between consecutive W, H, B positions (multiples of 16)
+  int box[4];               // box extent per dimension, in elements (element strides included)
+  int estr[4];              // element (traversal) strides
+};
+
+bool make_map4d(CUtensorMap* m, const MapDesc& d) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(d.base) & 15) || d.box[0] * 2 > 128) return false;
+  cuuint64_t dims[4], strides[3];
+  cuuint32_t box[4], estr[4];
+  for (int i = 0; i < 4; ++i) {
+    dims[i] = static_cast<cuuint64_t>(d.dims[i]);
+    box[i] = static_cast<cuuint32_t>(d.box[i]);
+    estr[i] = static_cast<cuuint32_t>(d.estr[i]);
+    if (d.box[i] < 1 || d.box[i] > 256 || d.estr[i] < 1 || d.estr[i] > 8) return false;
+  }
+  for (int i = 0; i < 3; ++i) {
+    strides[i] = static_cast<cuuint64_t>(d.strides[i]);
+    if (d.strides[i] % 16) return false;
+  }
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(d.base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <int BN, bool A_MN, bool B_MN>
 int launch(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const Epilogue& ep, int splits,
-           cudaStream_t s) {
+           cudaStream_t s, const MapDesc* ad = nullptr, const MapDesc* bd = nullptr, const ConvCfg* conv = nullptr) {
   constexpr int STAGES = BN >= 256 ? 3 : 4;
   using C = Cfg<BN, A_MN, B_MN, STAGES>;
   auto kern = gemm_kernel<BN, A_MN, B_MN, STAGES>;
+  ConvCfg cc;
+  std::memset(&cc, 0, sizeof cc);
+  if (conv) cc = *conv;
   CUtensorMap ta, tb;
-  const bool okA = A_MN ? make_map(&ta, A, M, K, lda, 64, BK) : make_map(&ta, A, K, M, lda, BK, BM);
-  const bool okB = B_MN ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, BN);
+  const bool okA = ad ? make_map4d(&ta, *ad)
+                      : (A_MN ? make_map(&ta, A, M, K, lda, 64, BK) : make_map(&ta, A, K, M, lda, BK, BM));
+  const bool okB = bd ? make_map4d(&tb, *bd)
+                      : (B_MN ? make_map(&tb, B, N, K, ldb, 64, BK) : make_map(&tb, B, K, N, ldb, BK, BN));
   if (!okA || !okB) return static_cast<int>(cudaErrorInvalidValue);
   // TMA-store epilogue for plain stores with 16-byte aligned rows
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof tc);
   const int esize = ep.c_dtype == 1 ? 2 : 4;
-  int use_tma_c = ep.c && ep.c_mode == kStore && !ep.ct && ((reinterpret_cast<uintptr_t>(ep.c) & 15) == 0) &&
-                  ((ep.ldc * esize) % 16 == 0);
+  int use_tma_c = ep.c && ep.c_mode == kStore && !ep.ct && !cc.o.on &&
+                  ((reinterpret_cast<uintptr_t>(ep.c) & 15) == 0) && ((ep.ldc * esize) % 16 == 0);
   if (use_tma_c)
     use_tma_c = make_map(&tc, ep.c, N, M, ep.ldc, 32, 32, ep.c_dtype != 1,
                          ep.c_dtype == 1 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)
@@ -592,17 +719,18 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N,
   sc.group = 8;
   const int64_t ntiles = static_cast<int64_t>(sc.mt) * sc.nt * sc.splits;
   const int grid = static_cast<int>(ntiles < static_cast<int64_t>(sms) * resident ? ntiles : static_cast<int64_t>(sms) * resident);
-  kern<<<grid, kThreads, C::kSmem, s>>>(ta, tb, tc, use_tma_c, M, N, sc, ep);
+  kern<<<grid, kThreads, C::kSmem, s>>>(ta, tb, tc, use_tma_c, M, N, sc, ep, cc);
   SURF_RETURN_LAUNCH();
 }
 
 template <int BN>
 int dispatch_major(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn, int M, int N, int K,
-                   const Epilogue& ep, int splits, cudaStream_t s) {
-  if (a_mn && b_mn) return launch<BN, true, true>(A, lda, B, ldb, M, N, K, ep, splits, s);
-  if (a_mn) return launch<BN, true, false>(A, lda, B, ldb, M, N, K, ep, splits, s);
-  if (b_mn) return launch<BN, false, true>(A, lda, B, ldb, M, N, K, ep, splits, s);
-  return launch<BN, false, false>(A, lda, B, ldb, M, N, K, ep, splits, s);
+                   const Epilogue& ep, int splits, cudaStream_t s, const MapDesc* ad = nullptr,
+                   const MapDesc* bd = nullptr, const ConvCfg* cc = nullptr) {
+  if (a_mn && b_mn) return launch<BN, true, true>(A, lda, B, ldb, M, N, K, ep, splits, s, ad, bd, cc);
+  if (a_mn) return launch<BN, true, false>(A, lda, B, ldb, M, N, K, ep, splits, s, ad, bd, cc);
+  if (b_mn) return launch<BN, false, true>(A, lda, B, ldb, M, N, K, ep, splits, s, ad, bd, cc);
+  return launch<BN, false, false>(A, lda, B, ldb, M, N, K, ep, splits, s, ad, bd, cc);
 }
 
 }  // namespace
@@ -630,3 +758,40 @@ SURF_EXPORT int surf_gemm_bf16(const void* A, int64_t lda, int a_mn, const void*
 }
 
 SURF_EXPORT int surf_gemm_epilogue_size() { return static_cast<int>(sizeof(Epilogue)); }
+
+// Implicit-GEMM convolution: the same kernel with 4-D activation operands.
+// ad / bd (either may be null = a plain 2-D operand with lda / ldb) describe
+// NHWC activation views; cc gives the tile geometry of each operand and of a
+// convolution-grid output (see Geo / OutGeo). M for a mode-1 A is the number
+// of M tiles x 128; K for mode-2 operands is the number of position tiles x 64.
+SURF_EXPORT int surf_gemm_conv(const void* A, int64_t lda, const MapDesc* ad, int a_mn, const void* B, int64_t ldb,
+                               const MapDesc* bd, int b_mn, int M, int N, int K, const Epilogue* ep,
+                               const ConvCfg* cc, int bn, int splits, void* stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if (splits > 1 && ep->c_mode != kAtomic) return static_cast<int>(cudaErrorInvalidValue);
+  if (b_mn && bn < 64) return static_cast<int>(cudaErrorInvalidValue);
+  if ((cc->a.mode == 1 && a_mn) || (cc->a.mode == 2 && !a_mn) || (cc->b.mode == 2 && !b_mn) || cc->b.mode == 1)
+    return static_cast<int>(cudaErrorInvalidValue);
+  if ((cc->a.mode && !ad) || (cc->b.mode && !bd)) return static_cast<int>(cudaErrorInvalidValue);
+  if (cc->a.mode == 1 && cc->a.tw * cc->a.th * cc->a.tb != BM) return static_cast<int>(cudaErrorInvalidValue);
+  if (cc->a.mode == 2 && cc->a.tw * cc->a.th * cc->a.tb != BK) return static_cast<int>(cudaErrorInvalidValue);
+  if (cc->b.mode == 2 && cc->b.tw * cc->b.th * cc->b.tb != BK) return static_cast<int>(cudaErrorInvalidValue);
+  if (cc->o.on && cc->a.mode != 1) return static_cast<int>(cudaErrorInvalidValue);
+  if (cc->o.cls_cols && (cc->o.cls_cols % 32 || N != cc->o.cls_cols * cc->o.ys * cc->o.xs))
+    return static_cast<int>(cudaErrorInvalidValue);
+  if (ep->act_split < N && (ep->act_split & 31)) return static_cast<int>(cudaErrorInvalidValue);
+  auto s = static_cast<cudaStream_t>(stream);
+  switch (bn) {
+    case 32: return dispatch_major<32>(A, lda, a_mn, B, ldb, b_mn, M, N, K, *ep, splits, s, ad, bd, cc);
+    case 64: return dispatch_major<64>(A, lda, a_mn, B, ldb, b_mn, M, N, K, *ep, splits, s, ad, bd, cc);
+    case 128: return dispatch_major<128>(A, lda, a_mn, B, ldb, b_mn, M, N, K, *ep, splits, s, ad, bd, cc);
+    case 256: return dispatch_major<256>(A, lda, a_mn, B, ldb, b_mn, M, N, K, *ep, splits, s, ad, bd, cc);
+    default: return static_cast<int>(cudaErrorInvalidValue);
+  }
+}
+
+SURF_EXPORT int surf_gemm_conv_sizes(int* out) {
+  out[0] = static_cast<int>(sizeof(MapDesc));
+  out[1] = static_cast<int>(sizeof(ConvCfg));
+  return 0;
+}

@@ -194,6 +194,26 @@ __global__ void f32_to_bf16_kernel(const float* x, int64_t ldx, uint16_t* y, int
   }
 }
 
+// out[cls][c][a][b][co] = W[co][py + s*a][px + s*b][c], cls = py * s + px,
+// a, b < k / s: the sub-kernels of the stride-s parity classes, transposed so
+// that the input-gradient GEMM reads them K-major (K = (a, b, co)).
+__global__ void conv_weight_t_kernel(const uint16_t* w, int CO, int C, int k, int s, uint16_t* out) {
+  const int kt = k / s;
+  const int per_cls = C * kt * kt * CO;
+  const int total = s * s * per_cls;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int cls = i / per_cls;
+    int r = i - cls * per_cls;
+    const int c = r / (kt * kt * CO);
+    r -= c * kt * kt * CO;
+    const int a = r / (kt * CO);
+    r -= a * kt * CO;
+    const int b = r / CO, co = r - b * CO;
+    const int kh = cls / s + s * a, kw = cls % s + s * b;
+    out[i] = w[((static_cast<int64_t>(co) * k + kh) * k + kw) * C + c];
+  }
+}
+
 int blocks_for(int64_t work, int threads) {
   const int64_t b = surfk::ceil_div(work, threads);
   return static_cast<int>(b < 1 ? 1 : (b > 148 * 64 ? 148 * 64 : b));
@@ -255,5 +275,15 @@ SURF_EXPORT int surf_gather_rows(const void* src, int64_t src_stride_bytes, cons
 SURF_EXPORT int surf_f32_to_bf16(const float* x, int64_t ldx, void* y, int64_t ldy, int64_t rows, int cols, void* stream) {
   f32_to_bf16_kernel<<<blocks_for(rows * cols, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       x, ldx, static_cast<uint16_t*>(y), ldy, rows, cols);
+  SURF_RETURN_LAUNCH();
+}
+
+// Sub-kernels of the stride-s parity classes for the implicit input gradient
+// (see conv_weight_t_kernel); w: bf16 [CO, k, k, C]; out: bf16 [s*s, C, (k/s)^2 * CO].
+SURF_EXPORT int surf_conv_weight_t(const void* w, int CO, int C, int k, int s, void* out, void* stream) {
+  if (s < 1 || k % s) return static_cast<int>(cudaErrorInvalidValue);
+  const int64_t total = static_cast<int64_t>(s) * s * C * (k / s) * (k / s) * CO;
+  conv_weight_t_kernel<<<blocks_for(total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(w), CO, C, k, s, static_cast<uint16_t*>(out));
   SURF_RETURN_LAUNCH();
 }

@@ -81,7 +81,13 @@ def _digest(compiler: str, srcs: list[str], flags: list[str]) -> str:
         files |= {str(p) for p in d.glob("*.h*")} | {str(p) for p in d.glob("*.cuh")}
     files |= {str(p) for p in (CSRC / "common").glob("*")} if (CSRC / "common").is_dir() else set()
     for f in sorted(files):
-        h.update(f.encode())
+        # repository-relative names: the digest must not depend on where the
+        # checkout lives (the GPU box runs a copy under another path)
+        try:
+            name = str(Path(f).resolve().relative_to(ROOT))
+        except ValueError:
+            name = Path(f).name
+        h.update(name.encode())
         h.update(Path(f).read_bytes())
     return h.hexdigest()
 
@@ -123,7 +129,7 @@ def _compile(name: str, spec, force: bool) -> str:
     if not force and out.exists() and stamp.exists() and stamp.read_text() == dig:
         return f"{name}: up to date"
     LIB.mkdir(parents=True, exist_ok=True)
-    tmp = out.with_name(out.name + ".tmp")
+    tmp = out.with_name(f"{out.name}.{os.getpid()}.tmp")
     cmd[cmd.index(str(out))] = str(tmp)
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:

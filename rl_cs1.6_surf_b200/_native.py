@@ -31,10 +31,19 @@ def load(name: str, build_if_missing: bool = True) -> ctypes.CDLL:
             # wherever the framework runs)
             from . import _build
             if _build.is_stale(name):
-                try:
-                    _build.build(only=[name], verbose=False)
-                except Exception as e:                    # noqa: BLE001
-                    raise NativeLibraryMissing(f"{path} is stale and could not be rebuilt: {e}") from e
+                # one process builds while the others (data-parallel ranks
+                # starting together) wait on the lock, then find it fresh
+                import fcntl
+                LIB_DIR.mkdir(parents=True, exist_ok=True)
+                with open(LIB_DIR / ".build.lock", "w") as lk:
+                    fcntl.flock(lk, fcntl.LOCK_EX)
+                    try:
+                        if _build.is_stale(name):
+                            _build.build(only=[name], verbose=False)
+                    except Exception as e:                    # noqa: BLE001
+                        raise NativeLibraryMissing(f"{path} is stale and could not be rebuilt: {e}") from e
+                    finally:
+                        fcntl.flock(lk, fcntl.LOCK_UN)
         if not path.exists():
             raise NativeLibraryMissing(
                 f"{path} is not built; run `python -c 'import __graft_entry__ as g; g.build()'`")

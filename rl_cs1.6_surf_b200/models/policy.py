@@ -167,6 +167,7 @@ class PolicyNet:
         self.flat = torch.zeros(off, dtype=torch.float32, device=self.device)
         self.grad = torch.zeros(off, dtype=torch.float32, device=self.device)
         self.flat16 = torch.zeros(off, dtype=torch.bfloat16, device=self.device) if self.device.type == "cuda" else None
+        self.implicit_conv = True           # implicit-GEMM convolutions where supported (else im2col + GEMM)
         self.init_weights(seed)
 
     # ---- parameter views ------------------------------------------------------------
@@ -272,14 +273,29 @@ class Workspace:
     def __init__(self, net: "PolicyNet", batch: int):
         cfg, dev, bf = net.cfg, net.device, torch.bfloat16
         self.B = batch
-        self.col, self.y, self.dcol, self.dy = [], [], [], []
+        self.col, self.y, self.dcol, self.dy, self.wt = [], [], [], [], []
+        self.implicit = [False] * len(cfg.conv)
         if cfg.vision:
-            for g in cfg.conv_shapes():
+            from ..ops.conv import SLACK_BYTES, ConvShape
+            shapes = cfg.conv_shapes()
+            for i, g in enumerate(shapes):
                 rows = batch * g["OH"] * g["OW"]
-                self.col.append(torch.empty(rows, g["k"] * g["k"] * g["C"], dtype=bf, device=dev))
-                self.y.append(torch.empty(rows, g["CO"], dtype=bf, device=dev))
-                self.dcol.append(torch.empty(rows, g["k"] * g["k"] * g["C"], dtype=bf, device=dev))
+                sh = ConvShape(batch, g["H"], g["W"], g["C"], g["k"], g["s"], g["CO"])
+                # implicit GEMM (no patch matrix) wherever the input has >= 32
+                # channels; the first layer (one depth channel) keeps im2col
+                imp = i > 0 and net.implicit_conv and sh.supported() and sh.CO == 64 and sh.k % sh.s == 0
+                self.implicit[i] = imp
+                patch = g["k"] * g["k"] * g["C"]
+                self.col.append(None if imp else torch.empty(rows, patch, dtype=bf, device=dev))
+                self.dcol.append(None if (imp or i == 0) else torch.empty(rows, patch, dtype=bf, device=dev))
+                # activations carry slack after the last row: the implicit
+                # convolution reading them may fetch a little past the end
+                yb = torch.empty(rows * g["CO"] + SLACK_BYTES // 2, dtype=bf, device=dev)
+                self.y.append(yb[:rows * g["CO"]].view(rows, g["CO"]))
                 self.dy.append(torch.empty(rows, g["CO"], dtype=bf, device=dev))
+                s_ = g["s"]
+                self.wt.append(torch.empty(s_ * s_, g["C"], (g["k"] // s_) ** 2 * g["CO"], dtype=bf, device=dev)
+                               if imp else None)
             self.h0 = torch.empty(batch, cfg.fc + cfg.proprio, dtype=bf, device=dev)
             self.dh0 = torch.empty_like(self.h0)
             self.h = [torch.empty(batch, cfg.hidden, dtype=bf, device=dev)]
@@ -312,11 +328,16 @@ def forward_gpu(net: "PolicyNet", ws: Workspace, scal16: torch.Tensor, img16: Op
     B = ws.B if B is None else B
     w = net.w16
     if cfg.vision:
+        from ..ops import conv as CV
         x = img16
         for i, g in enumerate(cfg.conv_shapes()):
             rows = B * g["OH"] * g["OW"]
-            col = G.im2col(x, B, g["H"], g["W"], g["C"], g["k"], g["s"], out=ws.col[i][:rows])
-            G.gemm(col, w(f"conv{i + 1}.w"), out=ws.y[i][:rows], bias=net.p(f"conv{i + 1}.b"), act="relu")
+            if ws.implicit[i]:
+                sh = CV.ConvShape(B, g["H"], g["W"], g["C"], g["k"], g["s"], g["CO"])
+                CV.conv_forward(x, sh, w(f"conv{i + 1}.w"), net.p(f"conv{i + 1}.b"), ws.y[i][:rows])
+            else:
+                col = G.im2col(x, B, g["H"], g["W"], g["C"], g["k"], g["s"], out=ws.col[i][:rows])
+                G.gemm(col, w(f"conv{i + 1}.w"), out=ws.y[i][:rows], bias=net.p(f"conv{i + 1}.b"), act="relu")
             x = ws.y[i][:rows]
         feat = ws.y[-1][:B * cfg.conv_shapes()[-1]["OH"] * cfg.conv_shapes()[-1]["OW"]].view(B, cfg.flat_conv)
         G.gemm(feat, w("fc.w"), out=ws.h0[:B, :cfg.fc], bias=net.p("fc.b"), act="relu")
@@ -360,18 +381,27 @@ def backward_gpu(net: "PolicyNet", ws: Workspace, scal16: torch.Tensor, B: Optio
         G.colsum(df, net.g("fc.b"))
         dfeat = ws.dy[-1][:last_rows].view(B, cfg.flat_conv)
         G.gemm(df, w("fc.w"), b_mn=True, out=dfeat, act="relu_grad", aux=feat)
+        from ..ops import conv as CV
         for i in range(len(shapes) - 1, -1, -1):
             g = shapes[i]
             rows = B * g["OH"] * g["OW"]
             dy = ws.dy[i][:rows]
-            _wgrad(G, dy, ws.col[i][:rows], net.g(f"conv{i + 1}.w"), rows)
+            prev_rows = B * g["H"] * g["W"]
+            if ws.implicit[i]:
+                sh = CV.ConvShape(B, g["H"], g["W"], g["C"], g["k"], g["s"], g["CO"])
+                CV.conv_weight_grad(dy, ws.y[i - 1], sh, net.g(f"conv{i + 1}.w"))
+            else:
+                _wgrad(G, dy, ws.col[i][:rows], net.g(f"conv{i + 1}.w"), rows)
             G.colsum(dy, net.g(f"conv{i + 1}.b"))
             if i == 0:
                 break
-            G.gemm(dy, w(f"conv{i + 1}.w"), b_mn=True, out=ws.dcol[i][:rows])
-            prev = shapes[i - 1]
-            G.col2im(ws.dcol[i][:rows], ws.y[i - 1][:B * prev["OH"] * prev["OW"]], B, g["H"], g["W"], g["C"], g["k"],
-                     g["s"], out=ws.dy[i - 1][:B * prev["OH"] * prev["OW"]].view(B, g["H"], g["W"], g["C"]))
+            if ws.implicit[i]:
+                CV.weight_classes(w(f"conv{i + 1}.w"), sh, out=ws.wt[i])
+                CV.conv_input_grad(dy, sh, ws.wt[i], ws.dy[i - 1][:prev_rows], ws.y[i - 1][:prev_rows])
+            else:
+                G.gemm(dy, w(f"conv{i + 1}.w"), b_mn=True, out=ws.dcol[i][:rows])
+                G.col2im(ws.dcol[i][:rows], ws.y[i - 1][:prev_rows], B, g["H"], g["W"], g["C"], g["k"], g["s"],
+                         out=ws.dy[i - 1][:prev_rows].view(B, g["H"], g["W"], g["C"]))
     else:
         for i in range(len(cfg.mlp) - 1, -1, -1):
             dh = ws.dh[i][:B]
