@@ -1,7 +1,8 @@
 """Small, self-contained launches of each hot kernel, for ncu captures.
 
-    python bench/profile_kernels.py --only march|conv1_fwd|conv2_dgrad|fc_wgrad|col2im|im2col|sample|gae|
-                                           ppo_loss|reward|adam|p2p1|edt|geodesic [--reps 2]
+    python bench/profile_kernels.py --only march|conv1_fwd|conv2_dgrad|fc_wgrad|col2im|im2col|conv2_ifwd|
+                                           conv2_iwgrad|conv2_idgrad|conv3_ifwd|conv3_idgrad|sample|gae|
+                                           ppo_loss|reward|adam|p2p1|edt|geodesic|surfnz|framestack [--reps 2]
 
 Each case builds its inputs (a few GB on the device at most, larger than L2
 where the kernel streams memory), warms up once, then launches the kernel
@@ -107,6 +108,39 @@ def main():
             fn = lambda: G.im2col(x, B, g["H"], g["W"], g["C"], g["k"], g["s"], out=col)
             info["bytes"] = 2.0 * (rows * g["k"] ** 2 * g["C"] + B * g["H"] * g["W"] * g["C"])
         info["ms"] = _time(fn, args.reps)
+    elif k in ("conv2_ifwd", "conv2_iwgrad", "conv2_idgrad", "conv3_ifwd", "conv3_idgrad"):
+        # implicit-GEMM convolutions (4-D TMA boxes over the NHWC activations),
+        # 4,096 images as above
+        from surfb200.ops import conv as CV
+        layout = HeadLayout(("yaw", "pitch", "fwd", "side", "jump", "duck"), False)
+        net = PolicyNet(NetConfig(heads=layout), dev)
+        B = 4096
+        li = 1 if k.startswith("conv2") else 2
+        g = net.cfg.conv_shapes()[li]
+        sh = CV.ConvShape(B, g["H"], g["W"], g["C"], g["k"], g["s"], g["CO"])
+        rows_in, rows = B * g["H"] * g["W"], B * g["OH"] * g["OW"]
+        rnd = lambda *shape: (torch.randn(*shape, device=dev, generator=gen) * 0.1).to(torch.bfloat16)
+        slack = CV.SLACK_BYTES // 2
+        xb = torch.relu(rnd(rows_in * g["C"] + slack).float()).to(torch.bfloat16)
+        x = xb[:rows_in * g["C"]].view(rows_in, g["C"])
+        w = net.w16(f"conv{li + 1}.w")
+        flops = 2.0 * rows * g["CO"] * g["k"] ** 2 * g["C"]
+        if k.endswith("ifwd"):
+            y = torch.empty(rows, g["CO"], dtype=torch.bfloat16, device=dev)
+            fn = lambda: CV.conv_forward(x, sh, w, net.p(f"conv{li + 1}.b"), y)
+        elif k.endswith("iwgrad"):
+            dy = rnd(rows, g["CO"])
+            gw = torch.zeros(g["CO"], g["k"] ** 2 * g["C"], device=dev)
+            fn = lambda: CV.conv_weight_grad(dy, x, sh, gw)
+        else:
+            dyb = rnd(rows * g["CO"] + slack)
+            dy = dyb[:rows * g["CO"]].view(rows, g["CO"])
+            wt = CV.weight_classes(w, sh)
+            dx = torch.empty(rows_in, g["C"], dtype=torch.bfloat16, device=dev)
+            fn = lambda: CV.conv_input_grad(dy, sh, wt, dx, x)
+        info["flops"] = flops
+        info["ms"] = _time(fn, args.reps)
+        info["tflops"] = flops / (info["ms"] * 1e-3) / 1e12
     elif k in ("sample", "ppo_loss", "gae"):
         layout = HeadLayout(("yaw", "pitch", "fwd", "side", "jump", "duck"), False)
         heads = R.HeadArgs(layout, dev)
@@ -176,6 +210,29 @@ def main():
         occ = (torch.rand(256, 512, 512, device=dev, generator=gen) > 0.999).to(torch.uint8)
         info["ms"] = _time(lambda: vision.distance_field(occ, 16.0), args.reps)
         info["voxels"] = occ.numel()
+    elif k == "framestack":
+        # the update's minibatch gather of 4-frame stacks: 16,384 rows of 4 x 8,192 bf16
+        from surfb200.ops.framestack import FrameStacker
+        st = FrameStacker(4, 128 * 64)
+        T, N, mb = 32, 2048, 16384
+        frames = (torch.randn(st.pro + T + 1, N, st.fr, device=dev, generator=gen)).to(torch.bfloat16)
+        ages = torch.randint(0, st.pro + 1, (T * N,), dtype=torch.int32, device=dev, generator=gen)
+        idx = torch.randperm(T * N, device=dev, generator=gen)[:mb]
+        out = torch.empty(mb, st.width, dtype=torch.bfloat16, device=dev)
+        info["ms"] = _time(lambda: st.gather(frames, idx, ages, out), args.reps)
+        info["bytes"] = 2.0 * 2 * mb * st.width
+    elif k == "surfnz":
+        from surfb200.ops import surfmask, vision
+        from surfb200.sim import mapgen
+        from surfb200.sim.core import SimCore, default_config
+        m = mapgen.generate("field", 0)
+        core = SimCore.from_bytes(m.image, default_config(1), threads=4)
+        tris = surfmask.solid_triangles(core)
+        mn, mx = core.map_bounds()
+        mins, nx, ny, nz = vision.grid_dims(mn, mx, 16.0)
+        info["ms"] = _time(lambda: surfmask.bake(tris, mins, 16.0, (nx, ny, nz), core=core, linear=False), 1)
+        info["triangles"] = len(tris)
+        info["voxels"] = nx * ny * nz
     elif k == "geodesic":
         from surfb200.ops.geodesic import geodesic
         occ = torch.zeros(128, 256, 256, dtype=torch.uint8, device=dev)

@@ -7,6 +7,8 @@
 //     with the ReLU derivative of the layer below;
 //   * colsum: bias gradients (sum of dY over rows), fp32 accumulation;
 //   * gather_rows: minibatch rows of the rollout buffers (any element size);
+//   * frame_stack: the policy input of a decision from the frames of earlier
+//     decisions (rollout, truncation bootstrap and minibatch gather);
 //   * cast kernels between fp32 and bf16.
 #include <cstdint>
 
@@ -219,6 +221,113 @@ int blocks_for(int64_t work, int threads) {
   return static_cast<int>(b < 1 ? 1 : (b > 148 * 64 ? 148 * 64 : b));
 }
 
+// Frame stacking (reference: python/train_fast.py:177-293, FrameRing and
+// stack_from_buffer): decision t of env n sees its current frame and the
+// frames of the decisions offs[1..K-1] before it, each reach-back clamped to
+// the episode's age (the number of earlier decisions in the episode, capped at
+// the deepest offset), so at a spawn every slot shows the spawn frame. Frames
+// live slot-major in one buffer: frames[slot][env][ld], slot = pro + t in the
+// trainer's rollout buffer (slots 0..pro-1 carry the previous rollout's last
+// frames), or a ring of `ring` slots. The output row interleaves pixel-major:
+// out[px][j][c] = frame_j[px][c] (frame index outer to the frame's own
+// channels), the NHWC input of the first convolution.
+struct StackArgs {
+  const uint16_t* frames;   // bf16, slot 0
+  int64_t slot_stride;      // elements between slots
+  int ld;                   // elements between env rows of a slot
+  int fr;                   // elements per frame (P * C0), multiple of 8
+  int pro;                  // deepest offset (age cap)
+  int ring;                 // > 0: slots are taken modulo ring
+  int offs[8];              // offsets, newest (0) first
+  int mode;                 // 0 rollout decision, 1 terminal (bootstrap), 2 minibatch gather
+  int N;                    // envs per slot
+  int lo;                   // mode 0: first env of the rows
+  int slot0;                // modes 0/1: slot of the decision (mode 1: one past the newest stored)
+  const float* done;        // mode 0: episode-ended flags of the previous decision, per row (NULL: keep ages)
+  int* age_cur;             // modes 0/1: [N] running age
+  int* age_rec;             // mode 0: ages recorded per row; mode 2: ages per flat sample (read)
+  const int64_t* idx;       // mode 1: env per row; mode 2: flat sample t * N + n per row
+  const uint16_t* cur;      // mode 1: the terminal frames, row r at cur + r * cur_ld
+  int64_t cur_ld;
+  uint16_t* out;
+  int64_t out_ld;
+};
+
+template <int K, int C0>
+__global__ void __launch_bounds__(256) frame_stack_kernel(StackArgs a) {
+  __shared__ int s_age, s_env, s_slot;
+  const int r = blockIdx.x;
+  if (threadIdx.x == 0) {
+    int n, age, slot;
+    if (a.mode == 0) {
+      n = a.lo + r;
+      age = a.age_cur[n];
+      if (a.done) age = a.done[r] != 0.0f ? 0 : min(age + 1, a.pro);
+      a.age_cur[n] = age;
+      a.age_rec[r] = age;
+      slot = a.slot0;
+    } else if (a.mode == 1) {
+      n = static_cast<int>(a.idx[r]);
+      age = min(a.age_cur[n] + 1, a.pro);
+      slot = a.slot0;
+    } else {
+      const int64_t i = a.idx[r];
+      n = static_cast<int>(i % a.N);
+      age = a.age_rec[i];
+      slot = a.pro + static_cast<int>(i / a.N);
+    }
+    s_age = age;
+    s_env = n;
+    s_slot = slot;
+  }
+  __syncthreads();
+  const int age = s_age, n = s_env, slot0 = s_slot;
+  const uint4* src[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    const int back = min(age, a.offs[j]);
+    if (back == 0 && a.mode == 1) {
+      src[j] = reinterpret_cast<const uint4*>(a.cur + r * a.cur_ld);
+    } else {
+      int sl = slot0 - back;
+      if (a.ring > 0) sl = ((sl % a.ring) + a.ring) % a.ring;
+      src[j] = reinterpret_cast<const uint4*>(a.frames + sl * a.slot_stride + static_cast<int64_t>(n) * a.ld);
+    }
+  }
+  uint4* dst = reinterpret_cast<uint4*>(a.out + r * a.out_ld);
+  const int chunks = a.fr / 8;
+  for (int q = threadIdx.x; q < chunks; q += blockDim.x) {
+    uint16_t in[K][8];
+#pragma unroll
+    for (int j = 0; j < K; ++j) *reinterpret_cast<uint4*>(in[j]) = __ldg(src[j] + q);
+    // 8 frame elements = 8 / C0 pixels; their K frames form K output chunks
+#pragma unroll
+    for (int o8 = 0; o8 < K; ++o8) {
+      uint16_t ov[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int o = o8 * 8 + e;
+        const int px = o / (K * C0), j = (o / C0) % K, c = o % C0;
+        ov[e] = in[j][px * C0 + c];
+      }
+      dst[q * K + o8] = *reinterpret_cast<const uint4*>(ov);
+    }
+  }
+}
+
+template <int C0>
+int launch_stack(const StackArgs& a, int K, int rows, cudaStream_t s) {
+  switch (K) {
+    case 1: frame_stack_kernel<1, C0><<<rows, 256, 0, s>>>(a); break;
+    case 2: frame_stack_kernel<2, C0><<<rows, 256, 0, s>>>(a); break;
+    case 3: frame_stack_kernel<3, C0><<<rows, 256, 0, s>>>(a); break;
+    case 4: frame_stack_kernel<4, C0><<<rows, 256, 0, s>>>(a); break;
+    case 5: frame_stack_kernel<5, C0><<<rows, 256, 0, s>>>(a); break;
+    default: return static_cast<int>(cudaErrorInvalidValue);
+  }
+  SURF_RETURN_LAUNCH();
+}
+
 }  // namespace
 
 SURF_EXPORT int surf_im2col(const void* x, int B, int H, int W, int C, int KH, int KW, int S, void* col, int64_t ldcol,
@@ -286,4 +395,46 @@ SURF_EXPORT int surf_conv_weight_t(const void* w, int CO, int C, int k, int s, v
   conv_weight_t_kernel<<<blocks_for(total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(w), CO, C, k, s, static_cast<uint16_t*>(out));
   SURF_RETURN_LAUNCH();
+}
+
+// Build `rows` stacked policy inputs (see frame_stack_kernel). offs: K offsets
+// (offs[0] == 0); every pointer row 16-byte aligned, fr % 8 == 0.
+SURF_EXPORT int surf_frame_stack(const void* frames, int64_t slot_stride, int ld, int fr, int C0, int K,
+                                 const int* offs, int pro, int ring, int mode, int N, int lo, int slot0,
+                                 const float* done, int* age_cur, int* age_rec, const int64_t* idx, const void* cur,
+                                 int64_t cur_ld, void* out, int64_t out_ld, int rows, void* stream) {
+  if (K < 1 || K > 5 || (C0 != 1 && C0 != 2) || (fr & 7) || (ld & 7) || (slot_stride & 7) || (out_ld & 7) ||
+      (cur_ld & 7) || mode < 0 || mode > 2 || pro < 0 || rows < 0 || N < 1 ||
+      ((reinterpret_cast<uintptr_t>(frames) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(cur)) &
+       15))
+    return static_cast<int>(cudaErrorInvalidValue);
+  if ((mode == 0 && (!age_cur || !age_rec)) || (mode == 1 && (!age_cur || !idx || !cur)) ||
+      (mode == 2 && (!age_rec || !idx)))
+    return static_cast<int>(cudaErrorInvalidValue);
+  if (rows == 0) return 0;
+  StackArgs a{};
+  a.frames = static_cast<const uint16_t*>(frames);
+  a.slot_stride = slot_stride;
+  a.ld = ld;
+  a.fr = fr;
+  a.pro = pro;
+  a.ring = ring;
+  for (int j = 0; j < K; ++j) {
+    if (offs[j] < 0 || offs[j] > pro) return static_cast<int>(cudaErrorInvalidValue);
+    a.offs[j] = offs[j];
+  }
+  a.mode = mode;
+  a.N = N;
+  a.lo = lo;
+  a.slot0 = slot0;
+  a.done = done;
+  a.age_cur = age_cur;
+  a.age_rec = age_rec;
+  a.idx = idx;
+  a.cur = static_cast<const uint16_t*>(cur);
+  a.cur_ld = cur_ld;
+  a.out = static_cast<uint16_t*>(out);
+  a.out_ld = out_ld;
+  auto s = static_cast<cudaStream_t>(stream);
+  return C0 == 1 ? launch_stack<1>(a, K, rows, s) : launch_stack<2>(a, K, rows, s);
 }

@@ -271,3 +271,156 @@ SURF_EXPORT int surf_edt_noalloc(const uint8_t* occ, int nx, int ny, int nz, flo
   finish_kernel<<<grid_blocks(total, 256), 256, 0, s>>>(out, cell, total, out, nullptr);
   SURF_RETURN_LAUNCH();
 }
+
+// ---------------------------------------------------------------------------
+// Surface slope mask: per voxel, |n_z| * 127 of the solid face the voxel holds
+// (reference: python/surfgym/surfmask.py:112-179, the second lidar channel).
+// Depth alone cannot tell floor (n_z = 1), surf ramp (~0.3-0.7) and wall (0)
+// apart; the march reads this byte at the voxel where it stopped.
+//
+// Claims follow the reference's rules, resolved in one pass with a 64-bit
+// atomicMax instead of two ordered host passes: a triangle claims every voxel
+// of its dilated box whose centre lies within the margin radius
+// 0.5*cell*(|nx|+|ny|+|nz|) + 0.5*cell of its plane, EXACT when also within
+// the tight radius 0.5*cell*(|nx|+|ny|+|nz|). Key = exact (bit 63) | float32
+// bits of twice the area (bits 31..62) | triangle index (bits 7..30) | value
+// (bits 0..6), so an exact claim beats a margin claim, then the larger area
+// wins, then the later triangle (the reference's stable ascending-area write
+// order). The mesh here is the hull-0 solid-leaf polyhedra, which include
+// faces between two solid cells: a triangle whose outward side is solid at
+// all four probe points (centroid and the three centroid-vertex midpoints,
+// 0.25 units out) is inside geometry and claims nothing.
+namespace {
+
+__device__ bool outside_solid(const TreeView& t, int world_head, const SolidEnt* ents, int n_ents, float x, float y,
+                              float z) {
+  const int c = tree_contents(t, world_head, x, y, z);
+  if (c == kSolid || c == kSky) return true;
+  for (int e = 0; e < n_ents; ++e) {
+    const SolidEnt& se = ents[e];
+    if (x < se.lo[0] || x > se.hi[0] || y < se.lo[1] || y > se.hi[1] || z < se.lo[2] || z > se.hi[2]) continue;
+    if (tree_contents(t, se.head, x - se.ox, y - se.oy, z - se.oz) == kSolid) return true;
+  }
+  return false;
+}
+
+__global__ void __launch_bounds__(256) surfnz_claim_kernel(const float* tris, int n_tris, TreeView tv, int world_head,
+                                                           const SolidEnt* ents, int n_ents, double mnx, double mny,
+                                                           double mnz, double cell, int nx, int ny, int nz,
+                                                           unsigned long long* keys) {
+  const int ti = blockIdx.x;
+  if (ti >= n_tris) return;
+  const float* v = tris + 9 * static_cast<int64_t>(ti);
+  const double ax = v[0], ay = v[1], az = v[2], bx = v[3], by = v[4], bz = v[5], cx = v[6], cy = v[7], cz = v[8];
+  const double ux = bx - ax, uy = by - ay, uz = bz - az, wx = cx - ax, wy = cy - ay, wz = cz - az;
+  // explicit round-to-nearest products and sums (no FMA contraction): every
+  // decision below is reproducible bit for bit by a float64 host oracle
+  const double crx = __dsub_rn(__dmul_rn(uy, wz), __dmul_rn(uz, wy));
+  const double cry = __dsub_rn(__dmul_rn(uz, wx), __dmul_rn(ux, wz));
+  const double crz = __dsub_rn(__dmul_rn(ux, wy), __dmul_rn(uy, wx));
+  const double area2 = sqrt(__dadd_rn(__dadd_rn(__dmul_rn(crx, crx), __dmul_rn(cry, cry)), __dmul_rn(crz, crz)));
+  if (!(area2 > 1e-9)) return;                              // degenerate fan triangle
+  const double n0 = crx / area2, n1 = cry / area2, n2 = crz / area2;
+  const unsigned val = static_cast<unsigned>(rint(fabs(n2) * 127.0));
+  const double tight = __dmul_rn(0.5 * cell, fabs(n0) + fabs(n1) + fabs(n2));
+  const double margin = tight + 0.5 * cell;
+  const double pd = __dadd_rn(__dadd_rn(__dmul_rn(n0, ax), __dmul_rn(n1, ay)), __dmul_rn(n2, az));
+  const double lo_v[3] = {fmin(ax, fmin(bx, cx)), fmin(ay, fmin(by, cy)), fmin(az, fmin(bz, cz))};
+  const double hi_v[3] = {fmax(ax, fmax(bx, cx)), fmax(ay, fmax(by, cy)), fmax(az, fmax(bz, cz))};
+  const double mn[3] = {mnx, mny, mnz};
+  const int dim[3] = {nx, ny, nz};
+  int lo[3], span[3];
+  for (int a = 0; a < 3; ++a) {
+    const double l = floor((lo_v[a] - cell - mn[a]) / cell), h = floor((hi_v[a] + cell - mn[a]) / cell) + 1.0;
+    const int li = static_cast<int>(fmin(fmax(l, 0.0), static_cast<double>(dim[a])));
+    const int hi = static_cast<int>(fmin(fmax(h, 0.0), static_cast<double>(dim[a])));
+    lo[a] = li;
+    span[a] = hi - li;
+    if (span[a] <= 0) return;                               // entirely outside the grid
+  }
+  const unsigned long long base = (static_cast<unsigned long long>(__float_as_uint(static_cast<float>(area2))) << 31) |
+                                  (static_cast<unsigned long long>(ti & 0xFFFFFF) << 7) | val;
+  const int64_t plane = static_cast<int64_t>(span[0]) * span[1];
+  const int64_t total = plane * span[2];
+  if (blockIdx.y * static_cast<int64_t>(blockDim.x) >= total) return;   // no voxels for this slice
+  if (tv.nodes) {                                           // internal face filter
+    const double gx = (ax + bx + cx) / 3.0, gy = (ay + by + cy) / 3.0, gz = (az + bz + cz) / 3.0;
+    bool open = false;
+    for (int s = 0; s < 4 && !open; ++s) {
+      double px = gx, py = gy, pz = gz;
+      if (s > 0) {
+        const float* q = v + 3 * (s - 1);
+        px = 0.5 * (gx + q[0]); py = 0.5 * (gy + q[1]); pz = 0.5 * (gz + q[2]);
+      }
+      open = !outside_solid(tv, world_head, ents, n_ents, static_cast<float>(px + 0.25 * n0),
+                            static_cast<float>(py + 0.25 * n1), static_cast<float>(pz + 0.25 * n2));
+    }
+    if (!open) return;
+  }
+  for (int64_t i = blockIdx.y * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.y) * blockDim.x) {
+    const int x = lo[0] + static_cast<int>(i % span[0]);
+    const int y = lo[1] + static_cast<int>((i / span[0]) % span[1]);
+    const int z = lo[2] + static_cast<int>(i / plane);
+    const double pz = __dmul_rn(__dadd_rn(__dmul_rn(z + 0.5, cell), mnz), n2);
+    const double py = __dmul_rn(__dadd_rn(__dmul_rn(y + 0.5, cell), mny), n1);
+    const double px = __dmul_rn(__dadd_rn(__dmul_rn(x + 0.5, cell), mnx), n0);
+    const double dist = __dsub_rn(__dadd_rn(__dadd_rn(pz, py), px), pd);
+    const double ad = fabs(dist);
+    if (ad > margin) continue;
+    const unsigned long long key = base | (ad <= tight ? (1ull << 63) : 0ull);
+    atomicMax(keys + (static_cast<int64_t>(z) * ny + y) * nx + x, key);
+  }
+}
+
+__global__ void surfnz_finish_kernel(const unsigned long long* keys, int nx, int ny, int nz, surfk::BrickGrid g,
+                                     int8_t* linear, int8_t* bricked) {
+  const int64_t total = static_cast<int64_t>(nx) * ny * nz;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const unsigned long long k = keys[i];
+    const int8_t v = static_cast<int8_t>(k ? (k & 127ull) : 0ull);
+    if (linear) linear[i] = v;
+    if (bricked) {
+      const int ix = static_cast<int>(i % nx), iy = static_cast<int>((i / nx) % ny);
+      const int iz = static_cast<int>(i / (static_cast<int64_t>(nx) * ny));
+      bricked[g.index(ix, iy, iz)] = v;
+    }
+  }
+}
+
+}  // namespace
+
+// Bake the slope mask. tris: n_tris x 9 float32 (three xyz vertices, outward
+// winding). planes4/ptype/nodes3/world_head/ents: the hull-0 tree and solid
+// entities (the occupancy bake's inputs) for the internal-face filter; pass
+// nodes3 = NULL to skip the filter. keys: nx*ny*nz uint64 workspace. Outputs
+// (either may be NULL): linear int8 [nz][ny][nx] and the 4x4x4-bricked int8
+// grid (surf_brick_size(nx, ny, nz) bytes, padding voxels zero).
+SURF_EXPORT int surf_surfnz_bake(const float* tris, int n_tris, const float* planes4, const int* ptype,
+                                 const int* nodes3, int world_head, const void* ents, int n_ents, double mnx,
+                                 double mny, double mnz, double cell, int nx, int ny, int nz, void* keys,
+                                 int8_t* linear, int8_t* bricked, void* stream) {
+  if (n_tris < 0 || n_tris > (1 << 24) || nx < 1 || ny < 1 || nz < 1 || !keys || !(cell > 0.0))
+    return static_cast<int>(cudaErrorInvalidValue);
+  auto s = static_cast<cudaStream_t>(stream);
+  const int64_t total = static_cast<int64_t>(nx) * ny * nz;
+  cudaError_t e = cudaMemsetAsync(keys, 0, static_cast<size_t>(total) * 8, s);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  const surfk::BrickGrid g = surfk::make_brick_grid(nx, ny, nz);
+  if (bricked) {
+    e = cudaMemsetAsync(bricked, 0, static_cast<size_t>(g.size()), s);
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  TreeView tv{reinterpret_cast<const float4*>(planes4), ptype, reinterpret_cast<const int3*>(nodes3)};
+  if (n_tris > 0) {
+    surfnz_claim_kernel<<<dim3(static_cast<unsigned>(n_tris), 8), 256, 0, s>>>(
+        tris, n_tris, tv, world_head, static_cast<const SolidEnt*>(ents), n_ents, mnx, mny, mnz, cell, nx, ny, nz,
+        static_cast<unsigned long long*>(keys));
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  surfnz_finish_kernel<<<grid_blocks(total, 256), 256, 0, s>>>(static_cast<const unsigned long long*>(keys), nx, ny,
+                                                                nz, g, linear, bricked);
+  SURF_RETURN_LAUNCH();
+}

@@ -21,6 +21,13 @@ Commands (reference tools they replace in brackets):
   compare-runs      runs side by side at step marks (tools/compare_runs.py)
   serve-metrics     JSON metrics API over a runs directory (tools/dashboard.py)
   bench-env         env step throughput per thread count (tools/bench_env.py)
+  strafe-audit      air-acceleration capture of recorded episodes
+                    (tools/strafe_audit.py)
+  route-bound       time floors and energy budget of a recorded route
+                    (tools/route_bound.py)
+  tas-search        batched hill climb over one action window of a run
+                    (tools/tas_search.py)
+  tas-chain         window-by-window search of a whole run (tools/tas_chain.py)
 
 Train flags mirror the reference's (--envs, --n-steps, --epochs, --lr,
 --gamma, --reward, --int-coef, ...): every ``TrainConfig`` field is a flag.
@@ -37,6 +44,8 @@ import sys
 import time
 from pathlib import Path
 from typing import Optional, get_args, get_origin
+
+import numpy as np
 
 from .trainer.config import TrainConfig
 from .rewards.spec import RewardSpec
@@ -330,6 +339,81 @@ def cmd_bench_env(args) -> int:
     return 0
 
 
+def _episodes_arg(args):
+    from .utils import tas
+    eps = tas.episodes(args.traj)
+    if not eps:
+        raise SystemExit(f"no episodes in {args.traj}")
+    return eps
+
+
+def cmd_strafe_audit(args) -> int:
+    from .utils import tas
+    eps = _episodes_arg(args)
+    sel = [eps[args.ep - 1]] if args.ep else eps
+    print(json.dumps(tas.strafe_audit_many(sel)))
+    return 0
+
+
+def cmd_route_bound(args) -> int:
+    from .utils import tas
+    eps = _episodes_arg(args)
+    if args.ep is None:
+        for k, e in enumerate(eps, 1):
+            print(json.dumps({"episode": k, "ticks": len(e), "z_drop": float(e[0, 3] - e[:, 3].min()),
+                              "peak_speed": float(np.hypot(e[:, 4], e[:, 5]).max())}))
+        return 0
+    e = eps[args.ep - 1]
+    if args.from_drop:
+        e = tas.from_drop(e)
+    print(json.dumps(tas.route_bound(e, gravity=args.gravity, segments=args.segments, target=args.target)))
+    return 0
+
+
+def _search_env(args):
+    from .sim import mapgen
+    from .sim.core import SimCore, default_config
+    from .sim.zones import load_zones
+    from .utils import tas
+    cfg = default_config(args.envs, max_episode_ticks=1_000_000, sv_maxvelocity=args.maxvel)
+    if args.map in mapgen.MAP_KINDS:
+        m = mapgen.generate(args.map, args.seed)
+        core, zones = SimCore.from_bytes(m.image, cfg, threads=args.threads), m.zones
+    else:
+        core, zones = SimCore(args.map, cfg, threads=args.threads), load_zones(args.map)
+    core.reset(0)
+    return core, tas.make_scorer(core, zones, cell=args.cell)
+
+
+def cmd_tas_search(args) -> int:
+    from .utils import tas
+    e = _episodes_arg(args)[args.ep - 1]
+    core, score = _search_env(args)
+    r = tas.tas_search(core, score, e, args.t0, args.window, args.iters, args.p_mutate, args.seed,
+                       log=lambda m: print(m, flush=True))
+    acts = r.pop("actions")
+    if args.out:
+        np.save(args.out, acts)
+    print(json.dumps(r))
+    core.close()
+    return 0
+
+
+def cmd_tas_chain(args) -> int:
+    from .utils import tas
+    e = _episodes_arg(args)[args.ep - 1]
+    if args.from_drop:
+        e = tas.from_drop(e)
+    core, score = _search_env(args)
+    r = tas.tas_chain(core, score, e, args.window, args.iters, args.p_mutate, args.max_windows, args.seed,
+                      finish_score=getattr(score, "finish", None), log=lambda m: print(m, flush=True))
+    out = Path(args.out) if args.out else Path(args.traj).with_suffix(".chained.npy")
+    np.save(out, r.pop("actions"))
+    print(json.dumps({**r, "actions": str(out)}))
+    core.close()
+    return 0
+
+
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="surfb200", description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -390,6 +474,36 @@ def build_parser() -> argparse.ArgumentParser:
     be.add_argument("--envs", type=int, default=2048)
     be.add_argument("--k", type=int, default=3)
     be.add_argument("--reps", type=int, default=20)
+    sa = sub.add_parser("strafe-audit", help="air-acceleration capture of recorded episodes")
+    sa.add_argument("traj")
+    sa.add_argument("--ep", type=int, default=None, help="1-based episode (default: all)")
+    rb = sub.add_parser("route-bound", help="time floors and energy budget of a recorded route")
+    rb.add_argument("traj")
+    rb.add_argument("--ep", type=int, default=None, help="1-based episode (default: list them)")
+    rb.add_argument("--target", type=float, default=None, help="target time, s")
+    rb.add_argument("--segments", type=int, default=10)
+    rb.add_argument("--gravity", type=float, default=800.0)
+    rb.add_argument("--from-drop", action="store_true", help="start the clock at the opening drop")
+    for name, hlp in (("tas-search", "batched hill climb over one window of a recorded run"),
+                      ("tas-chain", "window-by-window search of a whole recorded run")):
+        ts = sub.add_parser(name, help=hlp)
+        ts.add_argument("traj")
+        ts.add_argument("--map", required=True, help="a .bsp path or a procedural kind")
+        ts.add_argument("--seed", type=int, default=0)
+        ts.add_argument("--ep", type=int, default=1, help="1-based episode")
+        ts.add_argument("--window", type=int, default=300 if name == "tas-search" else 150)
+        ts.add_argument("--iters", type=int, default=40 if name == "tas-search" else 25)
+        ts.add_argument("--envs", type=int, default=2048 if name == "tas-search" else 1024)
+        ts.add_argument("--p-mutate", type=float, default=0.06 if name == "tas-search" else 0.05)
+        ts.add_argument("--cell", type=float, default=32.0, help="goal-field voxel size")
+        ts.add_argument("--maxvel", type=float, default=4000.0)
+        ts.add_argument("--threads", type=int, default=None)
+        ts.add_argument("--out", default=None, help=".npy file for the best action sequence")
+        if name == "tas-search":
+            ts.add_argument("--t0", type=int, default=0, help="tick to branch at")
+        else:
+            ts.add_argument("--max-windows", type=int, default=0, help="0 = the whole run")
+            ts.add_argument("--from-drop", action="store_true", help="start at the opening drop")
     gh = sub.add_parser("gpu-health", help="HBM and bf16 GEMM health check")
     gh.add_argument("--seconds", type=float, default=2.0)
     gh.add_argument("--peaks", default=None)
@@ -401,7 +515,9 @@ def main(argv=None) -> int:
     fn = {"train": cmd_train, "eval": cmd_eval, "mapgen": cmd_mapgen, "bake": cmd_bake,
           "export-map": cmd_export_map, "export-goalfield": cmd_export_goalfield, "perf-report": cmd_perf_report,
           "gpu-health": cmd_gpu_health, "render-pov": cmd_render_pov, "sample-traj": cmd_sample_traj,
-          "compare-runs": cmd_compare_runs, "serve-metrics": cmd_serve_metrics, "bench-env": cmd_bench_env}[args.cmd]
+          "compare-runs": cmd_compare_runs, "serve-metrics": cmd_serve_metrics, "bench-env": cmd_bench_env,
+          "strafe-audit": cmd_strafe_audit, "route-bound": cmd_route_bound, "tas-search": cmd_tas_search,
+          "tas-chain": cmd_tas_chain}[args.cmd]
     return int(fn(args) or 0)
 
 

@@ -74,6 +74,7 @@ class NetConfig:
     vision: bool = True
     img_h: int = 64
     img_w: int = 128
+    img_c: int = 1                  # image channels, fastest (surface mask, stacked frames)
     n_scalar: int = 10              # proprioception features fed to the net
     scalar_pad: int = 16            # columns of the scalar operand (>= n_scalar, multiple of 8)
     conv: tuple = ((8, 4, 32), (4, 2, 64), (3, 1, 64))   # (kernel, stride, out channels)
@@ -85,7 +86,7 @@ class NetConfig:
     out_pad: int = 64               # head output columns (logits + value, padded)
 
     def conv_shapes(self):
-        h, w, c = self.img_h, self.img_w, 1
+        h, w, c = self.img_h, self.img_w, self.img_c
         out = []
         for k, s, co in self.conv:
             oh, ow = (h - k) // s + 1, (w - k) // s + 1
@@ -230,13 +231,14 @@ class PolicyNet:
 
     # ---- float32 autograd path (CPU training and the GPU path's oracle) ---------------
     def forward_reference(self, scal: torch.Tensor, img: Optional[torch.Tensor], params: Optional[dict] = None):
-        """scal [B, scalar_pad] (padding columns zero), img [B, H*W] NHW ->
+        """scal [B, scalar_pad] (padding columns zero), img [B, H*W*C] NHWC ->
         head output [B, out_pad] fp32 (logits, value at value_col)."""
         cfg = self.cfg
         P = params if params is not None else {n: self.p(n) for n, *_ in self.specs}
         if cfg.vision:
             B = scal.shape[0]
-            x = img.float().reshape(B, 1, cfg.img_h, cfg.img_w)
+            x = img[:, :cfg.img_h * cfg.img_w * cfg.img_c].float().reshape(B, cfg.img_h, cfg.img_w, cfg.img_c)
+            x = x.permute(0, 3, 1, 2)
             for i, g in enumerate(cfg.conv_shapes()):
                 w = P[f"conv{i + 1}.w"].reshape(g["CO"], g["k"], g["k"], g["C"]).permute(0, 3, 1, 2)
                 x = F.relu(F.conv2d(x, w, P[f"conv{i + 1}.b"], stride=g["s"]))
@@ -322,7 +324,7 @@ def _wgrad(G, dy, x, gw, rows):
 def forward_gpu(net: "PolicyNet", ws: Workspace, scal16: torch.Tensor, img16: Optional[torch.Tensor],
                 B: Optional[int] = None) -> torch.Tensor:
     """Head output [B, out_pad] fp32 into ws.out (bf16 operands, fp32 accumulate).
-    scal16: [B, scalar_pad] bf16; img16: [B, H*W] bf16 NHW (vision)."""
+    scal16: [B, scalar_pad] bf16; img16: [B, H*W*C] bf16 NHWC (vision)."""
     from ..ops import gemm as G
     cfg = net.cfg
     B = ws.B if B is None else B

@@ -8,7 +8,7 @@ error code and raises.
 from __future__ import annotations
 
 import ctypes
-from ctypes import c_float, c_int, c_int64, c_void_p
+from ctypes import c_double, c_float, c_int, c_int64, c_void_p
 
 import torch
 
@@ -18,6 +18,7 @@ _V = c_void_p
 _I = c_int
 _L = c_int64
 _F = c_float
+_D = c_double
 
 _SIGS = {
     "libsurf_vision.so": {
@@ -29,6 +30,7 @@ _SIGS = {
         "surf_occupancy": (_I, [_V, _V, _V, _I, _V, _I, _F, _F, _F, _F, _I, _I, _I, _I, _V, _V]),
         "surf_edt_workspace_bytes": (_L, [_I, _I, _I]),
         "surf_edt": (_I, [_V, _I, _I, _I, _F, _V, _V, _V, _V, _V]),
+        "surf_surfnz_bake": (_I, [_V, _I, _V, _V, _V, _I, _V, _I, _D, _D, _D, _D, _I, _I, _I, _V, _V, _V, _V]),
     },
 }
 

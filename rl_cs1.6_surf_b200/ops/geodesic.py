@@ -94,8 +94,25 @@ def geodesic_reference(occ: np.ndarray, cell: float, lo, hi, max_sweeps: int = 1
     return d
 
 
+def geodesic_cpu(occ: np.ndarray, cell: float, lo, hi) -> np.ndarray:
+    """Host geodesic (native Dijkstra, csrc/sim/geodesic.cpp): the same fixed
+    point as the GPU relaxation and ``geodesic_reference``, one settle per voxel."""
+    from ctypes import c_int32, c_void_p
+    from ..sim.core import simlib
+    occ = np.ascontiguousarray(occ, np.uint8)
+    nz, ny, nx = occ.shape
+    out = np.empty((nz, ny, nx), np.float32)
+    lo3 = (c_int32 * 3)(*[int(v) for v in lo])
+    hi3 = (c_int32 * 3)(*[int(v) for v in hi])
+    r = simlib().surfsim_geodesic(c_void_p(occ.ctypes.data), nx, ny, nz, float(cell), lo3, hi3,
+                                  c_void_p(out.ctypes.data))
+    if r < 0:
+        raise ValueError("grid too large for the host geodesic (32-bit voxel indices)")
+    return out
+
+
 def bake_goal_field(core, zone, cell: float = 16.0, device="cuda", mins=None, dims=None) -> GoalFieldData:
-    """Occupancy + geodesic + uint16 quantisation (GPU; numpy on CPU)."""
+    """Occupancy + geodesic + uint16 quantisation (GPU kernels; native host code on CPU)."""
     from .vision import grid_dims, occupancy, occupancy_reference
     if mins is None or dims is None:
         mn, mx = core.map_bounds()
@@ -122,7 +139,7 @@ def bake_goal_field(core, zone, cell: float = 16.0, device="cuda", mins=None, di
         grid = q.cpu().numpy().view(np.uint16)
     else:
         occ = occupancy_reference(core, mins, cell, dims, slab=True)
-        dist = geodesic_reference(occ, cell, lo, hi)
+        dist = geodesic_cpu(occ, cell, lo, hi)
         fin = dist < 1e30
         reach_max = float(dist[fin].max())
         quant = cell / 8.0

@@ -226,16 +226,20 @@ class DepthCamera:
             1 if self.vol.padded else 0, stream if stream is not None else stream_ptr(pose.device)), "surf_march")
         return out
 
-    def reference(self, pose: np.ndarray, return_steps: bool = False):
-        """CPU oracle (float32 numpy, same rules) -> (N, H, W) encoded depth."""
+    def reference(self, pose: np.ndarray, return_steps: bool = False, surf_nz: Optional[np.ndarray] = None):
+        """CPU oracle (float32 numpy, same rules) -> (N, H, W) encoded depth
+        ((N, H, W, 2) with the linear slope grid ``surf_nz``)."""
         return march_reference(self.vol.linear.float().cpu().numpy(), self.vol.mins, self.vol.cell, pose,
                                *self.offsets(), self.range, self.near, self.max_steps, self.pinhole,
-                               return_steps=return_steps)
+                               return_steps=return_steps, surf_nz=surf_nz)
 
 
 def march_reference(sdf: np.ndarray, mins, cell: float, pose: np.ndarray, col_off, row_off, rng: float, near: float,
-                    max_steps: int, pinhole: bool = False, return_steps: bool = False):
-    """Lock-step numpy restatement of the sphere trace (the kernel's oracle)."""
+                    max_steps: int, pinhole: bool = False, return_steps: bool = False,
+                    surf_nz: Optional[np.ndarray] = None):
+    """Lock-step numpy restatement of the sphere trace (the kernel's oracle).
+    With ``surf_nz`` (linear int8 [nz, ny, nx]) the depth comes back as
+    (N, H, W, 2): depth and the slope byte / 127 of the voxel the ray stopped in."""
     f = np.float32
     pose = np.asarray(pose, f)
     n = pose.shape[0]
@@ -286,6 +290,11 @@ def march_reference(sdf: np.ndarray, mins, cell: float, pose: np.ndarray, col_of
         steps += alive
     t = np.minimum(t, f(rng))
     enc = (np.minimum(t, f(near)) / f(near) + f(0.25) * (f(1) - np.exp(-np.maximum(t - f(near), 0) / f(2500)))).astype(f)
+    if surf_nz is not None:
+        ix = vox(ex + dx * t, mn[0], nx)
+        iy = vox(ey + dy * t, mn[1], ny)
+        iz = vox(ez + dz * t, mn[2], nz)
+        enc = np.stack([enc, surf_nz[iz, iy, ix].astype(f) * f(1.0 / 127.0)], -1)
     return (enc, steps) if return_steps else enc
 
 

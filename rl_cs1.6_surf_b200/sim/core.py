@@ -196,6 +196,7 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
         "surfsim_map_counts": (None, [c_void_p, _P_I]),
         "surfsim_export_hull0": (None, [c_void_p, c_void_p, c_void_p, c_void_p, _P_I]),
         "surfsim_export_mesh": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_int32, _P_I]),
+        "surfsim_geodesic": (c_int64, [c_void_p, c_int32, c_int32, c_int32, c_float, c_void_p, c_void_p, c_void_p]),
         "surfsim_solid_entities": (c_int32, [c_void_p, c_void_p, c_int32]),
         "surfsim_triggers": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32]),
         "surfsim_trigger_contains": (None, [c_void_p, c_int32, c_void_p, c_int64, c_int32, c_void_p]),

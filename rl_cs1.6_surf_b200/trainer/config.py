@@ -17,6 +17,7 @@ RUN_DEFINING = (
     "map", "map_seed", "ep_ticks", "n_steps", "act_every", "epochs", "minibatches", "lr", "gamma", "gae", "clip",
     "ent", "ent_final", "vf", "max_grad_norm", "spawn", "teleport_fail", "yaw_jitter", "maxvel", "airaccelerate",
     "vision", "lidar_w", "lidar_h", "lidar_range", "lidar_near", "lidar_cell", "pinhole", "march_steps",
+    "surf_mask", "frame_stack",
     "continuous_yaw", "gps", "heads", "hidden", "fc", "proprio", "mlp", "reward", "pitch_rate", "yaw_adaptive",
     "respawn_frac", "respawn_margin", "respawn_reservoir", "train_stride", "drop_frac", "drop_min", "drop_max",
     "punch_min", "punch_max", "respawn_speed", "respawn_binned", "respawn_pool", "rnd_coef",
@@ -66,6 +67,8 @@ class TrainConfig:
     lidar_cell: float = 16.0
     pinhole: bool = False
     march_steps: int = 64
+    surf_mask: bool = False            # second image channel: the hit surface's |n_z| (floor / ramp / wall)
+    frame_stack: int = 0               # K > 1: current frame + the decisions 1, 2, 4, 8 back as K channels
     # network
     continuous_yaw: bool = False
     gps: bool = False

@@ -80,8 +80,36 @@ def read_trajectory(path) -> list:
     return eps
 
 
-def _policy_actions(trainer, h: np.ndarray, greedy: bool, gen: Optional[torch.Generator]):
-    """Action rows [n, 8] int32 for host records h [n, 64]."""
+class _EvalFrames:
+    """Frame history of an evaluation (one episode per env, all started
+    together): a ring of the last ``pro + 1`` renders, composed by the same
+    stacking kernel as the trainer's rollout."""
+
+    def __init__(self, trainer, n: int):
+        from ..ops.framestack import FrameStacker
+        st = trainer.stacker
+        self.ring = st.pro + 1
+        self.stacker = FrameStacker(trainer.n_frames, st.fr, st.C0, ring=self.ring)
+        dev = trainer.device
+        self.frames = torch.zeros((self.ring, n, st.fr), dtype=torch.bfloat16, device=dev)
+        self.age = torch.zeros(n, dtype=torch.int32, device=dev)
+        self.rec = torch.zeros(n, dtype=torch.int32, device=dev)
+        self.zero = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.out = torch.zeros((n, st.fr * st.K), dtype=torch.bfloat16, device=dev)
+        self.d = 0
+
+    def __call__(self, camera, pose: torch.Tensor) -> torch.Tensor:
+        slot = self.d % self.ring
+        camera.render(pose, out=self.frames[slot])
+        out = self.stacker.rollout(self.frames, slot, 0, self.frames.shape[1], self.zero if self.d > 0 else None,
+                                   self.age, self.rec, self.out)
+        self.d += 1
+        return out
+
+
+def _policy_actions(trainer, h: np.ndarray, greedy: bool, gen: Optional[torch.Generator], frames=None):
+    """Action rows [n, 8] int32 for host records h [n, 64] (``frames``: the
+    frame history when the policy stacks frames)."""
     from ..models.policy import Workspace, forward_gpu
     from ..ops import rl as R
     net, layout = trainer.net, trainer.layout
@@ -91,7 +119,10 @@ def _policy_actions(trainer, h: np.ndarray, greedy: bool, gen: Optional[torch.Ge
         hd = torch.as_tensor(h, device=dev)
         scal = torch.zeros((n, 16), dtype=torch.bfloat16, device=dev)
         trainer._features(hd[:, C_OBS:C_OBS + 15].contiguous(), scal)
-        img = trainer.camera.render(hd[:, C_REC:C_REC + 6].contiguous()) if trainer.cfg.vision else None
+        img = None
+        if trainer.cfg.vision:
+            pose = hd[:, C_REC:C_REC + 6].contiguous()
+            img = frames(trainer.camera, pose) if frames is not None else trainer.camera.render(pose)
         ws = getattr(trainer, "_eval_ws", None)
         if ws is None or ws.B < n:
             ws = trainer._eval_ws = Workspace(net, max(n, 8))
@@ -146,8 +177,9 @@ def evaluate(trainer, episodes: int = 3, greedy: bool = True, max_ticks: int = 6
     rows: list = [[] for _ in range(n)]
     K = cfg.act_every
     t = 0
+    frames = _EvalFrames(trainer, n) if getattr(trainer, "stacker", None) is not None else None
     while active.any() and t < max_ticks:
-        act = np.ascontiguousarray(_policy_actions(trainer, h, greedy, gen).astype(np.int32))
+        act = np.ascontiguousarray(_policy_actions(trainer, h, greedy, gen, frames).astype(np.int32))
         for _ in range(K):
             pre = st.copy()
             hp = h.ctypes.data

@@ -145,7 +145,12 @@ class Trainer:
             heads = tuple(h for h in heads if h != "pitch")
         self.layout = HeadLayout(heads, cfg.continuous_yaw)
         self.feat_idx = tuple(range(15)) if cfg.gps else NOGPS
-        ncfg = NetConfig(vision=cfg.vision, img_h=cfg.lidar_h, img_w=cfg.lidar_w, n_scalar=len(self.feat_idx),
+        self.frame_ch = 2 if (cfg.vision and cfg.surf_mask) else 1
+        self.n_frames = max(1, int(cfg.frame_stack)) if cfg.vision else 1
+        if cfg.vision and (cfg.surf_mask or self.n_frames > 1) and not self.gpu:
+            raise RuntimeError("the surface mask and frame stacking need a CUDA device")
+        ncfg = NetConfig(vision=cfg.vision, img_h=cfg.lidar_h, img_w=cfg.lidar_w,
+                         img_c=self.frame_ch * self.n_frames, n_scalar=len(self.feat_idx),
                          scalar_pad=16, fc=cfg.fc, proprio=cfg.proprio, hidden=cfg.hidden, mlp=tuple(cfg.mlp),
                          heads=self.layout)
         self.net = PolicyNet(ncfg, self.device, seed=cfg.seed)
@@ -161,9 +166,17 @@ class Trainer:
                                               dims=tuple(m["dims"]), device=self.device)
             else:
                 self.volume = SdfVolume.build(self.core, cell=cfg.lidar_cell, device=self.device)
+            self.surf_nz = None
+            if cfg.surf_mask:
+                from ..ops import surfmask
+                self.surf_nz, lin = surfmask.for_volume(self.core, self.volume)
+                h = surfmask.histogram(lin.cpu().numpy())
+                self._log(f"surface mask: {h['surfaced']:,} surfaced voxels ({h['surfable']:,} surfable, "
+                          f"{h['walkable'] + h['flat']:,} walkable)")
+                del lin
             self.camera = DepthCamera(self.volume, cfg.lidar_w, cfg.lidar_h, range_units=cfg.lidar_range,
                                       near_range=cfg.lidar_near, max_steps=cfg.march_steps, pinhole=cfg.pinhole,
-                                      dtype=torch.bfloat16)
+                                      dtype=torch.bfloat16, surf_nz=self.surf_nz)
         self._log(f"policy: {self.net.n_params:,} parameters, heads {self.layout.heads}"
                   f"{' + continuous yaw' if self.layout.continuous_yaw else ''}")
 
@@ -171,13 +184,28 @@ class Trainer:
         cfg, dev = self.cfg, self.device
         N, T = cfg.envs, cfg.n_steps
         self.N, self.T, self.K = N, T, cfg.act_every
-        self.frame = cfg.lidar_w * cfg.lidar_h if cfg.vision else 0
+        self.frame = cfg.lidar_w * cfg.lidar_h * self.frame_ch if cfg.vision else 0
+        self.stacker = None
+        if cfg.vision and self.n_frames > 1:
+            from ..ops.framestack import FrameStacker
+            self.stacker = FrameStacker(self.n_frames, self.frame, self.frame_ch)
+            if self.stacker.pro > T:
+                raise ValueError(f"frame_stack {self.n_frames} reaches {self.stacker.pro} decisions back: "
+                                 f"n_steps must be at least that")
+        # decision t's frame lives in slot pro + t; slots [0, pro) hold the
+        # previous rollout's last frames (the stack's reach-back)
+        self.pro = self.stacker.pro if self.stacker is not None else 0
+        self.img_w = self.frame * self.n_frames
         pin = self.gpu
         self.hrec = torch.zeros((N, H_COLS), dtype=torch.float32, pin_memory=pin)
         self.act_pin = torch.zeros((N, 8), dtype=torch.int32, pin_memory=pin)
         self.hdev = torch.zeros((N, H_COLS), dtype=torch.float32, device=dev)
         bf = torch.bfloat16 if self.gpu else torch.float32
-        self.b_img = torch.zeros((T + 1, N, max(self.frame, 8)), dtype=bf, device=dev) if cfg.vision else None
+        self.b_img = torch.zeros((self.pro + T + 1, N, max(self.frame, 8)), dtype=bf, device=dev) \
+            if cfg.vision else None
+        if self.stacker is not None:
+            self.b_age = torch.zeros((T + 1, N), dtype=torch.int32, device=dev)
+            self.age_cur = torch.zeros(N, dtype=torch.int32, device=dev)
         self.b_scal = torch.zeros((T + 1, N, 16), dtype=bf, device=dev)
         self.b_act = torch.zeros((T, N, 8), dtype=torch.int32, device=dev)
         self.b_logp = torch.zeros((T, N), device=dev)
@@ -196,12 +224,14 @@ class Trainer:
             step = N // G
             self.groups = [(g * step, (g + 1) * step) for g in range(G)]
             self.ws_grp = [Workspace(self.net, step) for _ in range(G)]
+            self.stk_grp = [torch.zeros((step, self.img_w), dtype=torch.bfloat16, device=dev) for _ in range(G)] \
+                if self.stacker is not None else None
             self.grp_events = [torch.cuda.Event() for _ in range(G)]
             self.ws_upd = Workspace(self.net, self.mb)
             self.perm = torch.zeros(T * N, dtype=torch.int64, device=dev)
             self.perm_key = torch.tensor([cfg.seed * 7919 + self.rank], dtype=torch.int64, device=dev)
             self.mom_mb = torch.zeros((cfg.minibatches, 2), dtype=torch.float64, device=dev)
-            self.img_mb = torch.zeros((self.mb, max(self.frame, 8)), dtype=torch.bfloat16, device=dev)
+            self.img_mb = torch.zeros((self.mb, max(self.img_w, 8)), dtype=torch.bfloat16, device=dev)
             self.scal_mb = torch.zeros((self.mb, 16), dtype=torch.bfloat16, device=dev)
             self.coef = torch.tensor([cfg.clip, cfg.vf, cfg.ent], dtype=torch.float32, device=dev)
             self.loss_stats = torch.zeros(6, dtype=torch.float32, device=dev)
@@ -286,6 +316,8 @@ class Trainer:
         if self.gpu:
             self.hdev.copy_(self.hrec, non_blocking=True)
             self.reward.init(self.hdev[:, C_REC:C_REC + REC_COLS])
+            if self.stacker is not None:
+                self.age_cur.zero_()
         else:
             self.reward.init(h[:, C_REC:C_REC + REC_COLS].copy())
 
@@ -318,8 +350,12 @@ class Trainer:
                 self.b_rew[t - 1, lo:hi].add_(self.cfg.rnd_coef * self.rnd.bonus(self.rnd_obs[t, lo:hi]))
         img = None
         if self.cfg.vision:
-            img = self.b_img[t, lo:hi]
+            img = self.b_img[self.pro + t, lo:hi]
             self.camera.render(self.hdev[lo:hi, C_REC:C_REC + 6], out=img)
+            if self.stacker is not None:
+                done = self.b_done[t - 1, lo:hi] if t > 0 else None      # t == 0 continues the last tail
+                img = self.stacker.rollout(self.b_img, self.pro + t, lo, hi, done, self.age_cur, self.b_age[t, lo:hi],
+                                           self.stk_grp[g])
         self._features(self.hdev[lo:hi, C_OBS:C_OBS + 15], self.b_scal[t, lo:hi])
         out = forward_gpu(self.net, self.ws_grp[g], self.b_scal[t, lo:hi], img)
         vc = self.layout.value_col
@@ -384,7 +420,7 @@ class Trainer:
                                obs=(base + 4 * C_OBS, stride), term_obs=(base + 4 * C_TOBS, stride),
                                rec=(base + 4 * C_REC, stride), term_rec=(base + 4 * C_TREC, stride))
 
-    def _bootstrap_truncations(self, g: int) -> None:
+    def _bootstrap_truncations(self, g: int, t: int) -> None:
         """gamma * V(s_T) for envs of group g whose episode was truncated this
         decision (their states are already the next episode's): render the
         terminal poses, run the value head, stage the bonus for the group's
@@ -402,6 +438,9 @@ class Trainer:
         img = None
         if self.cfg.vision:
             img = self.camera.render(rows[:, C_TREC:C_TREC + 6].contiguous())
+            if self.stacker is not None:      # the terminal state is one decision past slot pro + t
+                stk = torch.empty((M, self.img_w), dtype=torch.bfloat16, device=self.device)
+                img = self.stacker.terminal(self.b_img, self.pro + t, idx, img, self.age_cur, stk)
         out = forward_gpu(self.net, self.ws_grp[g], scal, img, B=M)
         self.reward.boot.index_copy_(0, idx, self.cfg.gamma * out[:, self.layout.value_col])
 
@@ -412,6 +451,8 @@ class Trainer:
         tm = self.timer
         if self.cfg.graphs and not self.rew_graphs:
             self._capture()
+        if self.pro:                          # carry the last frames over as the reach-back prologue
+            self.b_img[:self.pro].copy_(self.b_img[T:T + self.pro])
         for g in range(G):
             self._run_group(g, 0)
         for t in range(T):
@@ -423,7 +464,7 @@ class Trainer:
                 self._env_step_group(g)
                 tm.add("env", t0)
                 if self.cfg.ep_ticks:
-                    self._bootstrap_truncations(g)
+                    self._bootstrap_truncations(g, t)
                 self._run_group(g, t + 1)
             self._observe_respawn(t)
             self.global_step += self.N * self.K * self.world
@@ -441,11 +482,13 @@ class Trainer:
         R.adv_moments(self.adv.view(-1), self.perm, mb, nmb, self.mom_mb)
         if self.comm is not None:
             self.comm.allreduce_moments(self.mom_mb)
-        f_img = self.b_img[:T].view(T * N, -1) if self.cfg.vision else None
+        f_img = self.b_img[self.pro:self.pro + T].view(T * N, -1) if self.cfg.vision else None
         f_scal = self.b_scal[:T].view(T * N, 16)
         for m in range(nmb):
             idx = self.perm[m * mb:(m + 1) * mb]
-            if self.cfg.vision:
+            if self.stacker is not None:
+                self.stacker.gather(self.b_img, idx, self.b_age[:T].view(-1), self.img_mb)
+            elif self.cfg.vision:
                 G.gather_rows(f_img, idx, self.img_mb)
             G.gather_rows(f_scal, idx, self.scal_mb)
             out = forward_gpu(self.net, self.ws_upd, self.scal_mb, self.img_mb if self.cfg.vision else None)

@@ -314,3 +314,78 @@ def test_operator_tools(tmp_path):
     srv.server_close()
     sweep = tools.env_thread_sweep("ramps", envs=64, k=3, reps=2, threads=[1, 2])
     assert len(sweep) == 2 and all(r["ticks_per_s"] > 0 for r in sweep)
+
+
+def test_native_geodesic_matches_relaxation_oracle():
+    """Host Dijkstra (csrc/sim/geodesic.cpp) reaches the Bellman-Ford fixed point bit for bit."""
+    from surfb200.ops.geodesic import geodesic_cpu, geodesic_reference
+    rng = np.random.default_rng(1)
+    occ = (rng.random((10, 30, 44)) < 0.3).astype(np.uint8)
+    occ[:, 15, 3:40] = 1
+    occ[1:4, 1:4, 1:4] = 0
+    for cell in (16.0, 37.5):
+        ref = geodesic_reference(occ, cell, (1, 1, 1), (3, 3, 3))
+        got = geodesic_cpu(occ, cell, (1, 1, 1), (3, 3, 3))
+        assert np.array_equal(ref, got)
+    assert (ref < 1e30).sum() > 1000
+
+
+def _strafer_recording(tmp_path, ticks=240):
+    """A ramp-map episode of the scripted strafer, written as a trajectory file."""
+    from surfb200.sim import mapgen
+    from surfb200.sim.core import SimCore, default_config
+    from surfb200.sim.policies import ScriptedStrafer
+    from surfb200.trainer.evaluate import TrajectoryWriter
+    m = mapgen.generate("ramps", 0)
+    core = SimCore.from_bytes(m.image, default_config(1, spawn_mode=2, max_episode_ticks=5000), threads=1)
+    core.set_spawn_pool(m.spawn_pool[:1])
+    core.reset(3)
+    pol = ScriptedStrafer(core, period_ticks=60)
+    w = TrajectoryWriter(tmp_path / "s.traj.jsonl", m.name, {})
+    w.header(0)
+    for t in range(ticks):
+        st = core.states_view[0].copy()
+        a = pol.act(None)
+        _, rew, done, trunc, _ = core.step(a)
+        w.tick(t, st, a[0], float(rew[0]))
+        if done[0] or trunc[0]:
+            break
+    w.trailer("trunc", t + 1, 0.0)
+    w.close()
+    core.close()
+    return m, tmp_path / "s.traj.jsonl"
+
+
+def test_strafe_audit_and_route_bound(tmp_path):
+    from surfb200.utils import tas
+    _, path = _strafer_recording(tmp_path)
+    e = tas.episodes(path)[0]
+    a = tas.strafe_audit(e)
+    assert a["ticks"] == len(e) - 1 and -1.0 <= a["capture"] <= 1.0 and a["mean_speed"] > 0
+    assert 0.0 <= a["in_window"] <= 1.0
+    many = tas.strafe_audit_many([e, e])
+    assert many["episodes"] == 2 and abs(many["capture"] - a["capture"]) < 1e-9
+    r = tas.route_bound(e, segments=4, target=1.0)
+    assert r["rigorous_floor_s"] <= r["actual_s"] + 0.05
+    s = [r["loss_cut_sensitivity_s"][c] for c in (0, 10, 20, 30, 40)]
+    assert all(b <= a_ + 1e-9 for a_, b in zip(s, s[1:]))       # less contact loss is never slower
+    assert len(r["segments"]) >= 1 and r["route_can_host_target"] in (True, False)
+    # inferred actions reproduce the recorded fwd / side / yaw bins
+    act = tas.infer_actions(e)
+    assert act.shape == (len(e) - 1, 6) and (act[:, 0] < 15).all()
+
+
+def test_tas_search_and_chain_replay_the_recording(tmp_path):
+    from surfb200.sim.core import SimCore, default_config
+    from surfb200.utils import tas
+    m, path = _strafer_recording(tmp_path)
+    e = tas.episodes(path)[0]
+    core = SimCore.from_bytes(m.image, default_config(16, max_episode_ticks=1_000_000), threads=2)
+    core.reset(0)
+    score = lambda st: -np.asarray(st["origin"], np.float64)[:, 0]     # progress along +x
+    r = tas.tas_search(core, score, e, t0=20, window=40, iters=3, p_mutate=0.1, seed=1)
+    assert r["window"] == 40 and r["replay_error"] < 5.0        # restore + inferred actions track the recording
+    assert r["best"] <= r["replay"] and r["actions"].shape == (40, 6)
+    c = tas.tas_chain(core, score, e, window=40, iters=2, max_windows=2, seed=1)
+    assert len(c["windows"]) == 2 and c["actions"].shape == (80, 6)
+    core.close()

@@ -33,3 +33,36 @@ def test_vision_ppo_iterations(graphs, cont):
     # actions decode within range
     a = tr.b_act.view(-1, 8)
     assert int(a[:, 2].min()) >= 0 and int(a[:, 2].max()) <= 2
+
+
+@pytest.mark.parametrize("stack,mask", [(5, False), (3, True), (1, True)])
+def test_frame_stack_and_surface_mask_training(stack, mask):
+    """Rollout composition == update gather (same decision, same bytes), the
+    next rollout's first decision reaches back into the carried prologue,
+    and evaluation stacks through its own ring."""
+    from surfb200.trainer.evaluate import evaluate
+    cfg = TrainConfig(map="field", envs=256, n_steps=16, act_every=3, epochs=1, minibatches=4, ep_ticks=60,
+                      frame_stack=stack, surf_mask=mask, reward=RewardSpec(mode="speed"))
+    tr = Trainer(cfg, verbose=False)
+    assert tr.net.cfg.img_c == (2 if mask else 1) * max(stack, 1)
+    N, T = tr.N, tr.T
+    s = tr.train_iteration()
+    assert math.isfinite(s["policy_loss"]) and torch.isfinite(tr.net.flat).all()
+    if mask:
+        slope = tr.b_img[tr.pro:tr.pro + T].float()[..., 1::2]
+        assert 0.0 <= float(slope.min()) and float(slope.max()) <= 1.0
+        assert (slope > 0).float().mean() > 0.2
+    if stack > 1:
+        st = tr.stacker
+        idx = torch.arange(T * N, (T + 1) * N, device="cuda")
+        tail = torch.zeros((N, tr.img_w), dtype=torch.bfloat16, device="cuda")
+        st.gather(tr.b_img, idx, tr.b_age.view(-1), tail)
+        assert torch.equal(tail, torch.cat(tr.stk_grp, 0))        # what the policy saw at the tail decision
+        assert int(tr.b_age.max()) > 0 and int(tr.b_age.max()) <= st.pro
+        tr.train_iteration()
+        first = torch.zeros_like(tail)
+        st.gather(tr.b_img, torch.arange(0, N, device="cuda"), tr.b_age.view(-1), first)
+        assert torch.equal(first, tail)                              # t = 0 continues the previous tail
+    summ = evaluate(tr, episodes=2, greedy=True, max_ticks=30)
+    assert summ["episodes"] == 2
+    tr.release_graphs()
