@@ -27,17 +27,22 @@ def main():
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--json", default=None)
     ap.add_argument("--explicit", action="store_true", help="im2col + GEMM for every convolution (A/B baseline)")
+    ap.add_argument("--nhw", action="store_true", help="64 x 128 NHW image with the 8x8 stride-4 first layer")
     args = ap.parse_args()
     import torch
     import surfb200  # noqa: F401
-    from surfb200.models.policy import HeadLayout, NetConfig, PolicyNet, Workspace, backward_gpu, forward_gpu
+    from surfb200.models.policy import (HeadLayout, NetConfig, PolicyNet, Workspace, backward_gpu, forward_gpu,
+                                        space_to_depth_config)
     from surfb200.ops import conv as CV
     from surfb200.ops import gemm as G
     from surfb200.ops import rl as R
 
     dev = torch.device("cuda")
     layout = HeadLayout(("yaw", "pitch", "fwd", "side", "jump", "duck"), False)
-    net = PolicyNet(NetConfig(vision=True, img_h=64, img_w=128, n_scalar=10, scalar_pad=16, heads=layout), dev)
+    ncfg = NetConfig(vision=True, img_h=64, img_w=128, n_scalar=10, scalar_pad=16, heads=layout)
+    if not args.nhw:                     # the trainer's layout: 4x4 space-to-depth image, conv1 as 2x2 stride 1
+        ncfg = space_to_depth_config(ncfg)
+    net = PolicyNet(ncfg, dev)
     B = args.rows
     net.implicit_conv = not args.explicit
     ws = Workspace(net, B)

@@ -1,6 +1,7 @@
 """Small, self-contained launches of each hot kernel, for ncu captures.
 
-    python bench/profile_kernels.py --only march|conv1_fwd|conv2_dgrad|fc_wgrad|col2im|im2col|conv2_ifwd|
+    python bench/profile_kernels.py --only march|conv1_fwd|conv2_dgrad|fc_wgrad|col2im|im2col|conv1_ifwd|
+                                           conv1_iwgrad|conv2_ifwd|
                                            conv2_iwgrad|conv2_idgrad|conv3_ifwd|conv3_idgrad|sample|gae|
                                            ppo_loss|reward|adam|p2p1|edt|geodesic|surfnz|framestack [--reps 2]
 
@@ -41,6 +42,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", required=True)
     ap.add_argument("--reps", type=int, default=2)
+    ap.add_argument("--dbg", type=int, default=0, help="convolution kernel diagnostics (timing studies): "
+                    "1 skip epilogue stores, 2 skip MMAs")
     args = ap.parse_args()
     import numpy as np
     import torch
@@ -108,14 +111,18 @@ def main():
             fn = lambda: G.im2col(x, B, g["H"], g["W"], g["C"], g["k"], g["s"], out=col)
             info["bytes"] = 2.0 * (rows * g["k"] ** 2 * g["C"] + B * g["H"] * g["W"] * g["C"])
         info["ms"] = _time(fn, args.reps)
-    elif k in ("conv2_ifwd", "conv2_iwgrad", "conv2_idgrad", "conv3_ifwd", "conv3_idgrad"):
+    elif k in ("conv1_ifwd", "conv1_iwgrad", "conv2_ifwd", "conv2_iwgrad", "conv2_idgrad", "conv3_ifwd",
+               "conv3_idgrad"):
         # implicit-GEMM convolutions (4-D TMA boxes over the NHWC activations),
         # 4,096 images as above
         from surfb200.ops import conv as CV
+        CV.DEBUG = args.dbg
+        info["dbg"] = args.dbg
         layout = HeadLayout(("yaw", "pitch", "fwd", "side", "jump", "duck"), False)
-        net = PolicyNet(NetConfig(heads=layout), dev)
+        from surfb200.models.policy import space_to_depth_config
+        net = PolicyNet(space_to_depth_config(NetConfig(heads=layout)), dev)    # the trainer's network
         B = 4096
-        li = 1 if k.startswith("conv2") else 2
+        li = int(k[4]) - 1
         g = net.cfg.conv_shapes()[li]
         sh = CV.ConvShape(B, g["H"], g["W"], g["C"], g["k"], g["s"], g["CO"])
         rows_in, rows = B * g["H"] * g["W"], B * g["OH"] * g["OW"]

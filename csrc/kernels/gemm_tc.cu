@@ -77,7 +77,15 @@ struct Epilogue {
 //   mode 2 (MN-major, weight-gradient operands): the 64 rows of a k-block are
 //          a tw x th x tb box of output positions (k-block = position tile),
 //          the MN coordinate picks the channels: for A the output channel
-//          chunk (m0), for B the tap of each 64-wide n sub-block.
+//          chunk (m0), for B the tap of each 64-wide n sub-block;
+//   mode 3 (16-channel activations, e.g. a depth image in 4x4 space-to-depth
+//          order): one tap is 16 channels = 32 bytes, so a tap is loaded as
+//          a slab of 32-byte rows with the 32-byte swizzle. A (K-major,
+//          forward): k-block kb is taps 4 kb .. 4 kb + 3, one 128 x 32 B slab
+//          each, and the MMA's 16-wide k step is exactly one slab. B (MN-major,
+//          weight gradient): n sub-block j of 16 columns is tap n0 / 16 + j,
+//          a 64 x 32 B slab of the k-block's positions; one MMA spans the
+//          BN / 16 slabs (leading byte offset = slab size).
 // Out-of-range coordinates (negative ones included) load zeros, which is
 // what makes the padded tile edges and the transposed-convolution halo free.
 struct Geo {
@@ -173,14 +181,15 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
 }
 
 // Shared-memory matrix descriptor (sm100 UMMA): start, LBO, SBO (>> 4),
-// descriptor version 1, 128-byte swizzle (layout type 2).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+// descriptor version 1, layout type (2: 128-byte swizzle, 6: 32-byte swizzle).
+constexpr uint32_t kSw128 = 2, kSw32 = 6;
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout = kSw128) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((addr >> 4) & 0x3FFF);
   d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16;
   d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32;
   d |= 1ull << 46;
-  d |= 2ull << 61;
+  d |= static_cast<uint64_t>(layout & 7) << 61;
   return d;
 }
 
@@ -299,8 +308,12 @@ struct Cfg {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kAcc = BN <= 64 ? 4 : 2;           // accumulator buffers in TMEM
+  static constexpr int kAcc = BN <= 32 ? 8 : (BN <= 64 ? 4 : 2);   // accumulator buffers in TMEM
   static constexpr int kTmemCols = kAcc * BN;
+  // epilogue warps per tile: with one 32-column chunk per tile (BN = 32) the
+  // two warps of a TMEM lane quadrant take alternate tiles instead of
+  // alternate chunks, so all eight epilogue warps stay busy
+  static constexpr int kEpiPerTile = BN == 32 ? kEpiWarps / 2 : kEpiWarps;
   // per epilogue warp: two 32x32 fp32 staging tiles for TMA stores (4 KB each)
   static constexpr int kStageOutBytes = kEpiWarps * 2 * 4096;
   // alignment slack + operand stages + barrier block (1 KB) + output staging
@@ -335,14 +348,19 @@ struct Sched {             // static persistent schedule over (m block, n block,
 };
 
 // Register-path stores of a processed 32-column chunk (transposed output,
-// fp32 atomics, or rows that TMA cannot address).
+// fp32 atomics, or rows that TMA cannot address). Every loop over the chunk
+// is fully unrolled with a column predicate: a loop with a run-time trip
+// count would index v[] dynamically and put the whole accumulator chunk of
+// every epilogue in local memory.
 __device__ __forceinline__ void store_chunk32(const Epilogue& ep, const float* v, int64_t row, bool row_ok, int col0,
                                               int N) {
   if (!row_ok) return;
   const int ncol = min(32, N - col0);
   if (ep.ct) {
     // for a fixed column the warp's 32 lanes write 32 consecutive rows
-    for (int i = 0; i < ncol; ++i) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (i >= ncol) break;
       if (ep.ct_dtype == 1) static_cast<uint16_t*>(ep.ct)[(col0 + i) * ep.ldct + row] = surfk::f32_to_bf16(v[i]);
       else static_cast<float*>(ep.ct)[(col0 + i) * ep.ldct + row] = v[i];
     }
@@ -350,7 +368,9 @@ __device__ __forceinline__ void store_chunk32(const Epilogue& ep, const float* v
   if (!ep.c) return;
   if (ep.c_mode == kAtomic) {
     float* dst = static_cast<float*>(ep.c) + row * ep.ldc + col0;
-    for (int i = 0; i < ncol; ++i) atomicAdd(dst + i, v[i]);
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < ncol) atomicAdd(dst + i, v[i]);
   } else if (ep.c_dtype == 1) {
     uint16_t* dst = static_cast<uint16_t*>(ep.c) + row * ep.ldc + col0;
     if (ncol == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
@@ -364,7 +384,9 @@ __device__ __forceinline__ void store_chunk32(const Epilogue& ep, const float* v
         reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[0], w[1], w[2], w[3]);
       }
     } else {
-      for (int i = 0; i < ncol; ++i) dst[i] = surfk::f32_to_bf16(v[i]);
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < ncol) dst[i] = surfk::f32_to_bf16(v[i]);
     }
   } else {
     float* dst = static_cast<float*>(ep.c) + row * ep.ldc + col0;
@@ -372,7 +394,9 @@ __device__ __forceinline__ void store_chunk32(const Epilogue& ep, const float* v
 #pragma unroll
       for (int i = 0; i < 8; ++i) reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     } else {
-      for (int i = 0; i < ncol; ++i) dst[i] = v[i];
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < ncol) dst[i] = v[i];
     }
   }
 }
@@ -404,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < C::kAcc; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
-      mbar_init(smem_u32(&acc_empty[b]), kEpiWarps);     // one arrival per epilogue warp
+      mbar_init(smem_u32(&acc_empty[b]), C::kEpiPerTile);     // one arrival per epilogue warp of the tile
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -431,7 +455,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = it % STAGES;
           if (it >= STAGES && !mbar_wait(smem_u32(&bars[STAGES + s]), ((it / STAGES) & 1) ^ 1, ep.err, 1, abort)) break;
           const uint32_t full = smem_u32(&bars[s]);
-          mbar_expect_tx(full, C::kStageBytes);
+          // an MN-major A is loaded as two 64-row halves; with M <= m0 + 64
+          // the second half is out of range: skip it (its stale smem rows
+          // only reach accumulator rows >= M, which the epilogue drops)
+          const bool a_half = (cc.a.mode == 2 || (A_MN && cc.a.mode == 0)) && m0 + 64 >= M;
+          mbar_expect_tx(full, C::kStageBytes - (a_half ? BK * 128 : 0));
           const uint32_t a_dst = smem_u32(tiles + s * C::kStageBytes);
           const uint32_t b_dst = a_dst + C::kABytes;
           const int kb = kt0 + i;
@@ -446,14 +474,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             int b0, h0, w0;
             tile_origin(cc.a, kb, &b0, &h0, &w0);
             tma_load_4d(a_dst, &tma_a, m0, w0, h0, b0, full);
-            tma_load_4d(a_dst + BK * 128, &tma_a, m0 + 64, w0, h0, b0, full);
+            if (!a_half) tma_load_4d(a_dst + BK * 128, &tma_a, m0 + 64, w0, h0, b0, full);
+          } else if (cc.a.mode == 3) {
+            int b0, h0, w0;
+            tile_origin(cc.a, m0 / BM, &b0, &h0, &w0);
+#pragma unroll
+            for (int j = 0; j < BK / 16; ++j) {
+              const int tap = kb * (BK / 16) + j;
+              const int kh = tap / cc.a.kw_n, kw = tap - kh * cc.a.kw_n;
+              tma_load_4d(a_dst + j * (BM * 32), &tma_a, 0, w0 * cc.a.sw + kw, h0 * cc.a.sh + kh, b0, full);
+            }
           } else if (A_MN) {
             tma_load_2d(a_dst, &tma_a, m0, k, full);
-            tma_load_2d(a_dst + BK * 128, &tma_a, m0 + 64, k, full);
+            if (!a_half) tma_load_2d(a_dst + BK * 128, &tma_a, m0 + 64, k, full);
           } else {
             tma_load_2d(a_dst, &tma_a, k, m0, full);
           }
-          if (cc.b.mode == 2) {
+          if (cc.b.mode == 3) {
+            int b0, h0, w0;
+            tile_origin(cc.b, kb, &b0, &h0, &w0);
+#pragma unroll 1
+            for (int j = 0; j < BN / 16; ++j) {
+              const int tap = n0 / 16 + j;
+              const int kh = tap / cc.b.kw_n, kw = tap - kh * cc.b.kw_n;
+              tma_load_4d(b_dst + j * (BK * 32), &tma_b, 0, w0 * cc.b.sw + kw, h0 * cc.b.sh + kh, b0, full);
+            }
+          } else if (cc.b.mode == 2) {
             int b0, h0, w0;
             tile_origin(cc.b, kb, &b0, &h0, &w0);
 #pragma unroll
@@ -493,8 +539,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < BK / 16; ++j) {
             // K-major: +32 B per 16-element k step inside the 128 B swizzled row;
             // MN-major: +2 k-groups (2 x 1024 B) per step; MN blocks BK*128 B apart.
-            const uint64_t da = A_MN ? smem_desc(a_base + j * 2048, BK * 128, 1024) : smem_desc(a_base + j * 32, 16, 1024);
-            const uint64_t db = B_MN ? smem_desc(b_base + j * 2048, BK * 128, 1024) : smem_desc(b_base + j * 32, 16, 1024);
+            // Mode 3 (32 B swizzle): A steps one 128-row slab per k step (8-row
+            // groups 256 B apart); B steps 16 positions (512 B) inside every
+            // 16-column slab, the slabs BK*32 B apart.
+            const uint64_t da = cc.a.mode == 3 ? smem_desc(a_base + j * (BM * 32), 16, 256, kSw32)
+                                : A_MN ? smem_desc(a_base + j * 2048, BK * 128, 1024)
+                                       : smem_desc(a_base + j * 32, 16, 1024);
+            const uint64_t db = cc.b.mode == 3 ? smem_desc(b_base + j * 512, BK * 32, 256, kSw32)
+                                : B_MN ? smem_desc(b_base + j * 2048, BK * 128, 1024)
+                                       : smem_desc(b_base + j * 32, 16, 1024);
             if (!(ep.dbg & 2)) mma_bf16(dtm, da, db, C::kIdesc, (i > 0 || j > 0) ? 1u : 0u);
           }
           mma_commit(smem_u32(&bars[STAGES + s]));      // frees the stage when these MMAs finish
@@ -515,6 +568,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       sc.tile(t, &m0, &nb, &kt0, &nkt);
       const int n0 = nb * BN;
       const int buf = tc % C::kAcc, use = tc / C::kAcc;
+      if (BN == 32 && (tc & 1) != half) continue;      // the other warp of this quadrant takes the tile
       if (!mbar_wait(smem_u32(&acc_full[buf]), use & 1, ep.err, 3, abort)) break;
       fence_after();
       int row = m0 + quad * 32 + lane;
@@ -543,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool bf = ep.c_dtype == 1;
         uint8_t* my_stage = stage_out + (warp - 2) * 8192;
 #pragma unroll 1
-        for (int c0 = 32 * half; c0 < BN; c0 += 64) {
+        for (int c0 = BN == 32 ? 0 : 32 * half; c0 < BN; c0 += 64) {
           if (n0 + c0 >= N) break;
           float v[32];
           tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + c0, v);
@@ -580,7 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c0 = 32 * half; c0 < BN; c0 += 64) {
+        for (int c0 = BN == 32 ? 0 : 32 * half; c0 < BN; c0 += 64) {
           if (n0 + c0 >= N) break;
           float v[32];
           tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + c0, v);
@@ -652,7 +706,10 @@ struct MapDesc {
 bool make_map4d(CUtensorMap* m, const MapDesc& d) {
   auto fn = encode_fn();
   if (!fn) return false;
-  if ((reinterpret_cast<uintptr_t>(d.base) & 15) || d.box[0] * 2 > 128) return false;
+  const int inner = d.box[0] * 2;     // bytes: the swizzle span follows the box's inner extent
+  if ((reinterpret_cast<uintptr_t>(d.base) & 15) || (inner != 32 && inner != 64 && inner != 128)) return false;
+  const CUtensorMapSwizzle swz = inner == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                 : inner == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
   cuuint64_t dims[4], strides[3];
   cuuint32_t box[4], estr[4];
   for (int i = 0; i < 4; ++i) {
@@ -666,7 +723,7 @@ bool make_map4d(CUtensorMap* m, const MapDesc& d) {
     if (d.strides[i] % 16) return false;
   }
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(d.base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -674,7 +731,10 @@ bool make_map4d(CUtensorMap* m, const MapDesc& d) {
 template <int BN, bool A_MN, bool B_MN>
 int launch(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const Epilogue& ep, int splits,
            cudaStream_t s, const MapDesc* ad = nullptr, const MapDesc* bd = nullptr, const ConvCfg* conv = nullptr) {
-  constexpr int STAGES = BN >= 256 ? 3 : 4;
+  // as many stages as fit next to the output staging (227 KB per CTA): the
+  // implicit convolutions re-read every input tile once per tap from L2, so
+  // their throughput is bytes in flight / latency
+  constexpr int STAGES = BN <= 32 ? 8 : (BN <= 64 ? 6 : (BN <= 128 ? 5 : 3));
   using C = Cfg<BN, A_MN, B_MN, STAGES>;
   auto kern = gemm_kernel<BN, A_MN, B_MN, STAGES>;
   ConvCfg cc;
@@ -770,13 +830,20 @@ SURF_EXPORT int surf_gemm_conv(const void* A, int64_t lda, const MapDesc* ad, in
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if (splits > 1 && ep->c_mode != kAtomic) return static_cast<int>(cudaErrorInvalidValue);
   if (b_mn && bn < 64) return static_cast<int>(cudaErrorInvalidValue);
-  if ((cc->a.mode == 1 && a_mn) || (cc->a.mode == 2 && !a_mn) || (cc->b.mode == 2 && !b_mn) || cc->b.mode == 1)
+  if ((cc->a.mode == 1 && a_mn) || (cc->a.mode == 2 && !a_mn) || (cc->a.mode == 3 && a_mn) ||
+      (cc->b.mode == 2 && !b_mn) || (cc->b.mode == 3 && !b_mn) || cc->b.mode == 1 || cc->a.mode > 3 ||
+      cc->b.mode > 3)
     return static_cast<int>(cudaErrorInvalidValue);
   if ((cc->a.mode && !ad) || (cc->b.mode && !bd)) return static_cast<int>(cudaErrorInvalidValue);
-  if (cc->a.mode == 1 && cc->a.tw * cc->a.th * cc->a.tb != BM) return static_cast<int>(cudaErrorInvalidValue);
+  if ((cc->a.mode == 1 || cc->a.mode == 3) && cc->a.tw * cc->a.th * cc->a.tb != BM)
+    return static_cast<int>(cudaErrorInvalidValue);
   if (cc->a.mode == 2 && cc->a.tw * cc->a.th * cc->a.tb != BK) return static_cast<int>(cudaErrorInvalidValue);
-  if (cc->b.mode == 2 && cc->b.tw * cc->b.th * cc->b.tb != BK) return static_cast<int>(cudaErrorInvalidValue);
-  if (cc->o.on && cc->a.mode != 1) return static_cast<int>(cudaErrorInvalidValue);
+  if ((cc->b.mode == 2 || cc->b.mode == 3) && cc->b.tw * cc->b.th * cc->b.tb != BK)
+    return static_cast<int>(cudaErrorInvalidValue);
+  // mode 3 slabs: 16-channel boxes (32-byte rows); B spans whole taps of 16 columns
+  if (cc->a.mode == 3 && (!ad || ad->box[0] != 16)) return static_cast<int>(cudaErrorInvalidValue);
+  if (cc->b.mode == 3 && (!bd || bd->box[0] != 16 || bn != 64)) return static_cast<int>(cudaErrorInvalidValue);
+  if (cc->o.on && cc->a.mode != 1 && cc->a.mode != 3) return static_cast<int>(cudaErrorInvalidValue);
   if (cc->o.cls_cols && (cc->o.cls_cols % 32 || N != cc->o.cls_cols * cc->o.ys * cc->o.xs))
     return static_cast<int>(cudaErrorInvalidValue);
   if (ep->act_split < N && (ep->act_split & 31)) return static_cast<int>(cudaErrorInvalidValue);

@@ -22,7 +22,7 @@ Conv weights are stored (out, kh, kw, in) — the GEMM's patch order.
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass, field, replace
 from typing import Optional
 
 import numpy as np
@@ -113,6 +113,21 @@ class NetConfig:
         d["conv"] = tuple(tuple(c) for c in d["conv"])
         d["mlp"] = tuple(d["mlp"])
         return cls(**d)
+
+
+def space_to_depth_config(cfg: NetConfig) -> NetConfig:
+    """The same network on the 4x4 space-to-depth image: an H x W x C depth
+    image becomes H/4 x W/4 x 16C (pixel (r, c) -> super-pixel (r/4, c/4),
+    channel ((r%4)*4 + c%4) * C + ch), and a first layer with kernel 4k' and
+    stride 4 becomes kernel k', stride 1 over it — the identical convolution
+    (the weight tensor is the same 64 numbers per output channel in
+    (kh', kw', r, c) order). The depth camera renders this layout directly, and
+    the tensor cores read its 16-channel taps as 32-byte slabs."""
+    k, s_, co = cfg.conv[0]
+    if cfg.img_h % 4 or cfg.img_w % 4 or k % 4 or s_ != 4:
+        raise ValueError("space-to-depth needs H, W multiples of 4 and a first layer of stride 4, kernel 4k")
+    return replace(cfg, img_h=cfg.img_h // 4, img_w=cfg.img_w // 4, img_c=cfg.img_c * 16,
+                   conv=((k // 4, 1, co),) + tuple(cfg.conv[1:]))
 
 
 def _param_specs(cfg: NetConfig):
@@ -277,15 +292,21 @@ class Workspace:
         self.B = batch
         self.col, self.y, self.dcol, self.dy, self.wt = [], [], [], [], []
         self.implicit = [False] * len(cfg.conv)
+        self.img = None                         # conv1 input of the last forward (implicit weight gradient)
         if cfg.vision:
             from ..ops.conv import SLACK_BYTES, ConvShape
             shapes = cfg.conv_shapes()
             for i, g in enumerate(shapes):
                 rows = batch * g["OH"] * g["OW"]
                 sh = ConvShape(batch, g["H"], g["W"], g["C"], g["k"], g["s"], g["CO"])
-                # implicit GEMM (no patch matrix) wherever the input has >= 32
-                # channels; the first layer (one depth channel) keeps im2col
-                imp = i > 0 and net.implicit_conv and sh.supported() and sh.CO == 64 and sh.k % sh.s == 0
+                # implicit GEMM (no patch matrix) wherever the kernel has an
+                # operand mode for the input: >= 32 channels, or the 16-channel
+                # space-to-depth depth image of the first layer (forward and
+                # weight gradient only: the image needs no gradient)
+                if i == 0:
+                    imp = net.implicit_conv and sh.supported() and (sh.slabs or sh.C == 64) and sh.CO <= 64
+                else:
+                    imp = net.implicit_conv and sh.supported() and sh.CO == 64 and sh.k % sh.s == 0
                 self.implicit[i] = imp
                 patch = g["k"] * g["k"] * g["C"]
                 self.col.append(None if imp else torch.empty(rows, patch, dtype=bf, device=dev))
@@ -336,6 +357,8 @@ def forward_gpu(net: "PolicyNet", ws: Workspace, scal16: torch.Tensor, img16: Op
             rows = B * g["OH"] * g["OW"]
             if ws.implicit[i]:
                 sh = CV.ConvShape(B, g["H"], g["W"], g["C"], g["k"], g["s"], g["CO"])
+                if i == 0:
+                    ws.img = x                  # the weight gradient reads the image again
                 CV.conv_forward(x, sh, w(f"conv{i + 1}.w"), net.p(f"conv{i + 1}.b"), ws.y[i][:rows])
             else:
                 col = G.im2col(x, B, g["H"], g["W"], g["C"], g["k"], g["s"], out=ws.col[i][:rows])
@@ -391,7 +414,7 @@ def backward_gpu(net: "PolicyNet", ws: Workspace, scal16: torch.Tensor, B: Optio
             prev_rows = B * g["H"] * g["W"]
             if ws.implicit[i]:
                 sh = CV.ConvShape(B, g["H"], g["W"], g["C"], g["k"], g["s"], g["CO"])
-                CV.conv_weight_grad(dy, ws.y[i - 1], sh, net.g(f"conv{i + 1}.w"))
+                CV.conv_weight_grad(dy, ws.y[i - 1] if i > 0 else ws.img, sh, net.g(f"conv{i + 1}.w"))
             else:
                 _wgrad(G, dy, ws.col[i][:rows], net.g(f"conv{i + 1}.w"), rows)
             G.colsum(dy, net.g(f"conv{i + 1}.b"))

@@ -68,6 +68,9 @@ _lib.register(NLIB, {
 })
 
 SLACK_BYTES = 128          # allocate activations with this much room after the last element
+# Kernel diagnostics for timing studies only (Epilogue.dbg): bit 0 skips the
+# epilogue's stores, bit 1 skips the MMAs. Results are wrong when non-zero.
+DEBUG = 0
 
 
 def _cdiv(a, b):
@@ -101,11 +104,18 @@ class ConvShape:
 
     @property
     def superpixel(self) -> int:
-        return 64 // self.C
+        return 64 // self.C if self.C in (32, 64) else 1
+
+    @property
+    def slabs(self) -> bool:
+        """16-channel input: taps load as 32-byte-swizzled slabs (kernel mode 3)."""
+        return self.C == 16
 
     def supported(self) -> bool:
         if self.C == 64:
             return True
+        if self.C == 16:                  # 4 taps per 64-wide k-block
+            return self.k % 2 == 0
         return self.C == 32 and self.s == 2 and self.k % 2 == 0
 
 
@@ -136,7 +146,7 @@ def _input_map(x: torch.Tensor, sh: ConvShape, tw: int, th: int, tb: int) -> Map
     else:
         d.dims[:] = [sh.C, sh.W, sh.H, sh.B]
         d.strides[:] = [sh.C * 2, sh.W * sh.C * 2, sh.H * sh.W * sh.C * 2]
-        d.box[:] = [64, tw * sh.s, th * sh.s, tb]
+        d.box[:] = [min(64, sh.C), tw * sh.s, th * sh.s, tb]     # 16 channels: one 32-byte slab row
         d.estr[:] = [1, sh.s, sh.s, 1]
     return d
 
@@ -164,6 +174,7 @@ def _epilogue(out, accumulate=False, bias=None, act="none", aux=None, ld=None) -
         ep.aux = ptr(aux)
         ep.ld_aux = ld if ld is not None else aux.shape[-1]
     ep.err = ptr(error_flag(out.device))
+    ep.dbg = int(DEBUG)
     return ep
 
 
@@ -182,7 +193,7 @@ def conv_forward(x: torch.Tensor, sh: ConvShape, w16: torch.Tensor, bias: torch.
     p = sh.superpixel
     tw, th, tb = _tile(sh.OW, sh.OH, 128)
     cc = ConvCfg()
-    cc.a.mode, cc.a.tw, cc.a.th, cc.a.tb = 1, tw, th, tb
+    cc.a.mode, cc.a.tw, cc.a.th, cc.a.tb = (3 if sh.slabs else 1), tw, th, tb
     cc.a.tiles_w, cc.a.tiles_h = _cdiv(sh.OW, tw), _cdiv(sh.OH, th)
     cc.a.sw, cc.a.sh = (1 if p == 2 else sh.s), sh.s
     cc.a.kw_n = sh.k // p
@@ -193,8 +204,8 @@ def conv_forward(x: torch.Tensor, sh: ConvShape, w16: torch.Tensor, bias: torch.
     ad = _input_map(x, sh, tw, th, tb)
     ep = _epilogue(out, bias=bias, act=act, ld=sh.CO)
     K = sh.k * sh.k * sh.C
-    _run(x, ad, 0, w16, None, 0, ntiles * 128, sh.CO, K, ep, cc, bn=64 if sh.CO <= 64 else 128,
-         ldb=w16.stride(0), dev=x.device)
+    bn = 32 if sh.CO <= 32 else (64 if sh.CO <= 64 else 128)
+    _run(x, ad, 0, w16, None, 0, ntiles * 128, sh.CO, K, ep, cc, bn=bn, ldb=w16.stride(0), dev=x.device)
     return out
 
 
@@ -208,13 +219,15 @@ def conv_weight_grad(dy: torch.Tensor, x: torch.Tensor, sh: ConvShape, gw: torch
     for g in (cc.a, cc.b):
         g.mode, g.tw, g.th, g.tb = 2, tw, th, tb
         g.tiles_w, g.tiles_h = _cdiv(sh.OW, tw), _cdiv(sh.OH, th)
+    if sh.slabs:
+        cc.b.mode = 3
     cc.b.sw, cc.b.sh = (1 if p == 2 else sh.s), sh.s
     cc.b.kw_n = sh.k // p
     ktiles = cc.a.tiles_w * cc.a.tiles_h * _cdiv(sh.B, tb)
     ad = _grid_map(dy, sh.CO, sh.OW, sh.OH, sh.B, tw, th, tb)
     bd = _input_map(x, sh, tw, th, tb)
     N = sh.k * sh.k * sh.C
-    bn = 256 if N >= 256 else (128 if N >= 128 else 64)
+    bn = 64 if sh.slabs else (256 if N >= 256 else (128 if N >= 128 else 64))
     if not splits:
         tiles = _cdiv(N, bn)
         splits = max(1, min(ktiles, 296 // max(tiles, 1)))

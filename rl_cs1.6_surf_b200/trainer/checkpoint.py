@@ -32,7 +32,7 @@ from .config import RUN_DEFINING, TrainConfig
 FORMAT = "surfb200-ckpt-1"
 
 # keys whose change alters parameter shapes: never overridden on resume
-SHAPE_KEYS = ("vision", "lidar_w", "lidar_h", "surf_mask", "frame_stack", "heads", "continuous_yaw", "gps", "hidden",
+SHAPE_KEYS = ("vision", "lidar_w", "lidar_h", "vision_s2d", "surf_mask", "frame_stack", "heads", "continuous_yaw", "gps", "hidden",
               "fc", "proprio", "mlp")
 
 

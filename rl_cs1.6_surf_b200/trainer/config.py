@@ -17,7 +17,7 @@ RUN_DEFINING = (
     "map", "map_seed", "ep_ticks", "n_steps", "act_every", "epochs", "minibatches", "lr", "gamma", "gae", "clip",
     "ent", "ent_final", "vf", "max_grad_norm", "spawn", "teleport_fail", "yaw_jitter", "maxvel", "airaccelerate",
     "vision", "lidar_w", "lidar_h", "lidar_range", "lidar_near", "lidar_cell", "pinhole", "march_steps",
-    "surf_mask", "frame_stack",
+    "vision_s2d", "surf_mask", "frame_stack",
     "continuous_yaw", "gps", "heads", "hidden", "fc", "proprio", "mlp", "reward", "pitch_rate", "yaw_adaptive",
     "respawn_frac", "respawn_margin", "respawn_reservoir", "train_stride", "drop_frac", "drop_min", "drop_max",
     "punch_min", "punch_max", "respawn_speed", "respawn_binned", "respawn_pool", "rnd_coef",
@@ -67,6 +67,7 @@ class TrainConfig:
     lidar_cell: float = 16.0
     pinhole: bool = False
     march_steps: int = 64
+    vision_s2d: bool = True            # camera renders 4x4 space-to-depth; conv1 runs as an implicit GEMM on it
     surf_mask: bool = False            # second image channel: the hit surface's |n_z| (floor / ramp / wall)
     frame_stack: int = 0               # K > 1: current frame + the decisions 1, 2, 4, 8 back as K channels
     # network
@@ -113,6 +114,8 @@ class TrainConfig:
     def from_dict(cls, d: dict) -> "TrainConfig":
         kw = {}
         names = {f.name for f in fields(cls)}
+        if "vision_s2d" not in d:
+            kw["vision_s2d"] = False          # saved before the space-to-depth layout: NHW image, 8x8 conv1
         for k, v in d.items():
             if k not in names:
                 continue

@@ -31,7 +31,8 @@ from typing import Optional
 import numpy as np
 import torch
 
-from ..models.policy import HeadLayout, NetConfig, PolicyNet, Workspace, backward_gpu, forward_gpu
+from ..models.policy import (HeadLayout, NetConfig, PolicyNet, Workspace, backward_gpu, forward_gpu,
+                             space_to_depth_config)
 from ..ops import rl as R
 from ..rewards.spec import CpuReward, GpuReward, RewardSpec
 from ..sim import mapgen
@@ -153,6 +154,9 @@ class Trainer:
                          img_c=self.frame_ch * self.n_frames, n_scalar=len(self.feat_idx),
                          scalar_pad=16, fc=cfg.fc, proprio=cfg.proprio, hidden=cfg.hidden, mlp=tuple(cfg.mlp),
                          heads=self.layout)
+        self.s2d = bool(cfg.vision and cfg.vision_s2d and self.gpu)
+        if self.s2d:
+            ncfg = space_to_depth_config(ncfg)
         self.net = PolicyNet(ncfg, self.device, seed=cfg.seed)
         if self.comm is not None:
             self.comm.broadcast_params(self.net)
@@ -174,9 +178,11 @@ class Trainer:
                 self._log(f"surface mask: {h['surfaced']:,} surfaced voxels ({h['surfable']:,} surfable, "
                           f"{h['walkable'] + h['flat']:,} walkable)")
                 del lin
+            from ..ops.vision import LAYOUT_NHW, LAYOUT_S2D4
             self.camera = DepthCamera(self.volume, cfg.lidar_w, cfg.lidar_h, range_units=cfg.lidar_range,
                                       near_range=cfg.lidar_near, max_steps=cfg.march_steps, pinhole=cfg.pinhole,
-                                      dtype=torch.bfloat16, surf_nz=self.surf_nz)
+                                      dtype=torch.bfloat16, surf_nz=self.surf_nz,
+                                      layout=LAYOUT_S2D4 if self.s2d else LAYOUT_NHW)
         self._log(f"policy: {self.net.n_params:,} parameters, heads {self.layout.heads}"
                   f"{' + continuous yaw' if self.layout.continuous_yaw else ''}")
 

@@ -13,7 +13,9 @@ pytestmark = pytest.mark.gpu
 
 SHAPES = [CV.ConvShape(B=6, H=15, W=31, C=32, k=4, s=2, CO=64),      # the policy's conv2
           CV.ConvShape(B=5, H=6, W=14, C=64, k=3, s=1, CO=64),       # the policy's conv3
-          CV.ConvShape(B=3, H=9, W=20, C=64, k=3, s=2, CO=64)]
+          CV.ConvShape(B=3, H=9, W=20, C=64, k=3, s=2, CO=64),
+          CV.ConvShape(B=7, H=16, W=32, C=16, k=2, s=1, CO=32),      # conv1 on the space-to-depth image
+          CV.ConvShape(B=3, H=16, W=32, C=64, k=2, s=1, CO=32)]      # conv1 with four stacked frames
 
 
 def _nhwc(sh, gen, slack=True):
@@ -66,6 +68,8 @@ def test_weight_grad(sh):
 def test_input_grad(sh):
     if sh.k % sh.s:
         pytest.skip("parity classes need k divisible by the stride")
+    if sh.CO != 64 or sh.C % 32:
+        pytest.skip("first-layer shapes: the image needs no input gradient")
     g = torch.Generator(device="cuda").manual_seed(3)
     buf, x = _nhwc(sh, g)
     x_act = torch.relu(x.float()).to(torch.bfloat16).reshape(-1, sh.C).contiguous()

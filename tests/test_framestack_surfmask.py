@@ -229,3 +229,26 @@ def test_frame_stack_kernel_modes(K, C0):
     tt, nn = (idx // N).cpu(), (idx % N).cpu()
     ref2 = FS.stack_reference(frames.cpu(), K, nn, st.pro + tt, ages.cpu()[idx.cpu()], fr=fr, channels=C0)
     assert torch.equal(out2.cpu(), ref2)
+
+
+def test_space_to_depth_network_is_the_same_convolution():
+    """conv1 (8x8, stride 4) on the H x W image == conv1 (2x2, stride 1) on the
+    4x4 space-to-depth image with the weights in (kh', kw', r, c) order."""
+    from surfb200.models.policy import space_to_depth_config
+    from surfb200.ops.vision import to_s2d4
+    base = NetConfig()
+    s2d = space_to_depth_config(base)
+    assert (s2d.img_h, s2d.img_w, s2d.img_c) == (16, 32, 16) and s2d.conv[0] == (2, 1, 32)
+    assert [g["OH"] for g in s2d.conv_shapes()] == [g["OH"] for g in base.conv_shapes()]
+    a, b = PolicyNet(base, "cpu", seed=0), PolicyNet(s2d, "cpu", seed=1)
+    assert a.numel == b.numel
+    pa = {n: a.p(n) for n, *_ in a.specs}
+    pb = dict(pa)
+    w = pa["conv1.w"].view(32, 2, 4, 2, 4)                      # co, kh', r, kw', c
+    pb["conv1.w"] = w.permute(0, 1, 3, 2, 4).reshape(32, 64)     # co, kh', kw', r, c
+    img = torch.rand(3, 64 * 128)
+    ya = a.forward_reference(torch.zeros(3, 16), img, pa)
+    yb = b.forward_reference(torch.zeros(3, 16), to_s2d4(img, 64, 128), pb)
+    torch.testing.assert_close(ya, yb, rtol=1e-4, atol=1e-5)
+    from surfb200.trainer.config import TrainConfig
+    assert TrainConfig().vision_s2d and not TrainConfig.from_dict({"map": "field"}).vision_s2d

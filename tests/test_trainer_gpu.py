@@ -44,7 +44,7 @@ def test_frame_stack_and_surface_mask_training(stack, mask):
     cfg = TrainConfig(map="field", envs=256, n_steps=16, act_every=3, epochs=1, minibatches=4, ep_ticks=60,
                       frame_stack=stack, surf_mask=mask, reward=RewardSpec(mode="speed"))
     tr = Trainer(cfg, verbose=False)
-    assert tr.net.cfg.img_c == (2 if mask else 1) * max(stack, 1)
+    assert tr.net.cfg.img_c == (16 if tr.s2d else 1) * (2 if mask else 1) * max(stack, 1)
     N, T = tr.N, tr.T
     s = tr.train_iteration()
     assert math.isfinite(s["policy_loss"]) and torch.isfinite(tr.net.flat).all()
