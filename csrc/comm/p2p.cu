@@ -238,31 +238,29 @@ __global__ void __launch_bounds__(256) grad_step_kernel(Plan P) {
   const int64_t lo = static_cast<int64_t>(P.rank) * P.shard;
   const int64_t hi = lo + P.shard < P.n ? lo + P.shard : P.n;
   const int64_t cnt = hi > lo ? hi - lo : 0;
-  const int64_t n8 = cnt >> 3;                          // 8-element groups (the shard start is 32-byte aligned)
+  // 4-element groups (the shard start is 32-byte aligned): one float4 per
+  // thread and array, so every warp-wide load or store (peer memory
+  // included) covers 512 contiguous bytes
+  const int64_t n4 = cnt >> 2;
   const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   float* mine = P.grad_peer[P.rank];
   // B: reduce-scatter of the owned shard
   double ss = 0.0;
-  for (int64_t j = tid; j < n8; j += stride) {
-    const int64_t i = lo + 8 * j;
-    float4 v0[kMaxW], v1[kMaxW];
+  for (int64_t j = tid; j < n4; j += stride) {
+    const int64_t i = lo + 4 * j;
+    float4 v[kMaxW];
 #pragma unroll
-    for (int q = 0; q < kMaxW; ++q) {
-      if (q < P.world) {
-        v0[q] = *reinterpret_cast<const float4*>(P.grad_peer[q] + i);
-        v1[q] = *reinterpret_cast<const float4*>(P.grad_peer[q] + i + 4);
-      }
-    }
-    float4 a0 = v0[0], a1 = v1[0];
+    for (int q = 0; q < kMaxW; ++q)
+      if (q < P.world) v[q] = *reinterpret_cast<const float4*>(P.grad_peer[q] + i);
+    float4 a = v[0];
 #pragma unroll
     for (int q = 1; q < kMaxW; ++q)
-      if (q < P.world) { add4(a0, v0[q]); add4(a1, v1[q]); }
-    *reinterpret_cast<float4*>(mine + i) = a0;
-    *reinterpret_cast<float4*>(mine + i + 4) = a1;
-    ss += sq4(a0) + sq4(a1);
+      if (q < P.world) add4(a, v[q]);
+    *reinterpret_cast<float4*>(mine + i) = a;
+    ss += sq4(a);
   }
-  for (int64_t i = lo + 8 * n8 + tid; i < hi; i += stride) {
+  for (int64_t i = lo + 4 * n4 + tid; i < hi; i += stride) {
     float a = P.grad_peer[0][i];
     for (int q = 1; q < P.world; ++q) a += P.grad_peer[q][i];
     mine[i] = a;
@@ -280,11 +278,16 @@ __global__ void __launch_bounds__(256) grad_step_kernel(Plan P) {
     double part = 0.0;
     for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) part += partial[b];
     const double tot_b = block_sum(part);
-    if (threadIdx.x == 0) {
-      for (int q = 0; q < P.world; ++q)
-        st_relaxed_sys(reinterpret_cast<double*>(P.sync_peer[q] + kNormSlots) + par * kMaxW + P.rank, tot_b);
-      __threadfence_system();
-      for (int q = 0; q < P.world; ++q) st_release_sys(P.sync_peer[q] + flag_word(kFNorm, P.rank), target);
+    __shared__ double s_tot;
+    if (threadIdx.x == 0) s_tot = tot_b;
+    __syncthreads();
+    // one thread per peer: its norm slot, then its flag with release order
+    // (a single thread releasing to every peer in turn would serialise one
+    // system-scope fence per peer and skew the peers' wake-ups)
+    if (static_cast<int>(threadIdx.x) < P.world) {
+      const int q = threadIdx.x;
+      st_relaxed_sys(reinterpret_cast<double*>(P.sync_peer[q] + kNormSlots) + par * kMaxW + P.rank, s_tot);
+      st_release_sys(P.sync_peer[q] + flag_word(kFNorm, P.rank), target);
     }
   }
   if (!block_wait_all(P, kFNorm, target, 0x200)) return;
@@ -320,31 +323,24 @@ __global__ void __launch_bounds__(256) grad_step_kernel(Plan P) {
   auto pack2 = [](float a, float b) {
     return static_cast<uint32_t>(surfk::f32_to_bf16(a)) | (static_cast<uint32_t>(surfk::f32_to_bf16(b)) << 16);
   };
-  for (int64_t j = tid; j < n8; j += stride) {
-    const int64_t i = lo + 8 * j;
-    float4 m0 = *reinterpret_cast<const float4*>(P.m + i), m1 = *reinterpret_cast<const float4*>(P.m + i + 4);
-    float4 w0 = *reinterpret_cast<const float4*>(P.v + i), w1 = *reinterpret_cast<const float4*>(P.v + i + 4);
+  for (int64_t j = tid; j < n4; j += stride) {
+    const int64_t i = lo + 4 * j;
+    float4 m0 = *reinterpret_cast<const float4*>(P.m + i);
+    float4 w0 = *reinterpret_cast<const float4*>(P.v + i);
     const float4 p0 = adam4(*reinterpret_cast<const float4*>(mine + i), m0, w0, *reinterpret_cast<const float4*>(pl + i));
-    const float4 p1 = adam4(*reinterpret_cast<const float4*>(mine + i + 4), m1, w1,
-                            *reinterpret_cast<const float4*>(pl + i + 4));
     *reinterpret_cast<float4*>(P.m + i) = m0;
-    *reinterpret_cast<float4*>(P.m + i + 4) = m1;
     *reinterpret_cast<float4*>(P.v + i) = w0;
-    *reinterpret_cast<float4*>(P.v + i + 4) = w1;
-    const uint4 b = make_uint4(pack2(p0.x, p0.y), pack2(p0.z, p0.w), pack2(p1.x, p1.y), pack2(p1.z, p1.w));
-    const bool all32 = i >= P.push32_from;          // 64-aligned region boundary: never inside a group of 8
+    const uint2 b = make_uint2(pack2(p0.x, p0.y), pack2(p0.z, p0.w));
+    const bool all32 = i >= P.push32_from;          // 64-aligned region boundary: never inside a group of 4
 #pragma unroll
     for (int q = 0; q < kMaxW; ++q) {
       if (q < P.world) {
-        if (all32 || q == P.rank) {
-          *reinterpret_cast<float4*>(P.p_peer[q] + i) = p0;
-          *reinterpret_cast<float4*>(P.p_peer[q] + i + 4) = p1;
-        }
-        *reinterpret_cast<uint4*>(P.p16_peer[q] + i) = b;
+        if (all32 || q == P.rank) *reinterpret_cast<float4*>(P.p_peer[q] + i) = p0;
+        *reinterpret_cast<uint2*>(P.p16_peer[q] + i) = b;
       }
     }
   }
-  for (int64_t i = lo + 8 * n8 + tid; i < hi; i += stride) {
+  for (int64_t i = lo + 4 * n4 + tid; i < hi; i += stride) {
     float mi = P.m[i], vi = P.v[i];
     const float pi = adam1(mine[i], mi, vi, pl[i]);
     P.m[i] = mi;
