@@ -8,6 +8,8 @@
 #pragma once
 #include <cstdint>
 
+#include "hd.hpp"
+
 namespace surf {
 
 constexpr int32_t kBspVersion = 30;
@@ -59,7 +61,7 @@ extern const float kPlayerMaxs[4][3];
 extern const float kHullMins[4][3];
 extern const float kHullMaxs[4][3];
 // pmove usehull -> BSP hull index.
-inline int bsp_hull_of_usehull(int usehull) {
+SURF_HD inline int bsp_hull_of_usehull(int usehull) {
   return usehull == 1 ? 3 : usehull == 2 ? 0 : usehull == 3 ? 2 : 1;
 }
 

@@ -4,8 +4,19 @@
 //
 // All arithmetic is float32 in the same operation order as the engine so that
 // a trace here returns bit-identical fractions/endpoints to the reference core
-// (src/trace.c:12-236) on the same map. Build with -ffp-contract=off.
+// (src/trace.c:12-236) on the same map. Build with -ffp-contract=off (host)
+// or -fmad=false (device). Header-only: the host env and the GPU env compile
+// the same functions (SURF_HD).
+//
+// The descent is the classic GoldSrc pmove hull check: split the segment
+// at each node plane (nudged by DIST_EPSILON toward the near side), recurse into
+// the near child, and if the far side of the split point is solid, report the
+// split plane; if the split point itself lands in solid, back it off in 0.05
+// steps of the parameter. Float expression order matters for parity and is
+// kept identical to the engine's (reference: src/trace.c:26-119).
 #pragma once
+#include <cstring>
+
 #include "map.hpp"
 
 namespace surf {
@@ -22,20 +33,186 @@ struct Trace {
 constexpr float kDistEpsilon = 0.03125f;
 
 // Contents at point p (tree-local coordinates) starting at node `num`.
-int hull_point_contents(const HullView& h, int num, const float p[3]);
+SURF_HD inline int hull_point_contents(const HullView& h, int num, const float p[3]);
 
 // Trace a box (pmove usehull 0 stand, 1 duck, 2 point) through the world and
-// every solid brush entity whose padded bounds overlap the move.
-void trace_player(const Map& m, int usehull, const float start[3], const float end[3], Trace* tr);
+// every solid brush entity whose padded bounds overlap the move:
+//   trace_player(const MapView&, int usehull, start, end, Trace*)
+// Trace against one brush model only (point or player hull):
+//   trace_model(const MapView&, int model, origin, usehull, start, end, Trace*)
+// World hull-0 contents with currents folded into water, then contents volumes:
+//   point_contents(const MapView&, p)
+// True if a player with `usehull` at `origin` is inside trigger t's expanded hull:
+//   trigger_contains(const MapView&, const Trigger&, usehull, origin)
+// The Map overloads at the end forward to the view (host code).
+namespace detail {
 
-// Trace against one brush model only (point or player hull).
-void trace_model(const Map& m, int model, const float origin[3], int usehull, const float start[3],
-                 const float end[3], Trace* tr);
+SURF_HD inline float dot3(const float* a, const float* b) { return a[0] * b[0] + a[1] * b[1] + a[2] * b[2]; }
 
-// World hull-0 contents with currents folded into water, then contents volumes.
-int point_contents(const Map& m, const float p[3]);
+SURF_HD inline float plane_side(const DPlane& pl, const float* p) {
+  return pl.type < 3 ? p[pl.type] - pl.dist : dot3(p, pl.normal) - pl.dist;
+}
 
-// True if a player with `usehull` at `origin` is inside trigger t's expanded hull.
-bool trigger_contains(const Map& m, const Trigger& t, int usehull, const float origin[3]);
+struct HullDescent {
+  const HullView& h;
+  Trace* tr;
+
+  // Returns false once an impact has been recorded (stop walking).
+  SURF_HD bool run(int num, float f1, float f2, const float* p1, const float* p2) {
+    if (num < 0) {
+      if (num == kSolid) {
+        tr->startsolid = true;
+      } else {
+        tr->allsolid = false;
+        if (num == kEmpty) tr->inopen = true; else tr->inwater = true;
+      }
+      return true;
+    }
+    if (h.first >= h.last) {            // empty tree
+      tr->allsolid = false;
+      tr->inopen = true;
+      return true;
+    }
+    const DClipnode& node = h.nodes[num];
+    const DPlane& pl = h.planes[node.plane];
+    float t1 = plane_side(pl, p1);
+    float t2 = plane_side(pl, p2);
+    if (t1 >= 0.f && t2 >= 0.f) return run(node.child[0], f1, f2, p1, p2);
+    float s;
+    if (t1 >= 0.f) {
+      s = t1 - kDistEpsilon;
+    } else {
+      if (t2 < 0.f) return run(node.child[1], f1, f2, p1, p2);
+      s = t1 + kDistEpsilon;
+    }
+    s = s / (t1 - t2);
+    if (s >= 0.f) { if (s > 1.f) s = 1.f; } else { s = 0.f; }
+    const float df = f2 - f1;
+    float fmid = df * s + f1;
+    float mid[3];
+    for (int k = 0; k < 3; ++k) mid[k] = (p2[k] - p1[k]) * s + p1[k];
+    const int near = t1 >= 0.f ? 0 : 1;
+    if (!run(node.child[near], f1, fmid, p1, mid)) return false;
+    if (hull_point_contents(h, node.child[near ^ 1], mid) != kSolid)
+      return run(node.child[near ^ 1], fmid, f2, mid, p2);
+    if (tr->allsolid) return false;
+    if (near) {
+      for (int k = 0; k < 3; ++k) tr->normal[k] = -pl.normal[k];
+      tr->dist = -pl.dist;
+    } else {
+      for (int k = 0; k < 3; ++k) tr->normal[k] = pl.normal[k];
+      tr->dist = pl.dist;
+    }
+    // Back the impact point off until it is outside solid (numeric safety).
+    while (hull_point_contents(h, h.first, mid) == kSolid) {
+      s = static_cast<float>(s - 0.05);
+      if (s < 0.f) break;
+      fmid = df * s + f1;
+      for (int k = 0; k < 3; ++k) mid[k] = (p2[k] - p1[k]) * s + p1[k];
+    }
+    tr->fraction = fmid;
+    for (int k = 0; k < 3; ++k) tr->endpos[k] = mid[k];
+    return false;
+  }
+};
+
+// Sweep one brush model; mirrors the per-entity body of PM_PlayerTrace.
+SURF_HD inline void clip_model(const MapView& m, int model, const float ent_origin[3], int usehull, const float start[3],
+                const float end[3], Trace* out) {
+  HullView h = m.hull(model, bsp_hull_of_usehull(usehull));
+  float off[3], a[3], b[3];
+  for (int k = 0; k < 3; ++k) {
+    off[k] = h.clip_mins[k] - player_mins(usehull, k) + ent_origin[k];
+    a[k] = start[k] - off[k];
+    b[k] = end[k] - off[k];
+  }
+  *out = Trace();
+  out->allsolid = true;
+  out->fraction = 1.f;
+  for (int k = 0; k < 3; ++k) out->endpos[k] = end[k];
+  HullDescent d{h, out};
+  d.run(h.first, 0.f, 1.f, a, b);
+  if (out->allsolid) out->startsolid = true;
+  if (out->startsolid) out->fraction = 0.f;
+  if (out->fraction != 1.f)
+    for (int k = 0; k < 3; ++k) out->endpos[k] = (end[k] - start[k]) * out->fraction + start[k];
+}
+
+}  // namespace detail
+
+SURF_HD inline int hull_point_contents(const HullView& h, int num, const float p[3]) {
+  if (h.first >= h.last) return kEmpty;
+  while (num >= 0) {
+    const DClipnode& node = h.nodes[num];
+    num = detail::plane_side(h.planes[node.plane], p) >= 0.f ? node.child[0] : node.child[1];
+  }
+  return num;
+}
+
+SURF_HD inline void trace_model(const MapView& m, int model, const float origin[3], int usehull, const float start[3],
+                 const float end[3], Trace* tr) {
+  detail::clip_model(m, model, origin, usehull, start, end, tr);
+  tr->ent = 0;
+}
+
+SURF_HD inline void trace_player(const MapView& m, int usehull, const float start[3], const float end[3], Trace* tr) {
+  Trace t;
+  detail::clip_model(m, 0, m.models[0].origin, usehull, start, end, &t);
+  *tr = t;
+  tr->ent = (t.fraction == 1.f && !t.startsolid) ? -1 : 0;
+  const float pad = 40.f;                 // broad-phase margin >= largest hull half-extent
+  float lo[3], hi[3];
+  for (int k = 0; k < 3; ++k) {
+    lo[k] = (start[k] < end[k] ? start[k] : end[k]) - pad;
+    hi[k] = (start[k] > end[k] ? start[k] : end[k]) + pad;
+  }
+  for (int i = 0; i < m.solids.size(); ++i) {
+    const BrushEntity& s = m.solids[i];
+    if (lo[0] > s.absmax[0] || hi[0] < s.absmin[0] || lo[1] > s.absmax[1] || hi[1] < s.absmin[1] ||
+        lo[2] > s.absmax[2] || hi[2] < s.absmin[2])
+      continue;
+    detail::clip_model(m, s.model, s.origin, usehull, start, end, &t);
+    if (t.fraction < tr->fraction) {
+      *tr = t;
+      tr->ent = i + 1;
+    }
+  }
+}
+
+SURF_HD inline int point_contents(const MapView& m, const float p[3]) {
+  HullView h0 = m.hull(0, 0);
+  int c = hull_point_contents(h0, h0.first, p);
+  if (c <= kCurrent0 && c >= kCurrentDown) c = kWater;
+  else if (c == kSolid) return kSolid;
+  for (const BrushEntity& v : m.volumes) {
+    if (v.contents == kEmpty) continue;
+    if (p[0] < v.absmin[0] || p[0] > v.absmax[0] || p[1] < v.absmin[1] || p[1] > v.absmax[1] ||
+        p[2] < v.absmin[2] || p[2] > v.absmax[2])
+      continue;
+    float local[3] = {p[0] - v.origin[0], p[1] - v.origin[1], p[2] - v.origin[2]};
+    HullView vh = m.hull(v.model, 0);
+    if (hull_point_contents(vh, vh.first, local) != kEmpty) return v.contents;
+  }
+  return c;
+}
+
+SURF_HD inline bool trigger_contains(const MapView& m, const Trigger& t, int usehull, const float origin[3]) {
+  HullView h = m.hull(t.model, bsp_hull_of_usehull(usehull));
+  float local[3];
+  for (int k = 0; k < 3; ++k) local[k] = origin[k] - (h.clip_mins[k] - player_mins(usehull, k) + t.origin[k]);
+  return hull_point_contents(h, h.first, local) == kSolid;
+}
+
+inline void trace_player(const Map& m, int usehull, const float start[3], const float end[3], Trace* tr) {
+  trace_player(m.view(), usehull, start, end, tr);
+}
+inline void trace_model(const Map& m, int model, const float origin[3], int usehull, const float start[3],
+                        const float end[3], Trace* tr) {
+  trace_model(m.view(), model, origin, usehull, start, end, tr);
+}
+inline int point_contents(const Map& m, const float p[3]) { return point_contents(m.view(), p); }
+inline bool trigger_contains(const Map& m, const Trigger& t, int usehull, const float origin[3]) {
+  return trigger_contains(m.view(), t, usehull, origin);
+}
 
 }  // namespace surf

@@ -10,52 +10,19 @@
 //     one pinned host buffer and ship it to the GPU with a single async copy;
 //   * a continuous yaw action (degrees-per-tick fraction in [-1, 1]) may
 //     replace the discrete yaw bin;
-//   * a persistent thread pool replaces the per-call OpenMP team.
+//   * a persistent thread pool replaces the per-call OpenMP team;
+//   * the per-env rules live in env_core.hpp (EnvCore, host + device code):
+//     this class owns the host arrays and runs EnvCore over them, the GPU env
+//     (csrc/kernels/env_gpu.cu) runs the same EnvCore over device copies.
 #pragma once
 #include <cstdint>
 #include <memory>
 #include <vector>
 
-#include "movement.hpp"
+#include "env_core.hpp"
 #include "thread_pool.hpp"
 
 namespace surf {
-
-struct EnvConfig {                 // SurfEnvConfig-compatible (128 bytes)
-  int32_t num_envs = 1;
-  int32_t max_episode_ticks = 6000;
-  int32_t lookahead_k = 8;
-  float lookahead_dt = 0.25f;
-  int32_t spawn_mode = 1;          // 0 map spawns, 1 spline curriculum, 2 spawn pool
-  float spawn_curriculum_frac = 0.99f;
-  float yaw_rate_max_deg = 10.f;
-  float yaw_jitter_deg = 5.f;
-  float kill_z = -1e38f;           // <= -1e30 -> world min z - 256
-  int32_t water_fail = 1;
-  float pitch_rate_max_deg = 10.f;
-  int32_t lidar_w = 0, lidar_h = 0;
-  float lidar_hfov_deg = 120.f, lidar_vfov_deg = 90.f, lidar_range = 2000.f;
-  Physics phys;
-  int32_t yaw_adaptive = 0;
-};
-static_assert(sizeof(EnvConfig) == 128, "EnvConfig layout");
-
-constexpr int kObsFixed = 15;
-constexpr int kActionDim = 6;
-// Per-env record written by step_k (float32 columns).
-enum RecCol : int {
-  kRecOrigin = 0, kRecYaw = 3, kRecPitch = 4, kRecDucked = 5, kRecVel = 6, kRecTick = 9,
-  kRecReward = 10, kRecDone = 11, kRecTrunc = 12, kRecGoal = 13, kRecEnded = 14, kRecOnground = 15,
-  kRecCols = 16,
-};
-// Terminal pose of the last episode that ended inside a step_k call.
-enum TermCol : int { kTermOrigin = 0, kTermYaw = 3, kTermPitch = 4, kTermDucked = 5, kTermTick = 6, kTermCols = 8 };
-
-struct RowOut {                    // a strided float32 row target (nullptr = skip)
-  float* ptr = nullptr;
-  int64_t stride = 0;              // floats between consecutive env rows
-  float* row(int i) const { return ptr + static_cast<int64_t>(i) * stride; }
-};
 
 class EnvBatch {
  public:
@@ -67,7 +34,7 @@ class EnvBatch {
 
   int set_waypoints(const float* xyz, int count);
   int set_spawn_pool(const PlayerState* pool, int n);
-  void set_teleport_fail(bool on) { teleport_fail_ = on; }
+  void set_teleport_fail(bool on) { teleport_fail_ = on; sync_core(); }
   void set_goal_box(const float* mins, const float* maxs);
   void force_fail(const uint8_t* mask);
   const uint8_t* goal_hits() const { return goal_hit_.data(); }
@@ -95,21 +62,20 @@ class EnvBatch {
   void pm_step_single(PlayerState* st, const int32_t action[6]);
   void occupancy_grid(const float* mins, float cell, int nx, int ny, int nz, uint8_t* out);
 
+ // The EnvCore over this batch's arrays (rebuilt whenever an array changes).
+  const EnvCore& core() const { return core_; }
+  const std::vector<float>& waypoints() const { return wp_; }
+  const std::vector<float>& cumulative() const { return cum_; }
+  const std::vector<float>& tangents() const { return tang_; }
+  const std::vector<float>& teleport_progress() const { return tele_progress_; }
+  const std::vector<PlayerState>& spawn_pool() const { return spawn_pool_; }
+
  private:
-  struct TickOut { float reward; bool done, trunc, goal; };
-  float yaw_delta(const PlayerState& s, int bin) const;
-  float spline_project(const float* p, int32_t* hint) const;
-  void spline_sample(float u, float* pos, float* tang, int* seg) const;
-  void reset_env(int i);
-  int apply_triggers(int env, PlayerState* s);
-  void write_obs(const PlayerState& s, float last_yd, float last_pd, float* o) const;
+  void sync_core();
   void write_lidar(const PlayerState& s, float* o) const;
-  TickOut tick_env(int i, float yd, float pd, float fmove, float smove, int buttons, bool forced, float* obs_row,
-                   float* term_row, float* term_rec);
 
   std::shared_ptr<const Map> map_;
   EnvConfig cfg_;
-  PlayerMove mover_;
   std::unique_ptr<ThreadPool> pool_;
   int obs_dim_ = kObsFixed;
   float kill_z_ = 0, map_center_[3] = {0, 0, 0};
@@ -128,6 +94,7 @@ class EnvBatch {
   int push_words_ = 1;
   std::vector<uint8_t> goal_hit_, pending_fail_;
   StuckMemo single_memo_;
+  EnvCore core_;
 };
 
 }  // namespace surf

@@ -172,19 +172,27 @@ bool Map::load_memory(const uint8_t* data, size_t size, std::string* err) {
   return parse_entities();
 }
 
-HullView Map::hull(int model, int bsp_hull) const {
-  HullView v;
-  v.planes = planes.data();
-  const DModel& m = models[static_cast<size_t>(model)];
-  if (bsp_hull == 0) {
-    v.nodes = hull0.data();
-    v.last = static_cast<int>(hull0.size()) - 1;
-  } else {
-    v.nodes = clipnodes.data();
-    v.last = static_cast<int>(clipnodes.size()) - 1;
-  }
-  v.first = m.headnode[bsp_hull];
-  for (int k = 0; k < 3; ++k) { v.clip_mins[k] = kHullMins[bsp_hull][k]; v.clip_maxs[k] = kHullMaxs[bsp_hull][k]; }
+namespace {
+template <typename T>
+Span<T> span_of(const std::vector<T>& v) {
+  Span<T> s;
+  s.p = v.data();
+  s.n = static_cast<int32_t>(v.size());
+  return s;
+}
+}  // namespace
+
+MapView Map::view() const {
+  MapView v;
+  v.planes = span_of(planes);
+  v.clipnodes = span_of(clipnodes);
+  v.hull0 = span_of(hull0);
+  v.models = span_of(models);
+  v.solids = span_of(solids);
+  v.volumes = span_of(volumes);
+  v.triggers = span_of(triggers);
+  v.spawns = span_of(spawns);
+  for (int k = 0; k < 3; ++k) { v.world_mins[k] = world_mins[k]; v.world_maxs[k] = world_maxs[k]; }
   return v;
 }
 

@@ -47,13 +47,47 @@ struct BrushEntity {                 // solid brush entity or contents volume
 
 struct SpawnPoint { float origin[3]; float yaw; };
 
+// Plain-pointer view of a loaded map: what the per-player simulation code
+// reads (traces, contents, triggers). The host builds it over Map's vectors;
+// the GPU env builds the same struct over device copies of those arrays.
+struct MapView {
+  Span<DPlane> planes;
+  Span<DClipnode> clipnodes;          // hulls 1..3 of every model
+  Span<DClipnode> hull0;              // render nodes mirrored into clipnode form
+  Span<DModel> models;
+  Span<BrushEntity> solids;
+  Span<BrushEntity> volumes;
+  Span<Trigger> triggers;
+  Span<SpawnPoint> spawns;
+  float world_mins[3] = {0, 0, 0}, world_maxs[3] = {0, 0, 0};
+
+  SURF_HD HullView hull(int model, int bsp_hull) const {
+    HullView v;
+    v.planes = planes.data();
+    const DModel& m = models[model];
+    if (bsp_hull == 0) {
+      v.nodes = hull0.data();
+      v.last = hull0.size() - 1;
+    } else {
+      v.nodes = clipnodes.data();
+      v.last = clipnodes.size() - 1;
+    }
+    v.first = m.headnode[bsp_hull];
+    for (int k = 0; k < 3; ++k) { v.clip_mins[k] = hull_mins(bsp_hull, k); v.clip_maxs[k] = hull_maxs(bsp_hull, k); }
+    return v;
+  }
+};
+
 class Map {
  public:
   // Parse a BSP v30 image. Returns false and fills *err on malformed input.
   bool load_memory(const uint8_t* data, size_t size, std::string* err);
   bool load_file(const std::string& path, std::string* err);
 
-  HullView hull(int model, int bsp_hull) const;
+  HullView hull(int model, int bsp_hull) const { return view().hull(model, bsp_hull); }
+  // Views over the vectors below (valid while the map is alive; a loaded map
+  // never changes).
+  MapView view() const;
 
   std::vector<DPlane> planes;
   std::vector<DClipnode> clipnodes;   // hulls 1..3 of every model
