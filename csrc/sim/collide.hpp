@@ -53,68 +53,150 @@ SURF_HD inline float plane_side(const DPlane& pl, const float* p) {
   return pl.type < 3 ? p[pl.type] - pl.dist : dot3(p, pl.normal) - pl.dist;
 }
 
+#if defined(__CUDA_ARCH__)
+constexpr int kDescentDepth = 64;      // device: local-memory continuation stack
+#else
+constexpr int kDescentDepth = 512;
+#endif
+
+// The recursive descent written as a loop with an explicit stack of pending
+// continuations (a CUDA thread has no deep call stack). Only the non-tail
+// call (into the near child of a straddled node) pushes a frame; the tail
+// calls reuse the current one. Every arithmetic expression is the recursive
+// version's, so results are bit-identical. Returns false once an impact has
+// been recorded. A tree deeper than the stack sets tr->allsolid (and
+// startsolid), reported as a stuck trace; callers check tree depths up front.
 struct HullDescent {
   const HullView& h;
   Trace* tr;
 
-  // Returns false once an impact has been recorded (stop walking).
-  SURF_HD bool run(int num, float f1, float f2, const float* p1, const float* p2) {
-    if (num < 0) {
-      if (num == kSolid) {
-        tr->startsolid = true;
-      } else {
-        tr->allsolid = false;
-        if (num == kEmpty) tr->inopen = true; else tr->inwater = true;
+  struct Frame {
+    int num, near;
+    float f1, f2, s;
+    float p1[3], p2[3];
+  };
+
+  SURF_HD bool run(int num, float f1, float f2, const float* p1_in, const float* p2_in) {
+    Frame stack[kDescentDepth];
+    int sp = 0;
+    float p1[3] = {p1_in[0], p1_in[1], p1_in[2]};
+    float p2[3] = {p2_in[0], p2_in[1], p2_in[2]};
+    bool ret = true, returning = false;
+    for (;;) {
+      if (!returning) {
+        if (num < 0) {
+          if (num == kSolid) {
+            tr->startsolid = true;
+          } else {
+            tr->allsolid = false;
+            if (num == kEmpty) tr->inopen = true; else tr->inwater = true;
+          }
+          ret = true;
+          returning = true;
+          continue;
+        }
+        if (h.first >= h.last) {            // empty tree
+          tr->allsolid = false;
+          tr->inopen = true;
+          ret = true;
+          returning = true;
+          continue;
+        }
+        const DClipnode& node = h.nodes[num];
+        const DPlane& pl = h.planes[node.plane];
+        float t1 = plane_side(pl, p1);
+        float t2 = plane_side(pl, p2);
+        if (t1 >= 0.f && t2 >= 0.f) { num = node.child[0]; continue; }
+        float s;
+        if (t1 >= 0.f) {
+          s = t1 - kDistEpsilon;
+        } else {
+          if (t2 < 0.f) { num = node.child[1]; continue; }
+          s = t1 + kDistEpsilon;
+        }
+        s = s / (t1 - t2);
+        if (s >= 0.f) { if (s > 1.f) s = 1.f; } else { s = 0.f; }
+        const float df = f2 - f1;
+        float fmid = df * s + f1;
+        float mid[3];
+        for (int k = 0; k < 3; ++k) mid[k] = (p2[k] - p1[k]) * s + p1[k];
+        const int near = t1 >= 0.f ? 0 : 1;
+        if (sp == kDescentDepth) {          // deeper than any map this build accepts
+          tr->allsolid = true;
+          tr->startsolid = true;
+          return false;
+        }
+        Frame& fr = stack[sp++];
+        fr.num = num;
+        fr.near = near;
+        fr.f1 = f1;
+        fr.f2 = f2;
+        fr.s = s;
+        for (int k = 0; k < 3; ++k) { fr.p1[k] = p1[k]; fr.p2[k] = p2[k]; }
+        num = node.child[near];             // run(child[near], f1, fmid, p1, mid)
+        f2 = fmid;
+        for (int k = 0; k < 3; ++k) p2[k] = mid[k];
+        continue;
       }
-      return true;
+      // a call returned `ret` to the frame on top of the stack
+      if (sp == 0) return ret;
+      const Frame fr = stack[--sp];
+      if (!ret) continue;                   // if (!run(near ...)) return false;
+      const DClipnode& node = h.nodes[fr.num];
+      const DPlane& pl = h.planes[node.plane];
+      const int near = fr.near;
+      float s = fr.s;
+      const float df = fr.f2 - fr.f1;
+      float fmid = df * s + fr.f1;
+      float mid[3];
+      for (int k = 0; k < 3; ++k) mid[k] = (fr.p2[k] - fr.p1[k]) * s + fr.p1[k];
+      if (hull_point_contents(h, node.child[near ^ 1], mid) != kSolid) {
+        num = node.child[near ^ 1];         // return run(child[near ^ 1], fmid, f2, mid, p2);
+        f1 = fmid;
+        f2 = fr.f2;
+        for (int k = 0; k < 3; ++k) { p1[k] = mid[k]; p2[k] = fr.p2[k]; }
+        returning = false;
+        continue;
+      }
+      ret = false;
+      if (tr->allsolid) continue;
+      if (near) {
+        for (int k = 0; k < 3; ++k) tr->normal[k] = -pl.normal[k];
+        tr->dist = -pl.dist;
+      } else {
+        for (int k = 0; k < 3; ++k) tr->normal[k] = pl.normal[k];
+        tr->dist = pl.dist;
+      }
+      // Back the impact point off until it is outside solid (numeric safety).
+      while (hull_point_contents(h, h.first, mid) == kSolid) {
+        s = static_cast<float>(s - 0.05);
+        if (s < 0.f) break;
+        fmid = df * s + fr.f1;
+        for (int k = 0; k < 3; ++k) mid[k] = (fr.p2[k] - fr.p1[k]) * s + fr.p1[k];
+      }
+      tr->fraction = fmid;
+      for (int k = 0; k < 3; ++k) tr->endpos[k] = mid[k];
     }
-    if (h.first >= h.last) {            // empty tree
-      tr->allsolid = false;
-      tr->inopen = true;
-      return true;
-    }
-    const DClipnode& node = h.nodes[num];
-    const DPlane& pl = h.planes[node.plane];
-    float t1 = plane_side(pl, p1);
-    float t2 = plane_side(pl, p2);
-    if (t1 >= 0.f && t2 >= 0.f) return run(node.child[0], f1, f2, p1, p2);
-    float s;
-    if (t1 >= 0.f) {
-      s = t1 - kDistEpsilon;
-    } else {
-      if (t2 < 0.f) return run(node.child[1], f1, f2, p1, p2);
-      s = t1 + kDistEpsilon;
-    }
-    s = s / (t1 - t2);
-    if (s >= 0.f) { if (s > 1.f) s = 1.f; } else { s = 0.f; }
-    const float df = f2 - f1;
-    float fmid = df * s + f1;
-    float mid[3];
-    for (int k = 0; k < 3; ++k) mid[k] = (p2[k] - p1[k]) * s + p1[k];
-    const int near = t1 >= 0.f ? 0 : 1;
-    if (!run(node.child[near], f1, fmid, p1, mid)) return false;
-    if (hull_point_contents(h, node.child[near ^ 1], mid) != kSolid)
-      return run(node.child[near ^ 1], fmid, f2, mid, p2);
-    if (tr->allsolid) return false;
-    if (near) {
-      for (int k = 0; k < 3; ++k) tr->normal[k] = -pl.normal[k];
-      tr->dist = -pl.dist;
-    } else {
-      for (int k = 0; k < 3; ++k) tr->normal[k] = pl.normal[k];
-      tr->dist = pl.dist;
-    }
-    // Back the impact point off until it is outside solid (numeric safety).
-    while (hull_point_contents(h, h.first, mid) == kSolid) {
-      s = static_cast<float>(s - 0.05);
-      if (s < 0.f) break;
-      fmid = df * s + f1;
-      for (int k = 0; k < 3; ++k) mid[k] = (p2[k] - p1[k]) * s + p1[k];
-    }
-    tr->fraction = fmid;
-    for (int k = 0; k < 3; ++k) tr->endpos[k] = mid[k];
-    return false;
   }
 };
+
+// Depth of a clip tree below `num` (iterative; callers size the descent stack).
+SURF_HD inline int hull_depth(const HullView& h, int num, int limit) {
+  if (num < 0 || h.first >= h.last) return 0;
+  int stack_n[256], stack_d[256];
+  int sp = 0, best = 0;
+  stack_n[sp] = num;
+  stack_d[sp++] = 1;
+  while (sp) {
+    const int n = stack_n[--sp], d = stack_d[sp];
+    if (d > best) best = d;
+    if (best > limit) return best;
+    const DClipnode& node = h.nodes[n];
+    for (int c = 0; c < 2; ++c)
+      if (node.child[c] >= 0 && sp < 256) { stack_n[sp] = node.child[c]; stack_d[sp++] = d + 1; }
+  }
+  return best;
+}
 
 // Sweep one brush model; mirrors the per-entity body of PM_PlayerTrace.
 SURF_HD inline void clip_model(const MapView& m, int model, const float ent_origin[3], int usehull, const float start[3],
