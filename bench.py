@@ -40,6 +40,8 @@ def parse():
     ap.add_argument("--envs", type=int, default=2048)
     ap.add_argument("--comm", choices=["p2p", "nccl"], default="p2p")
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--env-device", choices=["cpu", "cuda"], default="cpu",
+                    help="cpu: C++ env threads + pinned rows (the headline); cuda: the same env rules on the GPU")
     ap.add_argument("--json", default=None)
     ap.add_argument("--timing", action="store_true", help="print per-phase times of each timed iteration to stderr")
     return ap.parse_args()
@@ -111,6 +113,7 @@ def run_ours(args) -> None:
     cfg.graphs = not args.no_graphs
     cfg.seed = 0
     cfg.timing = args.timing
+    cfg.env_device = args.env_device
     tr = Trainer(cfg, rank=rank, world=world, comm=comm, verbose=(rank == 0))
     for _ in range(args.warmup):
         tr.train_iteration()
@@ -145,8 +148,8 @@ def run_ours(args) -> None:
     value = ticks_per_iter * args.steps / (ms / 1e3)
     # end-to-end through the public API: the same iterations, wall clock incl.
     # every host<->device copy of the step (env records in, actions out, stats out)
-    h2d = (cfg.n_steps + 1) * cfg.envs * 64 * 4
-    d2h = cfg.n_steps * cfg.envs * 8 * 4 + 6 * 4 + 8 * 4
+    h2d = (cfg.n_steps + 1) * cfg.envs * 64 * 4 if cfg.env_device == "cpu" else 0
+    d2h = (cfg.n_steps * cfg.envs * 8 * 4 if cfg.env_device == "cpu" else 0) + 6 * 4 + 8 * 4
     e2e = ticks_per_iter * args.steps / wall
     if rank == 0:
         out = {
@@ -159,6 +162,7 @@ def run_ours(args) -> None:
                        "act_every": cfg.act_every, "epochs": cfg.epochs, "minibatches": cfg.minibatches,
                        "map": "procedural random field, 512 brushes, 16u SDF 1024x1024x256",
                        "comm": args.comm if world > 1 else "none", "cuda_graphs": cfg.graphs,
+                       "env_device": cfg.env_device,
                        "l2": "inputs larger than L2 (4.3 GB rollout images per GPU)"},
             "clocks": clocks,
             "e2e": {"value": round(e2e, 1), "unit": "ticks/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},

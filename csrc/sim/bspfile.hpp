@@ -46,12 +46,25 @@ struct DModel {
 };
 #pragma pack(pop)
 
+// Naturally aligned mirrors of the packed records with identical layouts
+// (every field is a 4- or 2-byte value at an aligned offset): the types the
+// simulation code reads through MapView / HullView, so device code loads
+// whole words instead of single bytes.
+struct alignas(4) Plane { float normal[3]; float dist; int32_t type; };
+struct alignas(4) Clipnode { int32_t plane; int16_t child[2]; };
+struct alignas(4) Model {
+  float mins[3], maxs[3], origin[3];
+  int32_t headnode[4]; int32_t visleafs, first_face, num_faces;
+};
+
 static_assert(sizeof(DHeader) == 124, "BSP header");
 static_assert(sizeof(DPlane) == 20, "BSP plane");
 static_assert(sizeof(DClipnode) == 8, "BSP clipnode");
 static_assert(sizeof(DNode) == 24, "BSP node");
 static_assert(sizeof(DLeaf) == 28, "BSP leaf");
 static_assert(sizeof(DModel) == 64, "BSP model");
+static_assert(sizeof(Plane) == sizeof(DPlane) && sizeof(Clipnode) == sizeof(DClipnode) &&
+                  sizeof(Model) == sizeof(DModel), "aligned mirrors keep the packed layouts");
 
 // Player hull boxes by pmove "usehull" (0 stand, 1 duck, 2 point, 3 large).
 // GoldSrc engine constants (pm_shared player_mins/maxs).

@@ -261,3 +261,13 @@ SURFSIM_API int64_t surfsim_compile_bsp(const float* brushes, int64_t nfloats, c
   if (out && static_cast<int64_t>(img.size()) <= cap) std::memcpy(out, img.data(), img.size());
   return static_cast<int64_t>(img.size());
 }
+
+// The env batch's per-env rule set with host pointers (EnvCore bytes) — what a
+// GPU env (libsurf_env.so, same process) copies to the device. Returns
+// sizeof(EnvCore); copies only when cap is large enough.
+SURFSIM_API int32_t surfsim_core_bytes(void* h, void* out, int32_t cap) {
+  const EnvCore& c = ENV(h)->core();
+  const int32_t n = static_cast<int32_t>(sizeof(EnvCore));
+  if (out && cap >= n) std::memcpy(out, &c, sizeof(EnvCore));
+  return n;
+}

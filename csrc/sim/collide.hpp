@@ -49,14 +49,16 @@ namespace detail {
 
 SURF_HD inline float dot3(const float* a, const float* b) { return a[0] * b[0] + a[1] * b[1] + a[2] * b[2]; }
 
-SURF_HD inline float plane_side(const DPlane& pl, const float* p) {
+SURF_HD inline float plane_side(const Plane& pl, const float* p) {
   return pl.type < 3 ? p[pl.type] - pl.dist : dot3(p, pl.normal) - pl.dist;
 }
 
+constexpr int kDescentDepthDevice = 64;   // device: local-memory continuation stack
+constexpr int kDescentDepthHost = 512;
 #if defined(__CUDA_ARCH__)
-constexpr int kDescentDepth = 64;      // device: local-memory continuation stack
+constexpr int kDescentDepth = kDescentDepthDevice;
 #else
-constexpr int kDescentDepth = 512;
+constexpr int kDescentDepth = kDescentDepthHost;
 #endif
 
 // The recursive descent written as a loop with an explicit stack of pending
@@ -102,8 +104,8 @@ struct HullDescent {
           returning = true;
           continue;
         }
-        const DClipnode& node = h.nodes[num];
-        const DPlane& pl = h.planes[node.plane];
+        const Clipnode& node = h.nodes[num];
+        const Plane& pl = h.planes[node.plane];
         float t1 = plane_side(pl, p1);
         float t2 = plane_side(pl, p2);
         if (t1 >= 0.f && t2 >= 0.f) { num = node.child[0]; continue; }
@@ -142,8 +144,8 @@ struct HullDescent {
       if (sp == 0) return ret;
       const Frame fr = stack[--sp];
       if (!ret) continue;                   // if (!run(near ...)) return false;
-      const DClipnode& node = h.nodes[fr.num];
-      const DPlane& pl = h.planes[node.plane];
+      const Clipnode& node = h.nodes[fr.num];
+      const Plane& pl = h.planes[node.plane];
       const int near = fr.near;
       float s = fr.s;
       const float df = fr.f2 - fr.f1;
@@ -191,7 +193,7 @@ SURF_HD inline int hull_depth(const HullView& h, int num, int limit) {
     const int n = stack_n[--sp], d = stack_d[sp];
     if (d > best) best = d;
     if (best > limit) return best;
-    const DClipnode& node = h.nodes[n];
+    const Clipnode& node = h.nodes[n];
     for (int c = 0; c < 2; ++c)
       if (node.child[c] >= 0 && sp < 256) { stack_n[sp] = node.child[c]; stack_d[sp++] = d + 1; }
   }
@@ -199,7 +201,7 @@ SURF_HD inline int hull_depth(const HullView& h, int num, int limit) {
 }
 
 // Sweep one brush model; mirrors the per-entity body of PM_PlayerTrace.
-SURF_HD inline void clip_model(const MapView& m, int model, const float ent_origin[3], int usehull, const float start[3],
+SURF_HD SURF_HD_NOINLINE void clip_model(const MapView& m, int model, const float ent_origin[3], int usehull, const float start[3],
                 const float end[3], Trace* out) {
   HullView h = m.hull(model, bsp_hull_of_usehull(usehull));
   float off[3], a[3], b[3];
@@ -225,7 +227,7 @@ SURF_HD inline void clip_model(const MapView& m, int model, const float ent_orig
 SURF_HD inline int hull_point_contents(const HullView& h, int num, const float p[3]) {
   if (h.first >= h.last) return kEmpty;
   while (num >= 0) {
-    const DClipnode& node = h.nodes[num];
+    const Clipnode& node = h.nodes[num];
     num = detail::plane_side(h.planes[node.plane], p) >= 0.f ? node.child[0] : node.child[1];
   }
   return num;

@@ -11,6 +11,13 @@
 #else
 #define SURF_HD
 #endif
+// Device code: keep one out-of-line copy (one stack frame) of a function that
+// would otherwise be inlined at every call site with its own local arrays.
+#if defined(__CUDA_ARCH__)
+#define SURF_HD_NOINLINE __noinline__
+#else
+#define SURF_HD_NOINLINE inline
+#endif
 
 namespace surf {
 

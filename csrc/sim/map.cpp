@@ -180,14 +180,24 @@ Span<T> span_of(const std::vector<T>& v) {
   s.n = static_cast<int32_t>(v.size());
   return s;
 }
+// The aligned mirror of a packed record array (same bytes; vector storage is
+// at least 8-byte aligned).
+template <typename A, typename D>
+Span<A> span_as(const std::vector<D>& v) {
+  static_assert(sizeof(A) == sizeof(D), "layout");
+  Span<A> s;
+  s.p = reinterpret_cast<const A*>(v.data());
+  s.n = static_cast<int32_t>(v.size());
+  return s;
+}
 }  // namespace
 
 MapView Map::view() const {
   MapView v;
-  v.planes = span_of(planes);
-  v.clipnodes = span_of(clipnodes);
-  v.hull0 = span_of(hull0);
-  v.models = span_of(models);
+  v.planes = span_as<Plane>(planes);
+  v.clipnodes = span_as<Clipnode>(clipnodes);
+  v.hull0 = span_as<Clipnode>(hull0);
+  v.models = span_as<Model>(models);
   v.solids = span_of(solids);
   v.volumes = span_of(volumes);
   v.triggers = span_of(triggers);

@@ -16,8 +16,8 @@ namespace surf {
 
 // One BSP clip tree view: nodes + planes + the box the tree was expanded by.
 struct HullView {
-  const DClipnode* nodes = nullptr;
-  const DPlane* planes = nullptr;
+  const Clipnode* nodes = nullptr;
+  const Plane* planes = nullptr;
   int first = 0, last = 0;          // root node index, last valid node index
   float clip_mins[3] = {0, 0, 0};
   float clip_maxs[3] = {0, 0, 0};
@@ -51,10 +51,10 @@ struct SpawnPoint { float origin[3]; float yaw; };
 // reads (traces, contents, triggers). The host builds it over Map's vectors;
 // the GPU env builds the same struct over device copies of those arrays.
 struct MapView {
-  Span<DPlane> planes;
-  Span<DClipnode> clipnodes;          // hulls 1..3 of every model
-  Span<DClipnode> hull0;              // render nodes mirrored into clipnode form
-  Span<DModel> models;
+  Span<Plane> planes;
+  Span<Clipnode> clipnodes;           // hulls 1..3 of every model
+  Span<Clipnode> hull0;               // render nodes mirrored into clipnode form
+  Span<Model> models;
   Span<BrushEntity> solids;
   Span<BrushEntity> volumes;
   Span<Trigger> triggers;
@@ -64,7 +64,7 @@ struct MapView {
   SURF_HD HullView hull(int model, int bsp_hull) const {
     HullView v;
     v.planes = planes.data();
-    const DModel& m = models[model];
+    const Model& m = models[model];
     if (bsp_hull == 0) {
       v.nodes = hull0.data();
       v.last = hull0.size() - 1;

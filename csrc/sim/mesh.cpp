@@ -79,7 +79,7 @@ static void walk(const Map& map, const HullView& hv, int node, const float offse
     if (node == kSolid) emit_cell(path, verts, tris);
     return;
   }
-  const DClipnode& cn = hv.nodes[node];
+  const Clipnode& cn = hv.nodes[node];
   const DPlane& pl = map.planes[static_cast<size_t>(cn.plane)];
   const double d = static_cast<double>(pl.dist) + pl.normal[0] * static_cast<double>(offset[0]) +
                    pl.normal[1] * static_cast<double>(offset[1]) + pl.normal[2] * static_cast<double>(offset[2]);

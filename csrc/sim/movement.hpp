@@ -601,7 +601,7 @@ struct Mover {
 
   SURF_HD void ladder_move(int idx, int* movetype) {
     const BrushEntity& lad = map.volumes[idx];
-    const DModel& mod = map.models[lad.model];
+    const Model& mod = map.models[lad.model];
     float centre[3], floor_p[3];
     Trace tr;
     for (int i = 0; i < 3; ++i) centre[i] = (mod.mins[i] + mod.maxs[i]) * 0.5f;

@@ -69,6 +69,10 @@ def _targets():
         srcs = [s for s in srcs if Path(s).exists()]
         if srcs:
             t[name] = ("nvcc", srcs, [], ["-lcuda"] if name in ("libsurf_nn.so", "libsurf_comm.so") else [])
+    # the GPU env compiles the simulator's header-only per-env code for the
+    # device; no FMA contraction, so float expressions round as on the host
+    if (CSRC / "kernels" / "env_gpu.cu").exists():
+        t["libsurf_env.so"] = ("nvcc", kern("env_gpu.cu"), ["-fmad=false", "-I", str(CSRC / "sim")], [])
     return t
 
 
@@ -76,6 +80,8 @@ def _digest(compiler: str, srcs: list[str], flags: list[str]) -> str:
     h = hashlib.sha256()
     h.update(" ".join([compiler] + flags).encode())
     dirs = {Path(s).parent for s in srcs}
+    if any(Path(s).name == "env_gpu.cu" for s in srcs):
+        dirs.add(CSRC / "sim")              # the simulator headers it compiles for the device
     files = set(srcs)
     for d in dirs:
         files |= {str(p) for p in d.glob("*.h*")} | {str(p) for p in d.glob("*.cuh")}

@@ -197,6 +197,7 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
         "surfsim_export_hull0": (None, [c_void_p, c_void_p, c_void_p, c_void_p, _P_I]),
         "surfsim_export_mesh": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_int32, _P_I]),
         "surfsim_geodesic": (c_int64, [c_void_p, c_int32, c_int32, c_int32, c_float, c_void_p, c_void_p, c_void_p]),
+        "surfsim_core_bytes": (c_int32, [c_void_p, c_void_p, c_int32]),
         "surfsim_solid_entities": (c_int32, [c_void_p, c_void_p, c_int32]),
         "surfsim_triggers": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32]),
         "surfsim_trigger_contains": (None, [c_void_p, c_int32, c_void_p, c_int64, c_int32, c_void_p]),
@@ -461,6 +462,14 @@ class SimCore:
         self.lib.surfsim_export_hull0(self._h, c_void_p(planes.ctypes.data), c_void_p(types.ctypes.data),
                                       c_void_p(nodes.ctypes.data), ctypes.byref(head))
         return planes, types, nodes, int(head.value)
+
+    def core_bytes(self) -> bytes:
+        """The batch's per-env rule set (EnvCore, host pointers into this core)
+        as raw bytes: what ``GpuEnv`` copies to the device."""
+        n = self.lib.surfsim_core_bytes(self._h, None, 0)
+        buf = ctypes.create_string_buffer(n)
+        self.lib.surfsim_core_bytes(self._h, ctypes.cast(buf, c_void_p), n)
+        return buf.raw
 
     def export_mesh(self):
         """(vertices float32 [V, 3], triangles int32 [T, 3]) of the solid geometry."""

@@ -94,6 +94,7 @@ class TrainConfig:
     device: str = "cuda"
     graphs: bool = True
     env_groups: int = 2                # rollout: env groups alternating host stepping with GPU work
+    env_device: str = "cpu"            # cpu: C++ thread pool + pinned rows; cuda: the same env rules on the GPU
     comm: str = "p2p"                  # p2p (fused NVLink kernels) | nccl (library baseline)
     threads: Optional[int] = None
     run: str = "runs/default"

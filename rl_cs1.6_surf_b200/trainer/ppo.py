@@ -128,6 +128,16 @@ class Trainer:
         end = self.zones.get("end") if self.zones else None
         if end:
             self.core.set_goal_box(end["mins"], end["maxs"])
+        self.genv = None
+        if cfg.env_device == "cuda":
+            if not self.gpu:
+                raise ValueError("env_device cuda needs the GPU trainer (device cuda)")
+            if cfg.respawn_frac > 0:
+                raise ValueError("the respawn reservoir snapshots host env states: use env_device cpu with it")
+            from ..sim.gpu_env import GpuEnv
+            self.genv = GpuEnv(self.core, self.device)
+        elif cfg.env_device != "cpu":
+            raise ValueError(f"env_device must be cpu or cuda, got {cfg.env_device!r}")
         self.bounds = self.core.map_bounds()
         self.field = None
         self.d0 = None
@@ -230,6 +240,15 @@ class Trainer:
             step = N // G
             self.groups = [(g * step, (g + 1) * step) for g in range(G)]
             self.ws_grp = [Workspace(self.net, step) for _ in range(G)]
+            if self.genv is not None:
+                if self.stacker is not None:
+                    raise ValueError("frame stacking steps its reach-back on the host bootstrap: use env_device cpu")
+                self.boot_cap = min(step, 64)
+                self.ws_boot = Workspace(self.net, self.boot_cap)
+                self.boot_scal = torch.zeros((self.boot_cap, 16), dtype=torch.bfloat16, device=dev)
+                self.boot_img = torch.zeros((self.boot_cap, max(self.frame, 8)), dtype=torch.bfloat16, device=dev) \
+                    if cfg.vision else None
+                self.boot_overflow = torch.zeros((), dtype=torch.int64, device=dev)
             self.stk_grp = [torch.zeros((step, self.img_w), dtype=torch.bfloat16, device=dev) for _ in range(G)] \
                 if self.stacker is not None else None
             self.grp_events = [torch.cuda.Event() for _ in range(G)]
@@ -309,7 +328,15 @@ class Trainer:
 
     def reset(self) -> None:
         """Reset every env and write the spawn records (first decision)."""
-        obs = self.core.reset(self.cfg.seed * 1009 + self.rank * 100_003)
+        seed = self.cfg.seed * 1009 + self.rank * 100_003
+        if self.genv is not None:
+            self.hdev.zero_()
+            self.genv.reset(seed, obs=self.hdev[:, C_OBS:C_OBS + 15], rec=self.hdev[:, C_REC:C_REC + REC_COLS])
+            self.reward.init(self.hdev[:, C_REC:C_REC + REC_COLS])
+            if self.stacker is not None:
+                self.age_cur.zero_()
+            return
+        obs = self.core.reset(seed)
         st = self.core.states_view
         h = self.hrec.numpy()
         h[:] = 0
@@ -336,15 +363,18 @@ class Trainer:
                                                           obs.shape[0], None, 0, stream_ptr(obs.device)),
               "surf_obs_features")
 
-    def _group_body(self, g: int, t: int) -> None:
+    def _group_body(self, g: int, t: int, env: bool = True) -> None:
         """GPU work of env group g at decision slot t (t == T: the rollout
-        tail): upload the group's host records, reward of the previous
-        decision, depth render + features, policy forward, then sampling and
-        the async copy of the actions to pinned memory (or, at the tail, the
-        bootstrap value)."""
+        tail): upload the group's host records (GPU env: step the group's envs
+        unless ``env`` is False), reward of the previous decision, depth
+        render + features, policy forward, then sampling and the async copy of
+        the actions to pinned memory (or, at the tail, the bootstrap value)."""
         lo, hi = self.groups[g]
         T = self.T
-        self.hdev[lo:hi].copy_(self.hrec[lo:hi], non_blocking=True)
+        if self.genv is None:
+            self.hdev[lo:hi].copy_(self.hrec[lo:hi], non_blocking=True)
+        elif t > 0 and env:               # the env steps on the GPU with the previous decision's actions
+            self._env_body(g, t)
         if t > 0:
             last = g == len(self.groups) - 1
             self.reward(self.hdev[lo:hi, C_REC:C_REC + REC_COLS], self.b_rew[t - 1, lo:hi], self.b_done[t - 1, lo:hi],
@@ -370,7 +400,8 @@ class Trainer:
                            self.seed_base ^ (0x9E3779B97F4A7C15 * (g + 1) & 0xFFFFFFFFFFFF), 0,
                            value_src=out[:, vc], value_out=self.b_val[t, lo:hi], fail_src=self.reward.stall[lo:hi],
                            counter_ptr=self.sample_counter, counter_offset=t)
-            self.act_pin[lo:hi].copy_(self.b_act[t, lo:hi], non_blocking=True)
+            if self.genv is None:
+                self.act_pin[lo:hi].copy_(self.b_act[t, lo:hi], non_blocking=True)
         else:
             self.last_val[lo:hi].copy_(out[:, vc])
             if g == len(self.groups) - 1:
@@ -391,17 +422,29 @@ class Trainer:
         from ..ops import _lib
         self.rew_graphs = []
         self.graph_launches = []
+        self.env_graphs, self.env_launches = [], []
+        split = self.genv is not None          # GPU env: env steps and compute as separate graphs (two streams)
         for g in range(len(self.groups)):
             row, counts = [], []
+            erow, ecounts = [None], [0]
             for t in range(T + 1):
                 gr = torch.cuda.CUDAGraph()
                 c0 = _lib.launch_count()
                 with torch.cuda.graph(gr, stream=s):
-                    self._group_body(g, t)
+                    self._group_body(g, t, env=not split)
                 counts.append(_lib.launch_count() - c0)
                 row.append(gr)
+                if split and t > 0:
+                    ge = torch.cuda.CUDAGraph()
+                    c0 = _lib.launch_count()
+                    with torch.cuda.graph(ge, stream=s):
+                        self._env_body(g, t)
+                    ecounts.append(_lib.launch_count() - c0)
+                    erow.append(ge)
             self.rew_graphs.append(row)
             self.graph_launches.append(counts)
+            self.env_graphs.append(erow)
+            self.env_launches.append(ecounts)
         torch.cuda.synchronize()
         self.reset()                      # the warm-up touched env-facing reward state
         self._log(f"captured {len(self.groups) * (T + 1)} rollout graphs ({len(self.groups)} env groups)")
@@ -425,6 +468,38 @@ class Trainer:
                                yaw_slot=6 if self.layout.continuous_yaw else -1, fail_slot=7,
                                obs=(base + 4 * C_OBS, stride), term_obs=(base + 4 * C_TOBS, stride),
                                rec=(base + 4 * C_REC, stride), term_rec=(base + 4 * C_TREC, stride))
+
+    def _env_body(self, g: int, t: int) -> None:
+        """GPU env: K ticks of group g's envs with decision t-1's action rows,
+        writing the observation and record rows in place, then the truncation
+        bootstrap. Runs on the env stream, beside the other group's compute."""
+        lo, hi = self.groups[g]
+        h = self.hdev
+        self.genv.step_k(self.b_act[t - 1], self.K, lo, hi, yaw_slot=6 if self.layout.continuous_yaw else -1,
+                         fail_slot=7, obs=h[:, C_OBS:C_OBS + 15], term_obs=h[:, C_TOBS:C_TOBS + 15],
+                         rec=h[:, C_REC:C_REC + REC_COLS], term_rec=h[:, C_TREC:C_TREC + 8])
+        if self.cfg.ep_ticks:
+            self._bootstrap_truncations_gpu(lo, hi)
+
+    def _bootstrap_truncations_gpu(self, lo: int, hi: int) -> None:
+        """Device-side twin of _bootstrap_truncations for envs [lo, hi): up to
+        boot_cap truncated envs (stable order) get gamma * V(terminal state)
+        staged for the next reward kernel, with no host round trip; more in
+        one decision are counted in boot_overflow (their bootstrap is 0)."""
+        h = self.hdev
+        trunc = h[lo:hi, C_REC + 12] != 0
+        idx = torch.argsort(trunc.to(torch.int8), descending=True, stable=True)[:self.boot_cap] + lo
+        valid = h[:, C_REC + 12].index_select(0, idx) != 0
+        rows = h.index_select(0, idx)
+        self._features(rows[:, C_TOBS:C_TOBS + 15].contiguous(), self.boot_scal)
+        img = None
+        if self.cfg.vision:
+            img = self.camera.render(rows[:, C_TREC:C_TREC + 6].contiguous(), out=self.boot_img)
+        out = forward_gpu(self.net, self.ws_boot, self.boot_scal, img, B=self.boot_cap)
+        v = self.cfg.gamma * out[:, self.layout.value_col]
+        cur = self.reward.boot.index_select(0, idx)
+        self.reward.boot.index_copy_(0, idx, torch.where(valid, v, cur))
+        self.boot_overflow.add_((trunc.sum() - self.boot_cap).clamp_(min=0))
 
     def _bootstrap_truncations(self, g: int, t: int) -> None:
         """gamma * V(s_T) for envs of group g whose episode was truncated this
@@ -459,6 +534,9 @@ class Trainer:
             self._capture()
         if self.pro:                          # carry the last frames over as the reach-back prologue
             self.b_img[:self.pro].copy_(self.b_img[T:T + self.pro])
+        if self.genv is not None:
+            self._rollout_device()
+            return
         for g in range(G):
             self._run_group(g, 0)
         for t in range(T):
@@ -474,6 +552,45 @@ class Trainer:
                 self._run_group(g, t + 1)
             self._observe_respawn(t)
             self.global_step += self.N * self.K * self.world
+
+    def _rollout_device(self) -> None:
+        """The rollout with the env on the GPU: every step is device work, so
+        the host only enqueues. Group g's env step (env stream) waits for its
+        sampled actions and runs beside the other group's reward / render /
+        forward (compute stream); the compute stream keeps the groups'
+        decisions in order (the curiosity counts' two-phase rule)."""
+        from ..ops import _lib
+        T, G = self.T, len(self.groups)
+        C = torch.cuda.current_stream()
+        if getattr(self, "env_stream", None) is None:
+            self.env_stream = torch.cuda.Stream()
+            self.ev_env = [torch.cuda.Event() for _ in range(G)]
+            self.ev_sample = [torch.cuda.Event() for _ in range(G)]
+        E = self.env_stream
+        E.wait_stream(C)
+        for t in range(T + 1):
+            for g in range(G):
+                if t > 0:
+                    E.wait_event(self.ev_sample[g])
+                    with torch.cuda.stream(E):
+                        if self.cfg.graphs:
+                            self.env_graphs[g][t].replay()
+                            _lib.add_launches(self.env_launches[g][t])
+                        else:
+                            self._env_body(g, t)
+                    self.ev_env[g].record(E)
+                    C.wait_event(self.ev_env[g])
+                ev = self.timer.gpu_start("rollout_gpu")
+                if self.cfg.graphs:
+                    self.rew_graphs[g][t].replay()
+                    _lib.add_launches(self.graph_launches[g][t])
+                else:
+                    self._group_body(g, t, env=False)
+                self.timer.gpu_end(ev)
+                self.ev_sample[g].record(C)
+            if t < T:
+                self.global_step += self.N * self.K * self.world
+        C.wait_stream(E)
 
     # ---- GPU update ---------------------------------------------------------------------------
     def _epoch_body(self) -> None:
@@ -677,6 +794,7 @@ class Trainer:
         if self.gpu:
             torch.cuda.synchronize()
             self.rew_graphs = []
+            self.env_graphs = []
             self.upd_graph = None
             import gc
             gc.collect()

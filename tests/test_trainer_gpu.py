@@ -1,6 +1,7 @@
 """End-to-end GPU training iterations (small vision configuration)."""
 import math
 
+import numpy as np
 import pytest
 import torch
 
@@ -65,4 +66,23 @@ def test_frame_stack_and_surface_mask_training(stack, mask):
         assert torch.equal(first, tail)                              # t = 0 continues the previous tail
     summ = evaluate(tr, episodes=2, greedy=True, max_ticks=30)
     assert summ["episodes"] == 2
+    tr.release_graphs()
+
+
+def test_gpu_env_training_iterations():
+    """The rollout with the env on the GPU: no host stepping, same buffers."""
+    cfg = TrainConfig(map="field", envs=256, n_steps=16, act_every=3, epochs=1, minibatches=4, ep_ticks=60,
+                      env_device="cuda", reward=RewardSpec(mode="coverage", int_coef=0.25, int_view=8, int_speed=8))
+    tr = Trainer(cfg, verbose=False)
+    assert tr.genv is not None and len(tr.groups) == 2
+    flat0 = tr.net.flat.clone()
+    for _ in range(2):
+        s = tr.train_iteration()
+    torch.cuda.synchronize()
+    assert s["global_step"] == 2 * 256 * 16 * 3
+    assert math.isfinite(s["policy_loss"]) and s["episodes"] > 0
+    assert not torch.equal(flat0, tr.net.flat)
+    assert int(tr.boot_overflow) >= 0
+    st = tr.genv.get_states()
+    assert (st["tick"] > 0).all() and np.isfinite(st["origin"]).all()
     tr.release_graphs()
