@@ -44,6 +44,8 @@ def main():
     ap.add_argument("--reps", type=int, default=2)
     ap.add_argument("--dbg", type=int, default=0, help="convolution kernel diagnostics (timing studies): "
                     "1 skip epilogue stores, 2 skip MMAs")
+    ap.add_argument("--trace", action="store_true", help="convolution cases: add CTA 0's pipeline timeline "
+                    "(first 256 k-blocks / tiles of the last launch, microseconds) to the output")
     args = ap.parse_args()
     import numpy as np
     import torch
@@ -118,6 +120,8 @@ def main():
         from surfb200.ops import conv as CV
         CV.DEBUG = args.dbg
         info["dbg"] = args.dbg
+        if args.trace:
+            CV.TRACE = torch.zeros(5 * G.TRACE_N, dtype=torch.int64, device=dev)
         layout = HeadLayout(("yaw", "pitch", "fwd", "side", "jump", "duck"), False)
         from surfb200.models.policy import space_to_depth_config
         net = PolicyNet(space_to_depth_config(NetConfig(heads=layout)), dev)    # the trainer's network
@@ -148,6 +152,12 @@ def main():
         info["flops"] = flops
         info["ms"] = _time(fn, args.reps)
         info["tflops"] = flops / (info["ms"] * 1e-3) / 1e12
+        if args.trace:
+            tr = CV.TRACE.view(5, G.TRACE_N).cpu().numpy().astype(np.float64)
+            t0 = tr[0, 0]
+            us = lambda row: [round((x - t0) / 1e3, 3) if x > 0 else None for x in row]
+            info["trace_us"] = {"issue": us(tr[0]), "landed": us(tr[1]), "committed": us(tr[2]),
+                                "acc_ready": us(tr[3]), "tile_done": us(tr[4])}
     elif k in ("sample", "ppo_loss", "gae"):
         layout = HeadLayout(("yaw", "pitch", "fwd", "side", "jump", "duck"), False)
         heads = R.HeadArgs(layout, dev)

@@ -64,7 +64,13 @@ struct Epilogue {
   int64_t ld_aux;
   int* err;           // device error flag (0 = ok)
   int dbg;            // diagnostics: bit 0 skip epilogue stores, bit 1 skip MMAs (timing studies only)
+  // diagnostics: CTA 0 records %globaltimer stamps of its first kTraceN
+  // k-blocks / tiles here (null: off): [0,N) producer issue, [N,2N) TMA
+  // landed (seen by the MMA warp), [2N,3N) MMAs committed, [3N,4N) tile
+  // accumulator ready (epilogue warp 2), [4N,5N) tile epilogue done
+  unsigned long long* trace;
 };
+constexpr int kTraceN = 256;
 
 // Implicit-GEMM convolution operands. An operand with mode != 0 is read
 // through a 4-D tensor map over an NHWC activation (dims C, W, H, B; the map's
@@ -454,6 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < nkt; ++i, ++it) {
           const int s = it % STAGES;
           if (it >= STAGES && !mbar_wait(smem_u32(&bars[STAGES + s]), ((it / STAGES) & 1) ^ 1, ep.err, 1, abort)) break;
+          if (ep.trace && blockIdx.x == 0 && it < kTraceN) ep.trace[it] = globaltimer();
           const uint32_t full = smem_u32(&bars[s]);
           // an MN-major A is loaded as two 64-row halves; with M <= m0 + 64
           // the second half is out of range: skip it (its stale smem rows
@@ -533,6 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = it % STAGES;
           if (!mbar_wait(smem_u32(&bars[s]), (it / STAGES) & 1, ep.err, 2, abort)) { ok = false; break; }
           fence_after();
+          if (ep.trace && blockIdx.x == 0 && it < kTraceN) ep.trace[kTraceN + it] = globaltimer();
           const uint32_t a_base = smem_u32(tiles + s * C::kStageBytes);
           const uint32_t b_base = a_base + C::kABytes;
 #pragma unroll
@@ -551,6 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!(ep.dbg & 2)) mma_bf16(dtm, da, db, C::kIdesc, (i > 0 || j > 0) ? 1u : 0u);
           }
           mma_commit(smem_u32(&bars[STAGES + s]));      // frees the stage when these MMAs finish
+          if (ep.trace && blockIdx.x == 0 && it < kTraceN) ep.trace[2 * kTraceN + it] = globaltimer();
         }
         if (!ok) break;
         mma_commit(smem_u32(&acc_full[buf]));          // accumulator of this tile complete
@@ -571,6 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (BN == 32 && (tc & 1) != half) continue;      // the other warp of this quadrant takes the tile
       if (!mbar_wait(smem_u32(&acc_full[buf]), use & 1, ep.err, 3, abort)) break;
       fence_after();
+      if (ep.trace && blockIdx.x == 0 && warp == 2 && lane == 0 && tc < kTraceN) ep.trace[3 * kTraceN + tc] = globaltimer();
       int row = m0 + quad * 32 + lane;
       bool row_ok = row < M;
       int64_t roff = static_cast<int64_t>(row);         // row index in units of ldc / ld_aux
@@ -655,6 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_before();
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_empty[buf])) : "memory");
+      if (ep.trace && blockIdx.x == 0 && warp == 2 && lane == 0 && tc < kTraceN) ep.trace[4 * kTraceN + tc] = globaltimer();
     }
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }

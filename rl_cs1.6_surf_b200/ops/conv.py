@@ -71,6 +71,7 @@ SLACK_BYTES = 128          # allocate activations with this much room after the 
 # Kernel diagnostics for timing studies only (Epilogue.dbg): bit 0 skips the
 # epilogue's stores, bit 1 skips the MMAs. Results are wrong when non-zero.
 DEBUG = 0
+TRACE = None               # a uint64 CUDA tensor of 5 * 256 stamps: CTA 0's pipeline timeline (diagnostics)
 
 
 def _cdiv(a, b):
@@ -175,6 +176,7 @@ def _epilogue(out, accumulate=False, bias=None, act="none", aux=None, ld=None) -
         ep.ld_aux = ld if ld is not None else aux.shape[-1]
     ep.err = ptr(error_flag(out.device))
     ep.dbg = int(DEBUG)
+    ep.trace = ptr(TRACE)
     return ep
 
 

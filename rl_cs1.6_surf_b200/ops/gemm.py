@@ -30,7 +30,9 @@ ACT = {"none": 0, "relu": 1, "tanh": 2, "relu_grad": 3, "tanh_grad": 4}
 class Epilogue(ctypes.Structure):
     _fields_ = [("c", c_void_p), ("ldc", c_int64), ("c_dtype", c_int), ("c_mode", c_int), ("ct", c_void_p),
                 ("ldct", c_int64), ("ct_dtype", c_int), ("bias", c_void_p), ("act", c_int), ("act2", c_int),
-                ("act_split", c_int), ("aux", c_void_p), ("ld_aux", c_int64), ("err", c_void_p), ("dbg", c_int)]
+                ("act_split", c_int), ("aux", c_void_p), ("ld_aux", c_int64), ("err", c_void_p), ("dbg", c_int),
+                ("trace", c_void_p)]
+TRACE_N = 256              # stamps per kind in an Epilogue.trace buffer (kTraceN in gemm_tc.cu)
 
 
 _SIG = {
