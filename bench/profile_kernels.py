@@ -2,7 +2,7 @@
 
     python bench/profile_kernels.py --only march|conv1_fwd|conv2_dgrad|fc_wgrad|col2im|im2col|conv1_ifwd|
                                            conv1_iwgrad|conv2_ifwd|
-                                           conv2_iwgrad|conv2_idgrad|conv3_ifwd|conv3_idgrad|sample|gae|
+                                           conv2_iwgrad|conv2_idgrad|conv3_ifwd|conv3_iwgrad|conv3_idgrad|sample|gae|
                                            ppo_loss|reward|adam|p2p1|edt|geodesic|surfnz|framestack [--reps 2]
 
 Each case builds its inputs (a few GB on the device at most, larger than L2
@@ -43,9 +43,12 @@ def main():
     ap.add_argument("--only", required=True)
     ap.add_argument("--reps", type=int, default=2)
     ap.add_argument("--dbg", type=int, default=0, help="convolution kernel diagnostics (timing studies): "
-                    "1 skip epilogue stores, 2 skip MMAs")
+                    "1 skip epilogue stores, 2 skip MMAs, 4 stream B per k-block instead of keeping it resident")
     ap.add_argument("--trace", action="store_true", help="convolution cases: add CTA 0's pipeline timeline "
                     "(first 256 k-blocks / tiles of the last launch, microseconds) to the output")
+    ap.add_argument("--wgrad-splits", type=int, default=0, help="weight-gradient cases: K splits (0: the default)")
+    ap.add_argument("--no-pairs", action="store_true", help="16-channel convolution inputs: one 32-byte tap per "
+                    "box row instead of two-position windows")
     args = ap.parse_args()
     import numpy as np
     import torch
@@ -113,13 +116,15 @@ def main():
             fn = lambda: G.im2col(x, B, g["H"], g["W"], g["C"], g["k"], g["s"], out=col)
             info["bytes"] = 2.0 * (rows * g["k"] ** 2 * g["C"] + B * g["H"] * g["W"] * g["C"])
         info["ms"] = _time(fn, args.reps)
-    elif k in ("conv1_ifwd", "conv1_iwgrad", "conv2_ifwd", "conv2_iwgrad", "conv2_idgrad", "conv3_ifwd",
+    elif k in ("conv1_ifwd", "conv1_iwgrad", "conv2_ifwd", "conv2_iwgrad", "conv2_idgrad", "conv3_ifwd", "conv3_iwgrad",
                "conv3_idgrad"):
         # implicit-GEMM convolutions (4-D TMA boxes over the NHWC activations),
         # 4,096 images as above
         from surfb200.ops import conv as CV
         CV.DEBUG = args.dbg
+        CV.PAIR_WINDOWS = not args.no_pairs
         info["dbg"] = args.dbg
+        info["pairs"] = CV.PAIR_WINDOWS
         if args.trace:
             CV.TRACE = torch.zeros(5 * G.TRACE_N, dtype=torch.int64, device=dev)
         layout = HeadLayout(("yaw", "pitch", "fwd", "side", "jump", "duck"), False)
@@ -142,7 +147,7 @@ def main():
         elif k.endswith("iwgrad"):
             dy = rnd(rows, g["CO"])
             gw = torch.zeros(g["CO"], g["k"] ** 2 * g["C"], device=dev)
-            fn = lambda: CV.conv_weight_grad(dy, x, sh, gw)
+            fn = lambda: CV.conv_weight_grad(dy, x, sh, gw, splits=args.wgrad_splits)
         else:
             dyb = rnd(rows * g["CO"] + slack)
             dy = dyb[:rows * g["CO"]].view(rows, g["CO"])
@@ -220,6 +225,9 @@ def main():
                                 net.fp32_from)
             stream = c_void_p(torch.cuda.current_stream().cuda_stream)
             info["ms"] = _time(lambda: L.surf_p2p_grad_step(plan, stream), args.reps)
+            t = [int(x) for x in sync[P.W_PROF:P.W_PROF + 6].tolist()]
+            info["phases_us"] = {name: (t[i + 1] - t[i]) / 1e3 for i, name in enumerate(
+                ("barrier_in", "reduce_scatter", "norm_exchange", "adam_push", "done_wait"))}
             L.surf_p2p_destroy(plan)
         info["params"] = net.numel
     elif k == "edt":

@@ -11,19 +11,22 @@
 // launch is graph-capturable):
 //   A  barrier-in: tell every peer "my gradient is final"; wait for all.
 //   B  reduce-scatter: rank r sums shard r of all W gradients (fixed rank
-//      order, fp32, 8 elements per thread step) into its own gradient
-//      buffer; per-block sums of squares (fp64).            -- grid barrier
-//   C  block 0 adds the block sums in block order and publishes the shard's
-//      sum of squares to every peer; every block waits for all W shard
-//      norms and forms the clip coefficient (same values, same order on
-//      every rank, so every rank clips identically).
+//      order, fp32, several float4 groups per thread in flight) into its
+//      own gradient buffer; per-block sums of squares (fp64); each block
+//      then arrives on a counter and goes on (no grid-wide wait).
+//   C  the block that arrives last adds the block sums in block order and
+//      publishes the shard's sum of squares to every peer; every block
+//      waits for all W shard norms and forms the clip coefficient (same
+//      values, same order on every rank, so every rank clips identically).
 //   D  Adam on the owned shard (m, v local); the new bf16 parameters are
 //      pushed into every peer's buffers, the fp32 ones only for the tail
 //      region the kernels read in fp32 (biases, log-std): the fp32 master
-//      of the weight matrices stays sharded (16-byte stores). -- grid barrier
-//   E  block 0 raises "done" on every peer; every block waits for all
-//      peers' "done" (every parameter pushed here, every peer finished
-//      reading my gradient) and zeroes its part of the local gradient.
+//      of the weight matrices stays sharded (16-byte stores). Each block
+//      releases its stores at system scope and arrives on a second counter.
+//   E  the last block to arrive raises "done" on every peer; every block
+//      waits for all peers' "done" (every parameter pushed here, every peer
+//      finished reading my gradient) and zeroes its part of the local
+//      gradient.
 // Moments: one block, all-gather of a few doubles + ordered local sum.
 // Counts: one cooperative kernel: barrier-in, counts += every other rank's
 //   increments, grid barrier, "done", wait, clear the local increments.
@@ -42,6 +45,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -88,6 +92,11 @@ struct Plan {
   float* hyper = nullptr;
   int64_t push32_from = 0;                  // fp32 parameters pushed to peers only from this index on
   int coop_grid = 148;                      // co-resident blocks of the cooperative kernels
+  // timing studies only (SURF_P2P_DBG, read at plan creation): bit 0 skips
+  // the reduce-scatter loop, bit 1 the Adam loop, bit 2 gives the second grid
+  // barrier a device-scope fence instead of a system-scope one (results are
+  // then unordered across GPUs), bit 3 skips the gradient clear
+  int dbg = 0;
   // counts merge
   int64_t cn = 0;
   int* counts = nullptr;
@@ -116,6 +125,8 @@ __device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -190,11 +201,12 @@ __device__ bool grid_barrier(uint64_t* sync, int slot, bool fence_sys, uint64_t 
     unsigned long long* cnt = reinterpret_cast<unsigned long long*>(sync + kBar + 2 * slot);
     unsigned long long* gen = cnt + 1;
     const uint64_t g = ld_acquire_gpu(reinterpret_cast<uint64_t*>(gen));
-    if (fence_sys) __threadfence_system();
-    else __threadfence();
+    // release of this block's writes (system scope when peers will read them)
+    if (fence_sys) fence_acq_rel_sys();
+    else fence_acq_rel_gpu();
     if (atomicAdd(cnt, 1ull) == gridDim.x - 1) {
       atomicExch(cnt, 0ull);
-      __threadfence();
+      fence_acq_rel_gpu();
       atomicAdd(gen, 1ull);
     } else {
       const uint64_t t0 = globaltimer();
@@ -210,6 +222,28 @@ __device__ bool grid_barrier(uint64_t* sync, int slot, bool fence_sys, uint64_t 
   return ok != 0;
 }
 
+// One-shot arrival counter of a cooperative launch: every block arrives once
+// and goes on without waiting; the block that arrives last (the result is
+// block-uniform) has acquired every other block's writes made before their
+// arrival, and resets the counter for the kernel's next launch. `fence_sys`
+// releases this block's writes at system scope (peer stores made here).
+__device__ bool arrive_last(uint64_t* sync, int slot, bool fence_sys) {
+  __shared__ int last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (fence_sys) fence_acq_rel_sys();
+    else fence_acq_rel_gpu();
+    unsigned long long* cnt = reinterpret_cast<unsigned long long*>(sync + kBar + 2 * slot);
+    last = atomicAdd(cnt, 1ull) == gridDim.x - 1 ? 1 : 0;
+    if (last) {
+      fence_acq_rel_gpu();
+      atomicExch(cnt, 0ull);
+    }
+  }
+  __syncthreads();
+  return last != 0;
+}
+
 __device__ __forceinline__ void prof_mark(const Plan& P, int k) {
   if (blockIdx.x == 0 && threadIdx.x == 0) P.sync[kProf + k] = globaltimer();
 }
@@ -221,17 +255,23 @@ __device__ __forceinline__ double sq4(const float4& a) {
 }
 
 // ---- gradient step ---------------------------------------------------------------------------
+// W = world size (compile-time, so the peer loops hold exactly W float4 per
+// group in registers). Every thread keeps kU float4 groups per peer in flight
+// at once: the reduce-scatter is a read of (W-1)/W of the gradient over
+// NVLink, and its rate is bytes in flight / round-trip latency.
+template <int W>
 __global__ void __launch_bounds__(256) grad_step_kernel(Plan P) {
+  constexpr int kU = W <= 1 ? 8 : (W == 2 ? 4 : (W <= 4 ? 2 : 1));   // groups per thread per round (reduce-scatter)
+  constexpr int kUA = 4;                                              // groups per thread per round (Adam)
   uint64_t* sync = P.sync;
   if (ld_relaxed_sys_u64(sync + kErr) != 0ull) return;
   const uint64_t target = sync[kSeqGrad] + 1;
   const int par = static_cast<int>(target & 1);
   prof_mark(P, 0);
-  // A: barrier-in
-  if (blockIdx.x == 0 && static_cast<int>(threadIdx.x) < P.world) {
-    __threadfence_system();
+  // A: barrier-in (the release store orders the gradient, written by the
+  // earlier kernels of this stream, before the flag)
+  if (blockIdx.x == 0 && static_cast<int>(threadIdx.x) < P.world)
     st_release_sys(P.sync_peer[threadIdx.x] + flag_word(kFReady, P.rank), target);
-  }
   if (!block_wait_all(P, kFReady, target, 0x100)) return;
   prof_mark(P, 1);
 
@@ -245,34 +285,44 @@ __global__ void __launch_bounds__(256) grad_step_kernel(Plan P) {
   const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   float* mine = P.grad_peer[P.rank];
-  // B: reduce-scatter of the owned shard
+  // B: reduce-scatter of the owned shard (rank order 0..W-1 in every sum)
   double ss = 0.0;
-  for (int64_t j = tid; j < n4; j += stride) {
-    const int64_t i = lo + 4 * j;
-    float4 v[kMaxW];
+  for (int64_t j0 = tid; j0 < ((P.dbg & 1) ? 0 : n4); j0 += stride * kU) {
+    float4 v[W][kU];
 #pragma unroll
-    for (int q = 0; q < kMaxW; ++q)
-      if (q < P.world) v[q] = *reinterpret_cast<const float4*>(P.grad_peer[q] + i);
-    float4 a = v[0];
+    for (int u = 0; u < kU; ++u) {
+      const int64_t j = j0 + u * stride;
+      if (j < n4) {
 #pragma unroll
-    for (int q = 1; q < kMaxW; ++q)
-      if (q < P.world) add4(a, v[q]);
-    *reinterpret_cast<float4*>(mine + i) = a;
-    ss += sq4(a);
+        for (int q = 0; q < W; ++q) v[q][u] = *reinterpret_cast<const float4*>(P.grad_peer[q] + lo + 4 * j);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t j = j0 + u * stride;
+      if (j < n4) {
+        float4 a = v[0][u];
+#pragma unroll
+        for (int q = 1; q < W; ++q) add4(a, v[q][u]);
+        *reinterpret_cast<float4*>(mine + lo + 4 * j) = a;
+        ss += sq4(a);
+      }
+    }
   }
   for (int64_t i = lo + 4 * n4 + tid; i < hi; i += stride) {
     float a = P.grad_peer[0][i];
-    for (int q = 1; q < P.world; ++q) a += P.grad_peer[q][i];
+    for (int q = 1; q < W; ++q) a += P.grad_peer[q][i];
     mine[i] = a;
     ss += static_cast<double>(a) * a;
   }
   const double bs = block_sum(ss);
   double* partial = reinterpret_cast<double*>(sync + kPartial);
   if (threadIdx.x == 0) partial[blockIdx.x] = bs;
-  if (!grid_barrier(sync, kBarGrad1, false, P.timeout_ns, 0x710, target)) return;
+  const bool last1 = arrive_last(sync, kBarGrad1, false);
   prof_mark(P, 2);
-  // C: shard norm out, all norms in
-  if (blockIdx.x == 0) {
+  // C: shard norm out (by the block that finished the reduce-scatter last),
+  // all norms in
+  if (last1) {
     // ordered (deterministic) sum of the block partials by the whole block:
     // thread t adds blocks t, t+256, ... then a fixed-shape tree
     double part = 0.0;
@@ -323,20 +373,34 @@ __global__ void __launch_bounds__(256) grad_step_kernel(Plan P) {
   auto pack2 = [](float a, float b) {
     return static_cast<uint32_t>(surfk::f32_to_bf16(a)) | (static_cast<uint32_t>(surfk::f32_to_bf16(b)) << 16);
   };
-  for (int64_t j = tid; j < n4; j += stride) {
-    const int64_t i = lo + 4 * j;
-    float4 m0 = *reinterpret_cast<const float4*>(P.m + i);
-    float4 w0 = *reinterpret_cast<const float4*>(P.v + i);
-    const float4 p0 = adam4(*reinterpret_cast<const float4*>(mine + i), m0, w0, *reinterpret_cast<const float4*>(pl + i));
-    *reinterpret_cast<float4*>(P.m + i) = m0;
-    *reinterpret_cast<float4*>(P.v + i) = w0;
-    const uint2 b = make_uint2(pack2(p0.x, p0.y), pack2(p0.z, p0.w));
-    const bool all32 = i >= P.push32_from;          // 64-aligned region boundary: never inside a group of 4
+  for (int64_t j0 = tid; j0 < ((P.dbg & 2) ? 0 : n4); j0 += stride * kUA) {
+    float4 g4[kUA], m4[kUA], v4[kUA], p4[kUA];
 #pragma unroll
-    for (int q = 0; q < kMaxW; ++q) {
-      if (q < P.world) {
-        if (all32 || q == P.rank) *reinterpret_cast<float4*>(P.p_peer[q] + i) = p0;
-        *reinterpret_cast<uint2*>(P.p16_peer[q] + i) = b;
+    for (int u = 0; u < kUA; ++u) {
+      const int64_t j = j0 + u * stride;
+      if (j < n4) {
+        const int64_t i = lo + 4 * j;
+        g4[u] = *reinterpret_cast<const float4*>(mine + i);
+        m4[u] = *reinterpret_cast<const float4*>(P.m + i);
+        v4[u] = *reinterpret_cast<const float4*>(P.v + i);
+        p4[u] = *reinterpret_cast<const float4*>(pl + i);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUA; ++u) {
+      const int64_t j = j0 + u * stride;
+      if (j < n4) {
+        const int64_t i = lo + 4 * j;
+        const float4 p0 = adam4(g4[u], m4[u], v4[u], p4[u]);
+        *reinterpret_cast<float4*>(P.m + i) = m4[u];
+        *reinterpret_cast<float4*>(P.v + i) = v4[u];
+        const uint2 b = make_uint2(pack2(p0.x, p0.y), pack2(p0.z, p0.w));
+        const bool all32 = i >= P.push32_from;      // 64-aligned region boundary: never inside a group of 4
+#pragma unroll
+        for (int q = 0; q < W; ++q) {
+          if (all32 || q == P.rank) *reinterpret_cast<float4*>(P.p_peer[q] + i) = p0;
+          *reinterpret_cast<uint2*>(P.p16_peer[q] + i) = b;
+        }
       }
     }
   }
@@ -346,23 +410,27 @@ __global__ void __launch_bounds__(256) grad_step_kernel(Plan P) {
     P.m[i] = mi;
     P.v[i] = vi;
     const uint16_t b = surfk::f32_to_bf16(pi);
-    for (int q = 0; q < P.world; ++q) {
+    for (int q = 0; q < W; ++q) {
       if (i >= P.push32_from || q == P.rank) P.p_peer[q][i] = pi;
       P.p16_peer[q][i] = b;
     }
   }
-  if (!grid_barrier(sync, kBarGrad2, true, P.timeout_ns, 0x720, target)) return;
+  const bool last2 = arrive_last(sync, kBarGrad2, !(P.dbg & 4));
   prof_mark(P, 4);
-  // E: done out, all done in, clear the local gradient
-  if (blockIdx.x == 0 && static_cast<int>(threadIdx.x) < P.world)
-    st_release_sys(P.sync_peer[threadIdx.x] + flag_word(kFDone, P.rank), target);
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
-    reinterpret_cast<Hyper*>(P.hyper)->step = t;    // every block read the old step before the barrier
-    sync[kSeqGrad] = target;
+  // E: done out (by the block that pushed last), all done in, clear the
+  // local gradient (every peer finished reading it before it published its
+  // norm; "done" also says its parameters have landed here)
+  if (last2) {
+    if (static_cast<int>(threadIdx.x) < P.world)
+      st_release_sys(P.sync_peer[threadIdx.x] + flag_word(kFDone, P.rank), target);
+    if (threadIdx.x == 0) {
+      reinterpret_cast<Hyper*>(P.hyper)->step = t;  // every block read the old step before it arrived
+      sync[kSeqGrad] = target;
+    }
   }
   if (!block_wait_all(P, kFDone, target, 0x300)) return;
   prof_mark(P, 5);
-  const int64_t nv = P.n >> 2;
+  const int64_t nv = (P.dbg & 8) ? 0 : P.n >> 2;
   for (int64_t j = tid; j < nv; j += stride) reinterpret_cast<float4*>(mine)[j] = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int64_t i = 4 * nv + tid; i < P.n; i += stride) mine[i] = 0.0f;
 }
@@ -398,10 +466,8 @@ __global__ void __launch_bounds__(256) counts_merge_kernel(Plan P) {
   uint64_t* sync = P.sync;
   if (ld_relaxed_sys_u64(sync + kErr) != 0ull) return;
   const uint64_t target = sync[kSeqCnt] + 1;
-  if (blockIdx.x == 0 && static_cast<int>(threadIdx.x) < P.world) {
-    __threadfence_system();
+  if (blockIdx.x == 0 && static_cast<int>(threadIdx.x) < P.world)
     st_release_sys(P.sync_peer[threadIdx.x] + flag_word(kFCntReady, P.rank), target);
-  }
   if (!block_wait_all(P, kFCntReady, target, 0x500)) return;
   const int64_t nv = P.cn >> 2;
   const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
@@ -431,6 +497,20 @@ __global__ void __launch_bounds__(256) counts_merge_kernel(Plan P) {
   int* d = P.delta_peer[P.rank];
   for (int64_t j = tid; j < nv; j += stride) reinterpret_cast<int4*>(d)[j] = make_int4(0, 0, 0, 0);
   for (int64_t i = 4 * nv + tid; i < P.cn; i += stride) d[i] = 0;
+}
+
+using GradKernel = void (*)(Plan);
+GradKernel grad_kernel_for(int world) {
+  switch (world) {
+    case 1: return grad_step_kernel<1>;
+    case 2: return grad_step_kernel<2>;
+    case 3: return grad_step_kernel<3>;
+    case 4: return grad_step_kernel<4>;
+    case 5: return grad_step_kernel<5>;
+    case 6: return grad_step_kernel<6>;
+    case 7: return grad_step_kernel<7>;
+    default: return grad_step_kernel<8>;
+  }
 }
 
 // Cooperative launch (all blocks co-resident, so grid barriers are safe).
@@ -515,11 +595,23 @@ SURF_EXPORT void* surf_p2p_create(int rank, int world, void* const* sync_peers, 
   p->sync = p->sync_peer[rank];
   int dev = 0, sms = 148, per_sm = 1, per_sm2 = 1;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, grad_step_kernel, 256, 0);
+  // the largest instantiation bounds the co-resident blocks of all of them
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, grad_step_kernel<kMaxW>, 256, 0);
+  for (int w = 1; w < kMaxW; ++w) {
+    int b = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, grad_kernel_for(w), 256, 0);
+    if (b < per_sm) per_sm = b;
+  }
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm2, counts_merge_kernel, 256, 0);
   const int m = per_sm < per_sm2 ? per_sm : per_sm2;
   p->coop_grid = sms * (m < 2 ? (m < 1 ? 1 : m) : 2);
+  // SURF_P2P_BLOCKS_PER_SM (1 or 2) overrides the blocks per SM (tuning studies)
+  if (const char* e = std::getenv("SURF_P2P_BLOCKS_PER_SM")) {
+    const int b = std::atoi(e);
+    if (b >= 1 && b <= m) p->coop_grid = sms * b;
+  }
   if (p->coop_grid > kMaxBlocks) p->coop_grid = kMaxBlocks;
+  if (const char* e = std::getenv("SURF_P2P_DBG")) p->dbg = std::atoi(e);
   return p;
 }
 
@@ -569,7 +661,7 @@ SURF_EXPORT int surf_p2p_set_counts(void* plan, int64_t n, int* counts, void* co
 SURF_EXPORT int surf_p2p_grad_step(void* plan, void* stream) {
   const Plan& P = *static_cast<const Plan*>(plan);
   if (!P.n) return static_cast<int>(cudaErrorInvalidValue);
-  return launch_coop(grad_step_kernel, P.coop_grid, static_cast<cudaStream_t>(stream), P);
+  return launch_coop(grad_kernel_for(P.world), P.coop_grid, static_cast<cudaStream_t>(stream), P);
 }
 
 // Phase timestamps (ns, %globaltimer) of this rank's last gradient step:

@@ -21,8 +21,13 @@ A 64-byte-channel input (C = 32) with stride 2 along W is read as
 "super-pixels" of two neighbouring positions (128 bytes), which turns the
 stride along W into 1 and pairs the taps (kw, kw + 1); its buffer needs 64
 bytes of slack after the last row (the unused 16th super-pixel of the last
-row is fetched). Supported: C = 64 (any stride), or C = 32 with stride 2
-and even kernel; output-gradient channels (the dgrad A operand) = 64.
+row is fetched). A 16-channel input (the depth image in 4x4 space-to-depth
+order) is read as windows of two neighbouring positions: the tensor map's W
+stride is one position (32 bytes) and its inner extent two (64 bytes), so a
+box row holds the taps (kw, kw + 1) -- half the box rows of one 32-byte tap
+per row. Supported: C = 64 (any stride), C = 32 with stride 2 and even
+kernel, C = 16 with even kernel; output-gradient channels (the dgrad A
+operand) = 64.
 Reference layer: the conv trunk of python/train_fast.py:115-121 (cuDNN there).
 """
 from __future__ import annotations
@@ -72,10 +77,23 @@ SLACK_BYTES = 128          # allocate activations with this much room after the 
 # epilogue's stores, bit 1 skips the MMAs. Results are wrong when non-zero.
 DEBUG = 0
 TRACE = None               # a uint64 CUDA tensor of 5 * 256 stamps: CTA 0's pipeline timeline (diagnostics)
+# 16-channel inputs: two-position windows (kernel mode 4) when True, one
+# 32-byte tap per box row (mode 3) when False (A/B timing).
+PAIR_WINDOWS = True
 
 
 def _cdiv(a, b):
     return -(-a // b)
+
+
+_SMS = {}
+
+
+def _sm_count(dev) -> int:
+    i = dev.index if dev.index is not None else torch.cuda.current_device()
+    if i not in _SMS:
+        _SMS[i] = torch.cuda.get_device_properties(i).multi_processor_count
+    return _SMS[i]
 
 
 def _pow2_at_least(n: int) -> int:
@@ -109,8 +127,14 @@ class ConvShape:
 
     @property
     def slabs(self) -> bool:
-        """16-channel input: taps load as 32-byte-swizzled slabs (kernel mode 3)."""
+        """16-channel input: taps load as 32-byte-swizzled slabs (kernel mode 3)
+        or as two-position windows (mode 4)."""
         return self.C == 16
+
+    @property
+    def pairs(self) -> bool:
+        """16-channel input read as 64-byte windows of taps (kw, kw + 1)."""
+        return self.C == 16 and PAIR_WINDOWS
 
     def supported(self) -> bool:
         if self.C == 64:
@@ -139,7 +163,14 @@ def _input_map(x: torch.Tensor, sh: ConvShape, tw: int, th: int, tb: int) -> Map
     d = MapDesc()
     d.base = ptr(x)
     p = sh.superpixel
-    if p == 2:
+    if sh.pairs:
+        # overlapping rows: W stride 32 bytes, inner extent 64 bytes; the last
+        # position of a row has no right neighbour and is left out of the map
+        d.dims[:] = [32, sh.W - 1, sh.H, sh.B]
+        d.strides[:] = [sh.C * 2, sh.W * sh.C * 2, sh.H * sh.W * sh.C * 2]
+        d.box[:] = [32, tw * sh.s, th * sh.s, tb]
+        d.estr[:] = [1, sh.s, sh.s, 1]
+    elif p == 2:
         d.dims[:] = [64, _cdiv(sh.W, 2), sh.H, sh.B]
         d.strides[:] = [128, sh.W * sh.C * 2, sh.H * sh.W * sh.C * 2]
         d.box[:] = [64, tw, th * sh.s, tb]
@@ -195,10 +226,10 @@ def conv_forward(x: torch.Tensor, sh: ConvShape, w16: torch.Tensor, bias: torch.
     p = sh.superpixel
     tw, th, tb = _tile(sh.OW, sh.OH, 128)
     cc = ConvCfg()
-    cc.a.mode, cc.a.tw, cc.a.th, cc.a.tb = (3 if sh.slabs else 1), tw, th, tb
+    cc.a.mode, cc.a.tw, cc.a.th, cc.a.tb = (4 if sh.pairs else 3 if sh.slabs else 1), tw, th, tb
     cc.a.tiles_w, cc.a.tiles_h = _cdiv(sh.OW, tw), _cdiv(sh.OH, th)
     cc.a.sw, cc.a.sh = (1 if p == 2 else sh.s), sh.s
-    cc.a.kw_n = sh.k // p
+    cc.a.kw_n = sh.k // 2 if sh.pairs else sh.k // p
     cc.a.sign, cc.a.per_tap = 1, 1
     cc.o.on, cc.o.gw, cc.o.gh, cc.o.gb = 1, sh.OW, sh.OH, sh.B
     cc.o.out_w, cc.o.out_h, cc.o.ys, cc.o.xs = sh.OW, sh.OH, 1, 1
@@ -222,17 +253,19 @@ def conv_weight_grad(dy: torch.Tensor, x: torch.Tensor, sh: ConvShape, gw: torch
         g.mode, g.tw, g.th, g.tb = 2, tw, th, tb
         g.tiles_w, g.tiles_h = _cdiv(sh.OW, tw), _cdiv(sh.OH, th)
     if sh.slabs:
-        cc.b.mode = 3
+        cc.b.mode = 4 if sh.pairs else 3
     cc.b.sw, cc.b.sh = (1 if p == 2 else sh.s), sh.s
-    cc.b.kw_n = sh.k // p
+    cc.b.kw_n = sh.k // 2 if sh.pairs else sh.k // p
     ktiles = cc.a.tiles_w * cc.a.tiles_h * _cdiv(sh.B, tb)
     ad = _grid_map(dy, sh.CO, sh.OW, sh.OH, sh.B, tw, th, tb)
     bd = _input_map(x, sh, tw, th, tb)
     N = sh.k * sh.k * sh.C
     bn = 64 if sh.slabs else (256 if N >= 256 else (128 if N >= 128 else 64))
     if not splits:
+        # one (n tile, K split) per SM: a second tile per CTA would add a
+        # second round of fp32 atomics into gw without adding parallelism
         tiles = _cdiv(N, bn)
-        splits = max(1, min(ktiles, 296 // max(tiles, 1)))
+        splits = max(1, min(ktiles, _sm_count(dy.device) // max(tiles, 1)))
     ep = _epilogue(gw, accumulate=True, ld=gw.stride(0))
     _run(dy, ad, 1, x, bd, 1, sh.CO, N, ktiles * 64, ep, cc, bn=bn, splits=splits, dev=dy.device)
 

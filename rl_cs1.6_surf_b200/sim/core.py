@@ -237,8 +237,10 @@ class TraceResult:
 
 def default_threads() -> int:
     """Env worker threads: this process's share of the CPUs it may use (the
-    node's ranks, LOCAL_WORLD_SIZE, split them evenly), minus one for the
-    Python/GPU-driving thread, capped at 64 (overridable via SURF_THREADS)."""
+    node's ranks, LOCAL_WORLD_SIZE, split them evenly), capped at 64
+    (overridable via SURF_THREADS). The calling (Python/GPU-driving) thread is
+    one of them: it steps the first chunk of envs itself, and the GPU work of
+    the other env group was launched before the step."""
     env = os.environ.get("SURF_THREADS")
     if env:
         return max(1, int(env))
@@ -247,7 +249,7 @@ def default_threads() -> int:
     except AttributeError:   # pragma: no cover
         n = os.cpu_count() or 4
     local = max(1, int(os.environ.get("LOCAL_WORLD_SIZE", "1")))
-    return max(1, min(64, n // local - 1))
+    return max(1, min(64, n // local))
 
 
 class SimCore:

@@ -84,3 +84,65 @@ def test_input_grad(sh):
     y.backward(dy.float().view(sh.B, sh.OH, sh.OW, sh.CO).permute(0, 3, 1, 2))
     ref = xt.grad.permute(0, 2, 3, 1).reshape(-1, sh.C) * (x_act.float() > 0)
     torch.testing.assert_close(dx.float(), ref, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("sh", [CV.ConvShape(B=700, H=15, W=31, C=32, k=4, s=2, CO=64),
+                                CV.ConvShape(B=300, H=6, W=14, C=64, k=3, s=1, CO=64),
+                                CV.ConvShape(B=500, H=16, W=32, C=16, k=2, s=1, CO=32)],
+                         ids=lambda s: f"C{s.C}k{s.k}s{s.s}")
+def test_resident_weights_match_streamed(sh):
+    """The forward and input-gradient GEMMs keep the weight operand resident
+    in shared memory; streaming it per k-block instead (diagnostic bit 2)
+    issues the same MMAs in the same order, so the outputs are bit-identical.
+    The batches span several tiles per CTA."""
+    g = torch.Generator(device="cuda").manual_seed(4)
+    buf, x = _nhwc(sh, g)
+    w = _w(sh, g)
+    bias = torch.randn(sh.CO, device="cuda", generator=g) * 0.1
+    outs = []
+    try:
+        for dbg in (0, 4):
+            CV.DEBUG = dbg
+            y = torch.empty(sh.B * sh.OH * sh.OW, sh.CO, dtype=torch.bfloat16, device="cuda")
+            CV.conv_forward(buf, sh, w, bias, y)
+            res = [y]
+            if sh.CO == 64 and sh.C % 32 == 0:
+                dy = (torch.randn(sh.B * sh.OH * sh.OW, sh.CO, device="cuda",
+                                  generator=torch.Generator(device="cuda").manual_seed(5)) * 0.1).to(torch.bfloat16)
+                x_act = torch.relu(x.float()).to(torch.bfloat16).reshape(-1, sh.C).contiguous()
+                dx = torch.empty(sh.B * sh.H * sh.W, sh.C, dtype=torch.bfloat16, device="cuda")
+                CV.conv_input_grad(dy, sh, CV.weight_classes(w, sh), dx, x_act)
+                res.append(dx)
+            outs.append(res)
+    finally:
+        CV.DEBUG = 0
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    ref = torch.relu(_ref_conv(x, w, sh) + bias.view(1, -1, 1, 1)).permute(0, 2, 3, 1).reshape(-1, sh.CO)
+    torch.testing.assert_close(outs[0][0].float(), ref, rtol=2e-2, atol=3e-2)
+
+
+def test_pair_windows_match_single_taps():
+    """16-channel inputs read as two-position windows (64-byte rows of an
+    overlapping tensor map) give the forward of one-tap slabs bit for bit
+    (same MMAs, same order) and the same weight gradient up to the order of
+    the split-K atomics."""
+    sh = CV.ConvShape(B=300, H=16, W=32, C=16, k=2, s=1, CO=32)
+    g = torch.Generator(device="cuda").manual_seed(6)
+    buf, x = _nhwc(sh, g)
+    w = _w(sh, g)
+    bias = torch.randn(sh.CO, device="cuda", generator=g) * 0.1
+    dy = (torch.randn(sh.B * sh.OH * sh.OW, sh.CO, device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    res = []
+    try:
+        for pairs in (True, False):
+            CV.PAIR_WINDOWS = pairs
+            y = torch.empty(sh.B * sh.OH * sh.OW, sh.CO, dtype=torch.bfloat16, device="cuda")
+            CV.conv_forward(buf, sh, w, bias, y)
+            gw = torch.zeros(sh.CO, sh.k * sh.k * sh.C, device="cuda")
+            CV.conv_weight_grad(dy, buf, sh, gw)
+            res.append((y, gw))
+    finally:
+        CV.PAIR_WINDOWS = True
+    assert torch.equal(res[0][0], res[1][0])
+    torch.testing.assert_close(res[0][1], res[1][1], rtol=1e-4, atol=1e-4)
