@@ -43,7 +43,8 @@ def main():
     ap.add_argument("--only", required=True)
     ap.add_argument("--reps", type=int, default=2)
     ap.add_argument("--dbg", type=int, default=0, help="convolution kernel diagnostics (timing studies): "
-                    "1 skip epilogue stores, 2 skip MMAs, 4 stream B per k-block instead of keeping it resident")
+                    "1 skip epilogue stores, 2 skip MMAs, 4 stream B per k-block instead of keeping it resident, "
+                    "8 no saved-activation prefetch in the derivative epilogues")
     ap.add_argument("--trace", action="store_true", help="convolution cases: add CTA 0's pipeline timeline "
                     "(first 256 k-blocks / tiles of the last launch, microseconds) to the output")
     ap.add_argument("--wgrad-splits", type=int, default=0, help="weight-gradient cases: K splits (0: the default)")

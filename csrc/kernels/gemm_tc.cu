@@ -63,7 +63,8 @@ struct Epilogue {
   const uint16_t* aux;   // bf16 [M, N] saved activation for the derivative modes
   int64_t ld_aux;
   int* err;           // device error flag (0 = ok)
-  int dbg;            // diagnostics: bit 0 skip epilogue stores, bit 1 skip MMAs (timing studies only)
+  int dbg;            // diagnostics (timing studies only): bit 0 skip epilogue stores, bit 1 skip MMAs,
+                      // bit 2 stream a resident-able B per k-block, bit 3 no saved-activation prefetch
   // diagnostics: CTA 0 records %globaltimer stamps of its first kTraceN
   // k-blocks / tiles here (null: off): [0,N) producer issue, [N,2N) TMA
   // landed (seen by the MMA warp), [2N,3N) MMAs committed, [3N,4N) tile
@@ -259,7 +260,7 @@ __device__ __forceinline__ float tanh_fast(float x) {
 // 32), bias and the saved activation are loaded with vector loads, and each
 // activation has its own tight loop.
 __device__ __forceinline__ void process_chunk32(const Epilogue& ep, float* v, int64_t row, bool row_ok, int col0,
-                                                int N) {
+                                                int N, const uint4* pre = nullptr) {
   const bool full = col0 + 32 <= N;
   if (ep.bias) {
     if (full) {
@@ -291,7 +292,18 @@ __device__ __forceinline__ void process_chunk32(const Epilogue& ep, float* v, in
   float a[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) a[i] = 0.0f;
-  if (row_ok) {
+  if (pre) {
+    // loaded ahead by load_aux32 (a full, aligned chunk of a valid row)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t ww[4] = {pre[q].x, pre[q].y, pre[q].z, pre[q].w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        a[8 * q + 2 * k] = __uint_as_float(ww[k] << 16);
+        a[8 * q + 2 * k + 1] = __uint_as_float(ww[k] & 0xFFFF0000u);
+      }
+    }
+  } else if (row_ok) {
     const uint16_t* src = ep.aux + row * ep.ld_aux + col0;
     if (full && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
 #pragma unroll
@@ -319,6 +331,20 @@ __device__ __forceinline__ void process_chunk32(const Epilogue& ep, float* v, in
   }
 }
 
+// Saved-activation row of a derivative-mode chunk, loaded ahead of its
+// accumulator (4 x 16 bytes); false (nothing loaded) for other activations,
+// invalid rows, partial or unaligned chunks, which process_chunk32 loads itself.
+__device__ __forceinline__ bool load_aux32(const Epilogue& ep, int64_t row, bool row_ok, int col0, int N,
+                                           uint4 (&w)[4]) {
+  const int act = col0 < ep.act_split ? ep.act : ep.act2;
+  if ((act != kReluGrad && act != kTanhGrad) || !row_ok || col0 + 32 > N) return false;
+  const uint16_t* src = ep.aux + row * ep.ld_aux + col0;
+  if (reinterpret_cast<uintptr_t>(src) & 15) return false;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) w[q] = *reinterpret_cast<const uint4*>(src + 8 * q);
+  return true;
+}
+
 template <int BN, bool A_MN, bool B_MN, int STAGES, bool RB>
 struct Cfg {
   static constexpr int kABytes = BM * BK * 2;
@@ -336,8 +362,10 @@ struct Cfg {
   // two warps of a TMEM lane quadrant take alternate tiles instead of
   // alternate chunks, so all eight epilogue warps stay busy
   static constexpr int kEpiPerTile = BN == 32 ? kEpiWarps / 2 : kEpiWarps;
-  // per epilogue warp: two 32x32 fp32 staging tiles for TMA stores (4 KB each)
-  static constexpr int kStageOutBytes = kEpiWarps * 2 * 4096;
+  // per epilogue warp: two 32x32 fp32 staging tiles for TMA stores (4 KB
+  // each); the resident-B instantiation serves convolution-grid outputs,
+  // which are stored from registers, and spends that room on stages
+  static constexpr int kStageOutBytes = RB ? 0 : kEpiWarps * 2 * 4096;
   // alignment slack + operand stages + barrier block (1 KB) + output staging
   static constexpr size_t kSmem =
       1024 + STAGES * static_cast<size_t>(kStageBytes) + kResBytes + 1024 + kStageOutBytes;
@@ -636,9 +664,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n0 = nb * BN;
       const int buf = tc % C::kAcc, use = tc / C::kAcc;
       if (BN == 32 && (tc & 1) != half) continue;      // the other warp of this quadrant takes the tile
-      if (!mbar_wait(smem_u32(&acc_full[buf]), use & 1, ep.err, 3, abort)) break;
-      fence_after();
-      if (ep.trace && blockIdx.x == 0 && warp == 2 && lane == 0 && tc < kTraceN) ep.trace[3 * kTraceN + tc] = globaltimer();
       int row = m0 + quad * 32 + lane;
       bool row_ok = row < M;
       int64_t roff = static_cast<int64_t>(row);         // row index in units of ldc / ld_aux
@@ -655,6 +680,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         roff = (static_cast<int64_t>(gpos_b) * cc.o.out_h + gpos_h * cc.o.ys + cc.o.yo) * cc.o.out_w +
                gpos_w * cc.o.xs + cc.o.xo;
       }
+      // where this lane's row of the 32-column chunk at tile column c0 goes:
+      // output row, validity, first column and columns per row (a parity
+      // class of a strided input gradient has its own rows)
+      auto chunk_loc = [&](int c0, int64_t& off, bool& ok, int& col, int& ncol) {
+        if (cc.o.cls_cols) {
+          const int cls = (n0 + c0) / cc.o.cls_cols;
+          col = n0 + c0 - cls * cc.o.cls_cols;
+          const int hh = gpos_h * cc.o.ys + cls / cc.o.xs, ww = gpos_w * cc.o.xs + cls % cc.o.xs;
+          ok = row_ok && hh < cc.o.out_h && ww < cc.o.out_w;
+          off = (static_cast<int64_t>(gpos_b) * cc.o.out_h + hh) * cc.o.out_w + ww;
+          ncol = cc.o.cls_cols;
+        } else {
+          off = roff;
+          ok = row_ok;
+          col = n0 + c0;
+          ncol = N;
+        }
+      };
+      // the derivative modes read the saved activation of each output row:
+      // the first chunk's is loaded before the accumulator is waited for,
+      // each next chunk's while the current one is stored
+      const int c_first = BN == 32 ? 0 : 32 * half;
+      uint4 pre[4];
+      bool have = false;
+      auto prefetch = [&](int c0) {
+        have = false;
+        if (c0 < BN && n0 + c0 < N && !(ep.dbg & 8)) {
+          int64_t off;
+          bool ok;
+          int col, ncol;
+          chunk_loc(c0, off, ok, col, ncol);
+          have = load_aux32(ep, off, ok, col, ncol, pre);
+        }
+      };
+      if (!(ep.dbg & 1)) prefetch(c_first);
+      if (!mbar_wait(smem_u32(&acc_full[buf]), use & 1, ep.err, 3, abort)) break;
+      fence_after();
+      if (ep.trace && blockIdx.x == 0 && warp == 2 && lane == 0 && tc < kTraceN) ep.trace[3 * kTraceN + tc] = globaltimer();
       if (ep.dbg & 1) {
         float v[32];
         tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN, v);
@@ -665,11 +728,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool bf = ep.c_dtype == 1;
         uint8_t* my_stage = stage_out + (warp - 2) * 8192;
 #pragma unroll 1
-        for (int c0 = BN == 32 ? 0 : 32 * half; c0 < BN; c0 += 64) {
+        for (int c0 = c_first; c0 < BN; c0 += 64) {
           if (n0 + c0 >= N) break;
           float v[32];
           tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + c0, v);
-          process_chunk32(ep, v, roff, row_ok, n0 + c0, N);
+          process_chunk32(ep, v, roff, row_ok, n0 + c0, N, have ? pre : nullptr);
+          prefetch(c0 + 64);
           const int sb = stage_ctr & 1;
           if (lane == 0 && stage_ctr >= 2) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
           __syncwarp();
@@ -702,22 +766,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c0 = BN == 32 ? 0 : 32 * half; c0 < BN; c0 += 64) {
+        for (int c0 = c_first; c0 < BN; c0 += 64) {
           if (n0 + c0 >= N) break;
+          int64_t off;
+          bool ok;
+          int col, ncol;
+          chunk_loc(c0, off, ok, col, ncol);
           float v[32];
           tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN + c0, v);
-          if (cc.o.cls_cols) {
-            const int cls = (n0 + c0) / cc.o.cls_cols;
-            const int col = n0 + c0 - cls * cc.o.cls_cols;
-            const int hh = gpos_h * cc.o.ys + cls / cc.o.xs, ww = gpos_w * cc.o.xs + cls % cc.o.xs;
-            const bool ok = row_ok && hh < cc.o.out_h && ww < cc.o.out_w;
-            const int64_t off = (static_cast<int64_t>(gpos_b) * cc.o.out_h + hh) * cc.o.out_w + ww;
-            process_chunk32(ep, v, off, ok, col, cc.o.cls_cols);
-            store_chunk32(ep, v, off, ok, col, cc.o.cls_cols);
-          } else {
-            process_chunk32(ep, v, roff, row_ok, n0 + c0, N);
-            store_chunk32(ep, v, roff, row_ok, n0 + c0, N);
-          }
+          process_chunk32(ep, v, off, ok, col, ncol, have ? pre : nullptr);
+          prefetch(c0 + 64);
+          store_chunk32(ep, v, off, ok, col, ncol);
         }
       }
       fence_before();
@@ -859,13 +918,15 @@ int launch(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N,
   if constexpr (!A_MN && !B_MN && BN <= 64) {
     // implicit convolution with a K-major activation A and a plain weight B
     // of one N tile, unsplit: keep B resident (diagnostic bit 2 turns it off).
-    // Measured at 4,096 images: forward 7-11% and the stride-1 input gradient
-    // 9% faster; the 128-wide parity-class input gradient was 4% slower with
-    // a resident B and keeps streaming it.
-    constexpr int RB_STAGES = BN <= 32 ? 8 : 5;
+    // Measured at 4,096 images, resident against streamed in the same run:
+    // conv1 forward 8% faster, conv2 / conv3 forward and the stride-1 input
+    // gradient 0-11% depending on the machine; the 128-wide parity-class input
+    // gradient was 4% slower and keeps streaming B. 13 / 9 stages instead of
+    // 8 / 5 (the room of the unused output staging) measured the same.
+    constexpr int RB_STAGES = BN <= 32 ? 13 : 9;
     using R = Cfg<BN, false, false, RB_STAGES, true>;
     const int kt = (K + BK - 1) / BK;
-    if ((cc.a.mode == 1 || cc.a.mode == 3 || cc.a.mode == 4) && !bd && cc.b.mode == 0 && N <= BN && splits <= 1 && kt * R::kBBytes <= R::kResBytes &&
+    if ((cc.a.mode == 1 || cc.a.mode == 3 || cc.a.mode == 4) && cc.o.on && !bd && cc.b.mode == 0 && N <= BN && splits <= 1 && kt * R::kBBytes <= R::kResBytes &&
         !(ep.dbg & 4))
       return launch_cfg<BN, false, false, RB_STAGES, true>(A, lda, B, ldb, M, N, K, ep, 1, s, ad, bd, cc);
   }
