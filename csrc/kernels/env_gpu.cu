@@ -51,6 +51,22 @@ int upload(Span<T>* dst, const Span<T>& src, GpuEnv* g) {
   return 0;
 }
 
+// A start-node grid of the world model (its cells array) to the device.
+int upload_grid(surf::HullGrid* dst, const surf::HullGrid& src, GpuEnv* g) {
+  *dst = src;
+  dst->cells = nullptr;
+  if (!src.cells) return 0;
+  const size_t count = static_cast<size_t>(src.n[0]) * src.n[1] * src.n[2];
+  void* d = nullptr;
+  cudaError_t e = cudaMalloc(&d, sizeof(int32_t) * count);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  g->allocs.push_back(d);
+  e = cudaMemcpy(d, src.cells, sizeof(int32_t) * count, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  dst->cells = static_cast<const int32_t*>(d);
+  return 0;
+}
+
 template <typename T>
 int alloc_zero(T** dst, size_t count, GpuEnv* g) {
   void* d = nullptr;
@@ -124,6 +140,7 @@ SURF_EXPORT void* surf_genv_create(const void* host_core, int core_bytes, int* e
   g->n = h.cfg.num_envs;
   EnvCore& c = g->core;
   c = h;
+  for (auto& gr : c.map.world_grid) gr.cells = nullptr;   // host arrays until uploaded below
   int e = 0;
   e = e ? e : upload(&c.map.planes, h.map.planes, g);
   e = e ? e : upload(&c.map.clipnodes, h.map.clipnodes, g);
@@ -133,6 +150,7 @@ SURF_EXPORT void* surf_genv_create(const void* host_core, int core_bytes, int* e
   e = e ? e : upload(&c.map.volumes, h.map.volumes, g);
   e = e ? e : upload(&c.map.triggers, h.map.triggers, g);
   e = e ? e : upload(&c.map.spawns, h.map.spawns, g);
+  for (int hh = 0; hh < 4; ++hh) e = e ? e : upload_grid(&c.map.world_grid[hh], h.map.world_grid[hh], g);
   e = e ? e : upload(&c.wp, h.wp, g);
   e = e ? e : upload(&c.cum, h.cum, g);
   e = e ? e : upload(&c.tang, h.tang, g);

@@ -78,6 +78,12 @@ struct HullDescent {
     float p1[3], p2[3];
   };
 
+  // where a point query that would start at the root may start (HullGrid)
+  SURF_HD int root_of(const float* p) const {
+    const int32_t g = h.grid.point_start(p);
+    return g != HullGrid::kNone ? g : h.first;
+  }
+
   SURF_HD bool run(int num, float f1, float f2, const float* p1_in, const float* p2_in) {
     Frame stack[kDescentDepth];
     int sp = 0;
@@ -170,7 +176,8 @@ struct HullDescent {
         tr->dist = pl.dist;
       }
       // Back the impact point off until it is outside solid (numeric safety).
-      while (hull_point_contents(h, h.first, mid) == kSolid) {
+      // A point query from the root may start at its grid cell's node.
+      while (hull_point_contents(h, root_of(mid), mid) == kSolid) {
         s = static_cast<float>(s - 0.05);
         if (s < 0.f) break;
         fmid = df * s + fr.f1;
@@ -214,8 +221,12 @@ SURF_HD SURF_HD_NOINLINE void clip_model(const MapView& m, int model, const floa
   out->allsolid = true;
   out->fraction = 1.f;
   for (int k = 0; k < 3; ++k) out->endpos[k] = end[k];
+  // both endpoints in cells of the same start node: the descent from the
+  // root would reach it without a split (HullGrid), so start there
+  const int32_t g0 = h.grid.segment_start(a, b);
+  const int node0 = g0 != HullGrid::kNone ? g0 : h.first;
   HullDescent d{h, out};
-  d.run(h.first, 0.f, 1.f, a, b);
+  d.run(node0, 0.f, 1.f, a, b);
   if (out->allsolid) out->startsolid = true;
   if (out->startsolid) out->fraction = 0.f;
   if (out->fraction != 1.f)
@@ -265,7 +276,8 @@ SURF_HD inline void trace_player(const MapView& m, int usehull, const float star
 
 SURF_HD inline int point_contents(const MapView& m, const float p[3]) {
   HullView h0 = m.hull(0, 0);
-  int c = hull_point_contents(h0, h0.first, p);
+  const int32_t g = h0.grid.point_start(p);
+  int c = hull_point_contents(h0, g != HullGrid::kNone ? g : h0.first, p);
   if (c <= kCurrent0 && c >= kCurrentDown) c = kWater;
   else if (c == kSolid) return kSolid;
   for (const BrushEntity& v : m.volumes) {

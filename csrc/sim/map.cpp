@@ -169,7 +169,156 @@ bool Map::load_memory(const uint8_t* data, size_t size, std::string* err) {
   }
   if (models.empty()) { *err = "no models"; return false; }
   for (int k = 0; k < 3; ++k) { world_mins[k] = models[0].mins[k]; world_maxs[k] = models[0].maxs[k]; }
-  return parse_entities();
+  if (!parse_entities()) return false;
+  build_grids();
+  return true;
+}
+
+namespace {
+
+// Which child every point of the box [lo, hi) takes at this plane, decided
+// as the descent computes plane_side in float: 0 front (side >= 0), 1 back
+// (side < 0), -1 undecided. Axial planes are exact. For a sloped plane the
+// side is a float evaluation of dot(p, n) - d, whose error is below
+// 4 u (|p||n|_1 + |d|) with u = 2^-24; the margin is 16 times that bound.
+int classify_box(const Plane& pl, const double lo[3], const double hi[3]) {
+  const double d = pl.dist;
+  if (pl.type < 3) {
+    if (lo[pl.type] >= d) return 0;
+    if (hi[pl.type] <= d) return 1;
+    return -1;
+  }
+  double tmin = 1e300, tmax = -1e300, pmax = 0, n1 = 0;
+  for (int k = 0; k < 3; ++k) {
+    n1 += std::fabs(static_cast<double>(pl.normal[k]));
+    pmax = std::max(pmax, std::max(std::fabs(lo[k]), std::fabs(hi[k])));
+  }
+  for (int c = 0; c < 8; ++c) {
+    double t = -d;
+    for (int k = 0; k < 3; ++k) t += static_cast<double>(pl.normal[k]) * ((c >> k) & 1 ? hi[k] : lo[k]);
+    tmin = std::min(tmin, t);
+    tmax = std::max(tmax, t);
+  }
+  const double margin = 64.0 * 5.960464477539063e-08 * (n1 * pmax + std::fabs(d)) + 1e-3;
+  if (tmin > margin) return 0;
+  if (tmax < -margin) return 1;
+  return -1;
+}
+
+struct GridFill {
+  const Clipnode* nodes;
+  const Plane* planes;
+  const HullGrid* g;
+  int32_t* cells;
+  const std::vector<uint8_t>* shared;     // per node: reachable from the root along several paths
+  // Descend with the box of cell range [i0, i1) while every point agrees;
+  // assign the node reached, or split the range and go on from there.
+  void fill(int32_t node, const int32_t i0[3], const int32_t i1[3]) {
+    double lo[3], hi[3];
+    for (int k = 0; k < 3; ++k) {
+      lo[k] = static_cast<double>(g->mn[k]) + static_cast<double>(i0[k]) * g->size;
+      hi[k] = static_cast<double>(g->mn[k]) + static_cast<double>(i1[k]) * g->size;
+    }
+    while (node >= 0) {
+      const Clipnode& cn = nodes[node];
+      const int c = classify_box(planes[cn.plane], lo, hi);
+      if (c < 0) break;
+      node = cn.child[c];
+    }
+    int ax = 0;
+    for (int k = 1; k < 3; ++k)
+      if (i1[k] - i0[k] > i1[ax] - i0[ax]) ax = k;
+    if (node < 0 || i1[ax] - i0[ax] == 1) {
+      const int32_t v = node >= 0 && (*shared)[node] ? (node | HullGrid::kShared) : node;
+      for (int32_t z = i0[2]; z < i1[2]; ++z)
+        for (int32_t y = i0[1]; y < i1[1]; ++y)
+          for (int32_t x = i0[0]; x < i1[0]; ++x)
+            cells[(static_cast<int64_t>(z) * g->n[1] + y) * g->n[0] + x] = v;
+      return;
+    }
+    const int32_t mid = i0[ax] + (i1[ax] - i0[ax]) / 2;
+    int32_t a1[3] = {i1[0], i1[1], i1[2]}, b0[3] = {i0[0], i0[1], i0[2]};
+    a1[ax] = mid;
+    b0[ax] = mid;
+    fill(node, i0, a1);
+    fill(node, b0, i1);
+  }
+};
+
+}  // namespace
+
+void Map::build_grids() {
+  const MapView v = view();
+  for (int hull : {0, 1, 3}) {
+    grid_cells[hull].clear();
+    grid_meta[hull] = HullGrid();
+    const HullView h = v.hull(0, hull);
+    if (h.first < 0 || h.first >= h.last) continue;
+    // tree coordinates of the world model (origin 0): its bounds, padded
+    double lo[3], hi[3], ext = 0;
+    for (int k = 0; k < 3; ++k) {
+      lo[k] = static_cast<double>(world_mins[k]) - 64.0;
+      hi[k] = static_cast<double>(world_maxs[k]) + 64.0;
+      ext = std::max(ext, std::max(std::fabs(lo[k]), std::fabs(hi[k])));
+    }
+    if (!(ext < 1048576.0)) continue;      // cell bounds must stay exact floats
+    double size = 8.0;
+    int32_t n[3];
+    for (;;) {
+      int64_t total = 1;
+      for (int k = 0; k < 3; ++k) {
+        const double a = std::floor(lo[k] / size) * size;
+        n[k] = static_cast<int32_t>(std::ceil((hi[k] - a) / size));
+        total *= n[k];
+      }
+      if (total <= kGridCells) break;
+      size *= 2.0;
+    }
+    HullGrid& g = grid_meta[hull];
+    for (int k = 0; k < 3; ++k) {
+      g.mn[k] = static_cast<float>(std::floor(lo[k] / size) * size);
+      g.n[k] = n[k];
+    }
+    g.size = static_cast<float>(size);
+    g.inv = static_cast<float>(1.0 / size);
+    // nodes with more than one path from the root (a parent reached along
+    // several paths, or several parents): a segment's two endpoints reaching
+    // one of them may have taken different paths
+    const int nn = h.last + 1;
+    std::vector<int32_t> indeg(nn, 0);
+    std::vector<uint8_t> seen(nn, 0), shared(nn, 0);
+    std::vector<int32_t> order, stack{h.first};
+    while (!stack.empty()) {
+      const int32_t x = stack.back();
+      stack.pop_back();
+      if (x < 0 || x >= nn || seen[x]) continue;
+      seen[x] = 1;
+      order.push_back(x);
+      for (int c = 0; c < 2; ++c) {
+        const int32_t ch = h.nodes[x].child[c];
+        if (ch >= 0 && ch < nn) {
+          ++indeg[ch];
+          stack.push_back(ch);
+        }
+      }
+    }
+    // propagate down to a fixed point (the graph is acyclic)
+    for (int32_t x : order) if (indeg[x] > 1) shared[x] = 1;
+    for (bool changed = true; changed;) {
+      changed = false;
+      for (int32_t x : order) {
+        if (!shared[x]) continue;
+        for (int c = 0; c < 2; ++c) {
+          const int32_t ch = h.nodes[x].child[c];
+          if (ch >= 0 && ch < nn && !shared[ch]) { shared[ch] = 1; changed = true; }
+        }
+      }
+    }
+    grid_cells[hull].assign(static_cast<size_t>(n[0]) * n[1] * n[2], HullGrid::kNone);
+    GridFill f{h.nodes, h.planes, &g, grid_cells[hull].data(), &shared};
+    const int32_t i0[3] = {0, 0, 0};
+    f.fill(h.first, i0, n);
+  }
 }
 
 namespace {
@@ -203,6 +352,10 @@ MapView Map::view() const {
   v.triggers = span_of(triggers);
   v.spawns = span_of(spawns);
   for (int k = 0; k < 3; ++k) { v.world_mins[k] = world_mins[k]; v.world_maxs[k] = world_maxs[k]; }
+  for (int h = 0; h < 4; ++h) {
+    v.world_grid[h] = grid_meta[h];
+    v.world_grid[h].cells = grid_cells[h].empty() ? nullptr : grid_cells[h].data();
+  }
   return v;
 }
 

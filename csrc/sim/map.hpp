@@ -6,6 +6,7 @@
 // CLIPNODES, and the entity lump is parsed for spawns, trigger_teleport /
 // trigger_hurt / trigger_push, solid brush entities and contents volumes.
 #pragma once
+#include <climits>
 #include <cstdint>
 #include <string>
 #include <vector>
@@ -14,6 +15,68 @@
 
 namespace surf {
 
+// Start-node grid of one clip tree (an acceleration structure of this build;
+// the engine always descends from the root): a uniform grid of power-of-two
+// cells over the tree's bounds, in the tree's coordinates. A cell holds the
+// deepest node that the descent reaches, with the same plane-side decisions,
+// from EVERY point of the cell (or the leaf contents it reaches). A point
+// query takes exactly that root-to-node path, so it may start there. So may
+// a segment whose endpoints lie in one cell (the cell is convex), or in two
+// cells holding the same internal node that has a single path from the root
+// (kShared marks nodes with several parents -- a compiler may share
+// subtrees -- and leaf contents are not unique either). Either way the
+// result is bit-identical to a descent from the root. Axial planes decide
+// a cell exactly (cell bounds are floats and p - d keeps the sign of p - d);
+// sloped planes only when every corner clears the plane by a margin far
+// above the float error of dot(p, n) - d.
+struct HullGrid {
+  static constexpr int32_t kNone = INT32_MIN;
+  static constexpr int32_t kShared = 1 << 30;   // flag on a cell's node: reachable along several paths
+  const int32_t* cells = nullptr;   // null: no grid (descents start at the root)
+  float mn[3] = {0, 0, 0};          // grid origin: a multiple of the cell size
+  float size = 0, inv = 0;          // cell size (a power of two) and its inverse
+  int32_t n[3] = {0, 0, 0};
+
+  // The node of the cell containing p, or kNone (no grid, p outside it, or p
+  // on the far side of a rounding boundary of the index estimate); *cell
+  // receives the cell's index.
+  SURF_HD int32_t lookup(const float p[3], int64_t* cell = nullptr) const {
+    if (!cells) return kNone;
+    int32_t idx[3];
+    for (int k = 0; k < 3; ++k) {
+      const float f = (p[k] - mn[k]) * inv;
+      if (!(f >= 0.f) || f >= static_cast<float>(n[k])) return kNone;
+      const int32_t i = static_cast<int32_t>(f);
+      const float lo = mn[k] + static_cast<float>(i) * size;    // exact: integer multiples of a power of two
+      if (p[k] < lo || p[k] >= lo + size) return kNone;
+      idx[k] = i;
+    }
+    const int64_t c = (static_cast<int64_t>(idx[2]) * n[1] + idx[1]) * n[0] + idx[0];
+    if (cell) *cell = c;
+    return cells[c];
+  }
+
+  SURF_HD static int32_t node_of(int32_t v) { return v >= 0 ? (v & ~kShared) : v; }
+
+  // Where a point query at p may start (kNone: at the root).
+  SURF_HD int32_t point_start(const float p[3]) const {
+    const int32_t v = lookup(p);
+    return v == kNone ? kNone : node_of(v);
+  }
+
+  // Where a descent of the segment a -> b may start: the node of their one
+  // cell, or the single-path internal node both cells hold; else kNone.
+  SURF_HD int32_t segment_start(const float a[3], const float b[3]) const {
+    int64_t ca = -1, cb = -2;
+    const int32_t va = lookup(a, &ca);
+    if (va == kNone) return kNone;
+    const int32_t vb = lookup(b, &cb);
+    if (vb != va) return kNone;
+    if (va >= 0 && !(va & kShared)) return va;
+    return ca == cb ? node_of(va) : kNone;
+  }
+};
+
 // One BSP clip tree view: nodes + planes + the box the tree was expanded by.
 struct HullView {
   const Clipnode* nodes = nullptr;
@@ -21,6 +84,7 @@ struct HullView {
   int first = 0, last = 0;          // root node index, last valid node index
   float clip_mins[3] = {0, 0, 0};
   float clip_maxs[3] = {0, 0, 0};
+  HullGrid grid;                    // start-node grid (the world model only)
 };
 
 enum class TriggerKind : int32_t { kTeleport = 0, kHurt = 1, kPush = 2 };
@@ -60,6 +124,7 @@ struct MapView {
   Span<Trigger> triggers;
   Span<SpawnPoint> spawns;
   float world_mins[3] = {0, 0, 0}, world_maxs[3] = {0, 0, 0};
+  HullGrid world_grid[4];             // start-node grids of the world model's hulls
 
   SURF_HD HullView hull(int model, int bsp_hull) const {
     HullView v;
@@ -74,6 +139,7 @@ struct MapView {
     }
     v.first = m.headnode[bsp_hull];
     for (int k = 0; k < 3; ++k) { v.clip_mins[k] = hull_mins(bsp_hull, k); v.clip_maxs[k] = hull_maxs(bsp_hull, k); }
+    if (model == 0) v.grid = world_grid[bsp_hull];
     return v;
   }
 };
@@ -102,8 +168,15 @@ class Map {
 
   float world_mins[3] = {0, 0, 0}, world_maxs[3] = {0, 0, 0};
 
+  // Start-node grids of the world model's hulls 0 (point), 1 (standing) and
+  // 3 (crouched), built at load; at most kGridCells cells each.
+  static constexpr int64_t kGridCells = int64_t(1) << 21;
+  std::vector<int32_t> grid_cells[4];
+  HullGrid grid_meta[4];
+
  private:
   bool parse_entities();
+  void build_grids();
 };
 
 }  // namespace surf

@@ -14,6 +14,9 @@
 //      touches ground
 //   D  throughput: random actions through the env batch on one thread, no
 //      NaN in any state, >= 100k env ticks/s
+//   E  start-node grids: random traces and point contents starting at a grid
+//      cell's node equal the root-started ones bit for bit (no reference
+//      counterpart: the grids are this build's)
 // Exit status 0 when every gate passes; one line per check on stdout.
 #include <chrono>
 #include <cmath>
@@ -220,6 +223,41 @@ int main() {
     const double rate = static_cast<double>(ticks) * cfg.num_envs / dt;
     check(finite, "D no NaN / inf in any observation", finite ? 1 : 0, 1);
     check(rate >= 1e5, "D single-thread env ticks/s", rate, 1e5);
+  }
+  // ---- E: start-node grids: traces and point contents that start at a grid
+  // cell's node equal those that start at the root, bit for bit
+  {
+    const MapView with = map->view();
+    MapView without = with;
+    for (auto& g : without.world_grid) g = HullGrid();
+    std::mt19937 rng(11);
+    std::uniform_real_distribution<float> ux(with.world_mins[0] - 40, with.world_maxs[0] + 40),
+        uy(with.world_mins[1] - 40, with.world_maxs[1] + 40), uz(with.world_mins[2] - 40, with.world_maxs[2] + 40);
+    std::uniform_real_distribution<float> step(-40.f, 40.f);
+    int mismatch = 0, from_grid = 0;
+    const int n = 200000;
+    for (int i = 0; i < n; ++i) {
+      const float a[3] = {ux(rng), uy(rng), uz(rng)};
+      // short moves (most pmove traces) and long ones
+      const float sc = i % 4 == 0 ? 20.f : 1.f;
+      const float b[3] = {a[0] + sc * step(rng), a[1] + sc * step(rng), a[2] + sc * step(rng)};
+      const int usehull = i % 3;
+      Trace t1, t2;
+      trace_player(with, usehull, a, b, &t1);
+      trace_player(without, usehull, a, b, &t2);
+      const HullView hv = with.hull(0, bsp_hull_of_usehull(usehull));
+      float la[3], lb[3];
+      for (int k = 0; k < 3; ++k) {
+        const float off = hv.clip_mins[k] - player_mins(usehull, k) + with.models[0].origin[k];
+        la[k] = a[k] - off;
+        lb[k] = b[k] - off;
+      }
+      from_grid += hv.grid.segment_start(la, lb) != HullGrid::kNone;
+      if (std::memcmp(&t1, &t2, sizeof t1) != 0) ++mismatch;
+      if (point_contents(with, a) != point_contents(without, a)) ++mismatch;
+    }
+    check(mismatch == 0, "E grid-started traces / contents == root-started", mismatch, 0);
+    check(from_grid > n / 4, "E grid starts most short traces below the root", from_grid, n / 4);
   }
   std::printf("%s: %d failed\n", g_fail ? "FAILED" : "OK", g_fail);
   return g_fail ? 1 : 0;
