@@ -12,6 +12,7 @@
 // which agrees with the host's to within the last bit of a double and so, after
 // the cast to float, almost always exactly (tests compare trajectories).
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -117,7 +118,30 @@ __global__ void reset_kernel(EnvCore c, int n, uint64_t seed, RowOut obs, RowOut
   }
 }
 
-int threads_for(int) { return 32; }
+// Envs per block: the step is a chain of dependent loads per env (hull
+// descents) whose lanes diverge (13 of 32 lanes active per instruction with
+// full warps), so warps run few envs and every SM holds many of them: about
+// 14 blocks per SM. Measured at 2048 envs: 2 or 4 envs per block 25M
+// ticks/s, 8: 20M, 32: 12M; at 16,384 envs: 8 per block 121M, 32: 97M.
+int threads_for(int n) {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        sms < 1)
+      sms = 148;
+  }
+  static int forced = -1;                 // SURF_GENV_THREADS: a fixed block size (timing studies)
+  if (forced < 0) {
+    const char* e = std::getenv("SURF_GENV_THREADS");
+    const int v = e ? std::atoi(e) : 0;
+    forced = (v >= 1 && v <= 128) ? v : 0;
+  }
+  if (forced) return forced;
+  int t = 2;
+  while (t < 32 && t * sms * 14 < n) t *= 2;
+  return t;
+}
 
 }  // namespace
 
