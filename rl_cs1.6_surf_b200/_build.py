@@ -76,6 +76,33 @@ def _targets():
     return t
 
 
+# Sanitizer builds of the simulator (host code only), built on demand by
+# tests/test_sanitizers.py rather than by build(): the native gates under
+# AddressSanitizer + UndefinedBehaviorSanitizer, and the worker-pool stress
+# program under ThreadSanitizer.
+_SAN_COMMON = ["-O1", "-g", "-fno-omit-frame-pointer", "-fno-sanitize-recover=all"]
+
+
+def _sanitizer_targets():
+    sim = [str(p) for p in sorted((CSRC / "sim").glob("*.cpp")) if not p.name.endswith("c_api.cpp")]
+    tests = CSRC / "sim" / "tests"
+    return {"surfsim_gates_asan": ("g++exe", sim + [str(tests / "gates.cpp")],
+                                   _SAN_COMMON + ["-fsanitize=address,undefined"], []),
+            "surfsim_pool_tsan": ("g++exe", sim + [str(tests / "pool_stress.cpp")],
+                                  _SAN_COMMON + ["-fsanitize=thread"], [])}
+
+
+def build_sanitized(verbose: bool = False) -> dict:
+    """Build the sanitizer executables (if stale); {name: path}."""
+    out = {}
+    for name, spec in _sanitizer_targets().items():
+        msg = _compile(name, spec, False)
+        if verbose:
+            print(msg, flush=True)
+        out[name] = LIB / name
+    return out
+
+
 def _digest(compiler: str, srcs: list[str], flags: list[str]) -> str:
     h = hashlib.sha256()
     h.update(" ".join([compiler] + flags).encode())

@@ -541,10 +541,10 @@ class Trainer:
             self._run_group(g, 0)
         for t in range(T):
             for g in range(G):
-                t0 = tm.now()
+                t0 = tm.begin("wait_gpu")
                 self.grp_events[g].synchronize()
                 tm.add("wait_gpu", t0)
-                t0 = tm.now()
+                t0 = tm.begin("env")
                 self._env_step_group(g)
                 tm.add("env", t0)
                 if self.cfg.ep_ticks:
@@ -752,20 +752,20 @@ class Trainer:
             self._env_ready = True
         self.iteration += 1
         self.reward.set_step(self.global_step)
-        t0 = tm.now()
+        t0 = tm.begin("rollout")
         if self.gpu:
             self.rollout_gpu()
         else:
             self.rollout_cpu()
         tm.add("rollout", t0)
         if self.rnd is not None:
-            t0 = tm.now()
+            t0 = tm.begin("rnd")
             self._train_rnd()
             tm.add("rnd", t0)
-        t0 = tm.now()
+        t0 = tm.begin("respawn")
         self._refresh_respawn_pool()
         tm.add("respawn", t0)
-        t0 = tm.now()
+        t0 = tm.begin("update")
         if self.gpu:
             ev = tm.gpu_start("update_gpu")
             self.update_gpu()

@@ -389,3 +389,25 @@ def test_tas_search_and_chain_replay_the_recording(tmp_path):
     c = tas.tas_chain(core, score, e, window=40, iters=2, max_windows=2, seed=1)
     assert len(c["windows"]) == 2 and c["actions"].shape == (80, 6)
     core.close()
+
+
+def test_phase_timer_nvtx_ranges_balance(monkeypatch):
+    """SURF_NVTX=1 turns every timer phase into an NVTX range (push at the
+    start, pop at the end), with timing off too."""
+    import torch
+    from surfb200.utils.timer import PhaseTimer
+    calls = []
+    monkeypatch.setattr(torch.cuda.nvtx, "range_push", lambda name: calls.append(("push", name)))
+    monkeypatch.setattr(torch.cuda.nvtx, "range_pop", lambda: calls.append(("pop", None)))
+    monkeypatch.setenv("SURF_NVTX", "1")
+    tm = PhaseTimer(False, True)
+    t0 = tm.begin("update")
+    ev = tm.gpu_start("update_gpu")
+    tm.gpu_end(ev)
+    tm.add("update", t0)
+    assert calls == [("push", "update"), ("push", "update_gpu"), ("pop", None), ("pop", None)]
+    monkeypatch.setenv("SURF_NVTX", "0")
+    calls.clear()
+    tm = PhaseTimer(True, False)
+    tm.add("env", tm.begin("env"))
+    assert calls == [] and "env" in tm.acc
