@@ -102,6 +102,9 @@ class TrainConfig:
     record_every: float = 0.0
     eval_eps: int = 3
     timing: bool = False
+    # data parallel: every this many iterations all ranks compare a checksum of
+    # their parameter replicas and raise ReplicaDivergence if they differ (0: off)
+    replica_check_every: int = 0
 
     def to_dict(self) -> dict:
         d = asdict(self)

@@ -66,6 +66,10 @@ def build_spawn_pool(core, kind: str, cfg, procedural=None):
     raise ValueError(f"unknown spawn mode {kind!r}")
 
 
+class ReplicaDivergence(RuntimeError):
+    """Data-parallel parameter replicas no longer agree."""
+
+
 class Trainer:
     def __init__(self, cfg: TrainConfig, rank: int = 0, world: int = 1, comm=None, verbose: bool = True):
         self.cfg = cfg
@@ -744,6 +748,19 @@ class Trainer:
         return {"policy_loss": stats[0] / stats[3], "value_loss": stats[1] / stats[3], "entropy": stats[2] / stats[3]}
 
     # ---- iteration ------------------------------------------------------------------------------
+    def _check_replicas(self) -> None:
+        """Every ``replica_check_every`` iterations, compare the ranks'
+        parameter checksums (one collective pair, taken by every rank at the
+        same iteration, so all ranks raise together). Reference: the parameter
+        checksum of the data-parallel design, docs/ddp-plan.md:448-460."""
+        every = int(getattr(self.cfg, "replica_check_every", 0) or 0)
+        if self.comm is None or every <= 0 or self.iteration % every:
+            return
+        lo, hi = self.comm.checksum(self.net)
+        if lo != hi:
+            raise ReplicaDivergence(f"iteration {self.iteration}: parameter replicas differ across ranks "
+                                    f"(checksum min {lo!r}, max {hi!r})")
+
     def train_iteration(self) -> dict:
         tm = self.timer
         tm.start_iter()
@@ -781,6 +798,7 @@ class Trainer:
         else:
             loss = self.update_cpu()
         tm.add("update", t0)
+        self._check_replicas()
         stats = dict(self.reward.pop_stats(), **loss)
         stats["global_step"] = self.global_step
         stats["iteration"] = self.iteration

@@ -88,6 +88,64 @@ def gloo_dead_rank(rank: int, world: int, port: int, q) -> None:
     _report(q, rank, body)
 
 
+def gloo_stalled_rank(rank: int, world: int, port: int, q) -> None:
+    """Rank 1 stalls (alive, but never reaches the collective) for longer
+    than the process group's timeout; rank 0's collective must end with an
+    error instead of waiting for it."""
+    _env(rank, world, port)
+
+    def body():
+        import time
+        import torch
+        import torch.distributed as dist
+        import surfb200  # noqa: F401
+        from surfb200.parallel.dist import init_process_group
+        init_process_group("gloo", timeout_s=3)
+        dist.barrier()
+        if rank == 1:
+            time.sleep(10)                     # stalled between steps
+            return "stalled"
+        t = torch.ones(8)
+        t0 = time.time()
+        try:
+            dist.all_reduce(t)
+        except Exception as e:                 # noqa: BLE001
+            return f"detected after {time.time() - t0:.1f} s: {type(e).__name__}"
+        raise AssertionError("all_reduce with a stalled peer returned normally")
+
+    _report(q, rank, body)
+
+
+def gloo_corrupt_replica(rank: int, world: int, port: int, q) -> None:
+    """Two CPU ranks train with a replica check every iteration; after the
+    first iteration rank 1's parameters are corrupted, and the check of the
+    second iteration raises ReplicaDivergence on both ranks."""
+    _env(rank, world, port)
+
+    def body():
+        import surfb200  # noqa: F401
+        from surfb200.parallel.dist import NcclComm, init_process_group
+        from surfb200.rewards.spec import RewardSpec
+        from surfb200.trainer.config import TrainConfig
+        from surfb200.trainer.ppo import ReplicaDivergence, Trainer
+        init_process_group("gloo", timeout_s=60)
+        comm = NcclComm()
+        cfg = TrainConfig(map="ramps", envs=8, n_steps=4, epochs=1, minibatches=1, vision=False, device="cpu",
+                          graphs=False, ep_ticks=120, reward=RewardSpec(mode="speed"), replica_check_every=1)
+        tr = Trainer(cfg, rank=rank, world=world, comm=comm, verbose=False)
+        tr.train_iteration()                   # replicas agree: no error
+        if rank == 1:
+            tr.net.flat[7] += 1e-3             # a flipped parameter on one rank
+        try:
+            tr.train_iteration()
+        except ReplicaDivergence as e:
+            comm.close()
+            return f"detected: {e}"
+        raise AssertionError("diverged replicas were not detected")
+
+    _report(q, rank, body)
+
+
 # ---- GPU (NCCL + peer memory) ----------------------------------------------------------------
 def p2p_collectives(rank: int, world: int, port: int, q) -> None:
     """Peer-memory gradient step / moments / count merge vs plain torch."""
