@@ -13,6 +13,15 @@ namespace surfk {
 
 inline __host__ __device__ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Device error flag (one int per device, shared by the kernels and read by
+// the host after a step): the first error code wins. Codes 1-5 are the GEMM
+// pipeline's bounded waits; the index checks of the data-driven gathers use
+// the codes below (the offending access is skipped, its output zeroed).
+enum ErrCode : int { kErrGatherIndex = 0x100, kErrStackIndex = 0x101, kErrLossIndex = 0x102 };
+__device__ __forceinline__ void report_error(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
 __device__ __forceinline__ float bf16_to_f32(uint16_t h) { return __uint_as_float(static_cast<uint32_t>(h) << 16); }
 
 // Round-to-nearest-even float -> bf16 bits (NaN kept quiet).

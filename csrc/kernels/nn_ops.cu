@@ -172,9 +172,11 @@ __global__ void colsum_kernel(const T* x, int64_t ldx, int64_t M, int N, float* 
   }
 }
 
-// dst[i, :] = src[idx[i] + offset, :] for rows of `row_bytes` (multiple of 4)
+// dst[i, :] = src[idx[i] + offset, :] for rows of `row_bytes` (multiple of 4).
+// A source row outside [0, src_rows) is not read: the row is zeroed and the
+// device error flag records kErrGatherIndex.
 __global__ void gather_kernel(const uint8_t* src, int64_t src_stride, const int64_t* idx, int64_t offset, int64_t n,
-                              int row_bytes, uint8_t* dst, int64_t dst_stride) {
+                              int row_bytes, uint8_t* dst, int64_t dst_stride, int64_t src_rows, int* err) {
   const int words = row_bytes / 4;
   const int64_t total = n * words;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -182,7 +184,10 @@ __global__ void gather_kernel(const uint8_t* src, int64_t src_stride, const int6
     const int64_t r = i / words;
     const int w = static_cast<int>(i % words);
     const int64_t s = idx[r] + offset;
-    reinterpret_cast<uint32_t*>(dst + r * dst_stride)[w] = reinterpret_cast<const uint32_t*>(src + s * src_stride)[w];
+    uint32_t v = 0;
+    if (s >= 0 && s < src_rows) v = reinterpret_cast<const uint32_t*>(src + s * src_stride)[w];
+    else if (w == 0) surfk::report_error(err, surfk::kErrGatherIndex);
+    reinterpret_cast<uint32_t*>(dst + r * dst_stride)[w] = v;
   }
 }
 
@@ -247,6 +252,8 @@ struct StackArgs {
   int* age_cur;             // modes 0/1: [N] running age
   int* age_rec;             // mode 0: ages recorded per row; mode 2: ages per flat sample (read)
   const int64_t* idx;       // mode 1: env per row; mode 2: flat sample t * N + n per row
+  int64_t idx_bound;        // mode 2: flat samples stored (mode 1: N); an index outside is reported
+  int* err;                 // device error flag (may be null)
   const uint16_t* cur;      // mode 1: the terminal frames, row r at cur + r * cur_ld
   int64_t cur_ld;
   uint16_t* out;
@@ -255,10 +262,11 @@ struct StackArgs {
 
 template <int K, int C0>
 __global__ void __launch_bounds__(256) frame_stack_kernel(StackArgs a) {
-  __shared__ int s_age, s_env, s_slot;
+  __shared__ int s_age, s_env, s_slot, s_bad;
   const int r = blockIdx.x;
   if (threadIdx.x == 0) {
-    int n, age, slot;
+    int n = 0, age = 0, slot = 0;
+    s_bad = 0;
     if (a.mode == 0) {
       n = a.lo + r;
       age = a.age_cur[n];
@@ -267,20 +275,35 @@ __global__ void __launch_bounds__(256) frame_stack_kernel(StackArgs a) {
       a.age_rec[r] = age;
       slot = a.slot0;
     } else if (a.mode == 1) {
-      n = static_cast<int>(a.idx[r]);
-      age = min(a.age_cur[n] + 1, a.pro);
-      slot = a.slot0;
+      const int64_t i = a.idx[r];
+      if (i < 0 || i >= a.N) {
+        s_bad = 1;
+      } else {
+        n = static_cast<int>(i);
+        age = min(a.age_cur[n] + 1, a.pro);
+        slot = a.slot0;
+      }
     } else {
       const int64_t i = a.idx[r];
-      n = static_cast<int>(i % a.N);
-      age = a.age_rec[i];
-      slot = a.pro + static_cast<int>(i / a.N);
+      if (i < 0 || i >= a.idx_bound) {
+        s_bad = 1;
+      } else {
+        n = static_cast<int>(i % a.N);
+        age = a.age_rec[i];
+        slot = a.pro + static_cast<int>(i / a.N);
+      }
     }
+    if (s_bad) surfk::report_error(a.err, surfk::kErrStackIndex);
     s_age = age;
     s_env = n;
     s_slot = slot;
   }
   __syncthreads();
+  if (s_bad) {                        // invalid index: the row is zeroed, nothing is read
+    uint4* dst = reinterpret_cast<uint4*>(a.out + r * a.out_ld);
+    for (int q = threadIdx.x; q < a.fr / 8 * K; q += blockDim.x) dst[q] = make_uint4(0, 0, 0, 0);
+    return;
+  }
   const int age = s_age, n = s_env, slot0 = s_slot;
   const uint4* src[K];
 #pragma unroll
@@ -372,12 +395,15 @@ SURF_EXPORT int surf_colsum(const void* x, int bf16, int64_t ldx, int64_t M, int
   SURF_RETURN_LAUNCH();
 }
 
+// src_rows: rows of src (an index outside is reported through err, a device
+// int the kernels set once; may be null).
 SURF_EXPORT int surf_gather_rows(const void* src, int64_t src_stride_bytes, const int64_t* idx, int64_t offset,
-                                 int64_t n, int row_bytes, void* dst, int64_t dst_stride_bytes, void* stream) {
+                                 int64_t n, int row_bytes, void* dst, int64_t dst_stride_bytes, int64_t src_rows,
+                                 int* err, void* stream) {
   if (row_bytes & 3) return static_cast<int>(cudaErrorInvalidValue);
   gather_kernel<<<blocks_for(n * (row_bytes / 4), 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint8_t*>(src), src_stride_bytes, idx, offset, n, row_bytes, static_cast<uint8_t*>(dst),
-      dst_stride_bytes);
+      dst_stride_bytes, src_rows, err);
   SURF_RETURN_LAUNCH();
 }
 
@@ -402,7 +428,8 @@ SURF_EXPORT int surf_conv_weight_t(const void* w, int CO, int C, int k, int s, v
 SURF_EXPORT int surf_frame_stack(const void* frames, int64_t slot_stride, int ld, int fr, int C0, int K,
                                  const int* offs, int pro, int ring, int mode, int N, int lo, int slot0,
                                  const float* done, int* age_cur, int* age_rec, const int64_t* idx, const void* cur,
-                                 int64_t cur_ld, void* out, int64_t out_ld, int rows, void* stream) {
+                                 int64_t cur_ld, void* out, int64_t out_ld, int rows, int64_t idx_bound, int* err,
+                                 void* stream) {
   if (K < 1 || K > 5 || (C0 != 1 && C0 != 2) || (fr & 7) || (ld & 7) || (slot_stride & 7) || (out_ld & 7) ||
       (cur_ld & 7) || mode < 0 || mode > 2 || pro < 0 || rows < 0 || N < 1 ||
       ((reinterpret_cast<uintptr_t>(frames) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(cur)) &
@@ -430,6 +457,8 @@ SURF_EXPORT int surf_frame_stack(const void* frames, int64_t slot_stride, int ld
   a.done = done;
   a.age_cur = age_cur;
   a.age_rec = age_rec;
+  a.idx_bound = mode == 1 ? N : idx_bound;
+  a.err = err;
   a.idx = idx;
   a.cur = static_cast<const uint16_t*>(cur);
   a.cur_ld = cur_ld;

@@ -179,6 +179,8 @@ struct LossArgs {
   const float* coef;    // device: clip range, value coefficient, entropy coefficient
   float count;          // samples the loss averages over (global minibatch size)
   int norm_adv;
+  int64_t n_src;        // rows of act / old_logp / adv / ret (an idx outside is reported, the row skipped)
+  int* err;             // device error flag (may be null)
 };
 
 // stats[0..5]: policy loss, value loss, entropy, approx_kl, clip fraction, samples (sums)
@@ -192,8 +194,14 @@ __global__ void ppo_loss_kernel(const T* logits, int64_t ld_logits, const float*
   const int lane = threadIdx.x & 31;
   float pg = 0, vl = 0, ent = 0, kl = 0, clipped = 0, dls = 0;
   const float clip = la.coef[0], vf_coef = la.coef[1], ent_coef = la.coef[2];
-  if (warp < n) {
-    const int64_t src = idx ? idx[warp] : warp;
+  const int64_t src = warp < n ? (idx ? idx[warp] : warp) : 0;
+  const bool bad = warp < n && (src < 0 || src >= la.n_src);
+  if (bad && lane == 0) surfk::report_error(la.err, surfk::kErrLossIndex);
+  if (bad) {                        // no gradient from a row that cannot be read
+    for (int c = lane; c < hs.width; c += 32) dlogits[warp * ld_dlogits + c] = 0.0f;
+    if (lane == 0) dvalue[warp * ld_dvalue] = 0.0f;
+  }
+  if (warp < n && !bad) {
     const T* row = logits + warp * ld_logits;
     const int32_t* a = act + src * ld_act;
     // pass 1: log-prob and entropy of every head
@@ -266,7 +274,7 @@ __global__ void ppo_loss_kernel(const T* logits, int64_t ld_logits, const float*
   __shared__ float red[8][8];
   const int wib = threadIdx.x >> 5;
   if (lane == 0) {
-    const bool live = warp < n;
+    const bool live = warp < n && !bad;
     red[wib][0] = live ? pg : 0.f;
     red[wib][1] = live ? vl : 0.f;
     red[wib][2] = live ? ent : 0.f;
@@ -350,10 +358,10 @@ SURF_EXPORT int surf_ppo_loss(const void* logits, int logits_bf16, int64_t ld_lo
                               const int* sizes, int n_heads, const int* slots, int cont, const float* log_std,
                               const float* coef, float count, int norm_adv, int n,
                               float* dlogits, int64_t ld_dlogits, float* dvalue, int64_t ld_dvalue, float* dlog_std,
-                              float* stats, void* stream) {
+                              float* stats, int64_t n_src, int* err, void* stream) {
   const int neutral[6] = {-1, -1, -1, -1, -1, -1};
   HeadSpec hs = make_spec(sizes, n_heads, slots, cont, neutral);
-  LossArgs la{coef, count, norm_adv};
+  LossArgs la{coef, count, norm_adv, n_src, err};
   const int threads = 256, blocks = static_cast<int>(surfk::ceil_div(static_cast<int64_t>(n) * 32, threads));
   auto s = static_cast<cudaStream_t>(stream);
   if (logits_bf16)

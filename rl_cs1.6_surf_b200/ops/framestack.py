@@ -39,7 +39,7 @@ MAX_FRAMES = len(STACK_STRIDES) + 1
 _V, _I, _L = _lib._V, _lib._I, _lib._L
 _lib.register(NLIB, {
     "surf_frame_stack": (_I, [_V, _L, _I, _I, _I, _I, _V, _I, _I, _I, _I, _I, _I, _V, _V, _V, _V, _V, _L, _V, _L,
-                              _I, _V]),
+                              _I, _L, _V, _V]),
 })
 
 MODE_ROLLOUT, MODE_TERMINAL, MODE_GATHER = 0, 1, 2
@@ -61,10 +61,14 @@ def _launch(frames: torch.Tensor, fr: int, C0: int, offs: Sequence[int], pro: in
     arr = (c_int * K)(*offs)
     if frames.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
         raise ValueError("frame stacking works on bf16 frames")
+    from .gemm import error_flag
+    # gather mode: flat sample indices must address the recorded ages
+    bound = age_rec.numel() if (mode == MODE_GATHER and age_rec is not None) else 0
     check(_lib.lib(NLIB).surf_frame_stack(
         ptr(frames), frames.stride(0), frames.stride(1), int(fr), int(C0), K, arr, int(pro), int(ring), int(mode),
         int(N), int(lo), int(slot0), ptr(done), ptr(age_cur), ptr(age_rec), ptr(idx), ptr(cur),
-        cur.stride(0) if cur is not None else 0, ptr(out), out.stride(0), int(rows), stream_ptr(out.device)),
+        cur.stride(0) if cur is not None else 0, ptr(out), out.stride(0), int(rows), int(bound),
+        ptr(error_flag(out.device)), stream_ptr(out.device)),
         "surf_frame_stack")
     return out
 

@@ -42,7 +42,8 @@ _SIG = {
     "surf_im2col": (c_int, [c_void_p] + [c_int] * 7 + [c_void_p, c_int64, c_void_p]),
     "surf_col2im": (c_int, [c_void_p, c_int64, c_void_p, c_void_p] + [c_int] * 8 + [c_void_p]),
     "surf_colsum": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int, c_void_p, c_void_p]),
-    "surf_gather_rows": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_void_p]),
+    "surf_gather_rows": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_int64,
+                                 c_void_p, c_void_p]),
     "surf_f32_to_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_void_p]),
     "surf_adam_norm": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
     "surf_adam_update": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
@@ -53,20 +54,30 @@ _lib.register(NLIB, _SIG)
 _err_flags: dict = {}
 
 
+ERROR_CODES = {1: "GEMM producer wait timed out", 2: "GEMM MMA wait timed out", 3: "GEMM epilogue wait timed out",
+               4: "GEMM accumulator wait timed out", 5: "GEMM resident-operand wait timed out",
+               0x100: "row gather index out of range", 0x101: "frame-stack index out of range",
+               0x102: "PPO loss sample index out of range"}
+
+
 def error_flag(device) -> torch.Tensor:
-    """Per-device int32 flag the kernels set when a bounded wait expires."""
+    """Per-device int32 flag the kernels set on a bounded-wait timeout or an
+    out-of-range index (first code wins; see ERROR_CODES)."""
     key = torch.device(device)
+    if key.type == "cuda" and key.index is None:      # "cuda" and "cuda:<current>" share one flag
+        key = torch.device("cuda", torch.cuda.current_device())
     if key not in _err_flags:
         _err_flags[key] = torch.zeros(1, dtype=torch.int32, device=key)
     return _err_flags[key]
 
 
 def check_error_flag(device) -> None:
+    """Raise KernelError (and clear the flag) if a kernel reported an error."""
     f = error_flag(device)
     v = int(f.item())
     if v:
         f.zero_()
-        raise _lib.KernelError(f"tensor-core kernel pipeline timed out (code {v})")
+        raise _lib.KernelError(f"device error {v:#x}: {ERROR_CODES.get(v, 'unknown code')}")
 
 
 def _pick_bn(n: int, b_mn: bool) -> int:
@@ -192,7 +203,8 @@ def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: torch.Tensor, offset:
     row_bytes = src.shape[1] * src.element_size()
     check(_lib.lib(NLIB).surf_gather_rows(ptr(src), src.stride(0) * src.element_size(), ptr(idx), int(offset),
                                           idx.numel(), row_bytes, ptr(out), out.stride(0) * out.element_size(),
-                                          stream_ptr(src.device)), "surf_gather_rows")
+                                          src.shape[0], ptr(error_flag(src.device)), stream_ptr(src.device)),
+          "surf_gather_rows")
     return out
 
 

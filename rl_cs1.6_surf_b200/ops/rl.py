@@ -36,10 +36,15 @@ _lib.register(RLIB, {
     "surf_ppo_loss": (c_int, [c_void_p, c_int, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p,
                               c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
                               c_float, c_int, c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p,
-                              c_void_p]),
+                              c_int64, c_void_p, c_void_p]),
 })
 
 LOG_SQRT_2PI = 0.9189385332046727
+
+
+def _error_flag(device):
+    from .gemm import error_flag
+    return error_flag(device)
 
 
 class HeadArgs:
@@ -169,6 +174,7 @@ def ppo_loss(out: torch.Tensor, value_col: int, act: torch.Tensor, old_logp, adv
         ptr(adv), ptr(ret), ptr(idx), ptr(moments), heads.host_ptr(heads.sizes), heads.n_heads,
         heads.host_ptr(heads.slots), heads.cont, ptr(log_std), ptr(coef), float(count), 1 if norm_adv else 0, B,
         ptr(dout), dout.stride(0), ptr(dout[:, value_col:]), dout.stride(0), ptr(dlog_std), ptr(stats),
+        min(act.shape[0], old_logp.numel(), adv.numel(), ret.numel()), ptr(_error_flag(out.device)),
         stream_ptr(out.device)), "surf_ppo_loss")
 
 

@@ -790,6 +790,10 @@ class Trainer:
             if self.comm is not None:
                 self.comm.merge_counts(self.reward)
             ls = self.loss_stats.tolist()
+            # kernels record bounded-wait timeouts and out-of-range indices in
+            # the device error flag instead of faulting: raise here
+            from ..ops.gemm import check_error_flag
+            check_error_flag(self.device)
             if self.comm is not None and hasattr(self.comm, "check"):
                 self.comm.check()
             n = max(ls[5], 1.0)
