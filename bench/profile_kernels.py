@@ -48,6 +48,7 @@ def main():
     ap.add_argument("--trace", action="store_true", help="convolution cases: add CTA 0's pipeline timeline "
                     "(first 256 k-blocks / tiles of the last launch, microseconds) to the output")
     ap.add_argument("--wgrad-splits", type=int, default=0, help="weight-gradient cases: K splits (0: the default)")
+    ap.add_argument("--march-flags", type=int, default=0, help="march case: extra kernel flag bits (timing studies)")
     ap.add_argument("--no-pairs", action="store_true", help="16-channel convolution inputs: one 32-byte tap per "
                     "box row instead of two-position windows")
     args = ap.parse_args()
@@ -72,6 +73,7 @@ def main():
         core = SimCore.from_bytes(m.image, default_config(1), threads=4)
         vol = vision.SdfVolume.build(core, cell=m.meta["cell"], mins=np.array(m.meta["grid_mins"]),
                                      dims=tuple(m.meta["dims"]))
+        vision.MARCH_DIAG_FLAGS = args.march_flags
         cam = vision.DepthCamera(vol, 128, 64, range_units=2000.0, max_steps=64, dtype=torch.bfloat16)
         pose = free_space_poses(vol, 2048, 1)
         out = torch.empty((2048, 128 * 64), dtype=torch.bfloat16, device=dev)

@@ -42,6 +42,8 @@ struct MarchParams {
   int64_t out_stride;     // elements between env images
   const int8_t* surf_nz;  // optional bricked |n_z|*127 grid (second channel)
   int exit_outside;       // grid padded by >= 1 free layer: skip loads once a ray leaves it
+  int flags;              // bit 2: 64-bit voxel addressing even for small grids (timing comparisons)
+  int idx32;              // the bricked grid has < 2^31 elements: 32-bit voxel addressing
   uint8_t* steps;         // optional per-ray step census [n_env, H, W]
 };
 
@@ -109,11 +111,26 @@ __global__ void __launch_bounds__(128) march_kernel(MarchParams p) {
       const float fx = (ex + dx * t - p.mnx) * p.inv_cell;
       const float fy = (ey + dy * t - p.mny) * p.inv_cell;
       const float fz = (ez + dz * t - p.mnz) * p.inv_cell;
-      const int ix = static_cast<int>(fminf(fmaxf(fx, 0.0f), gx - 1.0f));
-      const int iy = static_cast<int>(fminf(fmaxf(fy, 0.0f), gy - 1.0f));
-      const int iz = static_cast<int>(fminf(fmaxf(fz, 0.0f), gz - 1.0f));
-      d = __half2float(__ldg(p.sdf + p.grid.index(ix, iy, iz)));
-      outside = p.exit_outside && !(fx >= 0.0f && fx < gx && fy >= 0.0f && fy < gy && fz >= 0.0f && fz < gz);
+      const bool inside = fx >= 0.0f && fx < gx && fy >= 0.0f && fy < gy && fz >= 0.0f && fz < gz;
+      int ix, iy, iz;
+      if (inside) {
+        // 0 <= f < n: the clamp below would change nothing (int(f) <= n - 1)
+        ix = static_cast<int>(fx);
+        iy = static_cast<int>(fy);
+        iz = static_cast<int>(fz);
+      } else {
+        ix = static_cast<int>(fminf(fmaxf(fx, 0.0f), gx - 1.0f));
+        iy = static_cast<int>(fminf(fmaxf(fy, 0.0f), gy - 1.0f));
+        iz = static_cast<int>(fminf(fmaxf(fz, 0.0f), gz - 1.0f));
+      }
+      // 32-bit brick addressing when the grid has < 2^31 voxels (the host checks)
+      const int64_t vi = p.idx32 ? static_cast<int64_t>(
+                                       ((static_cast<uint32_t>(iz >> 2) * p.grid.by + static_cast<uint32_t>(iy >> 2)) *
+                                            p.grid.bx + static_cast<uint32_t>(ix >> 2)) << 6 |
+                                       ((iz & 3) << 4) | ((iy & 3) << 2) | (ix & 3))
+                                 : p.grid.index(ix, iy, iz);
+      d = __half2float(__ldg(p.sdf + vi));
+      outside = p.exit_outside && !inside;
     }
     if (!(d > hit_eps && t < p.range)) break;
     t += fmaxf(d * 0.9f, min_step);
@@ -205,6 +222,8 @@ SURF_EXPORT int surf_march(const float* pose, int64_t pose_stride, int n_env, in
   p.surf_nz = surf_nz;
   p.steps = steps;
   p.exit_outside = flags & 1;
+  p.flags = flags;
+  p.idx32 = p.grid.size() < (int64_t(1) << 31) && !(flags & 4);
   if (layout == kS2D4 && ((H & 3) || (W & 3))) return static_cast<int>(cudaErrorInvalidValue);
   auto s = static_cast<cudaStream_t>(stream);
   if (camera == 1) return out_dtype == 1 ? dispatch_layout<1, uint16_t>(p, layout, s) : dispatch_layout<1, float>(p, layout, s);

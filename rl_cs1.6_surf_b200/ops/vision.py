@@ -25,6 +25,8 @@ from . import _lib
 from ._lib import check, ptr, require_cuda, stream_ptr
 
 VLIB = "libsurf_vision.so"
+# timing studies only: extra surf_march flag bits (4 = 64-bit voxel addressing for any grid size)
+MARCH_DIAG_FLAGS = 0
 LAYOUT_NHW, LAYOUT_S2D4 = 0, 1
 
 
@@ -223,7 +225,8 @@ class DepthCamera:
             float(v.mins[0]), float(v.mins[1]), float(v.mins[2]), float(v.cell), ptr(self.col_off),
             ptr(self.row_off), self.range, self.near, self.max_steps, 1 if self.pinhole else 0, ptr(out),
             out.stride(0), 1 if out.dtype == torch.bfloat16 else 0, self.layout, ptr(self.surf_nz), ptr(steps),
-            1 if self.vol.padded else 0, stream if stream is not None else stream_ptr(pose.device)), "surf_march")
+            (1 if self.vol.padded else 0) | MARCH_DIAG_FLAGS, stream if stream is not None else stream_ptr(pose.device)),
+            "surf_march")
         return out
 
     def reference(self, pose: np.ndarray, return_steps: bool = False, surf_nz: Optional[np.ndarray] = None):
