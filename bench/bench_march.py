@@ -28,6 +28,13 @@ from surfb200.sim import mapgen  # noqa: E402
 from surfb200.sim.core import SimCore, default_config  # noqa: E402
 
 
+
+def _warp_efficiency(st, H: int, W: int):
+    if H % 2 or W % 16:
+        return None
+    w = st.reshape(st.shape[0], H // 2, 2, W // 16, 16).permute(0, 1, 3, 2, 4).reshape(-1, 32)
+    return float(w.mean(1).sum() / w.amax(1).clamp(min=1).sum())
+
 def free_space_poses(vol: vision.SdfVolume, n: int, seed: int, clearance: float = 48.0) -> torch.Tensor:
     g = torch.Generator(device="cuda").manual_seed(seed)
     nx, ny, nz = vol.dims
@@ -120,6 +127,8 @@ def main() -> None:
         "max_steps": args.max_steps, "mean_steps": float(st.mean()), "p50_steps": float(st.median()),
         "p99_steps": float(torch.quantile(st.flatten()[::97], 0.99)),
         "exhausted_frac": float((st >= args.max_steps).float().mean()),
+        # SIMD efficiency of the 16 x 2 pixel warps: mean steps / longest ray's steps per warp
+        "warp_step_efficiency": _warp_efficiency(st, args.height, args.width),
         "median_abs_err_units": float(np.median(err)) if err.size else None, "checked_hits": int(hit.sum()),
         "bake_s": bake_s, "setup_s": time.time() - t0, "gpu": torch.cuda.get_device_name(),
     }
