@@ -49,6 +49,8 @@ def main():
                     "(first 256 k-blocks / tiles of the last launch, microseconds) to the output")
     ap.add_argument("--wgrad-splits", type=int, default=0, help="weight-gradient cases: K splits (0: the default)")
     ap.add_argument("--march-flags", type=int, default=0, help="march case: extra kernel flag bits (timing studies)")
+    ap.add_argument("--sort-poses", type=int, default=0, help="march case: order the envs by position cells of this "
+                    "many units (0: random order) -- the L2 reuse of neighbouring cameras")
     ap.add_argument("--no-pairs", action="store_true", help="16-channel convolution inputs: one 32-byte tap per "
                     "box row instead of two-position windows")
     args = ap.parse_args()
@@ -76,6 +78,13 @@ def main():
         vision.MARCH_DIAG_FLAGS = args.march_flags
         cam = vision.DepthCamera(vol, 128, 64, range_units=2000.0, max_steps=64, dtype=torch.bfloat16)
         pose = free_space_poses(vol, 2048, 1)
+        if args.sort_poses:
+            # Morton order of (x, y) cells: consecutive envs (blocks) are neighbours
+            c = ((pose[:, :2] - pose[:, :2].min(0).values) / args.sort_poses).long().cpu().numpy()
+            code = np.zeros(len(c), np.int64)
+            for b in range(16):
+                code |= ((c[:, 0] >> b) & 1) << (2 * b) | ((c[:, 1] >> b) & 1) << (2 * b + 1)
+            pose = pose[torch.as_tensor(np.argsort(code), device=pose.device)].contiguous()
         out = torch.empty((2048, 128 * 64), dtype=torch.bfloat16, device=dev)
         info["ms"] = _time(lambda: cam.render(pose, out=out), args.reps)
         info["rays"] = 2048 * 128 * 64
