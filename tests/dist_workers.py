@@ -74,13 +74,17 @@ def gloo_dead_rank(rank: int, world: int, port: int, q) -> None:
         import torch.distributed as dist
         import surfb200  # noqa: F401
         from surfb200.parallel.dist import NcclComm, init_process_group
-        init_process_group("gloo", timeout_s=5)
+        # a generous timeout for the rendezvous (a cold start imports slowly),
+        # a short one for the collective that must notice the dead peer
+        init_process_group("gloo", timeout_s=120)
         comm = NcclComm()
+        short = dist.new_group(ranks=list(range(world)), timeout=datetime.timedelta(seconds=5))
+        dist.barrier()
         if rank == 1:
             os._exit(3)                        # the rank dies between steps
         t = torch.ones(8)
         try:
-            dist.all_reduce(t)
+            dist.all_reduce(t, group=short)
         except Exception as e:                 # noqa: BLE001
             return f"detected: {type(e).__name__}"
         raise AssertionError("all_reduce with a dead peer returned normally")
@@ -100,7 +104,8 @@ def gloo_stalled_rank(rank: int, world: int, port: int, q) -> None:
         import torch.distributed as dist
         import surfb200  # noqa: F401
         from surfb200.parallel.dist import init_process_group
-        init_process_group("gloo", timeout_s=3)
+        init_process_group("gloo", timeout_s=120)       # rendezvous: cold starts import slowly
+        short = dist.new_group(ranks=list(range(world)), timeout=datetime.timedelta(seconds=3))
         dist.barrier()
         if rank == 1:
             time.sleep(10)                     # stalled between steps
@@ -108,7 +113,7 @@ def gloo_stalled_rank(rank: int, world: int, port: int, q) -> None:
         t = torch.ones(8)
         t0 = time.time()
         try:
-            dist.all_reduce(t)
+            dist.all_reduce(t, group=short)
         except Exception as e:                 # noqa: BLE001
             return f"detected after {time.time() - t0:.1f} s: {type(e).__name__}"
         raise AssertionError("all_reduce with a stalled peer returned normally")
