@@ -27,7 +27,7 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-BASELINE_TICKS_PER_S = 281482.0          # reference, 1x RTX 5090 (BASELINE.md main table)
+BASELINE_TICKS_PER_S = 281482.0          # the reference's published number, 1x RTX 5090 (docs/perf-results.md:5-6)
 METRIC = "vision-PPO env-steps/s"
 
 
@@ -163,6 +163,10 @@ def run_ours(args) -> None:
                        "map": "procedural random field, 512 brushes, 16u SDF 1024x1024x256",
                        "comm": args.comm if world > 1 else "none", "cuda_graphs": cfg.graphs,
                        "env_device": cfg.env_device,
+                       "reward": "coverage (revisit_pen 0.25) + count curiosity 0.25 (256u cell x 8 yaw x 8 speed)",
+                       "differs_from_reference_arm": ["network: Nature CNN + proprio 256 vs the reference's own trunk",
+                                                      "reward: curiosity 0.25 on top of coverage (the reference "
+                                                      "pays curiosity only in race mode)"],
                        "l2": "inputs larger than L2 (4.3 GB rollout images per GPU)"},
             "clocks": clocks,
             "e2e": {"value": round(e2e, 1), "unit": "ticks/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -179,8 +183,13 @@ def run_ours(args) -> None:
 
 
 def run_reference(args) -> None:
-    from surfb200.baseline_ref import run_reference_bench
-    run_reference_bench(args)
+    # loaded by file path: the reference arm's process imports no module of
+    # this framework's package (and so maps none of its native libraries)
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("surf_reference_arm", ROOT / "rl_cs1.6_surf_b200" / "baseline_ref.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    mod.run_reference_bench(args, ClockSampler)
 
 
 if __name__ == "__main__":

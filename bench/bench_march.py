@@ -64,7 +64,7 @@ def main() -> None:
     ap.add_argument("--height", type=int, default=64)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--max-steps", type=int, default=128)
+    ap.add_argument("--max-steps", type=int, default=64)
     ap.add_argument("--near", type=float, default=2000.0)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--check-rays", type=int, default=20000)

@@ -18,6 +18,9 @@
 // thread per grid line.
 #include <cuda_fp16.h>
 
+#include <atomic>
+
+#include "sdf_noalloc.h"
 #include "surf_cuda.cuh"
 
 namespace {
@@ -213,39 +216,41 @@ SURF_EXPORT int surf_edt(const uint8_t* occ, int nx, int ny, int nz, float cell,
 // ---------------------------------------------------------------------------
 // surf_edt_noalloc — the exact EDT without any device allocation.
 //
-// This entry point has no counterpart in the reference project (which runs
-// its distance transform through scipy on the host). It exists for callers
-// that cannot allocate device memory at the moment they need a distance
-// field: code running while a CUDA stream is being captured into a graph (a
-// cudaMalloc there breaks the capture), processes whose device memory is
-// fully reserved up front by another framework's caching allocator, or hosts
-// that forbid allocation after start-up. The caller passes the occupancy grid
-// and the float32 output; the output doubles as the squared-distance buffer
-// of the three passes, and the per-line workspace lives in the file-scope
-// array below.
+// Declared, with its full contract, in sdf_noalloc.h; it has no counterpart in
+// the reference project (which runs its distance transform through scipy on
+// the host). It serves callers that must not allocate GPU memory: a plugin in
+// a host program that reserved the whole device for its own pool, or a
+// real-time loop that forbids cudaMalloc/cudaFree after start-up because they
+// can stall the device. The caller passes the occupancy grid and the float32
+// output; the output doubles as the squared-distance buffer of the three
+// passes, and the per-line scratch lives in the file-scope array below.
 //
 // Limits and behaviour:
-//   * every grid axis must be <= kNoAllocMaxLine (256) voxels; larger grids
-//     return cudaErrorInvalidValue without launching anything;
-//   * the workspace is a static device array of 1024 lines x (3*256+8) ints
+//   * every grid axis must be <= SURF_EDT_NOALLOC_MAX_LINE (256) voxels;
+//     larger grids, empty axes and null pointers return cudaErrorInvalidValue
+//     without launching anything;
+//   * the scratch is a static device array of 1024 lines x (3*256+8) ints
 //     (about 3.2 MB); every GPU that loads this library keeps it until the
 //     process exits;
 //   * its device address is looked up once per device (cudaGetSymbolAddress,
 //     with that device current) by the first call made on the device, so that
-//     first call should happen before any stream capture begins;
-//   * every call on a device shares the one workspace: calls that can overlap
-//     on the GPU (different streams without ordering) race and corrupt each
-//     other's results. Calls on one stream are safe. No part of the workspace
-//     needs to start at zero (each line is written before it is read).
+//     first call should happen before any stream capture begins. Two host
+//     threads making that first call together both look it up and store the
+//     same value (atomic per-device slots). The cached address is not valid
+//     after cudaDeviceReset;
+//   * every call on a device shares the one scratch array: calls that can
+//     overlap on the GPU (different streams without ordering) race and corrupt
+//     each other's results. Calls on one stream are safe. No part of the
+//     scratch needs to start at zero (each line is written before it is read).
 // ---------------------------------------------------------------------------
 namespace {
-constexpr int kNoAllocMaxLine = 256;
+constexpr int kNoAllocMaxLine = SURF_EDT_NOALLOC_MAX_LINE;
 constexpr int kNoAllocBlocks = 16;                        // x kEdtThreads = 1024 concurrent lines
 constexpr int kNoAllocInts = kNoAllocBlocks * kEdtThreads * (3 * kNoAllocMaxLine + 8);
 static __device__ __align__(256) int g_edt_noalloc_ws[kNoAllocInts];
 
 constexpr int kMaxDevices = 64;
-int* g_ws_addr[kMaxDevices] = {nullptr};
+std::atomic<int*> g_ws_addr[kMaxDevices];                 // zero-initialised (static storage)
 }  // namespace
 
 SURF_EXPORT int surf_edt_noalloc(const uint8_t* occ, int nx, int ny, int nz, float cell, float* out, void* stream) {
@@ -256,13 +261,14 @@ SURF_EXPORT int surf_edt_noalloc(const uint8_t* occ, int nx, int ny, int nz, flo
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return static_cast<int>(e);
   if (dev < 0 || dev >= kMaxDevices) return static_cast<int>(cudaErrorInvalidDevice);
-  if (!g_ws_addr[dev]) {
+  int* ws = g_ws_addr[dev].load(std::memory_order_acquire);
+  if (!ws) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_edt_noalloc_ws);
     if (e != cudaSuccess) return static_cast<int>(e);
-    g_ws_addr[dev] = static_cast<int*>(p);
+    ws = static_cast<int*>(p);
+    g_ws_addr[dev].store(ws, std::memory_order_release);
   }
-  int* ws = g_ws_addr[dev];
   auto s = static_cast<cudaStream_t>(stream);
   edt_x_kernel<<<kNoAllocBlocks, kEdtThreads, 0, s>>>(occ, out, nx, ny, nz, ws, kNoAllocMaxLine);
   edt_yz_kernel<<<kNoAllocBlocks, kEdtThreads, 0, s>>>(out, nx, ny, nz, 1, ws, kNoAllocMaxLine);

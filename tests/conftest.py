@@ -14,7 +14,9 @@ ROOT = Path(__file__).resolve().parents[1]
 sys.path.insert(0, str(ROOT))
 import surfb200  # noqa: E402,F401  (binds the package alias)
 
-REF_MAP = Path("/root/reference/maps/surf_ski_2.bsp")
+# a real community map: the reference ships surf_ski_2.bsp, found in its
+# installed copy under baseline/_ref unless SURF_REF_MAP names another file
+REF_MAP = Path(os.environ.get("SURF_REF_MAP", ROOT / "baseline" / "_ref" / "maps" / "surf_ski_2.bsp"))
 
 
 def pytest_configure(config):
@@ -58,6 +60,6 @@ def ramps_map(maps_dir):
 @pytest.fixture(scope="session")
 def ski_map():
     """A real community map shipped with the reference, if present."""
-    if not REF_MAP.exists():
-        pytest.skip("reference map not present")
+    if not REF_MAP.is_file():
+        pytest.skip(f"community map not present ({REF_MAP.name}; set SURF_REF_MAP)")
     return REF_MAP

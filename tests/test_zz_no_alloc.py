@@ -1,28 +1,37 @@
 """The allocation-free EDT entry point (surf_edt_noalloc) vs the regular one.
 
-surf_edt_noalloc serves callers that cannot allocate device memory when they
-need a distance field (inside a stream capture, under a fully reserved
-memory pool): it keeps its line workspace in a static device array and uses
-the caller's float output as its working buffer. This test calls it through
-its exported C symbol and checks two consecutive calls (different grids, so
-the shared workspace is reused) against surf_edt, with the tolerance of the
-other EDT test; it also checks the size limit. Collected last on purpose.
+surf_edt_noalloc (declared in csrc/kernels/sdf_noalloc.h) is for callers
+that must not allocate GPU memory, such as a plugin inside a host program that
+reserved the whole device for its own pool, or a real-time loop that forbids
+cudaMalloc after start-up. It keeps its scratch in a static device array and
+uses the caller's float output as its working buffer. These tests call it
+through its exported C symbol and check two consecutive calls (different
+grids, so the shared scratch is reused) against surf_edt, with the tolerance
+of the other EDT test; they also check that bad arguments are rejected
+without a launch. The file is collected last on purpose, and passes alone in
+a fresh process as well as after the other tests.
 """
 import ctypes
+import re
 from ctypes import c_float, c_int, c_void_p
+from pathlib import Path
 
 import numpy as np
 import pytest
 import torch
 
-from surfb200._native import LIB_DIR
+from surfb200 import _native
 from surfb200.ops import vision
 
 pytestmark = pytest.mark.gpu
 
+HEADER = Path(__file__).resolve().parents[1] / "csrc" / "kernels" / "sdf_noalloc.h"
+INVALID_VALUE = 1                                        # cudaErrorInvalidValue
+
 
 def _lib():
-    lib = ctypes.CDLL(str(LIB_DIR / "libsurf_vision.so"))
+    _native.load("libsurf_vision.so")                    # builds the library first if it is stale
+    lib = ctypes.CDLL(str(_native.LIB_DIR / "libsurf_vision.so"))
     fn = lib.surf_edt_noalloc
     fn.restype = c_int
     fn.argtypes = [c_void_p, c_int, c_int, c_int, c_float, c_void_p, c_void_p]
@@ -41,6 +50,15 @@ def _occupancy(shape, seed):
     return torch.as_tensor(occ, device="cuda")
 
 
+def test_header_declares_the_called_signature():
+    text = HEADER.read_text()
+    proto = re.search(r"int surf_edt_noalloc\(([^)]*)\);", text)
+    assert proto, "sdf_noalloc.h must declare surf_edt_noalloc"
+    types = [a.rsplit(" ", 1)[0].replace(" *", "*").strip() for a in proto.group(1).split(",")]
+    assert types == ["const uint8_t*", "int", "int", "int", "float", "float*", "void*"]
+    assert "no counterpart in the reference" in text
+
+
 def test_noalloc_matches_regular_entry_point():
     fn = _lib()
     stream = torch.cuda.current_stream().cuda_stream
@@ -55,10 +73,17 @@ def test_noalloc_matches_regular_entry_point():
         np.testing.assert_allclose(out.cpu().numpy(), ref.cpu().numpy(), rtol=1e-5, atol=1e-2)
 
 
-def test_noalloc_rejects_oversized_grids():
+def test_noalloc_rejects_bad_arguments():
     fn = _lib()
-    out = torch.empty(1, dtype=torch.float32, device="cuda")
-    occ = torch.zeros(1, dtype=torch.uint8, device="cuda")
-    stream = torch.cuda.current_stream().cuda_stream
-    rc = fn(c_void_p(occ.data_ptr()), 257, 8, 8, 16.0, c_void_p(out.data_ptr()), c_void_p(stream))
-    assert rc == 1                                       # cudaErrorInvalidValue, nothing launched
+    out = torch.full((4,), -7.0, dtype=torch.float32, device="cuda")
+    occ = torch.zeros(4, dtype=torch.uint8, device="cuda")
+    stream = c_void_p(torch.cuda.current_stream().cuda_stream)
+    o, p = c_void_p(occ.data_ptr()), c_void_p(out.data_ptr())
+    assert fn(o, 257, 8, 8, 16.0, p, stream) == INVALID_VALUE       # beyond the 256-voxel line limit
+    assert fn(o, 8, 8, 300, 16.0, p, stream) == INVALID_VALUE
+    assert fn(o, 0, 2, 2, 16.0, p, stream) == INVALID_VALUE         # empty axis
+    assert fn(o, 2, -1, 2, 16.0, p, stream) == INVALID_VALUE
+    assert fn(None, 2, 2, 1, 16.0, p, stream) == INVALID_VALUE      # null input
+    assert fn(o, 2, 2, 1, 16.0, None, stream) == INVALID_VALUE      # null output
+    torch.cuda.synchronize()
+    assert torch.all(out == -7.0)                                   # nothing was launched
