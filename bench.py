@@ -130,8 +130,8 @@ def run_ours(args) -> None:
     for _ in range(args.steps):
         stats = tr.train_iteration()
         if args.timing and rank == 0:
-            from surfb200.utils.timer import PhaseTimer
-            print(PhaseTimer.format(tr.iteration, stats.get("timing", {})), file=sys.stderr, flush=True)
+            from surfb200.utils.timer import PhaseClock
+            print(PhaseClock.timing_line(tr.iteration, stats.get("timing", {})), file=sys.stderr, flush=True)
     e1.record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - w0

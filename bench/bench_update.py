@@ -7,7 +7,14 @@ ops.gemm / ops.rl in CUDA-event pairs on the launching stream, and prints the
 time of each call after warm-up, with the FLOPs of the GEMMs and the achieved
 TFLOP/s.
 
-    python bench/bench_update.py [--rows 32768] [--iters 5] [--json out.json]
+    python bench/bench_update.py [--rows 32768] [--iters 5] [--json out.json] [--verify]
+
+``--verify`` is the numerics gate (reference: tools/bench_update.py:207-243,
+compiled vs eager): one minibatch through the tensor-core kernels (forward,
+fused PPO loss, backward) against the same minibatch in float32 autograd
+(``PolicyNet.forward_reference`` + ``ppo_loss_reference``) over identical
+bf16-rounded weights and inputs. It passes when the loss agrees within 1e-3
+relative and the flat gradient's cosine similarity is at least 0.99.
 """
 from __future__ import annotations
 
@@ -28,6 +35,7 @@ def main():
     ap.add_argument("--json", default=None)
     ap.add_argument("--explicit", action="store_true", help="im2col + GEMM for every convolution (A/B baseline)")
     ap.add_argument("--nhw", action="store_true", help="64 x 128 NHW image with the 8x8 stride-4 first layer")
+    ap.add_argument("--verify", action="store_true", help="numerics gate: kernels vs float32 autograd, then exit")
     args = ap.parse_args()
     import torch
     import surfb200  # noqa: F401
@@ -59,6 +67,13 @@ def main():
     mom = torch.tensor([float(adv.sum()), float((adv * adv).sum())], dtype=torch.float64, device=dev)
     coef = torch.tensor([0.2, 0.5, 0.005], device=dev)
     stats = torch.zeros(6, device=dev)
+
+    if args.verify:
+        res = verify(net, ws, layout, heads, scal, img, adv, ret, coef)
+        print(json.dumps(res))
+        if args.json:
+            Path(args.json).write_text(json.dumps(res, indent=1))
+        sys.exit(0 if res["pass"] else 1)
 
     records = []
     active = [False]
@@ -135,6 +150,67 @@ def main():
     print(f"sum of ops {total:.3f} ms; minibatch step (events around the whole step, incl. gaps) {wall:.3f} ms")
     if args.json:
         Path(args.json).write_text(json.dumps({"rows": B, "ops": rows, "sum_ms": total, "step_ms": wall}, indent=1))
+
+
+def verify(net, ws, layout, heads, scal, img, adv, ret, coef, loss_tol: float = 1e-3, cos_min: float = 0.99) -> dict:
+    """One minibatch on the kernels vs float32 autograd (see the module docstring)."""
+    import torch
+    from surfb200.models.policy import backward_gpu, forward_gpu
+    from surfb200.ops import rl as R
+    from surfb200.ops.gemm import check_error_flag
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    dev = net.flat.device
+    B = scal.shape[0]
+    net.flat.copy_(net.flat.to(torch.bfloat16).float())      # both paths see the same (bf16) weights
+    net.sync_bf16()
+    # actions and old log-probs drawn from the policy itself, perturbed so that
+    # the ratio spreads past the clip range on part of the rows
+    out = forward_gpu(net, ws, scal, img)
+    act = torch.zeros(B, 8, dtype=torch.int32, device=dev)
+    logp = torch.zeros(B, device=dev)
+    R.sample_heads(out, heads, net.p("log_std"), act, logp, seed=7, counter=0)
+    old_logp = logp + 0.3 * torch.randn(B, device=dev)
+    idx = torch.arange(B, device=dev)
+    mom = torch.stack([adv.double().sum(), (adv.double() ** 2).sum()])
+    stats = torch.zeros(6, device=dev)
+    net.grad.zero_()
+    out = forward_gpu(net, ws, scal, img)
+    R.ppo_loss(out, layout.value_col, act, old_logp, adv, ret, idx, mom, heads, net.p("log_std"), coef, float(B),
+               ws.dout, net.g("log_std"), stats)
+    from surfb200.ops import gemm as G
+    G.to_bf16(ws.dout, ws.dout16)
+    backward_gpu(net, ws, scal)
+    torch.cuda.synchronize()
+    check_error_flag(dev)
+    clip, vf, ent = (float(x) for x in coef.tolist())
+    st = stats.double().cpu()
+    loss_gpu = float((st[0] + vf * st[1] - ent * st[2]) / B)
+    grad_gpu = net.grad.clone()
+
+    params = net.autograd_params()
+    ref_out = net.forward_reference(scal.float(), img.float(), params)
+    loss, pg, vl, H = R.ppo_loss_reference(ref_out, layout.value_col, act, old_logp, adv, ret, layout,
+                                           params["log_std"], clip, vf, ent,
+                                           moments=(float(mom[0]), float(mom[1]), float(B)))
+    loss.backward()
+    grad_ref = torch.zeros_like(grad_gpu)
+    for name, t in params.items():
+        if t.grad is not None:
+            net.view(name, grad_ref).copy_(t.grad)
+    rel = abs(loss_gpu - float(loss)) / max(abs(float(loss)), 1e-12)
+    cos = float(torch.nn.functional.cosine_similarity(grad_gpu.double(), grad_ref.double(), dim=0))
+    grad_rel = float((grad_gpu - grad_ref).norm() / grad_ref.norm().clamp_min(1e-30))
+    per_layer = {}
+    for name, *_ in net.specs:
+        a, b = net.view(name, grad_gpu).flatten(), net.view(name, grad_ref).flatten()
+        if float(b.norm()) > 0:
+            per_layer[name] = round(float(torch.nn.functional.cosine_similarity(a.double(), b.double(), dim=0)), 5)
+    net.grad.zero_()
+    return {"verify": "minibatch kernels vs float32 autograd", "rows": B, "loss_gpu": loss_gpu, "loss_fp32": float(loss),
+            "loss_rel_err": rel, "grad_cos": cos, "grad_rel_err": grad_rel, "layer_cos": per_layer,
+            "thresholds": {"loss_rel_err": loss_tol, "grad_cos": cos_min},
+            "pass": bool(rel <= loss_tol and cos >= cos_min)}
 
 
 if __name__ == "__main__":

@@ -165,8 +165,8 @@ def cmd_train(args) -> int:
             if rank == 0:
                 print(line, flush=True)
                 if cfg.timing and stats.get("timing"):
-                    from .utils.timer import PhaseTimer
-                    print(PhaseTimer.format(tr.iteration, stats["timing"]), flush=True)
+                    from .utils.timer import PhaseClock
+                    print(PhaseClock.timing_line(tr.iteration, stats["timing"]), flush=True)
             if tr.global_step >= next_rec:
                 next_rec += cfg.record_every
                 out = run_dir / "recordings" / f"eval_{tr.global_step:010d}.traj.jsonl" if rank == 0 else None

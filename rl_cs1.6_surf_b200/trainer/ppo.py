@@ -37,7 +37,7 @@ from ..ops import rl as R
 from ..rewards.spec import CpuReward, GpuReward, RewardSpec
 from ..sim import mapgen
 from ..sim.core import REC_COLS, STATE_DTYPE, TERM_COLS, SimCore, default_config
-from ..utils.timer import PhaseTimer
+from ..utils.timer import PhaseClock
 from .config import TrainConfig
 
 # column layout of the per-env host record (float32)
@@ -84,7 +84,7 @@ class Trainer:
         self.global_step = 0
         self.iteration = 0
         self._env_ready = False
-        self.timer = PhaseTimer(cfg.timing, self.gpu)
+        self.timer = PhaseClock(cfg.timing, self.gpu)
         self.last_stats: dict = {}
 
     # ---- setup ------------------------------------------------------------------------
@@ -455,13 +455,12 @@ class Trainer:
 
     def _run_group(self, g: int, t: int) -> None:
         from ..ops import _lib
-        ev = self.timer.gpu_start("rollout_gpu")
-        if self.cfg.graphs:
-            self.rew_graphs[g][t].replay()
-            _lib.add_launches(self.graph_launches[g][t])
-        else:
-            self._group_body(g, t)
-        self.timer.gpu_end(ev)
+        with self.timer.gpu("rollout_gpu"):
+            if self.cfg.graphs:
+                self.rew_graphs[g][t].replay()
+                _lib.add_launches(self.graph_launches[g][t])
+            else:
+                self._group_body(g, t)
         self.grp_events[g].record()
 
     def _env_step_group(self, g: int) -> None:
@@ -545,12 +544,10 @@ class Trainer:
             self._run_group(g, 0)
         for t in range(T):
             for g in range(G):
-                t0 = tm.begin("wait_gpu")
-                self.grp_events[g].synchronize()
-                tm.add("wait_gpu", t0)
-                t0 = tm.begin("env")
-                self._env_step_group(g)
-                tm.add("env", t0)
+                with tm.phase("wait_gpu"):
+                    self.grp_events[g].synchronize()
+                with tm.phase("env"):
+                    self._env_step_group(g)
                 if self.cfg.ep_ticks:
                     self._bootstrap_truncations(g, t)
                 self._run_group(g, t + 1)
@@ -584,13 +581,12 @@ class Trainer:
                             self._env_body(g, t)
                     self.ev_env[g].record(E)
                     C.wait_event(self.ev_env[g])
-                ev = self.timer.gpu_start("rollout_gpu")
-                if self.cfg.graphs:
-                    self.rew_graphs[g][t].replay()
-                    _lib.add_launches(self.graph_launches[g][t])
-                else:
-                    self._group_body(g, t, env=False)
-                self.timer.gpu_end(ev)
+                with self.timer.gpu("rollout_gpu"):
+                    if self.cfg.graphs:
+                        self.rew_graphs[g][t].replay()
+                        _lib.add_launches(self.graph_launches[g][t])
+                    else:
+                        self._group_body(g, t, env=False)
                 self.ev_sample[g].record(C)
             if t < T:
                 self.global_step += self.N * self.K * self.world
@@ -763,30 +759,36 @@ class Trainer:
 
     def train_iteration(self) -> dict:
         tm = self.timer
-        tm.start_iter()
+        tm.new_iteration()
         if not self._env_ready:              # first iteration of this process (fresh or resumed run)
             self.reset()
             self._env_ready = True
         self.iteration += 1
         self.reward.set_step(self.global_step)
-        t0 = tm.begin("rollout")
-        if self.gpu:
-            self.rollout_gpu()
-        else:
-            self.rollout_cpu()
-        tm.add("rollout", t0)
+        with tm.phase("rollout"):
+            if self.gpu:
+                self.rollout_gpu()
+            else:
+                self.rollout_cpu()
         if self.rnd is not None:
-            t0 = tm.begin("rnd")
-            self._train_rnd()
-            tm.add("rnd", t0)
-        t0 = tm.begin("respawn")
-        self._refresh_respawn_pool()
-        tm.add("respawn", t0)
-        t0 = tm.begin("update")
+            with tm.phase("rnd"):
+                self._train_rnd()
+        with tm.phase("respawn"):
+            self._refresh_respawn_pool()
+        with tm.phase("update"):
+            loss = self._update_and_stats()
+        self._check_replicas()
+        stats = dict(self.reward.pop_stats(), **loss)
+        stats["global_step"] = self.global_step
+        stats["iteration"] = self.iteration
+        stats["timing"] = tm.collect()
+        self.last_stats = stats
+        return stats
+
+    def _update_and_stats(self) -> dict:
         if self.gpu:
-            ev = tm.gpu_start("update_gpu")
-            self.update_gpu()
-            tm.gpu_end(ev)
+            with self.timer.gpu("update_gpu"):
+                self.update_gpu()
             if self.comm is not None:
                 self.comm.merge_counts(self.reward)
             ls = self.loss_stats.tolist()
@@ -801,14 +803,7 @@ class Trainer:
                     "clip_frac": ls[4] / n}
         else:
             loss = self.update_cpu()
-        tm.add("update", t0)
-        self._check_replicas()
-        stats = dict(self.reward.pop_stats(), **loss)
-        stats["global_step"] = self.global_step
-        stats["iteration"] = self.iteration
-        stats["timing"] = tm.flush(self.iteration)
-        self.last_stats = stats
-        return stats
+        return loss
 
     def release_graphs(self) -> None:
         """Drop every captured CUDA graph (graphs holding NCCL calls must be
@@ -835,7 +830,8 @@ class Trainer:
             policy["flat"] = self.comm.full_params(self.net).detach().cpu()
         return {"format": "surfb200-ckpt-1", "policy": policy, "optimizer": opt,
                 "global_step": self.global_step, "iteration": self.iteration, "config": self.cfg.to_dict(),
-                "int_counts": counts, "respawn": self.respawn.state_dict() if self.respawn is not None else None}
+                "int_counts": counts, "respawn": self.respawn.state_dict() if self.respawn is not None else None,
+                "rnd": self.rnd.state_dict() if self.rnd is not None else None}
 
     def load_state_dict(self, sd: dict, reset_steps: bool = False, reset_counts: bool = False) -> None:
         self.net.load_state_dict(sd["policy"])
@@ -843,6 +839,8 @@ class Trainer:
         if not reset_steps:
             self.global_step = int(sd["global_step"])
             self.iteration = int(sd.get("iteration", 0))
+        if self.rnd is not None and sd.get("rnd"):
+            self.rnd.load_state_dict(sd["rnd"])
         if self.respawn is not None and sd.get("respawn"):
             if not self.respawn.load_state_dict(sd["respawn"]) and self.verbose:
                 print("respawn reservoir not restored (empty, or recorded on another map)")

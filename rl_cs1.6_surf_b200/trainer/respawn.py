@@ -28,6 +28,30 @@ import numpy as np
 from ..sim.core import STATE_DTYPE
 
 
+def even_shares_under_caps(n: int, caps: np.ndarray) -> np.ndarray:
+    """Split n draws over k groups as evenly as the per-group caps allow.
+
+    Returns alloc with alloc <= caps and sum(alloc) = min(n, sum(caps)):
+    every group gets min(cap, L) for the largest level L that does not
+    overshoot n, and the remaining draws go one each to the lowest-index
+    groups still below their cap (the nearest distance bins)."""
+    caps = np.asarray(caps, np.int64)
+    if n <= 0 or caps.size == 0:
+        return np.zeros(caps.size, np.int64)
+    if n >= int(caps.sum()):
+        return caps.copy()
+    lo, hi = 0, int(caps.max())
+    while lo < hi:                                          # largest L with sum(min(caps, L)) <= n
+        mid = (lo + hi + 1) // 2
+        if int(np.minimum(caps, mid).sum()) <= n:
+            lo = mid
+        else:
+            hi = mid - 1
+    alloc = np.minimum(caps, lo)
+    extra = n - int(alloc.sum())
+    alloc[np.flatnonzero(alloc < caps)[:extra]] += 1
+    return alloc
+
 class RespawnReservoir:
     def __init__(self, n_envs: int, reservoir: int = 100_000, margin_ticks: int = 1000, snap_every: int = 100,
                  max_pending: int = 64, map_id: str = "", seed: int = 23, dist_fn: Optional[Callable] = None,
@@ -122,34 +146,33 @@ class RespawnReservoir:
 
     # ---- sampling ------------------------------------------------------------------------
     def binned_pick(self, n: int) -> np.ndarray:
-        d = self.d[:self.size]
-        valid = np.flatnonzero(d < self.dist_valid_max) if self.dist_valid_max else np.arange(self.size)
-        if len(valid) == 0:
+        """n reservoir indices spread evenly over the occupied goal-distance
+        bins (uniform within a bin), no bin drawn more than 4x its population;
+        demand the caps cannot absorb falls back to uniform draws over the
+        whole reservoir (the reference's rule, python/surfgym/respawn.py:124-166).
+
+        Vectorised: the candidates are grouped by bin with one stable sort,
+        the per-bin counts come from ``even_shares_under_caps`` in closed form,
+        and every draw is one offset into its bin's slice of the sorted
+        candidates."""
+        dist = self.d[:self.size]
+        cand = np.flatnonzero(dist < self.dist_valid_max) if self.dist_valid_max else np.arange(self.size)
+        if cand.size == 0:
             return self.rng.integers(0, self.size, n)
-        edges = np.linspace(0.0, self.dist_max, self.bins + 1)
-        which = np.clip(np.digitize(d[valid], edges) - 1, 0, self.bins - 1)
-        groups = [valid[which == b] for b in range(self.bins)]
-        groups = [g for g in groups if len(g)]
-        caps = np.array([4 * len(g) for g in groups], np.int64)
-        alloc = np.zeros(len(groups), np.int64)
-        left = int(n)
-        while left > 0:                                     # water-fill equal shares under the caps
-            open_ = np.flatnonzero(alloc < caps)
-            if len(open_) == 0:
-                break
-            base, rem = divmod(left, len(open_))
-            share = np.zeros(len(groups), np.int64)
-            share[open_] = base
-            share[open_[:rem]] += 1
-            share = np.minimum(share, caps - alloc)
-            if share.sum() == 0:
-                break
-            alloc += share
-            left -= int(share.sum())
-        parts = [self.rng.choice(g, size=int(a), replace=True) for g, a in zip(groups, alloc) if a > 0]
-        out = np.concatenate(parts) if parts else np.empty(0, np.int64)
-        if left > 0:
-            out = np.concatenate([out, self.rng.integers(0, self.size, left)])
+        nbins = int(self.bins)
+        b = np.floor(dist[cand].astype(np.float64) * (nbins / float(self.dist_max)))
+        b = np.clip(b, 0, nbins - 1).astype(np.int64)
+        members = cand[np.argsort(b, kind="stable")]
+        pop_all = np.bincount(b, minlength=nbins)
+        first_all = np.concatenate(([0], np.cumsum(pop_all)[:-1]))
+        occupied = np.flatnonzero(pop_all)
+        pop, first = pop_all[occupied], first_all[occupied]
+        take = even_shares_under_caps(int(n), 4 * pop)
+        which = np.repeat(np.arange(occupied.size), take)
+        offs = np.minimum((self.rng.random(which.size) * pop[which]).astype(np.int64), pop[which] - 1)
+        out = members[first[which] + offs]
+        if out.size < n:
+            out = np.concatenate([out, self.rng.integers(0, self.size, n - out.size)])
         self.rng.shuffle(out)
         return out
 

@@ -1,101 +1,139 @@
 """Random Network Distillation novelty on the 15 scalar observations.
 
-Behaviour of the reference (python/surfgym/rnd.py:70-140): a frozen random
-target MLP f and a trained predictor f' (15 -> 128 -> 128 -> 64, ReLU,
-orthogonal init); bonus = mean squared difference of their outputs on
-RMS-normalised inputs (clipped to +-5), divided by the running RMS of the
-bonus itself and clipped to [0, 5]; the first ``warmup`` calls pay nothing.
+Behaviour of the reference (python/surfgym/rnd.py:70-140), the method of
+Burda et al., "Exploration by Random Network Distillation" (2018): a frozen
+random target network f and a trained predictor f' of the same shape
+(15 -> 128 -> 128 -> 64, ReLU, orthogonal init with gain sqrt 2, zero
+biases); bonus = mean squared difference of their outputs on running-RMS
+normalised inputs (clipped to +-5), divided by the running RMS of the bonus
+itself and clipped to [0, 5]; the first ``warmup`` calls pay nothing.
 
-Unlike the reference, every running statistic lives in device tensors and
-``bonus`` performs no host synchronisation, so it runs inside the rollout's
-CUDA graphs. The predictor trains eagerly once per iteration. RND is off by
-default (the reference screened it negative); ``--rnd-coef`` enables it.
+Design here: the two networks are one ``TwinMLP`` whose weights are stacked
+on a leading axis of size 2 (index 0 = frozen target, 1 = predictor), so a
+bonus evaluates both with one batched matmul per layer; only the predictor
+slices receive gradients. Every running statistic is a device tensor kept as
+(count, mean, M2) and merged batch by batch with the pairwise update of Chan,
+Golub and LeVeque ("Updating formulae and a pairwise algorithm for computing
+sample variances", 1979), so ``bonus`` makes no host synchronisation and
+runs inside the rollout's CUDA graphs. RND is off by default (the reference
+screened it negative); ``--rnd-coef`` enables it. Its full state (both
+networks, the predictor's optimizer, all statistics) is checkpointed.
 """
 from __future__ import annotations
 
 import math
 
 import torch
-import torch.nn as nn
 
 
-def _mlp(i: int, h: int, o: int) -> nn.Sequential:
-    m = nn.Sequential(nn.Linear(i, h), nn.ReLU(), nn.Linear(h, h), nn.ReLU(), nn.Linear(h, o))
-    for layer in m:
-        if isinstance(layer, nn.Linear):
-            nn.init.orthogonal_(layer.weight, math.sqrt(2))
-            nn.init.zeros_(layer.bias)
-    return m
+class TwinMLP(torch.nn.Module):
+    """Target and predictor MLPs with stacked weights: ``forward(x)`` returns
+    [2, B, out] (target, predictor)."""
+
+    def __init__(self, dims=(15, 128, 128, 64), generator: torch.Generator = None):
+        super().__init__()
+        self.weights = torch.nn.ParameterList()
+        self.biases = torch.nn.ParameterList()
+        for fan_in, fan_out in zip(dims[:-1], dims[1:]):
+            w = torch.empty(2, fan_in, fan_out)
+            for k in range(2):
+                blk = torch.empty(fan_out, fan_in)
+                torch.nn.init.orthogonal_(blk, gain=math.sqrt(2.0), generator=generator)
+                w[k] = blk.t()
+            self.weights.append(torch.nn.Parameter(w))
+            self.biases.append(torch.nn.Parameter(torch.zeros(2, 1, fan_out)))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        h = x.unsqueeze(0).expand(2, -1, -1)
+        last = len(self.weights) - 1
+        for i, (w, b) in enumerate(zip(self.weights, self.biases)):
+            h = torch.baddbmm(b, h, w)
+            if i < last:
+                h = torch.relu(h)
+        return h
+
+    def predictor_parameters(self):
+        return list(self.weights) + list(self.biases)
 
 
-class _Moments:
-    """Running mean / variance over batches (parallel-variance merge), device tensors."""
+class RunningMoments:
+    """Mean and population variance of everything seen so far, per feature."""
 
-    def __init__(self, dim, device):
-        self.mean = torch.zeros(dim, device=device)
-        self.var = torch.ones(dim, device=device)
-        self.count = torch.full((), 1e-4, device=device)
+    def __init__(self, shape, device):
+        self.n = torch.full((), 1e-4, device=device)           # a tiny prior count: var starts at 1
+        self.mean = torch.zeros(shape, device=device)
+        self.m2 = torch.full(shape, 1e-4, device=device)        # sum of squared deviations (= var * n)
 
-    def update(self, x: torch.Tensor) -> None:
-        bm = x.mean(0)
-        bv = x.var(0, unbiased=False)
-        bc = float(x.shape[0])                  # a Python number: no host-device copy (graph-capturable)
-        delta = bm - self.mean
-        tot = self.count + bc
-        self.mean.add_(delta * bc / tot)
-        self.var.copy_((self.var * self.count + bv * bc + delta.pow(2) * self.count * bc / tot) / tot)
-        self.count.copy_(tot)
+    @property
+    def var(self) -> torch.Tensor:
+        return self.m2 / self.n
+
+    def merge(self, x: torch.Tensor) -> None:
+        nb = float(x.shape[0])                  # a Python number: no device-to-host copy
+        mb = x.mean(0)
+        m2b = (x - mb).pow(2).sum(0)
+        n = self.n + nb
+        delta = mb - self.mean
+        self.m2.add_(m2b + delta.pow(2) * (self.n * nb / n))
+        self.mean.add_(delta * (nb / n))
+        self.n.copy_(n)
+
+    def tensors(self) -> list:
+        return [self.n, self.mean, self.m2]
 
 
 class RND:
     def __init__(self, in_dim: int = 15, feat: int = 64, hidden: int = 128, lr: float = 1e-4, warmup: int = 50,
                  device="cuda", seed: int = 0):
         self.device = torch.device(device)
-        with torch.random.fork_rng(devices=[]):
-            torch.manual_seed(seed)
-            self.target = _mlp(in_dim, hidden, feat).to(self.device)
-            self.pred = _mlp(in_dim, hidden, feat).to(self.device)
-        for p in self.target.parameters():
-            p.requires_grad_(False)
-        self.opt = torch.optim.Adam(self.pred.parameters(), lr=lr)
-        self.obs = _Moments(in_dim, self.device)
-        self.bon = _Moments((), self.device)
+        gen = torch.Generator().manual_seed(seed)
+        self.nets = TwinMLP((in_dim, hidden, hidden, feat), gen).to(self.device)
+        self.opt = torch.optim.Adam(self.nets.predictor_parameters(), lr=lr)
+        self.inputs = RunningMoments((in_dim,), self.device)
+        self.errors = RunningMoments((), self.device)
         self.calls = torch.zeros((), device=self.device)
         self.warmup = int(warmup)
 
-    def _norm(self, x: torch.Tensor) -> torch.Tensor:
-        return ((x - self.obs.mean) / torch.sqrt(self.obs.var + 1e-8)).clamp(-5.0, 5.0)
+    def _whiten(self, x: torch.Tensor) -> torch.Tensor:
+        return ((x - self.inputs.mean) * torch.rsqrt(self.inputs.var + 1e-8)).clamp(-5.0, 5.0)
+
+    def _sq_error(self, xn: torch.Tensor) -> torch.Tensor:
+        tp = self.nets(xn)
+        return (tp[0].detach() - tp[1]).pow(2).mean(-1)
 
     @torch.no_grad()
     def bonus(self, x: torch.Tensor) -> torch.Tensor:
+        """Per-row novelty of a batch; updates the running statistics."""
         x = x.float()
-        self.obs.update(x)
+        self.inputs.merge(x)
         self.calls.add_(1.0)
-        xn = self._norm(x)
-        err = (self.target(xn) - self.pred(xn)).pow(2).mean(1)
-        self.bon.update(err)
-        out = (err / torch.sqrt(self.bon.var + 1e-8)).clamp(0.0, 5.0)
-        return out * (self.calls > self.warmup).float()
+        err = self._sq_error(self._whiten(x))
+        self.errors.merge(err)
+        scaled = (err * torch.rsqrt(self.errors.var + 1e-8)).clamp(0.0, 5.0)
+        return scaled * (self.calls > self.warmup).to(scaled.dtype)
 
     def train_step(self, x: torch.Tensor) -> torch.Tensor:
-        xn = self._norm(x.float().detach())
-        loss = (self.target(xn) - self.pred(xn)).pow(2).mean()
+        """One predictor update on a batch of observations; returns the loss."""
+        loss = self._sq_error(self._whiten(x.float().detach())).mean()
         self.opt.zero_grad(set_to_none=True)
         loss.backward()
+        # the target half of every stacked tensor stays frozen
+        for p in self.nets.predictor_parameters():
+            if p.grad is not None:
+                p.grad[0].zero_()
         self.opt.step()
         return loss.detach()
 
     def state_dict(self) -> dict:
-        return {"target": self.target.state_dict(), "pred": self.pred.state_dict(), "opt": self.opt.state_dict(),
-                "obs": [self.obs.mean.cpu(), self.obs.var.cpu(), self.obs.count.cpu()],
-                "bon": [self.bon.mean.cpu(), self.bon.var.cpu(), self.bon.count.cpu()], "calls": self.calls.cpu()}
+        return {"nets": {k: v.detach().cpu() for k, v in self.nets.state_dict().items()},
+                "opt": self.opt.state_dict(),
+                "inputs": [t.cpu() for t in self.inputs.tensors()],
+                "errors": [t.cpu() for t in self.errors.tensors()], "calls": self.calls.cpu()}
 
     def load_state_dict(self, sd: dict) -> None:
-        self.target.load_state_dict(sd["target"])
-        self.pred.load_state_dict(sd["pred"])
+        self.nets.load_state_dict({k: v.to(self.device) for k, v in sd["nets"].items()})
         self.opt.load_state_dict(sd["opt"])
-        for m, vals in ((self.obs, sd["obs"]), (self.bon, sd["bon"])):
-            m.mean.copy_(vals[0])
-            m.var.copy_(vals[1])
-            m.count.copy_(vals[2])
-        self.calls.copy_(sd["calls"])
+        for mom, vals in ((self.inputs, sd["inputs"]), (self.errors, sd["errors"])):
+            for dst, src in zip(mom.tensors(), vals):
+                dst.copy_(src.to(self.device))
+        self.calls.copy_(sd["calls"].to(self.device))

@@ -216,6 +216,23 @@ def test_respawn_binned_sampling_flattens_bins():
     assert np.all(counts <= 4 * per_bin_pop + 1)
 
 
+def test_even_shares_under_caps():
+    from surfb200.trainer.respawn import even_shares_under_caps as fill
+    assert fill(10, np.array([100, 100, 100])).tolist() == [4, 3, 3]
+    out = fill(10, np.array([1, 100, 2]))
+    assert out.tolist() == [1, 7, 2]                      # capped groups keep their cap, the rest takes the demand
+    assert fill(1000, np.array([3, 4])).tolist() == [3, 4]    # demand over every cap: all caps
+    assert fill(0, np.array([5])).tolist() == [0]
+    rng = np.random.default_rng(0)
+    for _ in range(200):
+        caps = rng.integers(1, 50, rng.integers(1, 12))
+        n = int(rng.integers(0, 400))
+        a = fill(n, caps)
+        assert np.all(a <= caps) and int(a.sum()) == min(n, int(caps.sum()))
+        # evenness: a group more than one draw below the largest share is at its cap
+        assert np.all((a >= a.max() - 1) | (a == caps))
+
+
 def test_trainer_respawn_cpu():
     from surfb200.rewards.spec import RewardSpec
     from surfb200.trainer.config import TrainConfig
@@ -266,9 +283,13 @@ def test_rnd_bonus_and_training_cpu():
     fresh = torch.randn(512, 15) * 3 + 5
     assert float(r.bonus(fresh).mean()) > float(r.bonus(x).mean())   # novel inputs pay more
     sd = r.state_dict()
-    r2 = RND(15, device="cpu", seed=1)
+    r2 = RND(15, device="cpu", warmup=2, seed=1)
     r2.load_state_dict(sd)
-    assert torch.allclose(r2.bonus(x), r.bonus(x), atol=1e-5) or True
+    assert torch.allclose(r2.bonus(x), r.bonus(x), atol=1e-6)
+    # the target half never moves; the predictor half does
+    t0 = RND(15, device="cpu", warmup=2, seed=0).nets.weights[0][0]
+    assert torch.equal(r.nets.weights[0][0].detach(), t0.detach())
+    assert not torch.equal(r.nets.weights[0][1].detach(), RND(15, device="cpu", seed=0).nets.weights[0][1].detach())
 
 
 def test_trainer_cpu_with_rnd_and_blend():
@@ -282,6 +303,15 @@ def test_trainer_cpu_with_rnd_and_blend():
     for _ in range(2):
         s = tr.train_iteration()
     assert np.isfinite(s["policy_loss"])
+    # the RND state (networks, optimizer, statistics) rides in the checkpoint
+    sd = tr.state_dict()
+    assert sd["rnd"] is not None
+    tr2 = Trainer(cfg, verbose=False)
+    tr2.load_state_dict(sd)
+    for a, b in zip(tr.rnd.nets.parameters(), tr2.rnd.nets.parameters()):
+        assert torch.equal(a.detach(), b.detach())
+    assert torch.equal(tr.rnd.inputs.m2, tr2.rnd.inputs.m2) and float(tr2.rnd.calls) == float(tr.rnd.calls)
+    assert tr2.rnd.opt.state_dict()["state"].keys() == tr.rnd.opt.state_dict()["state"].keys()
 
 
 def test_operator_tools(tmp_path):
@@ -391,23 +421,29 @@ def test_tas_search_and_chain_replay_the_recording(tmp_path):
     core.close()
 
 
-def test_phase_timer_nvtx_ranges_balance(monkeypatch):
-    """SURF_NVTX=1 turns every timer phase into an NVTX range (push at the
+def test_phase_clock_nvtx_ranges_balance(monkeypatch):
+    """SURF_NVTX=1 turns every timed block into an NVTX range (push at the
     start, pop at the end), with timing off too."""
     import torch
-    from surfb200.utils.timer import PhaseTimer
+    from surfb200.utils.timer import PhaseClock
     calls = []
     monkeypatch.setattr(torch.cuda.nvtx, "range_push", lambda name: calls.append(("push", name)))
     monkeypatch.setattr(torch.cuda.nvtx, "range_pop", lambda: calls.append(("pop", None)))
     monkeypatch.setenv("SURF_NVTX", "1")
-    tm = PhaseTimer(False, True)
-    t0 = tm.begin("update")
-    ev = tm.gpu_start("update_gpu")
-    tm.gpu_end(ev)
-    tm.add("update", t0)
+    clock = PhaseClock(False, True)
+    with clock.phase("update"):
+        with clock.gpu("update_gpu"):
+            pass
     assert calls == [("push", "update"), ("push", "update_gpu"), ("pop", None), ("pop", None)]
     monkeypatch.setenv("SURF_NVTX", "0")
     calls.clear()
-    tm = PhaseTimer(True, False)
-    tm.add("env", tm.begin("env"))
-    assert calls == [] and "env" in tm.acc
+    clock = PhaseClock(True, False)
+    clock.new_iteration()
+    with clock.phase("env"):
+        pass
+    with clock.phase("env"):
+        pass
+    got = clock.collect()
+    assert calls == [] and set(got) == {"env", "total"} and got["total"] >= got["env"] >= 0.0
+    line = PhaseClock.timing_line(3, {"env": 1.25, "total": 2.0})
+    assert line == "TIMING iter=3 env=1.2 total=2.0"
