@@ -29,6 +29,9 @@ sys.path.insert(0, str(ROOT))
 
 BASELINE_TICKS_PER_S = 281482.0          # the reference's published number, 1x RTX 5090 (docs/perf-results.md:5-6)
 METRIC = "vision-PPO env-steps/s"
+# trainer phases reported in the JSON line (host wall ms, and device ms of the
+# rollout / update event spans): rollout = env + wait_gpu + launch overheads
+PHASE_KEYS = ("rollout", "env", "wait_gpu", "rollout_gpu_ms", "respawn", "update", "update_gpu_ms", "total")
 
 
 def parse():
@@ -43,7 +46,9 @@ def parse():
     ap.add_argument("--env-device", choices=["cpu", "cuda"], default="cpu",
                     help="cpu: C++ env threads + pinned rows (the headline); cuda: the same env rules on the GPU")
     ap.add_argument("--json", default=None)
-    ap.add_argument("--timing", action="store_true", help="print per-phase times of each timed iteration to stderr")
+    ap.add_argument("--timing", action="store_true", help="also print each timed iteration's TIMING line to stderr")
+    ap.add_argument("--no-phases", action="store_true",
+                    help="skip the per-phase times (events and host clocks; on by default, reported max over ranks)")
     return ap.parse_args()
 
 
@@ -112,7 +117,7 @@ def run_ours(args) -> None:
     cfg = bench_config(args.envs)
     cfg.graphs = not args.no_graphs
     cfg.seed = 0
-    cfg.timing = args.timing
+    cfg.timing = args.timing or not args.no_phases
     cfg.env_device = args.env_device
     tr = Trainer(cfg, rank=rank, world=world, comm=comm, verbose=(rank == 0))
     for _ in range(args.warmup):
@@ -127,8 +132,11 @@ def run_ours(args) -> None:
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     w0 = time.perf_counter()
     e0.record()
+    phase_sum = {}
     for _ in range(args.steps):
         stats = tr.train_iteration()
+        for k, v in stats.get("timing", {}).items():
+            phase_sum[k] = phase_sum.get(k, 0.0) + v
         if args.timing and rank == 0:
             from surfb200.utils.timer import PhaseClock
             print(PhaseClock.timing_line(tr.iteration, stats.get("timing", {})), file=sys.stderr, flush=True)
@@ -141,9 +149,12 @@ def run_ours(args) -> None:
     clocks = sampler.stop()
     ms = e0.elapsed_time(e1)
     launches = L.launch_count() - launches0
+    # per-phase ms per timed iteration, max over ranks (every rank reports the same fixed key list)
+    phases = {k: phase_sum.get(k, 0.0) / args.steps for k in PHASE_KEYS} if phase_sum else {}
     if comm is not None:
         ms = comm.max_scalar(ms)
         wall = comm.max_scalar(wall)
+        phases = {k: comm.max_scalar(v) for k, v in phases.items()}
     ticks_per_iter = cfg.envs * cfg.n_steps * cfg.act_every * world
     value = ticks_per_iter * args.steps / (ms / 1e3)
     # end-to-end through the public API: the same iterations, wall clock incl.
@@ -171,6 +182,7 @@ def run_ours(args) -> None:
             "clocks": clocks,
             "e2e": {"value": round(e2e, 1), "unit": "ticks/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
+            "phases_ms_per_step": {k: round(v, 2) for k, v in phases.items()} or None,
             "last_iteration": {k: v for k, v in stats.items() if k != "timing"},
         }
         line = json.dumps(out)

@@ -342,7 +342,10 @@ __global__ void count_kernel(RewardParams p, const int64_t* new_key, int* counts
   if (delta) atomicAdd(delta + b, 1);
 }
 
-// proprioception features: out[i, j] = bf16(obs[i, idx[j]]) for j < nf, 0 beyond
+// proprioception features: out[i, j] = bf16(obs[i, idx[j]]) for j < nf, 0 beyond;
+// with `extra`, column extra_col instead holds tanh(extra[i] / 0.1): the
+// previous decision's reward fed back as an observation (reference
+// --obs-reward, python/train_fast.py:2104-2113)
 __global__ void features_kernel(const float* obs, int64_t ld_obs, const int* idx, int nf, int width, uint16_t* out,
                                 int64_t ld_out, int n, const float* extra, int extra_col) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -350,7 +353,7 @@ __global__ void features_kernel(const float* obs, int64_t ld_obs, const int* idx
   for (int j = 0; j < width; ++j) {
     float v = 0.0f;
     if (j < nf) v = obs[i * ld_obs + idx[j]];
-    if (extra && j == extra_col) v = extra[i];
+    if (extra && j == extra_col) v = tanhf(extra[i] * 10.0f);
     out[i * ld_out + j] = surfk::f32_to_bf16(v);
   }
 }
@@ -383,6 +386,35 @@ __global__ void perm_kernel(int64_t* out, int64_t n, int half_bits, const uint64
       x = (l << half_bits) | r;
     } while (x >= static_cast<uint64_t>(n));
     out[i] = x;
+  }
+}
+
+// The same keyed bijection over a pool whose size is read from device memory
+// (it changes between iterations without a host round trip): out[i] =
+// pool[pi(i)] for i < *count; the Feistel width follows *count.
+__global__ void perm_pool_kernel(int64_t* out, const int64_t* pool, int64_t n_max, const int64_t* count,
+                                 const uint64_t* key_ptr) {
+  const int64_t n = *count < n_max ? *count : n_max;
+  if (n <= 0) return;
+  int bits = 2;
+  while ((1ll << bits) < n) bits += 2;
+  const int half_bits = bits / 2;
+  const uint64_t key = *key_ptr;
+  const uint32_t mask = (1u << half_bits) - 1u;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    uint32_t x = static_cast<uint32_t>(i);
+    do {
+      uint32_t l = x >> half_bits, r = x & mask;
+      for (int round = 0; round < 4; ++round) {
+        const uint32_t f = feistel_round(r, static_cast<uint32_t>(key >> (16 * round)) * 0x2545F491u + round) & mask;
+        const uint32_t nl = r;
+        r = l ^ f;
+        l = nl;
+      }
+      x = (l << half_bits) | r;
+    } while (x >= static_cast<uint64_t>(n));
+    out[i] = pool[x];
   }
 }
 
@@ -435,6 +467,18 @@ SURF_EXPORT int surf_obs_features(const float* obs, int64_t ld_obs, const int* i
                                   int64_t ld_out, int n, const float* extra, int extra_col, void* stream) {
   features_kernel<<<static_cast<int>(surfk::ceil_div(n, 128)), 128, 0, static_cast<cudaStream_t>(stream)>>>(
       obs, ld_obs, idx, nf, width, static_cast<uint16_t*>(out), ld_out, n, extra, extra_col);
+  SURF_RETURN_LAUNCH();
+}
+
+// out[i] = pool[pi_key(i)] for i < *count (count <= n_max, read on the device);
+// the key advances as in surf_permutation.
+SURF_EXPORT int surf_permutation_pool(int64_t* out, const int64_t* pool, int64_t n_max, const int64_t* count,
+                                      uint64_t* key, void* stream) {
+  if (n_max < 1) return static_cast<int>(cudaErrorInvalidValue);
+  auto s = static_cast<cudaStream_t>(stream);
+  const int64_t blocks = surfk::ceil_div(n_max, 256);
+  perm_pool_kernel<<<static_cast<int>(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, s>>>(out, pool, n_max, count, key);
+  bump_key_kernel<<<1, 1, 0, s>>>(key);
   SURF_RETURN_LAUNCH();
 }
 

@@ -8,6 +8,8 @@
 //   * surf_gae: generalized advantage estimation, one thread per env scanning
 //     the T decisions backwards in registers (reference: a 128-iteration
 //     Python loop of tensor ops, python/train_fast.py:2119-2133).
+//   * surf_train_pool: the rows the update samples from (train stride, ez-greedy
+//     burst rows left out);
 //   * surf_adv_moments: per-minibatch sum / sum of squares of the advantages
 //     (double) for a whole epoch's permutation, so normalisation statistics
 //     can be reduced across ranks before the loss runs.
@@ -37,6 +39,22 @@ struct HeadSpec {
   int cont_col;
   int width;                   // logits row length
   int neutral[6];              // value of sim slots no head drives
+};
+
+// ez-greedy temporally-extended exploration (reference: --ez-eps / --ez-mu /
+// --ez-max, python/train_fast.py:748-761, 1952-1971): with probability eps per
+// decision an env that runs no burst starts one: a uniformly random category
+// for every discrete head, held for n ~ floor(u^(-1/(mu-1))) decisions
+// (u uniform, a zeta-like heavy tail) clamped to [1, max_len]. While a burst
+// runs, its action row replaces the sampled one and the decision is flagged
+// off-policy (the update leaves flagged rows out of its sample pool).
+struct EzArgs {
+  float eps;          // 0: off
+  float inv_mu1;      // 1 / (mu - 1)
+  int max_len;
+  int* left;          // [n] decisions left in the env's burst (persistent)
+  int32_t* act;       // [n, 8] the burst's action row (persistent)
+  uint8_t* flag;      // [n] out: 1 = burst action this decision
 };
 
 // ---- Philox-4x32-10 --------------------------------------------------------
@@ -72,7 +90,7 @@ template <typename T>
 __global__ void sample_kernel(const T* logits, int64_t ld_logits, HeadSpec hs, const float* log_std, int n,
                               uint64_t seed, uint64_t counter0, const int64_t* counter_ptr, int greedy, int32_t* act,
                               int64_t ld_act, float* logp_out, float* value_src, int64_t ld_value, float* value_out,
-                              const uint8_t* fail_src) {
+                              const uint8_t* fail_src, EzArgs ez) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= n) return;
@@ -131,7 +149,72 @@ __global__ void sample_kernel(const T* logits, int64_t ld_logits, HeadSpec hs, c
     out[7] = fail_src ? fail_src[warp] : 0;     // stall kill for the env's next step
     if (logp_out) logp_out[warp] = logp;
     if (value_out) value_out[warp] = value_src[warp * ld_value];
+    if (ez.eps > 0.0f) {
+      int left = ez.left[warp];
+      int32_t* row_ez = ez.act + warp * 8;
+      if (left == 0) {
+        const U4 r = philox(U4{static_cast<uint32_t>(warp), 0xE2E2u, static_cast<uint32_t>(counter),
+                               static_cast<uint32_t>(counter >> 32)}, k0 ^ 0x27D4EB2Fu, k1 ^ 0x165667B1u);
+        if (u01(r.x) < ez.eps) {
+          const float u = fmaxf(u01(r.y), 1e-6f);
+          const int len = static_cast<int>(powf(u, -ez.inv_mu1));
+          left = len < 1 ? 1 : (len > ez.max_len ? ez.max_len : len);
+          for (int s = 0; s < 6; ++s) row_ez[s] = hs.neutral[s] >= 0 ? hs.neutral[s] : 0;
+          for (int h0 = 0; h0 < hs.n_heads; h0 += 4) {
+            const U4 q = philox(U4{static_cast<uint32_t>(warp), 0xE3E3u + static_cast<uint32_t>(h0),
+                                   static_cast<uint32_t>(counter), static_cast<uint32_t>(counter >> 32)},
+                                k0 ^ 0x27D4EB2Fu, k1 ^ 0x165667B1u);
+            const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+            for (int j = 0; j < 4 && h0 + j < hs.n_heads; ++j) {
+              const int h = h0 + j, sz = hs.size[h];
+              const int cat = static_cast<int>(u01(words[j]) * static_cast<float>(sz));
+              row_ez[hs.slot[h]] = cat < sz ? cat : sz - 1;
+            }
+          }
+        }
+      }
+      const bool live = left > 0;
+      if (live) {
+        for (int s = 0; s < 6; ++s) out[s] = row_ez[s];
+        --left;
+      }
+      ez.left[warp] = left;
+      ez.flag[warp] = live ? 1 : 0;
+    }
   }
+}
+
+// ---- training pool ------------------------------------------------------------
+// Rows r = t * n + e of a rollout that the update samples from: decisions
+// t = offset, offset + stride, ... (reference --train-stride,
+// python/train_fast.py:2162-2168) whose action was on-policy (ez flag 0,
+// :2170-2177). One block: each thread compacts a contiguous run of rows, a
+// block-wide scan places the runs, so the pool keeps row order.
+__global__ void __launch_bounds__(1024) train_pool_kernel(const uint8_t* ez_flag, int T, int n, int stride,
+                                                          int offset, int64_t* pool, int64_t* count) {
+  const int64_t total = static_cast<int64_t>(T) * n;
+  const int64_t per = (total + blockDim.x - 1) / blockDim.x;
+  const int64_t lo = threadIdx.x * per, hi = min(total, lo + per);
+  auto keep = [&](int64_t r) {
+    const int t = static_cast<int>(r / n);
+    if (t < offset || (t - offset) % stride) return false;
+    return !(ez_flag && ez_flag[r]);
+  };
+  int64_t mine = 0;
+  for (int64_t r = lo; r < hi; ++r) mine += keep(r) ? 1 : 0;
+  __shared__ int64_t scan[1024];
+  scan[threadIdx.x] = mine;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {           // Hillis-Steele inclusive scan
+    const int64_t v = threadIdx.x >= o ? scan[threadIdx.x - o] : 0;
+    __syncthreads();
+    scan[threadIdx.x] += v;
+    __syncthreads();
+  }
+  int64_t at = scan[threadIdx.x] - mine;
+  for (int64_t r = lo; r < hi; ++r)
+    if (keep(r)) pool[at++] = r;
+  if (threadIdx.x == blockDim.x - 1) *count = scan[threadIdx.x];
 }
 
 // ---- GAE ---------------------------------------------------------------------
@@ -319,8 +402,13 @@ SURF_EXPORT int surf_sample_heads(const void* logits, int logits_bf16, int64_t l
                                   uint64_t seed, uint64_t counter, const int64_t* counter_ptr, int greedy,
                                   int32_t* act, int64_t ld_act,
                                   float* logp, const float* value_src, int64_t ld_value, float* value_out,
-                                  const uint8_t* fail_src, void* stream) {
+                                  const uint8_t* fail_src, const EzArgs* ez_in, void* stream) {
   if (n_heads > kMaxHeads) return static_cast<int>(cudaErrorInvalidValue);
+  EzArgs ez{};
+  if (ez_in && ez_in->eps > 0.0f) {
+    if (!ez_in->left || !ez_in->act || !ez_in->flag || ez_in->max_len < 1) return static_cast<int>(cudaErrorInvalidValue);
+    ez = *ez_in;
+  }
   for (int h = 0; h < n_heads; ++h)
     if (sizes[h] > 32) return static_cast<int>(cudaErrorInvalidValue);
   HeadSpec hs = make_spec(sizes, n_heads, slots, cont, neutral);
@@ -329,12 +417,13 @@ SURF_EXPORT int surf_sample_heads(const void* logits, int logits_bf16, int64_t l
   if (logits_bf16)
     sample_kernel<uint16_t><<<blocks, threads, 0, s>>>(static_cast<const uint16_t*>(logits), ld_logits, hs, log_std, n,
                                                        seed, counter, counter_ptr, greedy, act, ld_act, logp,
-                                                       const_cast<float*>(value_src), ld_value, value_out, fail_src);
+                                                       const_cast<float*>(value_src), ld_value, value_out, fail_src,
+                                                       ez);
   else
     sample_kernel<float><<<blocks, threads, 0, s>>>(static_cast<const float*>(logits), ld_logits, hs, log_std, n, seed,
                                                     counter, counter_ptr, greedy, act, ld_act, logp,
                                                     const_cast<float*>(value_src),
-                                                    ld_value, value_out, fail_src);
+                                                    ld_value, value_out, fail_src, ez);
   SURF_RETURN_LAUNCH();
 }
 
@@ -373,6 +462,14 @@ SURF_EXPORT int surf_ppo_loss(const void* logits, int logits_bf16, int64_t ld_lo
     ppo_loss_kernel<float><<<blocks, threads, 0, s>>>(static_cast<const float*>(logits), ld_logits, value, ld_value,
                                                       act, ld_act, old_logp, adv, ret, idx, moments, hs, log_std, la,
                                                       n, dlogits, ld_dlogits, dvalue, ld_dvalue, dlog_std, stats);
+  SURF_RETURN_LAUNCH();
+}
+
+// pool: int64 [T * n] (the first *count entries are written); count: one int64.
+SURF_EXPORT int surf_train_pool(const uint8_t* ez_flag, int T, int n, int stride, int offset, int64_t* pool,
+                                int64_t* count, void* stream) {
+  if (T < 1 || n < 1 || stride < 1 || offset < 0 || offset >= stride) return static_cast<int>(cudaErrorInvalidValue);
+  train_pool_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(ez_flag, T, n, stride, offset, pool, count);
   SURF_RETURN_LAUNCH();
 }
 

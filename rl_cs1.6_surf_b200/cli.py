@@ -104,6 +104,11 @@ def _train_parser(sub) -> None:
     ap.add_argument("--reset-steps", action="store_true", help="restart the step counter / schedules on resume")
     ap.add_argument("--reset-int-counts", action="store_true", help="drop the checkpoint's curiosity counts")
     ap.add_argument("--iterations", type=int, default=None, help="stop after this many iterations")
+    # reference spellings of two settings (python/train_fast.py:785, 804)
+    ap.add_argument("--keep-teleports", dest="teleport_fail", action="store_false", default=None,
+                    help="falling into a teleport does not end the episode (same as --no-teleport-fail)")
+    ap.add_argument("--free-pitch", action="store_true",
+                    help="drop a resumed checkpoint's fixed gaze (fix_pitch) and re-enable the pitch head")
 
 
 def _dist():
@@ -119,6 +124,8 @@ def cmd_train(args) -> int:
     from .utils.runlog import RunLogger
     rank, world, local = _dist()
     over, rew_over = _overrides(args)
+    if getattr(args, "free_pitch", False):
+        over["fix_pitch"] = None                 # an explicit override: wins over the checkpoint's value
     sd = None
     restored, changed = [], []
     if args.ckpt:
@@ -175,6 +182,12 @@ def cmd_train(args) -> int:
                 if rank == 0:
                     print(f"eval: return {summ['ep_return']:.2f} speed_max {summ['speed_max']:.0f} "
                           f"success {summ['success_rate']:.2f} -> {summ.get('file')}", flush=True)
+                if not cfg.eval_greedy_only:        # the stochastic recording beside the greedy one
+                    sout = out.with_name(out.name.replace(".traj.jsonl", "_stoch.traj.jsonl")) if out else None
+                    ss = evaluate(tr, episodes=cfg.eval_eps, greedy=False, max_ticks=cfg.ep_ticks, out=sout,
+                                  seed=tr.global_step & 0x7FFFFFFF)
+                    if rank == 0:
+                        print(f"eval (stochastic): return {ss['ep_return']:.2f} -> {ss.get('file')}", flush=True)
             numbered = cad.numbered(tr.global_step)
             latest = cad.latest_due(time.time())
             if comm is not None:

@@ -87,7 +87,7 @@ def ptr(t) -> int:
 
 # Kernel launches issued by each entry point (for launch accounting; entry
 # points not listed launch exactly one kernel).
-_KERNELS_PER_CALL = {"surf_reward": 2, "surf_permutation": 2, "surf_edt": 4, "surf_geodesic_pass": 3,
+_KERNELS_PER_CALL = {"surf_reward": 2, "surf_permutation": 2, "surf_permutation_pool": 2, "surf_edt": 4, "surf_geodesic_pass": 3,
                      "surf_geodesic_init": 3, "surf_geodesic_finish": 2}
 _launches = [0]
 

@@ -20,6 +20,7 @@ from typing import Optional
 import torch
 
 from . import _lib
+from ..rewards import spec as _spec  # noqa: F401  (registers surf_permutation_pool of libsurf_rl.so)
 from . import gemm as _gemm  # noqa: F401  (registers the libsurf_nn.so signatures the optimizer uses)
 from ._lib import check, ptr, stream_ptr
 
@@ -28,7 +29,8 @@ NLIB = "libsurf_nn.so"
 _lib.register(RLIB, {
     "surf_sample_heads": (c_int, [c_void_p, c_int, c_int64, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                   c_int, c_uint64, c_uint64, c_void_p, c_int, c_void_p, c_int64, c_void_p, c_void_p,
-                                  c_int64, c_void_p, c_void_p, c_void_p]),
+                                  c_int64, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "surf_train_pool": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "surf_counter_add": (c_int, [c_void_p, c_int64, c_void_p]),
     "surf_gae": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_float, c_void_p, c_void_p,
                          c_void_p, c_void_p]),
@@ -45,6 +47,78 @@ LOG_SQRT_2PI = 0.9189385332046727
 def _error_flag(device):
     from .gemm import error_flag
     return error_flag(device)
+
+
+class EzArgs(ctypes.Structure):
+    """ez-greedy burst state handed to the sampling kernel (see EzGreedy)."""
+    _fields_ = [("eps", c_float), ("inv_mu1", c_float), ("max_len", c_int), ("left", c_void_p), ("act", c_void_p),
+                ("flag", c_void_p)]
+
+
+class EzGreedy:
+    """Temporally-extended exploration state of N envs (reference --ez-eps,
+    --ez-mu, --ez-max; python/train_fast.py:748-761, 1952-1971). With
+    probability ``eps`` per decision an env without a running burst starts
+    one: every discrete head gets a uniformly random category, held for
+    floor(u^(-1/(mu-1))) decisions (u uniform) clamped to [1, max_len]. Burst
+    decisions are flagged off-policy; the update leaves them out of its pool."""
+
+    def __init__(self, n: int, eps: float, mu: float = 2.0, max_len: int = 60, device="cuda"):
+        if eps > 0 and mu <= 1.0:
+            raise ValueError("ez-greedy needs mu > 1")
+        self.eps, self.mu, self.max_len = float(eps), float(mu), int(max_len)
+        self.left = torch.zeros(n, dtype=torch.int32, device=device)
+        self.act = torch.zeros(n, 8, dtype=torch.int32, device=device)
+
+    def args(self, lo: int, hi: int, flag_out: torch.Tensor) -> EzArgs:
+        a = EzArgs()
+        a.eps, a.inv_mu1, a.max_len = self.eps, 1.0 / (self.mu - 1.0), self.max_len
+        a.left, a.act, a.flag = ptr(self.left[lo:hi]), ptr(self.act[lo:hi]), ptr(flag_out)
+        return a
+
+    def apply_reference(self, act: torch.Tensor, layout, generator: Optional[torch.Generator] = None) -> torch.Tensor:
+        """CPU statement of the burst rule on sampled action rows (in place);
+        returns the off-policy flags (uint8 [N])."""
+        n = act.shape[0]
+        fresh = (self.left == 0) & (torch.rand(n, generator=generator) < self.eps)
+        k = int(fresh.sum())
+        if k:
+            u = torch.rand(k, generator=generator).clamp_(1e-6, 1.0)
+            self.left[fresh] = u.pow(-1.0 / (self.mu - 1.0)).to(torch.int32).clamp_(1, self.max_len)
+            row = torch.zeros(k, 8, dtype=torch.int32)
+            for s, v in enumerate(layout.neutral):
+                if v >= 0:
+                    row[:, s] = v
+            for size, slot in zip(layout.sizes, layout.slots):
+                row[:, slot] = (torch.rand(k, generator=generator) * size).to(torch.int32).clamp_(0, size - 1)
+            self.act[fresh] = row
+        live = self.left > 0
+        act[live, :6] = self.act[live, :6]
+        self.left[live] -= 1
+        return live.to(torch.uint8)
+
+
+def train_pool(ez_flag: Optional[torch.Tensor], T: int, n: int, stride: int, offset: int, pool: torch.Tensor,
+               count: torch.Tensor) -> None:
+    """pool[:count] = the rollout rows t * n + e the update samples from:
+    decisions t = offset, offset + stride, ... whose action was on-policy."""
+    check(_lib.lib(RLIB).surf_train_pool(ptr(ez_flag), int(T), int(n), int(stride), int(offset), ptr(pool),
+                                         ptr(count), stream_ptr(pool.device)), "surf_train_pool")
+
+
+def train_pool_reference(ez_flag: Optional[torch.Tensor], T: int, n: int, stride: int, offset: int) -> torch.Tensor:
+    t = torch.arange(T).repeat_interleave(n)
+    keep = (t >= offset) & ((t - offset) % stride == 0)
+    if ez_flag is not None:
+        keep &= ez_flag.reshape(-1).cpu() == 0
+    return torch.nonzero(keep).squeeze(1)
+
+
+def permutation_pool(out: torch.Tensor, pool: torch.Tensor, count: torch.Tensor, key: torch.Tensor) -> None:
+    """out[:count] = pool[pi(i)], a keyed permutation of the pool's first
+    ``count`` entries (count read on the device); the key advances."""
+    check(_lib.lib(RLIB).surf_permutation_pool(ptr(out), ptr(pool), int(pool.numel()), ptr(count), ptr(key),
+                                               stream_ptr(out.device)), "surf_permutation_pool")
 
 
 class HeadArgs:
@@ -67,13 +141,14 @@ def sample_heads(logits: torch.Tensor, heads: HeadArgs, log_std: torch.Tensor, a
                  logp_out: Optional[torch.Tensor], seed: int, counter: int, greedy: bool = False,
                  value_src: Optional[torch.Tensor] = None, value_out: Optional[torch.Tensor] = None,
                  fail_src: Optional[torch.Tensor] = None, counter_ptr: Optional[torch.Tensor] = None,
-                 counter_offset: int = 0) -> None:
+                 counter_offset: int = 0, ez: Optional[EzArgs] = None) -> None:
     """Sample every head for each row of ``logits`` ([N, >=n_logits] fp32);
     writes the int32 action rows (``act_out`` [N, 8]) and summed log-probs;
     optionally copies a strided value column to ``value_out`` and the stall
     flags ``fail_src`` into action slot 7. The Philox counter is
     ``counter + counter_offset`` (+ ``*counter_ptr`` when given, a device
-    int64 the trainer advances, so graph replays draw fresh noise)."""
+    int64 the trainer advances, so graph replays draw fresh noise). ``ez``
+    (``EzGreedy.args``) applies ez-greedy bursts to the sampled rows."""
     n = logits.shape[0]
     check(_lib.lib(RLIB).surf_sample_heads(
         ptr(logits), 1 if logits.dtype == torch.bfloat16 else 0, logits.stride(0), heads.host_ptr(heads.sizes),
@@ -81,7 +156,7 @@ def sample_heads(logits: torch.Tensor, heads: HeadArgs, log_std: torch.Tensor, a
         int(seed) & (2 ** 64 - 1), (int(counter) + int(counter_offset)) & (2 ** 64 - 1), ptr(counter_ptr),
         1 if greedy else 0, ptr(act_out), act_out.stride(0),
         ptr(logp_out), ptr(value_src), value_src.stride(0) if value_src is not None else 0, ptr(value_out),
-        ptr(fail_src), stream_ptr(logits.device)), "surf_sample_heads")
+        ptr(fail_src), ctypes.byref(ez) if ez is not None else None, stream_ptr(logits.device)), "surf_sample_heads")
 
 
 def log_prob_reference(logits: torch.Tensor, act: torch.Tensor, layout, log_std: torch.Tensor):

@@ -104,6 +104,7 @@ _lib.register(RLIB, {
     "surf_obs_features": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_int64, c_int, c_void_p,
                                   c_int, c_void_p]),
     "surf_permutation": (c_int, [c_void_p, c_int64, c_void_p, c_void_p]),
+    "surf_permutation_pool": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
 })
 
 

@@ -21,6 +21,7 @@ RUN_DEFINING = (
     "continuous_yaw", "gps", "heads", "hidden", "fc", "proprio", "mlp", "reward", "pitch_rate", "yaw_adaptive",
     "respawn_frac", "respawn_margin", "respawn_reservoir", "train_stride", "drop_frac", "drop_min", "drop_max",
     "punch_min", "punch_max", "respawn_speed", "respawn_binned", "respawn_pool", "rnd_coef",
+    "ez_eps", "ez_mu", "ez_max", "fix_pitch", "reward_per_decision", "obs_reward", "eval_greedy_only",
 )
 
 
@@ -43,13 +44,21 @@ class TrainConfig:
     airaccelerate: float = 100.0
     pitch_rate: float = 10.0
     yaw_adaptive: bool = False
+    # fixed gaze: view pitch frozen at this angle (degrees, + up) for every
+    # spawn; the pitch head stays in the action space but cannot move the view
+    fix_pitch: Optional[float] = None
     # PPO
     steps: float = 1e9                 # physics ticks (all ranks)
     n_steps: int = 128                 # decisions per rollout
     act_every: int = 3                 # physics ticks per decision
     epochs: int = 4
     minibatches: int = 8
-    train_stride: int = 1
+    train_stride: int = 1              # update samples decisions t = offset, offset + S, ... (offset rotates)
+    # ez-greedy temporally-extended exploration (0 = off): burst start
+    # probability per decision, zeta exponent and cap of the burst length
+    ez_eps: float = 0.0
+    ez_mu: float = 2.0
+    ez_max: int = 60
     lr: float = 3e-4
     gamma: float = 0.9995              # per tick; GAE uses gamma ** act_every
     gae: float = 0.95
@@ -80,6 +89,13 @@ class TrainConfig:
     mlp: tuple = (256, 256)
     # reward
     reward: RewardSpec = field(default_factory=RewardSpec)
+    # rewards are evaluated once per decision of act_every ticks (potential
+    # terms telescope exactly; stall / finish bookkeeping has decision
+    # granularity); the per-tick evaluation is not provided
+    reward_per_decision: bool = True
+    # the previous decision's reward, tanh(r / 0.1), as an extra observation
+    # scalar (the heading slot 12 that the no-GPS policy hides); race only
+    obs_reward: bool = False
     # respawn reservoir (Go-Explore restarts)
     respawn_frac: float = 0.0          # share of episodes started from the reservoir (0 = off)
     respawn_margin: float = 10.0       # seconds before an episode's end that are still harvestable
@@ -101,10 +117,31 @@ class TrainConfig:
     ckpt_every: float = 50e6
     record_every: float = 0.0
     eval_eps: int = 3
+    eval_greedy_only: bool = False     # skip the stochastic eval recording
     timing: bool = False
     # data parallel: every this many iterations all ranks compare a checksum of
     # their parameter replicas and raise ReplicaDivergence if they differ (0: off)
     replica_check_every: int = 0
+
+    def validate(self) -> None:
+        """Reject settings this build cannot honour (with the reason)."""
+        if self.train_stride < 1:
+            raise ValueError("train_stride must be >= 1")
+        if self.ez_eps < 0 or self.ez_eps >= 1:
+            raise ValueError("ez_eps must be in [0, 1)")
+        if self.ez_eps > 0 and (self.ez_mu <= 1.0 or self.ez_max < 1):
+            raise ValueError("ez-greedy needs ez_mu > 1 and ez_max >= 1")
+        if self.ez_eps > 0 and self.continuous_yaw:
+            raise ValueError("ez-greedy bursts draw discrete head categories: not available with continuous_yaw")
+        if not self.reward_per_decision:
+            raise ValueError("rewards are evaluated once per decision in this framework (reward_per_decision must "
+                             "stay on); per-tick evaluation is not provided")
+        if self.obs_reward and self.reward.mode != "race":
+            raise ValueError("obs_reward needs the race reward (its observation mirrors the geodesic shaping)")
+        if self.obs_reward and self.gps:
+            raise ValueError("obs_reward uses scalar slot 12, which gps exposes as a position channel")
+        if self.fix_pitch is not None and not -70.0 <= self.fix_pitch <= 30.0:
+            raise ValueError("fix_pitch must lie in the view clamp [-70, 30] degrees")
 
     def to_dict(self) -> dict:
         d = asdict(self)

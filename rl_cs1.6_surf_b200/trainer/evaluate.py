@@ -107,9 +107,34 @@ class _EvalFrames:
         return out
 
 
-def _policy_actions(trainer, h: np.ndarray, greedy: bool, gen: Optional[torch.Generator], frames=None):
+class _RewardFeed:
+    """The obs-reward observation during evaluation (reference
+    _make_eval_reward_feed, python/train_fast.py:1478-1499): the eval env pays
+    no training reward, so the race shaping term is recomputed from the goal
+    field per decision, r = clip(d_prev - d, +-100 K) * scale - time_pen * K
+    (zeros on the first decision), and the policy reads tanh(r / 0.1)."""
+
+    def __init__(self, trainer, K: int):
+        spec = trainer.cfg.reward
+        self.field, self.K = trainer.field, K
+        self.scale = spec.resolved_scale(trainer.d0)
+        self.time_pen = spec.time_pen
+        self.d = None
+
+    def __call__(self, origins: np.ndarray) -> np.ndarray:
+        d = np.asarray(self.field.sample(origins.astype(np.float64)), np.float64)
+        prev, self.d = self.d, d
+        if prev is None:
+            return np.zeros(len(d), np.float32)
+        delta = np.clip(prev - d, -100.0 * self.K, 100.0 * self.K)
+        return (delta * self.scale - self.time_pen * self.K).astype(np.float32)
+
+
+def _policy_actions(trainer, h: np.ndarray, greedy: bool, gen: Optional[torch.Generator], frames=None,
+                    rew: Optional[np.ndarray] = None):
     """Action rows [n, 8] int32 for host records h [n, 64] (``frames``: the
-    frame history when the policy stacks frames)."""
+    frame history when the policy stacks frames; ``rew``: the obs-reward feed,
+    raw rewards of the previous decision)."""
     from ..models.policy import Workspace, forward_gpu
     from ..ops import rl as R
     net, layout = trainer.net, trainer.layout
@@ -118,7 +143,8 @@ def _policy_actions(trainer, h: np.ndarray, greedy: bool, gen: Optional[torch.Ge
         dev = trainer.device
         hd = torch.as_tensor(h, device=dev)
         scal = torch.zeros((n, 16), dtype=torch.bfloat16, device=dev)
-        trainer._features(hd[:, C_OBS:C_OBS + 15].contiguous(), scal)
+        trainer._features(hd[:, C_OBS:C_OBS + 15].contiguous(), scal,
+                          rew=torch.as_tensor(rew, device=dev) if rew is not None else None)
         img = None
         if trainer.cfg.vision:
             pose = hd[:, C_REC:C_REC + 6].contiguous()
@@ -130,6 +156,8 @@ def _policy_actions(trainer, h: np.ndarray, greedy: bool, gen: Optional[torch.Ge
     else:
         feats = np.zeros((n, 16), np.float32)
         feats[:, :len(trainer.feat_idx)] = h[:, [C_OBS + i for i in trainer.feat_idx]]
+        if trainer.rew_col >= 0:
+            feats[:, trainer.rew_col] = np.tanh((rew if rew is not None else np.zeros(n, np.float32)) / 0.1)
         with torch.no_grad():
             out = net.forward_reference(torch.from_numpy(feats), None)
     act, _ = R.sample_reference(out, layout, net.p("log_std").detach().float().cpu(), gen, greedy=greedy)
@@ -146,7 +174,8 @@ def evaluate(trainer, episodes: int = 3, greedy: bool = True, max_ticks: int = 6
     env_cfg = default_config(n, max_episode_ticks=max_ticks, spawn_mode=2 if (pool is not None or
                                                                                trainer.spawn_pool is not None) else 0,
                              sv_maxvelocity=cfg.maxvel, sv_airaccelerate=cfg.airaccelerate,
-                             pitch_rate_max_deg=cfg.pitch_rate, yaw_adaptive=int(cfg.yaw_adaptive))
+                             pitch_rate_max_deg=0.0 if cfg.fix_pitch is not None else cfg.pitch_rate,
+                             yaw_adaptive=int(cfg.yaw_adaptive))
     core = SimCore.from_bytes(trainer.map_image, env_cfg, threads=min(8, n))
     sp = pool if pool is not None else trainer.spawn_pool
     if sp is not None:
@@ -178,8 +207,10 @@ def evaluate(trainer, episodes: int = 3, greedy: bool = True, max_ticks: int = 6
     K = cfg.act_every
     t = 0
     frames = _EvalFrames(trainer, n) if getattr(trainer, "stacker", None) is not None else None
+    feed = _RewardFeed(trainer, K) if trainer.rew_col >= 0 else None
     while active.any() and t < max_ticks:
-        act = np.ascontiguousarray(_policy_actions(trainer, h, greedy, gen, frames).astype(np.int32))
+        rew_feed = feed(h[:, C_REC:C_REC + 3]) if feed is not None else None
+        act = np.ascontiguousarray(_policy_actions(trainer, h, greedy, gen, frames, rew_feed).astype(np.int32))
         for _ in range(K):
             pre = st.copy()
             hp = h.ctypes.data

@@ -43,6 +43,7 @@ from .config import TrainConfig
 # column layout of the per-env host record (float32)
 C_OBS, C_TOBS, C_REC, C_TREC, H_COLS = 0, 16, 32, 48, 64
 NOGPS = (0, 1, 2, 3, 4, 5, 6, 9, 10, 11)      # honest proprioception (no heading, no position)
+REWARD_SLOT = 12                               # observation slot that carries the obs-reward feed
 
 
 def build_spawn_pool(core, kind: str, cfg, procedural=None):
@@ -72,6 +73,7 @@ class ReplicaDivergence(RuntimeError):
 
 class Trainer:
     def __init__(self, cfg: TrainConfig, rank: int = 0, world: int = 1, comm=None, verbose: bool = True):
+        cfg.validate()
         self.cfg = cfg
         self.rank, self.world, self.comm = rank, world, comm
         self.verbose = verbose and rank == 0
@@ -114,15 +116,23 @@ class Trainer:
             probe = SimCore.from_bytes(image, default_config(1), threads=1)
             pool = build_spawn_pool(probe, cfg.spawn, cfg, procedural=pool)
             probe.close()
-        if cfg.respawn_frac > 0 and pool is None:        # the reservoir needs pool spawning
+        fixed = cfg.fix_pitch is not None
+        if (cfg.respawn_frac > 0 or fixed) and pool is None:   # the reservoir / a fixed gaze need pool spawning
             from ..sim import spawns
             probe = SimCore.from_bytes(image, default_config(1), threads=1)
             pool = spawns.map_pool(probe)
             probe.close()
-        spawn_mode = 2 if (cfg.spawn != "map" or cfg.respawn_frac > 0) and pool is not None else 0
+        if fixed:
+            # fixed gaze (reference --fix-pitch, python/train_fast.py:1320-1323,
+            # 1394): every start looks at the fixed pitch and the view pitch
+            # rate is zero, so the pitch head cannot move the view
+            pool = pool.copy()
+            pool["pitch"] = np.float32(cfg.fix_pitch)
+        spawn_mode = 2 if (cfg.spawn != "map" or cfg.respawn_frac > 0 or fixed) and pool is not None else 0
         env_cfg = default_config(cfg.envs, max_episode_ticks=cfg.ep_ticks, spawn_mode=spawn_mode,
                                  yaw_jitter_deg=cfg.yaw_jitter, sv_maxvelocity=cfg.maxvel,
-                                 sv_airaccelerate=cfg.airaccelerate, pitch_rate_max_deg=cfg.pitch_rate,
+                                 sv_airaccelerate=cfg.airaccelerate,
+                                 pitch_rate_max_deg=0.0 if fixed else cfg.pitch_rate,
                                  yaw_adaptive=int(cfg.yaw_adaptive))
         self.core = SimCore.from_bytes(image, env_cfg, threads=cfg.threads)
         if spawn_mode == 2:
@@ -160,6 +170,10 @@ class Trainer:
             heads = tuple(h for h in heads if h != "pitch")
         self.layout = HeadLayout(heads, cfg.continuous_yaw)
         self.feat_idx = tuple(range(15)) if cfg.gps else NOGPS
+        self.rew_col = -1
+        if cfg.obs_reward:                     # the previous reward rides in slot 12 (hidden heading / position)
+            self.feat_idx = tuple(sorted(set(self.feat_idx) | {REWARD_SLOT}))
+            self.rew_col = self.feat_idx.index(REWARD_SLOT)
         self.frame_ch = 2 if (cfg.vision and cfg.surf_mask) else 1
         self.n_frames = max(1, int(cfg.frame_stack)) if cfg.vision else 1
         if cfg.vision and (cfg.surf_mask or self.n_frames > 1) and not self.gpu:
@@ -239,6 +253,14 @@ class Trainer:
         self.feat_idx_t = torch.tensor(list(self.feat_idx) + [0] * (16 - len(self.feat_idx)), dtype=torch.int32,
                                        device=dev)
         self.mb = T * N // cfg.minibatches
+        self.ez = None
+        if cfg.ez_eps > 0:
+            self.ez = R.EzGreedy(N, cfg.ez_eps, cfg.ez_mu, cfg.ez_max, device=dev)
+            self.b_ez = torch.zeros((T, N), dtype=torch.uint8, device=dev)
+        # the update samples from a pool of rollout rows when it strides over
+        # decisions or leaves ez-greedy bursts out (else: every row)
+        self.pooled = cfg.train_stride > 1 or self.ez is not None
+        self.zero_rew = torch.zeros(N, device=dev)
         if self.gpu:
             G = cfg.env_groups if (cfg.env_groups > 1 and N % cfg.env_groups == 0 and N // cfg.env_groups >= 64) else 1
             step = N // G
@@ -258,6 +280,10 @@ class Trainer:
             self.grp_events = [torch.cuda.Event() for _ in range(G)]
             self.ws_upd = Workspace(self.net, self.mb)
             self.perm = torch.zeros(T * N, dtype=torch.int64, device=dev)
+            if self.pooled:
+                self.pool = torch.zeros(T * N, dtype=torch.int64, device=dev)
+                self.pool_count = torch.zeros(1, dtype=torch.int64, device=dev)
+                self.mb_graphs: list = []
             self.perm_key = torch.tensor([cfg.seed * 7919 + self.rank], dtype=torch.int64, device=dev)
             self.mom_mb = torch.zeros((cfg.minibatches, 2), dtype=torch.float64, device=dev)
             self.img_mb = torch.zeros((self.mb, max(self.img_w, 8)), dtype=torch.bfloat16, device=dev)
@@ -319,7 +345,8 @@ class Trainer:
         self.respawn.commit(self.comm if self.world > 1 else None)
         pool = self.respawn.build_pool(self.start_pool, pool_size=self.cfg.respawn_pool,
                                        fresh_frac=1.0 - self.cfg.respawn_frac,
-                                       vel_scale=tuple(self.cfg.respawn_speed))
+                                       vel_scale=tuple(self.cfg.respawn_speed),
+                                       pitch_jitter=0.0 if self.cfg.fix_pitch is not None else 5.0)
         self.core.set_spawn_pool(pool)
 
     # ---- environment plumbing -------------------------------------------------------------
@@ -359,12 +386,19 @@ class Trainer:
             self.reward.init(h[:, C_REC:C_REC + REC_COLS].copy())
 
     # ---- GPU rollout ------------------------------------------------------------------------
-    def _features(self, obs: torch.Tensor, out: torch.Tensor) -> None:
+    def _features(self, obs: torch.Tensor, out: torch.Tensor, rew: Optional[torch.Tensor] = None) -> None:
+        """Proprioception rows; with obs_reward, column ``rew_col`` holds
+        tanh(rew / 0.1) (the previous decision's reward; zeros when ``rew``
+        is None)."""
         from ..ops import _lib
         from ..ops._lib import check, ptr, stream_ptr
+        extra = None
+        if self.rew_col >= 0:
+            extra = rew if rew is not None else self.zero_rew[:obs.shape[0]]
         check(_lib.lib("libsurf_rl.so").surf_obs_features(ptr(obs), obs.stride(0), ptr(self.feat_idx_t),
                                                           len(self.feat_idx), 16, ptr(out), out.stride(0),
-                                                          obs.shape[0], None, 0, stream_ptr(obs.device)),
+                                                          obs.shape[0], ptr(extra), self.rew_col,
+                                                          stream_ptr(obs.device)),
               "surf_obs_features")
 
     def _group_body(self, g: int, t: int, env: bool = True) -> None:
@@ -396,14 +430,15 @@ class Trainer:
                 done = self.b_done[t - 1, lo:hi] if t > 0 else None      # t == 0 continues the last tail
                 img = self.stacker.rollout(self.b_img, self.pro + t, lo, hi, done, self.age_cur, self.b_age[t, lo:hi],
                                            self.stk_grp[g])
-        self._features(self.hdev[lo:hi, C_OBS:C_OBS + 15], self.b_scal[t, lo:hi])
+        self._features(self.hdev[lo:hi, C_OBS:C_OBS + 15], self.b_scal[t, lo:hi], rew=self.b_rew[(t - 1) % T, lo:hi])
         out = forward_gpu(self.net, self.ws_grp[g], self.b_scal[t, lo:hi], img)
         vc = self.layout.value_col
         if t < T:
             R.sample_heads(out, self.heads, self.net.p("log_std"), self.b_act[t, lo:hi], self.b_logp[t, lo:hi],
                            self.seed_base ^ (0x9E3779B97F4A7C15 * (g + 1) & 0xFFFFFFFFFFFF), 0,
                            value_src=out[:, vc], value_out=self.b_val[t, lo:hi], fail_src=self.reward.stall[lo:hi],
-                           counter_ptr=self.sample_counter, counter_offset=t)
+                           counter_ptr=self.sample_counter, counter_offset=t,
+                           ez=self.ez.args(lo, hi, self.b_ez[t, lo:hi]) if self.ez is not None else None)
             if self.genv is None:
                 self.act_pin[lo:hi].copy_(self.b_act[t, lo:hi], non_blocking=True)
         else:
@@ -593,37 +628,117 @@ class Trainer:
         C.wait_stream(E)
 
     # ---- GPU update ---------------------------------------------------------------------------
-    def _epoch_body(self) -> None:
-        from ..ops import gemm as G
+    def _epoch_prologue(self) -> None:
+        """The epoch's permutation of the sample rows (all rows, or the pool)
+        and the per-minibatch advantage moments (reduced across ranks)."""
         from ..ops import _lib
         from ..ops._lib import check, ptr, stream_ptr
         T, N, mb, nmb = self.T, self.N, self.mb, self.cfg.minibatches
-        lib = _lib.lib("libsurf_rl.so")
-        check(lib.surf_permutation(ptr(self.perm), T * N, ptr(self.perm_key), stream_ptr(self.device)),
-              "surf_permutation")
+        if self.pooled:
+            R.permutation_pool(self.perm, self.pool, self.pool_count, self.perm_key)
+        else:
+            check(_lib.lib("libsurf_rl.so").surf_permutation(ptr(self.perm), T * N, ptr(self.perm_key),
+                                                             stream_ptr(self.device)), "surf_permutation")
         self.mom_mb.zero_()
         R.adv_moments(self.adv.view(-1), self.perm, mb, nmb, self.mom_mb)
         if self.comm is not None:
             self.comm.allreduce_moments(self.mom_mb)
+
+    def _minibatch(self, m: int) -> None:
+        """Minibatch m of the epoch: row gathers, forward, fused PPO loss and
+        gradient, backward, optimizer step (fused across ranks)."""
+        from ..ops import gemm as G
+        T, N, mb = self.T, self.N, self.mb
         f_img = self.b_img[self.pro:self.pro + T].view(T * N, -1) if self.cfg.vision else None
         f_scal = self.b_scal[:T].view(T * N, 16)
-        for m in range(nmb):
-            idx = self.perm[m * mb:(m + 1) * mb]
-            if self.stacker is not None:
-                self.stacker.gather(self.b_img, idx, self.b_age[:T].view(-1), self.img_mb)
-            elif self.cfg.vision:
-                G.gather_rows(f_img, idx, self.img_mb)
-            G.gather_rows(f_scal, idx, self.scal_mb)
-            out = forward_gpu(self.net, self.ws_upd, self.scal_mb, self.img_mb if self.cfg.vision else None)
-            R.ppo_loss(out, self.layout.value_col, self.b_act.view(T * N, 8), self.b_logp.view(-1),
-                       self.adv.view(-1), self.ret.view(-1), idx, self.mom_mb[m], self.heads, self.net.p("log_std"),
-                       self.coef, float(mb * self.world), self.ws_upd.dout, self.net.g("log_std"), self.loss_stats)
-            G.to_bf16(self.ws_upd.dout, self.ws_upd.dout16)
-            backward_gpu(self.net, self.ws_upd, self.scal_mb)
-            if self.comm is not None:
-                self.comm.step(self.net, self.opt)          # fused all-reduce + clip + Adam
-            else:
-                self.opt.step()
+        idx = self.perm[m * mb:(m + 1) * mb]
+        if self.stacker is not None:
+            self.stacker.gather(self.b_img, idx, self.b_age[:T].view(-1), self.img_mb)
+        elif self.cfg.vision:
+            G.gather_rows(f_img, idx, self.img_mb)
+        G.gather_rows(f_scal, idx, self.scal_mb)
+        out = forward_gpu(self.net, self.ws_upd, self.scal_mb, self.img_mb if self.cfg.vision else None)
+        R.ppo_loss(out, self.layout.value_col, self.b_act.view(T * N, 8), self.b_logp.view(-1),
+                   self.adv.view(-1), self.ret.view(-1), idx, self.mom_mb[m], self.heads, self.net.p("log_std"),
+                   self.coef, float(mb * self.world), self.ws_upd.dout, self.net.g("log_std"), self.loss_stats)
+        G.to_bf16(self.ws_upd.dout, self.ws_upd.dout16)
+        backward_gpu(self.net, self.ws_upd, self.scal_mb)
+        if self.comm is not None:
+            self.comm.step(self.net, self.opt)          # fused all-reduce + clip + Adam
+        else:
+            self.opt.step()
+
+    def _epoch_body(self) -> None:
+        self._epoch_prologue()
+        for m in range(self.cfg.minibatches):
+            self._minibatch(m)
+
+    def _snapshot(self):
+        return (self.net.flat.clone(), self.opt.m.clone(), self.opt.v.clone(), self.opt.hyper.clone())
+
+    def _restore(self, snap) -> None:
+        """Undo a warm-up step so the first real update starts from the same weights."""
+        self.net.flat.copy_(snap[0]); self.opt.m.copy_(snap[1]); self.opt.v.copy_(snap[2])
+        self.opt.hyper.copy_(snap[3]); self.net.sync_bf16(); self.net.grad.zero_()
+        self.loss_stats.zero_()
+
+    def _pool_minibatches(self) -> int:
+        """Build this iteration's sample pool and return the minibatches per
+        epoch: floor(pool / mb), the same on every rank (reference: the pool
+        trimmed to a multiple of the minibatch, python/train_fast.py:2162-2186)."""
+        cfg = self.cfg
+        offset = (self.iteration - 1) % cfg.train_stride          # rotates so no phase goes unseen
+        R.train_pool(self.b_ez if self.ez is not None else None, self.T, self.N, cfg.train_stride, offset,
+                     self.pool, self.pool_count)
+        nmb = int(self.pool_count.item()) // self.mb                # one host read per iteration
+        if self.comm is not None:
+            nmb = -int(self.comm.max_scalar(-nmb))                  # every rank steps the optimizer alike
+        return min(nmb, cfg.minibatches)
+
+    def _update_pooled_gpu(self) -> None:
+        from ..ops import _lib
+        cfg = self.cfg
+        nmb = self._pool_minibatches()
+        self.last_minibatches = nmb
+        if not cfg.graphs:
+            for _ in range(cfg.epochs):
+                self._epoch_prologue()
+                for m in range(nmb):
+                    self._minibatch(m)
+            return
+        if not self.mb_graphs:
+            # one graph for the prologue and one per minibatch position: the
+            # number replayed follows the pool size of the iteration
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            snap = self._snapshot()
+            with torch.cuda.stream(s):
+                self._epoch_prologue()
+                self._minibatch(0)                              # warm-up outside capture
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            self._restore(snap)
+            self.pro_graph = torch.cuda.CUDAGraph()
+            c0 = _lib.launch_count()
+            with torch.cuda.graph(self.pro_graph, stream=s):
+                self._epoch_prologue()
+            self.pro_launches = _lib.launch_count() - c0
+            self.mb_launches = []
+            for m in range(cfg.minibatches):
+                g = torch.cuda.CUDAGraph()
+                c0 = _lib.launch_count()
+                with torch.cuda.graph(g, stream=s):
+                    self._minibatch(m)
+                self.mb_launches.append(_lib.launch_count() - c0)
+                self.mb_graphs.append(g)
+            torch.cuda.synchronize()
+            self._log(f"captured the pooled update graphs (prologue + {cfg.minibatches} minibatches)")
+        for _ in range(cfg.epochs):
+            self.pro_graph.replay()
+            _lib.add_launches(self.pro_launches)
+            for m in range(nmb):
+                self.mb_graphs[m].replay()
+                _lib.add_launches(self.mb_launches[m])
 
     def update_gpu(self) -> None:
         from ..ops import _lib
@@ -635,19 +750,19 @@ class Trainer:
         R.gae(self.b_rew, self.b_val, self.b_done, self.last_val, cfg.gamma ** self.K, cfg.gae, self.adv, self.ret,
               self.moments)
         self.loss_stats.zero_()
+        if self.pooled:
+            self._update_pooled_gpu()
+            return
         if cfg.graphs:
             if self.upd_graph is None:
                 s = torch.cuda.Stream()
                 s.wait_stream(torch.cuda.current_stream())
-                snap = (self.net.flat.clone(), self.opt.m.clone(), self.opt.v.clone(), self.opt.hyper.clone())
+                snap = self._snapshot()
                 with torch.cuda.stream(s):
                     self._epoch_body()                         # warm-up outside capture
                 torch.cuda.current_stream().wait_stream(s)
                 torch.cuda.synchronize()
-                # undo the warm-up step so the first real update starts from the same weights
-                self.net.flat.copy_(snap[0]); self.opt.m.copy_(snap[1]); self.opt.v.copy_(snap[2])
-                self.opt.hyper.copy_(snap[3]); self.net.sync_bf16(); self.net.grad.zero_()
-                self.loss_stats.zero_()
+                self._restore(snap)
                 self.upd_graph = torch.cuda.CUDAGraph()
                 c0 = _lib.launch_count()
                 with torch.cuda.graph(self.upd_graph, stream=s):
@@ -667,6 +782,8 @@ class Trainer:
         h = self.hrec.numpy()
         feats = np.zeros((self.N, 16), np.float32)
         feats[:, :len(self.feat_idx)] = h[:, [C_OBS + i for i in self.feat_idx]]
+        if self.rew_col >= 0:
+            feats[:, self.rew_col] = np.tanh(self.b_rew[(t - 1) % self.T].numpy() / 0.1)
         self.b_scal[t].copy_(torch.from_numpy(feats))
         if self.cfg.vision:
             raise RuntimeError("the vision policy needs a CUDA device (the depth camera is a GPU kernel)")
@@ -679,6 +796,8 @@ class Trainer:
             with torch.no_grad():
                 out = self.net.forward_reference(self.b_scal[t], None)
                 act, logp = R.sample_reference(out, self.layout, self.net.p("log_std"), gen)
+            if self.ez is not None:
+                self.b_ez[t].copy_(self.ez.apply_reference(act, self.layout, gen))
             stall = getattr(self, "_stall", None)
             if stall is not None:
                 act[:, 7] = torch.from_numpy(stall.astype(np.int32))
@@ -694,6 +813,8 @@ class Trainer:
             if len(trunc):
                 feats = np.zeros((len(trunc), 16), np.float32)
                 feats[:, :len(self.feat_idx)] = h[trunc][:, [C_TOBS + i for i in self.feat_idx]]
+                if self.rew_col >= 0:
+                    feats[:, self.rew_col] = 0.0
                 with torch.no_grad():
                     v = self.net.forward_reference(torch.from_numpy(feats), None)[:, self.layout.value_col]
                 boot = np.zeros(self.N, np.float32)
@@ -718,9 +839,18 @@ class Trainer:
         ent = cfg.ent if cfg.ent_final is None else cfg.ent + (cfg.ent_final - cfg.ent) * frac
         stats = np.zeros(4)
         gen = torch.Generator().manual_seed(self.cfg.seed * 7919 + self.rank * 104729 + self.iteration)
+        pool, nmb = None, cfg.minibatches
+        if self.pooled:
+            offset = (self.iteration - 1) % cfg.train_stride
+            pool = R.train_pool_reference(self.b_ez if self.ez is not None else None, T, N, cfg.train_stride, offset)
+            nmb = len(pool) // mb
+            if self.comm is not None:
+                nmb = -int(self.comm.max_scalar(-nmb))
+            nmb = min(nmb, cfg.minibatches)
+        self.last_minibatches = nmb
         for _ in range(cfg.epochs):
-            perm = torch.randperm(T * N, generator=gen)
-            for m in range(cfg.minibatches):
+            perm = torch.randperm(T * N, generator=gen) if pool is None else pool[torch.randperm(len(pool), generator=gen)]
+            for m in range(nmb):
                 idx = perm[m * mb:(m + 1) * mb]
                 a = self.adv.view(-1)[idx]
                 moments = None
@@ -741,7 +871,8 @@ class Trainer:
                 else:
                     self.opt.step_reference()
                 stats += [pg.item(), vl.item(), en.item(), 1.0]
-        return {"policy_loss": stats[0] / stats[3], "value_loss": stats[1] / stats[3], "entropy": stats[2] / stats[3]}
+        n = max(stats[3], 1.0)
+        return {"policy_loss": stats[0] / n, "value_loss": stats[1] / n, "entropy": stats[2] / n}
 
     # ---- iteration ------------------------------------------------------------------------------
     def _check_replicas(self) -> None:
@@ -813,6 +944,9 @@ class Trainer:
             self.rew_graphs = []
             self.env_graphs = []
             self.upd_graph = None
+            self.pro_graph = None
+            if self.pooled:
+                self.mb_graphs = []
             import gc
             gc.collect()
             torch.cuda.synchronize()

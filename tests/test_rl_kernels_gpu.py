@@ -256,3 +256,71 @@ def test_adam_matches_torch(grad_scale):
     torch.testing.assert_close(opt.v, ref_opt.v, rtol=1e-4, atol=1e-12)
     torch.testing.assert_close(net.flat16.float(), net.flat.to(torch.bfloat16).float())
     assert opt.steps == 5
+
+
+# ---- training pool and ez-greedy bursts -------------------------------------------------------
+def test_train_pool_matches_reference():
+    T, n = 128, 2048
+    ez = (torch.rand(T, n, device=DEV) < 0.07).to(torch.uint8)
+    pool = torch.full((T * n,), -1, dtype=torch.int64, device=DEV)
+    count = torch.zeros(1, dtype=torch.int64, device=DEV)
+    for stride, offset, flags in ((1, 0, None), (3, 2, ez), (1, 0, ez), (4, 1, None)):
+        R.train_pool(flags, T, n, stride, offset, pool, count)
+        ref = R.train_pool_reference(flags, T, n, stride, offset)
+        k = int(count)
+        assert k == len(ref) and torch.equal(pool[:k].cpu(), ref)
+
+
+def test_permutation_pool_is_a_bijection_of_the_pool():
+    n_max = 262144
+    pool = torch.randperm(n_max, device=DEV)[:100003].sort().values
+    pool_full = torch.zeros(n_max, dtype=torch.int64, device=DEV)
+    pool_full[:pool.numel()] = pool
+    count = torch.tensor([pool.numel()], dtype=torch.int64, device=DEV)
+    key = torch.tensor([99], dtype=torch.int64, device=DEV)
+    out = torch.full((n_max,), -7, dtype=torch.int64, device=DEV)
+    R.permutation_pool(out, pool_full, count, key)
+    k = pool.numel()
+    assert torch.equal(out[:k].sort().values, pool)
+    assert torch.all(out[k:] == -7)                                 # nothing written past the count
+    first = out[:k].clone()
+    R.permutation_pool(out, pool_full, count, key)
+    assert not torch.equal(out[:k], first)                          # the key advanced
+
+
+def test_sampling_kernel_ez_bursts():
+    """Burst rule in the sampling kernel: a running burst repeats its row, new
+    bursts start only in envs without one, lengths follow floor(u^-1/(mu-1))
+    clamped to [1, max]; rows without a burst are the plain samples."""
+    layout = LAYOUTS[0]
+    n = 65536
+    heads = R.HeadArgs(layout, DEV)
+    logits = _logits(n, layout, 21)
+    log_std = torch.zeros(1, device=DEV)
+    ez = R.EzGreedy(n, eps=0.05, mu=2.0, max_len=9, device=DEV)
+    plain = torch.zeros(n, 8, dtype=torch.int32, device=DEV)
+    act = torch.zeros(n, 8, dtype=torch.int32, device=DEV)
+    flag = torch.zeros(n, dtype=torch.uint8, device=DEV)
+    prev = None
+    lens, starts = [], 0
+    for c in range(40):
+        before = ez.left.clone()
+        R.sample_heads(logits, heads, log_std, plain, None, seed=3, counter=c)
+        R.sample_heads(logits, heads, log_std, act, None, seed=3, counter=c, ez=ez.args(0, n, flag))
+        f = flag.bool()
+        cont = before > 0
+        assert torch.all(f[cont])
+        assert torch.equal(act[~f], plain[~f])
+        if prev is not None:
+            assert torch.equal(act[cont, :6], prev[cont, :6])
+        for size, slot in zip(layout.sizes, layout.slots):
+            col = act[f, slot]
+            assert int(col.min()) >= 0 and int(col.max()) < size
+        fresh = f & ~cont
+        lens.append(ez.left[fresh] + 1)
+        starts += int(fresh.sum())
+        prev = act.clone()
+    lens = torch.cat(lens).float()
+    assert float(lens.min()) >= 1 and float(lens.max()) <= 9
+    assert abs(float((lens == 1).float().mean()) - 0.5) < 0.03
+    assert starts > 0.03 * 40 * n * 0.7

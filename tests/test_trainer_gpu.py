@@ -86,3 +86,30 @@ def test_gpu_env_training_iterations():
     st = tr.genv.get_states()
     assert (st["tick"] > 0).all() and np.isfinite(st["origin"]).all()
     tr.release_graphs()
+
+
+@pytest.mark.parametrize("graphs", [True, False])
+def test_pooled_update_stride_and_ez(graphs):
+    """Train stride + ez-greedy on the GPU path: the pool kernel leaves burst
+    rows and off-stride decisions out, the number of minibatches follows the
+    pool, and the graphed and eager updates both train."""
+    from surfb200.ops import rl as R
+    cfg = TrainConfig(map="field", envs=256, n_steps=16, act_every=3, epochs=2, minibatches=4, ep_ticks=60,
+                      graphs=graphs, train_stride=2, ez_eps=0.05, ez_max=8, fix_pitch=-10.0,
+                      reward=RewardSpec(mode="coverage"))
+    tr = Trainer(cfg, verbose=False)
+    flat0 = tr.net.flat.clone()
+    for it in range(3):
+        s = tr.train_iteration()
+        assert math.isfinite(s["policy_loss"])
+        n = int(tr.pool_count)
+        ref = R.train_pool_reference(tr.b_ez, tr.T, tr.N, 2, it % 2)
+        assert n == len(ref) and torch.equal(tr.pool[:n].cpu(), ref)
+        assert tr.last_minibatches == n // tr.mb
+    assert int(tr.b_ez.sum()) > 0
+    assert not torch.equal(flat0, tr.net.flat)
+    # burst actions are written into the action rows the env received
+    flags = tr.b_ez.bool()
+    assert torch.all(tr.b_act[flags][:, 0] < 15)
+    assert np.all(tr.core.states_view["pitch"] == np.float32(-10.0))        # fixed gaze held
+    tr.release_graphs()
