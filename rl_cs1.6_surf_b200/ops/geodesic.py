@@ -111,8 +111,65 @@ def geodesic_cpu(occ: np.ndarray, cell: float, lo, hi) -> np.ndarray:
     return out
 
 
-def bake_goal_field(core, zone, cell: float = 16.0, device="cuda", mins=None, dims=None) -> GoalFieldData:
-    """Occupancy + geodesic + uint16 quantisation (GPU kernels; native host code on CPU)."""
+def kill_voxel_mask(core, mins, cell: float, dims):
+    """[(z0, y0, x0, mask bool [dz, dy, dx])] of the voxel centres that lie
+    inside a kill volume (a teleport with a destination, or a hurt trigger of
+    at least 90 damage: the map's fail nets). Each trigger's AABB (grown by
+    1u) is only the broad phase; the centres are classified through the
+    trigger's own hull-1 clip tree, the simulator's kill test, because kill
+    triggers are often thin curtains inside large boxes (reference
+    --race-kill-aware, python/surfgym/goalfield.py:159-219)."""
+    nx, ny, nz = dims
+    mins = np.asarray(mins, np.float64)
+    out = []
+    for i, trg in enumerate(core.triggers()):
+        kill = (trg["kind"] == "teleport" and trg["has_dest"]) or (trg["kind"] == "hurt" and trg["damage"] >= 90.0)
+        if not kill:
+            continue
+        bmn = np.asarray(trg["mins"], np.float64) - 1.0
+        bmx = np.asarray(trg["maxs"], np.float64) + 1.0
+        lo = np.maximum(np.floor((bmn - mins) / cell - 0.5), 0).astype(int)
+        hi = np.minimum(np.ceil((bmx - mins) / cell - 0.5) + 1, [nx, ny, nz]).astype(int)
+        if (hi <= lo).any():
+            continue
+        axes = [mins[a] + (np.arange(lo[a], hi[a]) + 0.5) * cell for a in range(3)]
+        zz, yy, xx = np.meshgrid(axes[2], axes[1], axes[0], indexing="ij")
+        pts = np.stack([xx.ravel(), yy.ravel(), zz.ravel()], 1)
+        inside = core.trigger_contains(i, pts, usehull=1).reshape(zz.shape)
+        if inside.any():
+            out.append((int(lo[2]), int(lo[1]), int(lo[0]), inside))
+    return out
+
+
+def euclid_goal_field(zone, mins, cell: float, dims, device="cpu") -> GoalFieldData:
+    """Straight-line distance from every voxel centre to the goal AABB, in the
+    goal field's uint16 format (reference EuclidField / --race-dist euclid,
+    python/surfgym/goalfield.py:110-138): no geometry, no bake, every voxel
+    valid; a wall between agent and goal is invisible to this potential."""
+    nx, ny, nz = dims
+    dev = torch.device(device)
+    lo_b = torch.as_tensor(np.asarray(zone["mins"], np.float64), device=dev)
+    hi_b = torch.as_tensor(np.asarray(zone["maxs"], np.float64), device=dev)
+    m = torch.as_tensor(np.asarray(mins, np.float64), device=dev)
+    ax = [m[a] + (torch.arange(n, device=dev, dtype=torch.float64) + 0.5) * cell for a, n in enumerate((nx, ny, nz))]
+    dx = (ax[0] - ax[0].clamp(lo_b[0], hi_b[0])).view(1, 1, nx)
+    dy = (ax[1] - ax[1].clamp(lo_b[1], hi_b[1])).view(1, ny, 1)
+    dz = (ax[2] - ax[2].clamp(lo_b[2], hi_b[2])).view(nz, 1, 1)
+    dist = torch.sqrt(dx * dx + dy * dy + dz * dz).float()
+    reach_max = float(dist.max())
+    quant = cell / 8.0
+    while (reach_max + 2.0 * cell) / quant > 65535:       # stay inside uint16 on very large maps
+        quant *= 2.0
+    grid = torch.round(dist / quant).clamp(0, 65535).to(torch.int32).cpu().numpy().astype(np.uint16)
+    return GoalFieldData(grid, np.asarray(mins, np.float64), float(cell), float(quant), reach_max)
+
+
+def bake_goal_field(core, zone, cell: float = 16.0, device="cuda", mins=None, dims=None,
+                    kill_aware: bool = False) -> GoalFieldData:
+    """Occupancy + geodesic + uint16 quantisation (GPU kernels; native host
+    code on CPU). ``kill_aware``: kill volumes are walls of the goal graph
+    only (``kill_voxel_mask``), so the shaping routes around fail nets;
+    physics and vision are unchanged."""
     from .vision import grid_dims, occupancy, occupancy_reference
     if mins is None or dims is None:
         mn, mx = core.map_bounds()
@@ -120,8 +177,12 @@ def bake_goal_field(core, zone, cell: float = 16.0, device="cuda", mins=None, di
         dims = (nx, ny, nz)
     lo, hi = seed_box(zone, mins, cell, dims)
     dev = torch.device(device)
+    kills = kill_voxel_mask(core, mins, cell, dims) if kill_aware else []
     if dev.type == "cuda":
         occ = occupancy(core, mins, cell, dims, slab=True, device=dev)
+        for z0, y0, x0, m in kills:
+            sub = occ[z0:z0 + m.shape[0], y0:y0 + m.shape[1], x0:x0 + m.shape[2]]
+            sub |= torch.as_tensor(m.astype(np.uint8), device=dev)
         dist = geodesic(occ, cell, lo, hi)
         L = _lib.lib(VLIB)
         mx_bits = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -139,6 +200,8 @@ def bake_goal_field(core, zone, cell: float = 16.0, device="cuda", mins=None, di
         grid = q.cpu().numpy().view(np.uint16)
     else:
         occ = occupancy_reference(core, mins, cell, dims, slab=True)
+        for z0, y0, x0, m in kills:
+            occ[z0:z0 + m.shape[0], y0:y0 + m.shape[1], x0:x0 + m.shape[2]] |= m.astype(np.uint8)
         dist = geodesic_cpu(occ, cell, lo, hi)
         fin = dist < 1e30
         reach_max = float(dist[fin].max())

@@ -22,6 +22,7 @@ RUN_DEFINING = (
     "respawn_frac", "respawn_margin", "respawn_reservoir", "train_stride", "drop_frac", "drop_min", "drop_max",
     "punch_min", "punch_max", "respawn_speed", "respawn_binned", "respawn_pool", "rnd_coef",
     "ez_eps", "ez_mu", "ez_max", "fix_pitch", "reward_per_decision", "obs_reward", "eval_greedy_only",
+    "race_dist", "race_kill_aware",
 )
 
 
@@ -93,6 +94,11 @@ class TrainConfig:
     # terms telescope exactly; stall / finish bookkeeping has decision
     # granularity); the per-tick evaluation is not provided
     reward_per_decision: bool = True
+    # race shaping distance: geodesic (baked through the free voxels) or euclid
+    # (straight line to the finish box, no bake); kill-aware: fail nets are
+    # walls of the geodesic goal graph
+    race_dist: str = "geodesic"
+    race_kill_aware: bool = False
     # the previous decision's reward, tanh(r / 0.1), as an extra observation
     # scalar (the heading slot 12 that the no-GPS policy hides); race only
     obs_reward: bool = False
@@ -140,6 +146,10 @@ class TrainConfig:
             raise ValueError("obs_reward needs the race reward (its observation mirrors the geodesic shaping)")
         if self.obs_reward and self.gps:
             raise ValueError("obs_reward uses scalar slot 12, which gps exposes as a position channel")
+        if self.race_dist not in ("geodesic", "euclid"):
+            raise ValueError("race_dist must be geodesic or euclid")
+        if self.race_kill_aware and self.race_dist == "euclid":
+            raise ValueError("race_kill_aware masks the geodesic goal graph; the euclid field has no graph")
         if self.fix_pitch is not None and not -70.0 <= self.fix_pitch <= 30.0:
             raise ValueError("fix_pitch must lie in the view clamp [-70, 30] degrees")
 

@@ -156,11 +156,24 @@ class Trainer:
         self.field = None
         self.d0 = None
         if cfg.reward.mode == "race":
-            from ..ops.geodesic import bake_goal_field
-            self.field = bake_goal_field(self.core, end, cell=max(cfg.lidar_cell, 16.0),
-                                         device=self.device if self.gpu else "cpu")
+            from ..ops.geodesic import bake_goal_field, euclid_goal_field
+            from ..ops.vision import grid_dims
+            gcell = max(cfg.lidar_cell, 16.0)
+            if cfg.race_dist == "euclid":
+                mn, mx = self.core.map_bounds()
+                gmins, gx, gy, gz = grid_dims(mn, mx, gcell)
+                self.field = euclid_goal_field(end, gmins, gcell, (gx, gy, gz), device=self.device)
+            else:
+                self.field = bake_goal_field(self.core, end, cell=gcell, device=self.device if self.gpu else "cpu",
+                                             kill_aware=cfg.race_kill_aware)
             start = pool["origin"] if pool is not None else np.array([s[0] for s in self.core.spawns()])
-            self.d0 = float(np.median(self.field.sample(start)))
+            d_start = self.field.sample(start)
+            ok = d_start < self.field.valid_max
+            if ok.mean() < 0.5:
+                raise RuntimeError("race: most start states cannot reach the finish through the goal graph"
+                                   + (" (kill volumes masked as walls disconnect them)" if cfg.race_kill_aware
+                                      else ""))
+            self.d0 = float(np.median(d_start[ok]))
             self._log(f"goal field: reach_max {self.field.reach_max:.0f}u, start distance {self.d0:.0f}u")
 
     def _setup_net(self) -> None:

@@ -37,3 +37,24 @@ def test_goal_field_bake_gpu_matches_cpu():
     assert diff.max() <= 1
     start = m.spawn_pool["origin"][:64].astype(np.float64)
     assert np.all(np.isfinite(g.sample(start)))
+
+
+def test_kill_aware_goal_field_gpu_matches_cpu():
+    """The race map's fail nets as walls of the goal graph: the GPU bake and
+    the host bake agree, the starts stay connected, and no path through a
+    kill volume shortens the distance."""
+    from surfb200.sim import mapgen
+    from surfb200.sim.core import SimCore, default_config
+    m = mapgen.generate("race", 0)
+    core = SimCore.from_bytes(m.image, default_config(1), threads=4)
+    end = m.zones["end"]
+    g = bake_goal_field(core, end, cell=64.0, device="cuda", kill_aware=True)
+    c = bake_goal_field(core, end, cell=64.0, device="cpu", kill_aware=True)
+    plain = bake_goal_field(core, end, cell=64.0, device="cuda")
+    assert np.abs(g.grid.astype(np.int64) - c.grid.astype(np.int64)).max() <= 1
+    start = m.spawn_pool["origin"][:64].astype(np.float64)
+    d_k, d_p = g.sample(start), plain.sample(start)
+    assert np.all(d_k < g.valid_max)                       # the starts still reach the finish
+    assert np.all(d_k >= d_p - 1.0)                        # walls only lengthen the routes
+    assert int((g.grid == np.uint16(round(g.sentinel / g.quant))).sum()) > \
+        int((plain.grid == np.uint16(round(plain.sentinel / plain.quant))).sum())

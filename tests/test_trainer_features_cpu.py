@@ -123,3 +123,58 @@ def test_cli_flags_round_trip(tmp_path):
     assert r.returncode == 0, r.stderr[-2000:]
     assert "overridden fix_pitch" in r.stdout
     assert C.load(run / "ckpt_final.pt")["config"]["fix_pitch"] is None
+
+
+def _ramps_core():
+    from surfb200.sim import mapgen
+    from surfb200.sim.core import SimCore, default_config
+    m = mapgen.generate("ramps", 0)
+    return SimCore.from_bytes(m.image, default_config(1), threads=2)
+
+
+def test_kill_aware_goal_graph_cpu():
+    """Kill volumes become walls of the goal graph only: masked voxels are
+    unreachable, every masked centre is inside the trigger's hull-1 tree, and
+    paths elsewhere can only get longer."""
+    from surfb200.ops.geodesic import bake_goal_field, kill_voxel_mask
+    from surfb200.ops.vision import grid_dims
+    core = _ramps_core()
+    cell = 64.0
+    mn, mx = core.map_bounds()
+    mins, nx, ny, nz = grid_dims(mn, mx, cell)
+    kills = kill_voxel_mask(core, mins, cell, (nx, ny, nz))
+    assert len(kills) == 1
+    z0, y0, x0, m = kills[0]
+    zi, yi, xi = np.nonzero(m)
+    pts = np.stack([mins[0] + (x0 + xi + 0.5) * cell, mins[1] + (y0 + yi + 0.5) * cell,
+                    mins[2] + (z0 + zi + 0.5) * cell], 1)
+    assert core.trigger_contains(0, pts, usehull=1).all()
+    assert pts[:, 2].max() < 65 + 36 + cell                        # the floor net, grown by the player hull only
+    zone = {"mins": [-200.0, -200.0, 1200.0], "maxs": [200.0, 200.0, 1300.0]}
+    plain = bake_goal_field(core, zone, cell=cell, device="cpu")
+    masked = bake_goal_field(core, zone, cell=cell, device="cpu", kill_aware=True)
+    gp = plain.grid.astype(np.int64)
+    gm = masked.grid.astype(np.int64)
+    killed = np.zeros_like(gp, bool)
+    killed[z0:z0 + m.shape[0], y0:y0 + m.shape[1], x0:x0 + m.shape[2]] = m
+    sent_m = int(round(masked.sentinel / masked.quant))
+    assert np.all(gm[killed] == sent_m)
+    assert (gp[killed] < int(round(plain.sentinel / plain.quant))).sum() > 1000    # reachable in the plain graph
+    both = ~killed & (gp * plain.quant < plain.valid_max) & (gm * masked.quant < masked.valid_max)
+    assert np.all(gm[both] * masked.quant >= gp[both] * plain.quant - 1e-3)
+
+
+def test_euclid_goal_field_cpu():
+    from surfb200.ops.geodesic import euclid_goal_field
+    zone = {"mins": [100.0, -50.0, 0.0], "maxs": [300.0, 50.0, 40.0]}
+    mins, cell, dims = np.array([-1024.0, -1024.0, -512.0]), 16.0, (128, 128, 64)
+    f = euclid_goal_field(zone, mins, cell, dims)
+    rng = np.random.default_rng(0)
+    p = mins + rng.random((2000, 3)) * (np.array(dims) - 1) * cell + 0.5 * cell
+    q = np.clip(p, zone["mins"], zone["maxs"])
+    exact = np.linalg.norm(p - q, axis=1)
+    far = exact > 3 * cell
+    got = f.sample(p)
+    assert np.all(np.abs(got[far] - exact[far]) < 0.06 * cell + f.quant)
+    assert float(got[exact == 0].max(initial=0.0)) < cell
+    assert f.grid.dtype == np.uint16 and f.reach_max > 0
