@@ -34,6 +34,8 @@ def main():
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--json", default=None)
     ap.add_argument("--explicit", action="store_true", help="im2col + GEMM for every convolution (A/B baseline)")
+    ap.add_argument("--no-shift", action="store_true",
+                    help="4-D implicit GEMMs instead of the stacked shifted-grid trunk (A/B baseline)")
     ap.add_argument("--nhw", action="store_true", help="64 x 128 NHW image with the 8x8 stride-4 first layer")
     ap.add_argument("--verify", action="store_true", help="numerics gate: kernels vs float32 autograd, then exit")
     args = ap.parse_args()
@@ -53,6 +55,7 @@ def main():
     net = PolicyNet(ncfg, dev)
     B = args.rows
     net.implicit_conv = not args.explicit
+    net.shift_conv = not (args.no_shift or args.explicit)
     ws = Workspace(net, B)
     opt = R.Adam(net)
     heads = R.HeadArgs(layout, dev)
@@ -96,6 +99,8 @@ def main():
                 N = (Bm.shape[1] if k.get("b_mn") else Bm.shape[0])
                 desc = f"{M}x{N}x{Kd}{' mnA' if k.get('a_mn') else ''}{' mnB' if k.get('b_mn') else ''}"
                 flops = 2.0 * M * N * Kd
+            elif name in TRUNK_FLOPS:
+                flops = float(TRUNK_FLOPS[name]) * B
             else:
                 flops = 0.0
             records.append((name, desc, flops, e0, e1))
@@ -108,6 +113,13 @@ def main():
         wrap(R, n)
     for n in ("conv_forward", "conv_weight_grad", "conv_input_grad", "weight_classes"):
         wrap(CV, n)
+    # the stacked shifted-grid trunk: useful FLOPs per image of each product
+    c1, c2, c3 = 2 * 465 * 32 * 64, 2 * 84 * 64 * 512, 2 * 48 * 64 * 576
+    TRUNK_FLOPS = {"conv1_forward": c1, "conv2_forward": c2, "conv3_forward": c3, "conv3_input_grad": c3,
+                   "conv2_input_grad": c2, "conv3_weight_grad": c3, "conv2_weight_grad": c2, "conv1_weight_grad": c1}
+    if net.uses_shift_trunk():
+        for n in ("refresh", *TRUNK_FLOPS):
+            wrap(net.trunk, n)
 
 
     def step():

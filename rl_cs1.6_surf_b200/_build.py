@@ -62,7 +62,7 @@ def _targets():
     groups = {
         "libsurf_vision.so": kern("march.cu", "sdf.cu", "geodesic.cu"),
         "libsurf_rl.so": kern("rl.cu", "reward.cu"),
-        "libsurf_nn.so": kern("gemm_tc.cu", "nn_ops.cu", "adam.cu"),
+        "libsurf_nn.so": kern("gemm_tc.cu", "conv_shift.cu", "nn_ops.cu", "adam.cu"),
         "libsurf_comm.so": comm("p2p.cu"),
     }
     for name, srcs in groups.items():

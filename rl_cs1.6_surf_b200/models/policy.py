@@ -184,6 +184,10 @@ class PolicyNet:
         self.grad = torch.zeros(off, dtype=torch.float32, device=self.device)
         self.flat16 = torch.zeros(off, dtype=torch.bfloat16, device=self.device) if self.device.type == "cuda" else None
         self.implicit_conv = True           # implicit-GEMM convolutions where supported (else im2col + GEMM)
+        # the flagship trunk's stacked shifted-grid kernels (ops/conv_shift.py)
+        # where the geometry is theirs; else the 4-D implicit GEMMs above
+        self.shift_conv = True
+        self._trunk = None
         self.init_weights(seed)
 
     # ---- parameter views ------------------------------------------------------------
@@ -230,6 +234,18 @@ class PolicyNet:
             v.copy_(full.to(self.device))
         self.p("log_std").fill_(0.0)
         self.sync_bf16()
+
+    def uses_shift_trunk(self) -> bool:
+        from ..ops.conv_shift import Trunk
+        return self.device.type == "cuda" and self.shift_conv and Trunk.supported(self.cfg)
+
+    @property
+    def trunk(self):
+        """the stacked shifted-grid trunk over this network's bf16 weights (built on first use)"""
+        if self._trunk is None:
+            from ..ops.conv_shift import Trunk
+            self._trunk = Trunk(self.device, [self.offsets[f"conv{i}.w"][0] for i in (1, 2, 3)])
+        return self._trunk
 
     def sync_bf16(self) -> None:
         if self.flat16 is not None:
@@ -293,7 +309,21 @@ class Workspace:
         self.col, self.y, self.dcol, self.dy, self.wt = [], [], [], [], []
         self.implicit = [False] * len(cfg.conv)
         self.img = None                         # conv1 input of the last forward (implicit weight gradient)
-        if cfg.vision:
+        self.shift = cfg.vision and net.uses_shift_trunk()
+        if self.shift:
+            # padded-grid layouts of the shifted trunk (ops/conv_shift.py): the
+            # grids' padding rows are zeros that the kernels never write (dy3)
+            # or write as zeros (y2, dy2)
+            self.sy1 = torch.empty(batch * 512, 32, dtype=bf, device=dev)
+            self.sy2 = torch.zeros(batch * 128, 64, dtype=bf, device=dev)
+            self.y3 = torch.empty(batch * 48, 64, dtype=bf, device=dev)
+            self.dy3 = torch.zeros(batch * 128, 64, dtype=bf, device=dev)
+            self.dy2 = torch.zeros(batch * 128, 64, dtype=bf, device=dev)
+            self.dy1 = torch.empty(batch * 512, 32, dtype=bf, device=dev)
+            self.h0 = torch.empty(batch, cfg.fc + cfg.proprio, dtype=bf, device=dev)
+            self.dh0 = torch.empty_like(self.h0)
+            self.h = [torch.empty(batch, cfg.hidden, dtype=bf, device=dev)]
+        elif cfg.vision:
             from ..ops.conv import SLACK_BYTES, ConvShape
             shapes = cfg.conv_shapes()
             for i, g in enumerate(shapes):
@@ -350,7 +380,19 @@ def forward_gpu(net: "PolicyNet", ws: Workspace, scal16: torch.Tensor, img16: Op
     cfg = net.cfg
     B = ws.B if B is None else B
     w = net.w16
-    if cfg.vision:
+    if cfg.vision and ws.shift:
+        T = net.trunk
+        T.refresh(net.flat16)                   # stacked weight operands of the current parameters
+        img = img16[:B].reshape(B * 512, 16)
+        ws.img = img
+        T.conv1_forward(img, net.p("conv1.b"), ws.sy1, B)
+        T.conv2_forward(ws.sy1, net.p("conv2.b"), ws.sy2, B)
+        T.conv3_forward(ws.sy2, net.p("conv3.b"), ws.y3, B)
+        feat = ws.y3[:B * 48].view(B, cfg.flat_conv)
+        G.gemm(feat, w("fc.w"), out=ws.h0[:B, :cfg.fc], bias=net.p("fc.b"), act="relu")
+        G.gemm(scal16[:B], w("proprio.w"), out=ws.h0[:B, cfg.fc:], bias=net.p("proprio.b"), act="tanh")
+        G.gemm(ws.h0[:B], w("hidden.w"), out=ws.h[0][:B], bias=net.p("hidden.b"), act="tanh")
+    elif cfg.vision:
         from ..ops import conv as CV
         x = img16
         for i, g in enumerate(cfg.conv_shapes()):
@@ -399,6 +441,26 @@ def backward_gpu(net: "PolicyNet", ws: Workspace, scal16: torch.Tensor, B: Optio
         _wgrad(G, dp, scal16[:B], net.g("proprio.w"), B)
         G.colsum(dp, net.g("proprio.b"))
         df = ws.dh0[:B, :cfg.fc]
+        if ws.shift:
+            T = net.trunk
+            feat = ws.y3[:B * 48].view(B, cfg.flat_conv)
+            _wgrad(G, df, feat, net.g("fc.w"), B)
+            G.colsum(df, net.g("fc.b"))
+            # conv3's output gradient lands on its 8 x 16 input grid (row h*12 + w of the
+            # dense feature -> h*16 + w), the padding staying zero
+            dy3 = ws.dy3[:B * 128]
+            G.gemm(df, w("fc.w"), b_mn=True, out=dy3.view(B, 8192), act="relu_grad", aux=feat, cmap=(768, 1024))
+            T.conv3_weight_grad(dy3, ws.sy2, net.g("conv3.w"), B)
+            G.colsum(dy3, net.g("conv3.b"))
+            T.conv3_input_grad(dy3, ws.sy2, ws.dy2, B)
+            dy2 = ws.dy2[:B * 128]
+            T.conv2_weight_grad(dy2, ws.sy1, net.g("conv2.w"), B)
+            G.colsum(dy2, net.g("conv2.b"))
+            T.conv2_input_grad(dy2, ws.sy1, ws.dy1, B)
+            dy1 = ws.dy1[:B * 512]
+            T.conv1_weight_grad(dy1, ws.img, net.g("conv1.w"), B)
+            G.colsum(dy1, net.g("conv1.b"))
+            return
         shapes = cfg.conv_shapes()
         last_rows = B * shapes[-1]["OH"] * shapes[-1]["OW"]
         feat = ws.y[-1][:last_rows].view(B, cfg.flat_conv)

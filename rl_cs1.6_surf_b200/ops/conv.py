@@ -76,7 +76,9 @@ SLACK_BYTES = 128          # allocate activations with this much room after the 
 # Kernel diagnostics for timing studies only (Epilogue.dbg): bit 0 skips the
 # epilogue's stores, bit 1 skips the MMAs (results are wrong with either);
 # bit 2 streams a resident-able weight operand per k-block, bit 3 turns off the
-# saved-activation prefetch of the derivative epilogues (results unchanged).
+# saved-activation prefetch of the derivative epilogues (results unchanged);
+# shifted-grid kernels only: bit 4 reads every forward K step's A operand at
+# the stage start, bit 5 skips the whole epilogue.
 DEBUG = 0
 TRACE = None               # a uint64 CUDA tensor of 5 * 256 stamps: CTA 0's pipeline timeline (diagnostics)
 # 16-channel inputs: two-position windows (kernel mode 4) when True, one

@@ -31,7 +31,7 @@ class Epilogue(ctypes.Structure):
     _fields_ = [("c", c_void_p), ("ldc", c_int64), ("c_dtype", c_int), ("c_mode", c_int), ("ct", c_void_p),
                 ("ldct", c_int64), ("ct_dtype", c_int), ("bias", c_void_p), ("act", c_int), ("act2", c_int),
                 ("act_split", c_int), ("aux", c_void_p), ("ld_aux", c_int64), ("err", c_void_p), ("dbg", c_int),
-                ("trace", c_void_p)]
+                ("trace", c_void_p), ("cmap_in", c_int), ("cmap_out", c_int)]
 TRACE_N = 256              # stamps per kind in an Epilogue.trace buffer (kTraceN in gemm_tc.cu)
 
 
@@ -92,13 +92,15 @@ def gemm(A: torch.Tensor, B: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
          out_t: Optional[torch.Tensor] = None, bias: Optional[torch.Tensor] = None, act: str = "none",
          act2: Optional[str] = None, act_split: Optional[int] = None, aux: Optional[torch.Tensor] = None,
          splits: int = 1, bn: Optional[int] = None, M: Optional[int] = None, N: Optional[int] = None,
-         K: Optional[int] = None, debug: int = 0) -> Optional[torch.Tensor]:
+         K: Optional[int] = None, debug: int = 0, cmap: Optional[tuple] = None) -> Optional[torch.Tensor]:
     """D = A @ B^T (bf16 operands, fp32 accumulation) with a fused epilogue:
     ``+ bias``, activation (``relu``/``tanh``) or activation derivative
     (``relu_grad``/``tanh_grad`` against ``aux``, the saved activation), and
     stores to ``out`` (fp32/bf16, any row stride), ``out_t`` (transposed) or
     fp32 atomic accumulation (``accumulate=True``; required for ``splits>1``).
-    ``act2``/``act_split`` switch the activation at a column boundary."""
+    ``act2``/``act_split`` switch the activation at a column boundary.
+    ``cmap = (n_in, n_out)`` stores column n of ``out`` at (n // n_in) * n_out
+    + n % n_in (a dense row onto a zero-padded grid; bias and aux stay dense)."""
     if A.dtype != torch.bfloat16 or B.dtype != torch.bfloat16:
         raise TypeError("gemm operands must be bfloat16")
     _lib.require_cuda(A, "gemm")
@@ -137,6 +139,8 @@ def gemm(A: torch.Tensor, B: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
         raise ValueError("activation-derivative epilogues need aux")
     ep.err = ptr(error_flag(A.device))
     ep.dbg = int(debug)
+    if cmap is not None:
+        ep.cmap_in, ep.cmap_out = int(cmap[0]), int(cmap[1])
     lda, ldb = A.stride(0), B.stride(0)
     check(_lib.lib(NLIB).surf_gemm_bf16(ptr(A), lda, int(a_mn), ptr(B), ldb, int(b_mn), int(M), int(N), int(K),
                                         ctypes.byref(ep), int(bn or _pick_bn(N, b_mn)), int(splits),

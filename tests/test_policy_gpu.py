@@ -8,7 +8,8 @@ float32 autograd over identical (bf16-rounded) parameters and inputs.
 import pytest
 import torch
 
-from surfb200.models.policy import HeadLayout, NetConfig, PolicyNet, Workspace, backward_gpu, forward_gpu
+from surfb200.models.policy import (HeadLayout, NetConfig, PolicyNet, Workspace, backward_gpu, forward_gpu,
+                                    space_to_depth_config)
 
 pytestmark = pytest.mark.gpu
 
@@ -17,11 +18,19 @@ def rel(a, b):
     return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
 
 
-@pytest.mark.parametrize("vision,cont", [(True, False), (True, True), (False, True)])
-def test_forward_backward_match_autograd(vision, cont):
+@pytest.mark.parametrize("vision,cont,s2d,shift", [(True, False, False, True), (True, True, False, True),
+                                                    (False, True, False, True), (True, False, True, True),
+                                                    (True, True, True, False)])
+def test_forward_backward_match_autograd(vision, cont, s2d, shift):
+    """s2d: the flagship space-to-depth geometry, whose trunk runs on the
+    stacked shifted-grid kernels (shift) or on the 4-D implicit GEMMs."""
     torch.manual_seed(0)
     cfg = NetConfig(vision=vision, heads=HeadLayout(continuous_yaw=cont))
+    if s2d:
+        cfg = space_to_depth_config(cfg)
     net = PolicyNet(cfg, "cuda", seed=1)
+    net.shift_conv = shift
+    assert net.uses_shift_trunk() == (s2d and shift)
     # round master weights to bf16 so both paths see identical parameters
     net.flat.copy_(net.flat.to(torch.bfloat16).float())
     net.sync_bf16()
@@ -29,7 +38,8 @@ def test_forward_backward_match_autograd(vision, cont):
     scal = torch.zeros(B, cfg.scalar_pad, device="cuda")
     scal[:, :cfg.n_scalar] = torch.randn(B, cfg.n_scalar, device="cuda")
     scal16 = scal.to(torch.bfloat16)
-    img16 = torch.rand(B, cfg.img_h * cfg.img_w, device="cuda").to(torch.bfloat16) if vision else None
+    img16 = (torch.rand(B, cfg.img_h * cfg.img_w * cfg.img_c, device="cuda").to(torch.bfloat16)
+             if vision else None)
     ws = Workspace(net, B)
     out = forward_gpu(net, ws, scal16, img16).clone()
     params = net.autograd_params()
