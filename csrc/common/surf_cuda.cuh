@@ -1,5 +1,6 @@
 // surf_cuda.cuh — shared helpers for the framework's CUDA libraries.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -30,6 +31,13 @@ __device__ __forceinline__ uint16_t f32_to_bf16(float f) {
   if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x7fffffu)) return static_cast<uint16_t>((u >> 16) | 0x40);
   u += 0x7fffu + ((u >> 16) & 1u);
   return static_cast<uint16_t>(u >> 16);
+}
+
+// Two floats -> packed bf16 pair (lo in the low half), round to nearest even:
+// one hardware conversion instead of two integer sequences.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
 }
 
 // Bricked voxel addressing: 4x4x4 bricks of 64 elements, brick-major.

@@ -98,6 +98,10 @@ struct ShArgs {
   int a_off, a_krow;   // WGRAD: stage byte offset of A, bytes per k-row
   int subw, b_krow;    // WGRAD: N of one MMA group, bytes per k-row of B
   int b_noff[kShMaxSub];     // WGRAD: stage byte offset of MMA group g (global index n / subw)
+  int kgrid, kmask;    // WGRAD: K step ks of a unit covers grid row h = (A-box row / 16 + ks) mod kgrid;
+                       //   only the rows in kmask are issued (the others' output gradient is zero)
+  int bias_rows;       // WGRAD: > 0: also sum the first bias_rows rows of every unit's A box (128-byte rows)
+  int bias_mod;        //   into the bias gradient (Epilogue.ct, fp32): column c adds to channel c % bias_mod
   int erow[4];         // WGRAD: destination row of accumulator row m = (m & 31) + erow[m >> 5]
   short ecol[4][kShMaxNb16]; // WGRAD: destination column of 16-column block n >> 4 for rows m >> 5 (-1: skip)
   ShOut om;
@@ -171,7 +175,8 @@ __device__ __forceinline__ ShLoc sh_locate(const ShOut& o, int b, int h, int w, 
   return l;
 }
 
-template <int BN, int KIND>
+// KS: FWD K steps per tile (the issue loop unrolls over it; 0 for WGRAD)
+template <int BN, int KIND, int KS>
 __global__ void __launch_bounds__(kShThreads, 1)
     shconv_kernel(const __grid_constant__ CUtensorMap m0, const __grid_constant__ CUtensorMap m1,
                   const __grid_constant__ CUtensorMap m2, const __grid_constant__ CUtensorMap m3,
@@ -195,10 +200,12 @@ __global__ void __launch_bounds__(kShThreads, 1)
   float* bias_s = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(drain + 2) + 15) & ~uintptr_t(15));  // FWD bias
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // WGRAD with the bias gradient: the epilogue warps read every stage too
+  const bool bsum = KIND == kShWgrad && a.bias_rows > 0;
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(smem_u32(&bars[s]), 1);
-      mbar_init(smem_u32(&bars[kShMaxStages + s]), 1);
+      mbar_init(smem_u32(&bars[kShMaxStages + s]), bsum ? 1 + kShEpiWarps : 1);
     }
     for (int b = 0; b < C::kAcc; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
@@ -283,6 +290,10 @@ __global__ void __launch_bounds__(kShThreads, 1)
         fence_after();
       }
       const uint64_t db_res = smem_desc(smem_u32(b_res), 16, 1024);
+      // FWD: every K step's A descriptor offset (descriptor units), loaded once
+      uint32_t aoffs[KS > 0 ? KS : 1];
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) aoffs[ks] = static_cast<uint32_t>((ep.dbg & 16) ? (ks & 3) * 32 : a.a_koff[ks]) >> 4;
       int it = 0, tc = 0;
       for (int t = blockIdx.x; ok && t < nunits && !*abort; t += gridDim.x, ++tc) {
         const int buf = tc % C::kAcc, use = tc / C::kAcc;
@@ -299,11 +310,10 @@ __global__ void __launch_bounds__(kShThreads, 1)
           constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
                                      (static_cast<uint32_t>(BM >> 4) << 24);
           if (!(ep.dbg & 2)) {
-#pragma unroll 4
-            for (int ks = 0; ks < a.ksteps; ++ks) {
-              const uint32_t aoff = (ep.dbg & 16) ? (ks & 3) * 32 : a.a_koff[ks];
-              const uint32_t boff = (ks >> 2) * BN * 128 + (ks & 3) * 32;
-              mma_bf16(dtm, da0 + (aoff >> 4), db_res + (boff >> 4), idesc, ks > 0 ? 1u : 0u);
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+              constexpr uint32_t kBlk = BN * 128 / 16;     // one resident 64-wide K block, descriptor units
+              mma_bf16(dtm, da0 + aoffs[ks], db_res + (ks >> 2) * kBlk + (ks & 3) * 2, idesc, ks > 0 ? 1u : 0u);
             }
           }
           mma_commit(smem_u32(&bars[kShMaxStages + s]));
@@ -312,29 +322,44 @@ __global__ void __launch_bounds__(kShThreads, 1)
         } else {
           int n0, k0, nk;
           unit_range(t, &n0, &k0, &nk);
-          const int g0 = n0 / a.subw, ng = (min(BN, a.N - n0) + a.subw - 1) / a.subw;
+          // MMA groups per N tile: one (BN 64) or two (BN 256, 384), fixed by the instantiation
+          constexpr int NG = BN == 64 ? 1 : 2;
+          const int g0 = n0 / a.subw;
           const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) |
                                  (static_cast<uint32_t>(a.subw >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
           const uint32_t ka = a.a_krow, kb = a.b_krow;     // 16 k-rows = (16 * krow) bytes = krow descriptor units
+          const uint32_t all = (1u << a.ksteps) - 1u;
           bool good = true;
           for (int i = 0; i < nk; ++i, ++it) {
             const int s = it % stages;
+            // K steps worth issuing: the grid rows of kmask (the unit's first step always issues)
+            uint32_t issue = all;
+            if (a.kgrid) {
+              int h = (seg_row(a.seg[0], k0 + i) >> 4) % a.kgrid;
+              if (h < 0) h += a.kgrid;
+              issue = 0;
+              for (int ks = 0; ks < a.ksteps; ++ks) {
+                issue |= ((static_cast<uint32_t>(a.kmask) >> h) & 1u) << ks;
+                h = h + 1 == a.kgrid ? 0 : h + 1;
+              }
+              if (i == 0) issue |= 1u;
+            }
             if (!mbar_wait(smem_u32(&bars[s]), (it / stages) & 1, ep.err, 2, abort)) { good = false; break; }
             fence_after();
             if (ep.trace && blockIdx.x == 0 && it < kTraceN) ep.trace[kTraceN + it] = globaltimer();
             const uint32_t stage = smem_u32(tiles + s * a.stage_bytes);
             const uint64_t da0 = smem_desc(stage + a.a_off, a.a_lbo, a.a_sbo, a.a_layout);
-            uint64_t db0[4];
+            uint64_t db0[NG];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              db0[j] = smem_desc(stage + a.b_noff[g0 + (j < ng ? j : 0)], a.b_lbo, a.b_sbo, a.b_layout);
+            for (int j = 0; j < NG; ++j) db0[j] = smem_desc(stage + a.b_noff[g0 + j], a.b_lbo, a.b_sbo, a.b_layout);
             if (!(ep.dbg & 2)) {
-#pragma unroll 2
+              uint32_t acc = i > 0 ? 1u : 0u;
+#pragma unroll 4
               for (int ks = 0; ks < a.ksteps; ++ks) {
-                const uint32_t acc = (i > 0 || ks > 0) ? 1u : 0u;
+                if (!((issue >> ks) & 1u)) continue;
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                  if (j < ng) mma_bf16(dtm + j * a.subw, da0 + ks * ka, db0[j] + ks * kb, idesc, acc);
+                for (int j = 0; j < NG; ++j) mma_bf16(dtm + j * a.subw, da0 + ks * ka, db0[j] + ks * kb, idesc, acc);
+                acc = 1u;
               }
             }
             mma_commit(smem_u32(&bars[kShMaxStages + s]));
@@ -408,7 +433,7 @@ __global__ void __launch_bounds__(kShThreads, 1)
       }
       const bool xt = ep.trace && (ep.dbg & 64) && blockIdx.x == 0 && warp == 2 && lane == 0 && tc < kTraceN;
       if (xt) ep.trace[5 * kTraceN + tc] = globaltimer();
-      const bool got = mbar_wait(smem_u32(&acc_full[buf]), use & 1, ep.err, 3, abort);
+      const bool got = mbar_wait(smem_u32(&acc_full[buf]), use & 1, ep.err, 3, abort, true);
       if (grad && active) {
         asm volatile("cp.async.wait_group 0;" ::: "memory");
         __syncwarp();
@@ -473,8 +498,7 @@ __global__ void __launch_bounds__(kShThreads, 1)
               uint32_t pk[4];
 #pragma unroll
               for (int k = 0; k < 4; ++k)
-                pk[k] = static_cast<uint32_t>(surfk::f32_to_bf16(v[8 * q + 2 * k])) |
-                        (static_cast<uint32_t>(surfk::f32_to_bf16(v[8 * q + 2 * k + 1])) << 16);
+                pk[k] = surfk::pack_bf16x2(v[8 * q + 2 * k], v[8 * q + 2 * k + 1]);
               slots[stg_chunk(i0 + q)] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
           }
@@ -495,15 +519,44 @@ __global__ void __launch_bounds__(kShThreads, 1)
       if (ep.trace && blockIdx.x == 0 && warp == 2 && lane == 0 && tc < kTraceN) ep.trace[4 * kTraceN + tc] = globaltimer();
     }
   } else {
-    // ---- epilogue warps 2..9, WGRAD: the halves split the unit's columns
+    // ---- epilogue warps 2..9, WGRAD: the halves split the unit's columns;
+    // while the MMAs run they sum the output gradient's rows of every stage
+    // (the bias gradient; lane l owns columns 2l, 2l + 1, warp w rows w + 8i)
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int half = (warp - 2) >> 2, ew = warp - 2;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    int tc = 0;
+    float bs0 = 0.0f, bs1 = 0.0f;
+    int tc = 0, it = 0;
+    bool dead = false;
     for (int t = blockIdx.x; t < nunits; t += gridDim.x, ++tc) {
       const int buf = tc % C::kAcc, use = tc / C::kAcc;
       const int c_first = 32 * half;
-      if (!mbar_wait(smem_u32(&acc_full[buf]), use & 1, ep.err, 3, abort)) break;
+      if (bsum) {
+        int n0u, k0u, nku;
+        unit_range(t, &n0u, &k0u, &nku);
+        for (int i = 0; i < nku; ++i, ++it) {
+          const int s = it % stages;
+          if (!mbar_wait(smem_u32(&bars[s]), (it / stages) & 1, ep.err, 8, abort)) {
+            dead = true;
+            break;
+          }
+          if (n0u == 0) {
+            const uint8_t* box = tiles + s * a.stage_bytes + a.seg[0].soff;
+            const int cb = lane * 4;                       // byte of the column pair in the row
+#pragma unroll 4
+            for (int r = ew; r < a.bias_rows; r += kShEpiWarps) {
+              const uint32_t x =
+                  *reinterpret_cast<const uint32_t*>(box + r * 128 + (((cb >> 4) ^ (r & 7)) << 4) + (cb & 15));
+              bs0 += __uint_as_float(x << 16);
+              bs1 += __uint_as_float(x & 0xFFFF0000u);
+            }
+          }
+          __syncwarp();
+          if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&bars[kShMaxStages + s])) : "memory");
+        }
+        if (dead) break;
+      }
+      if (!mbar_wait(smem_u32(&acc_full[buf]), use & 1, ep.err, 3, abort, true)) break;
       fence_after();
       if (ep.trace && blockIdx.x == 0 && warp == 2 && lane == 0 && tc < kTraceN) ep.trace[3 * kTraceN + tc] = globaltimer();
       int n0, k0, nk;
@@ -534,6 +587,11 @@ __global__ void __launch_bounds__(kShThreads, 1)
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_empty[buf])) : "memory");
       if (ep.trace && blockIdx.x == 0 && warp == 2 && lane == 0 && tc < kTraceN) ep.trace[4 * kTraceN + tc] = globaltimer();
+    }
+    if (bsum && !(ep.dbg & 1)) {
+      float* gb = static_cast<float*>(ep.ct);
+      atomicAdd(gb + (2 * lane) % a.bias_mod, bs0);
+      atomicAdd(gb + (2 * lane + 1) % a.bias_mod, bs1);
     }
   }
   fence_before();
@@ -587,7 +645,7 @@ bool make_map3(CUtensorMap* m, const ShMap& s, int box_rows) {
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int KIND>
+template <int BN, int KIND, int KS>
 int sh_launch(const ShDesc& d, const Epilogue& ep, cudaStream_t s) {
   const ShArgs& a = d.a;
   CUtensorMap mp[4], mres;
@@ -629,7 +687,7 @@ int sh_launch(const ShDesc& d, const Epilogue& ep, cudaStream_t s) {
   if (stages > kShMaxStages) stages = kShMaxStages;
   if (stages < 2) return static_cast<int>(cudaErrorInvalidValue);
   const size_t smem = 1024 + static_cast<size_t>(stages) * a.stage_bytes + res_bytes + stg_total + 1024;
-  auto kern = shconv_kernel<BN, KIND>;
+  auto kern = shconv_kernel<BN, KIND, KS>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   const int units = KIND == kShFwd ? a.mt : a.nt * a.splits;
   const int grid = units < sms ? units : sms;
@@ -675,7 +733,11 @@ SURF_EXPORT int surf_shconv(const ShDesc* d, const Epilogue* ep, void* stream) {
   } else {
     if (a.subw < 16 || a.subw > 256 || (a.subw & 15) || d->bn % a.subw || a.splits < 1 || a.per < 1 ||
         a.nt * d->bn < a.N || a.N > 16 * kShMaxNb16 || (a.N + a.subw - 1) / a.subw > kShMaxSub || !ep->c ||
-        ep->c_mode != kAtomic || a.ksteps < 1 || (reinterpret_cast<uintptr_t>(ep->c) & 15) || (ep->ldc & 3))
+        ep->c_mode != kAtomic || a.ksteps < 1 || (reinterpret_cast<uintptr_t>(ep->c) & 15) || (ep->ldc & 3) ||
+        (a.bias_rows > 0 && (!ep->ct || a.seg[0].row_bytes != 128 || a.bias_rows > a.seg[0].rows ||
+                             a.bias_mod < 1 || a.bias_mod > 64)) ||
+        (a.kgrid && (a.kgrid > 32 || a.kgrid < 1 || a.seg[0].udiv != 1 || (a.seg[0].mul_hi & 15) || (a.seg[0].add & 15))) ||
+        a.ksteps > 32 || d->bn / a.subw != (d->bn == 64 ? 1 : 2) || a.nt != 1)
       return static_cast<int>(cudaErrorInvalidValue);
     // every MMA operand (the K steps' 16-row slices, both MN blocks of A and
     // every N block of a group) lies inside one stage
@@ -688,18 +750,20 @@ SURF_EXPORT int surf_shconv(const ShDesc* d, const Epilogue* ep, void* stream) {
   }
   auto s = static_cast<cudaStream_t>(stream);
   if (a.kind == kShFwd) {
-    switch (d->bn) {
-      case 64: return sh_launch<64, kShFwd>(*d, *ep, s);
-      case 128: return sh_launch<128, kShFwd>(*d, *ep, s);
-      case 192: return sh_launch<192, kShFwd>(*d, *ep, s);
-      case 256: return sh_launch<256, kShFwd>(*d, *ep, s);
+    // the trunk's forward-kind shapes: (N, K steps)
+    const int key = d->bn * 100 + a.ksteps;
+    switch (key) {
+      case 128 * 100 + 10: return sh_launch<128, kShFwd, 10>(*d, *ep, s);   // conv1 forward
+      case 128 * 100 + 16: return sh_launch<128, kShFwd, 16>(*d, *ep, s);   // conv2 forward
+      case 192 * 100 + 12: return sh_launch<192, kShFwd, 12>(*d, *ep, s);   // conv3 forward, input gradient
+      case 256 * 100 + 8: return sh_launch<256, kShFwd, 8>(*d, *ep, s);     // conv2 input gradient
       default: return static_cast<int>(cudaErrorInvalidValue);
     }
   }
   switch (d->bn) {
-    case 64: return sh_launch<64, kShWgrad>(*d, *ep, s);
-    case 256: return sh_launch<256, kShWgrad>(*d, *ep, s);
-    case 384: return sh_launch<384, kShWgrad>(*d, *ep, s);
+    case 64: return sh_launch<64, kShWgrad, 0>(*d, *ep, s);
+    case 256: return sh_launch<256, kShWgrad, 0>(*d, *ep, s);
+    case 384: return sh_launch<384, kShWgrad, 0>(*d, *ep, s);
     default: return static_cast<int>(cudaErrorInvalidValue);
   }
 }

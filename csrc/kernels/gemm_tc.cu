@@ -457,8 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint32_t w[4];
 #pragma unroll
               for (int k = 0; k < 4; ++k)
-                w[k] = static_cast<uint32_t>(surfk::f32_to_bf16(v[8 * c + 2 * k])) |
-                       (static_cast<uint32_t>(surfk::f32_to_bf16(v[8 * c + 2 * k + 1])) << 16);
+                w[k] = surfk::pack_bf16x2(v[8 * c + 2 * k], v[8 * c + 2 * k + 1]);
               const int pc = c ^ ((lane >> 1) & 3);
               *reinterpret_cast<uint4*>(tile + lane * 64 + pc * 16) = make_uint4(w[0], w[1], w[2], w[3]);
             }

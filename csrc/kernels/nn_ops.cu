@@ -110,8 +110,7 @@ __global__ void col2im_kernel(const uint16_t* dcol, int64_t ldcol, const uint16_
       uint32_t* o4 = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
       for (int q = 0; q < 4; ++q)
-        o4[q] = static_cast<uint32_t>(surfk::f32_to_bf16(acc[2 * q])) |
-                (static_cast<uint32_t>(surfk::f32_to_bf16(acc[2 * q + 1])) << 16);
+        o4[q] = surfk::pack_bf16x2(acc[2 * q], acc[2 * q + 1]);
       o.x &= mask.x; o.y &= mask.y; o.z &= mask.z; o.w &= mask.w;
       *reinterpret_cast<uint4*>(dx + off) = o;
     }

@@ -82,13 +82,29 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait that may suspend the thread up to `ns` nanoseconds (it resumes as
+// soon as the phase completes): waiting warps stop competing for issue slots
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait; returns false (and records `code`) on timeout or when another
 // role already gave up (*abort set).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code, volatile int* abort) {
+// `nap`: waits off the critical path (epilogue warps waiting for an
+// accumulator) may suspend between polls
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code, volatile int* abort,
+                                          bool nap = false) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try(bar, parity)) return true;
+    if (nap ? mbar_try_sleep(bar, parity, 20000u) : mbar_try(bar, parity)) return true;
     if ((i & 255) == 0) {
       if (*abort) return false;
       if (globaltimer() - t0 > kWaitNs) {
@@ -296,8 +312,7 @@ __device__ __forceinline__ void store_chunk32(const Epilogue& ep, const float* v
         uint32_t w[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          w[k] = static_cast<uint32_t>(surfk::f32_to_bf16(v[8 * q + 2 * k])) |
-                 (static_cast<uint32_t>(surfk::f32_to_bf16(v[8 * q + 2 * k + 1])) << 16);
+          w[k] = surfk::pack_bf16x2(v[8 * q + 2 * k], v[8 * q + 2 * k + 1]);
         reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[0], w[1], w[2], w[3]);
       }
     } else {

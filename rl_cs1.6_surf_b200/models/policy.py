@@ -450,16 +450,12 @@ def backward_gpu(net: "PolicyNet", ws: Workspace, scal16: torch.Tensor, B: Optio
             # dense feature -> h*16 + w), the padding staying zero
             dy3 = ws.dy3[:B * 128]
             G.gemm(df, w("fc.w"), b_mn=True, out=dy3.view(B, 8192), act="relu_grad", aux=feat, cmap=(768, 1024))
-            T.conv3_weight_grad(dy3, ws.sy2, net.g("conv3.w"), B)
-            G.colsum(dy3, net.g("conv3.b"))
+            # weight and bias gradients in one kernel per layer
+            T.conv3_weight_grad(dy3, ws.sy2, net.g("conv3.w"), B, net.g("conv3.b"))
             T.conv3_input_grad(dy3, ws.sy2, ws.dy2, B)
-            dy2 = ws.dy2[:B * 128]
-            T.conv2_weight_grad(dy2, ws.sy1, net.g("conv2.w"), B)
-            G.colsum(dy2, net.g("conv2.b"))
-            T.conv2_input_grad(dy2, ws.sy1, ws.dy1, B)
-            dy1 = ws.dy1[:B * 512]
-            T.conv1_weight_grad(dy1, ws.img, net.g("conv1.w"), B)
-            G.colsum(dy1, net.g("conv1.b"))
+            T.conv2_weight_grad(ws.dy2, ws.sy1, net.g("conv2.w"), B, net.g("conv2.b"))
+            T.conv2_input_grad(ws.dy2, ws.sy1, ws.dy1, B)
+            T.conv1_weight_grad(ws.dy1, ws.img, net.g("conv1.w"), B, net.g("conv1.b"))
             return
         shapes = cfg.conv_shapes()
         last_rows = B * shapes[-1]["OH"] * shapes[-1]["OW"]

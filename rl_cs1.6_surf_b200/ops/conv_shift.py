@@ -41,6 +41,7 @@ from __future__ import annotations
 
 import ctypes
 from ctypes import c_int, c_int64, c_short, c_void_p
+from typing import Optional
 
 import numpy as np
 import torch
@@ -71,7 +72,9 @@ class ShArgs(ctypes.Structure):
                 ("a_sbo", c_int), ("b_layout", c_int), ("b_lbo", c_int), ("b_sbo", c_int), ("ksteps", c_int),
                 ("a_koff", c_int * 64), ("nblk", c_int), ("bd", c_int * 4), ("zero_fill", c_int),
                 ("stg_bytes", c_int), ("a_off", c_int), ("a_krow", c_int),
-                ("subw", c_int), ("b_krow", c_int), ("b_noff", c_int * 16), ("erow", c_int * 4),
+                ("subw", c_int), ("b_krow", c_int), ("b_noff", c_int * 16), ("kgrid", c_int), ("kmask", c_int),
+                ("bias_rows", c_int), ("bias_mod", c_int),
+                ("erow", c_int * 4),
                 ("ecol", (c_short * 32) * 4), ("om", ShOut)]
 
 
@@ -201,7 +204,8 @@ def shift_forward(segs, maps, koffs, w: torch.Tensor, tiles: int, M: int, om: Sh
 
 
 def shift_wgrad(a_seg, a_map, b_segs, b_maps, groups, subw: int, b_lbo: int, R: int, L: int, kt: int, N: int,
-                erow, ecol, gw: torch.Tensor) -> None:
+                erow, ecol, gw: torch.Tensor, gb: Optional[torch.Tensor] = None, bias_mod: int = 64,
+                kgrid: int = 0, kmask: int = 0) -> None:
     """Weight-gradient product, k = grid positions in load units of R rows:
     A (MN-major, 128-byte rows) holds the output gradient of rows
     [u*R - L, u*R + R); its upper MN block starts L rows in, so the upper
@@ -209,7 +213,12 @@ def shift_wgrad(a_seg, a_map, b_segs, b_maps, groups, subw: int, b_lbo: int, R: 
     per MMA group, (B box index, row inside the box) of its first N block; the
     group's blocks sit ``b_lbo`` bytes apart. ``erow`` / ``ecol``: destination
     of every (32-row, 16-column) accumulator block in ``gw`` (fp32, accumulated;
-    column -1 = skipped)."""
+    column -1 = skipped). ``gb``: also accumulate the bias gradient, the sum
+    of the first R rows of every A box (every position once), column c into
+    channel c % bias_mod. ``kgrid`` / ``kmask``: K step ks of a unit covers
+    grid row ((first A-box row) / 16 + ks) mod kgrid (both halves' rows: that
+    row and the next); only rows whose bit is set in ``kmask`` are issued --
+    the others' output gradient must be zero."""
     d = ShDesc()
     a = d.a
     a.seg[0] = a_seg
@@ -242,8 +251,13 @@ def shift_wgrad(a_seg, a_map, b_segs, b_maps, groups, subw: int, b_lbo: int, R: 
     splits = max(1, min(kt, _sms(gw.device)))
     a.per = (kt + splits - 1) // splits
     a.splits = (kt + a.per - 1) // a.per
+    if gb is not None:
+        a.bias_rows, a.bias_mod = R, bias_mod
+    a.kgrid, a.kmask = kgrid, kmask
     d.bn = subw * len(groups)
-    _launch(d, _epi(gw, gw.stride(0), accumulate=True), gw.device)
+    ep = _epi(gw, gw.stride(0), accumulate=True)
+    ep.ct = ptr(gb)
+    _launch(d, ep, gw.device)
 
 
 # ---- stacked weight operands ----------------------------------------------------------------
@@ -361,6 +375,11 @@ class Trunk:
     conv2.w and conv3.w (``refresh`` gathers the stacked operands from them)."""
 
     R1, L = 192, 16                  # weight-gradient load unit (positions) and stacking offset
+    # weight-gradient K steps worth issuing on the 8 x 16 grids: a step covers
+    # grid rows h (lower half) and h + 1 (upper half); dy3 is nonzero in rows
+    # 0-3, dy2 in rows 0-5
+    KMASK3 = sum(1 << h for h in range(8) if h < 4 or (h + 1) % 8 < 4)
+    KMASK2 = sum(1 << h for h in range(8) if h < 6 or (h + 1) % 8 < 6)
 
     def __init__(self, device, offsets):
         dev = torch.device(device)
@@ -449,8 +468,9 @@ class Trunk:
                       nblk=2, act="relu_grad", aux=y1, ld_aux=64)
 
     # ---- weight gradients ----------------------------------------------------------------
-    def conv1_weight_grad(self, dy1, img, gw1, B):
-        """gw1 [32, 64] += dW of conv1 from dy1 [B*512, 32] and img [B*512, 16]."""
+    def conv1_weight_grad(self, dy1, img, gw1, B, gb1=None):
+        """gw1 [32, 64] += dW of conv1 from dy1 [B*512, 32] and img [B*512, 16]
+        (and gb1 [32] += the bias gradient)."""
         R, L = self.R1, self.L
         rows = B * 256                                   # rows of 2 positions
         kt = (rows + L + R - 1) // R
@@ -458,10 +478,11 @@ class Trunk:
         b_seg = _seg(R + 1, 64, 0, R)
         erow, ecol = self.maps["c1"]
         shift_wgrad(a_seg, _map(dy1, 64, rows), [b_seg], [_map(img, 32, rows)], [(0, 0)], 64, 64, R, L, kt, 64,
-                    erow, ecol, gw1)
+                    erow, ecol, gw1, gb1, 32)
 
-    def conv2_weight_grad(self, dy2, y1, gw2, B):
-        """gw2 [64, 512] += dW of conv2 from dy2 [B*128, 64] (zeros outside 6 x 14) and y1."""
+    def conv2_weight_grad(self, dy2, y1, gw2, B, gb2=None):
+        """gw2 [64, 512] += dW of conv2 from dy2 [B*128, 64] (zeros outside 6 x 14) and y1
+        (and gb2 [64] += the bias gradient)."""
         R, L = 128, self.L
         rows = B * 128
         kt = (rows + L + R - 1) // R
@@ -469,10 +490,11 @@ class Trunk:
         b_segs = [_seg(R + 16, 128, 0, R, gw=16) for _ in range(2)]
         erow, ecol = self.maps["c2"]
         shift_wgrad(a_seg, _map(dy2, 64, rows), b_segs, self._planes(y1, B), [(0, 0), (1, 0)], 128, 128, R, L, kt,
-                    256, erow, ecol, gw2)
+                    256, erow, ecol, gw2, gb2, kgrid=8, kmask=self.KMASK2)
 
-    def conv3_weight_grad(self, dy3, y2, gw3, B):
-        """gw3 [64, 576] += dW of conv3 from dy3 [B*128, 64] (zeros outside 4 x 12) and y2."""
+    def conv3_weight_grad(self, dy3, y2, gw3, B, gb3=None):
+        """gw3 [64, 576] += dW of conv3 from dy3 [B*128, 64] (zeros outside 4 x 12) and y2
+        (and gb3 [64] += the bias gradient)."""
         R, L = self.R1, self.L
         rows = B * 128
         kt = (rows + L + R - 1) // R
@@ -480,4 +502,4 @@ class Trunk:
         b_seg = _seg(R + 18, 128, 0, R)
         erow, ecol = self.maps["c3"]
         shift_wgrad(a_seg, _map(dy3, 64, rows), [b_seg], [_map(y2, 64, rows)], [(0, 0), (0, 16)], 192, 128, R, L,
-                    kt, 384, erow, ecol, gw3)
+                    kt, 384, erow, ecol, gw3, gb3, kgrid=8, kmask=self.KMASK3)

@@ -132,14 +132,24 @@ def _run_wgrad(d, ep):
     na, nbx = ra // 2, rbx // 2
     blocks = a.subw // nbx
     ngrp = (a.N + a.subw - 1) // a.subw
+    gb = _resolve(ep.ct) if a.bias_rows else None
     for sp in range(a.splits):
         D = torch.zeros(128, a.N)
         for u in range(sp * a.per, min(a.kt, (sp + 1) * a.per)):
             A = _rows(d.maps[0], a.seg[0], u)                         # A box [rows, 64]
+            if gb is not None:
+                bt, bo = gb
+                col_sum = A[:a.bias_rows].sum(0)
+                for c in range(col_sum.numel()):
+                    bt.reshape(-1)[bo + c % a.bias_mod] += col_sum[c]
             Bs = {}
             for g in range(1, a.nseg_a + a.nseg_b):
                 Bs[a.seg[g].soff] = _rows(d.maps[g], a.seg[g], u)
+            row0 = u * a.seg[0].mul_hi + a.seg[0].add
             for ks in range(a.ksteps):
+                if a.kgrid and (u, ks) != (sp * a.per, 0):
+                    if not (a.kmask >> ((row0 // 16 + ks) % a.kgrid)) & 1:
+                        continue
                 k0 = a.a_off // ra + ks * 16
                 Am = torch.cat([A[k0:k0 + 16], A[k0 + a.a_lbo // ra:k0 + a.a_lbo // ra + 16]], 1)  # [16, 128]
                 for g in range(ngrp):
@@ -271,12 +281,17 @@ def test_weight_grads(trunk):
         F.conv2d(x.permute(0, 3, 1, 2), w, stride=s).backward(d.permute(0, 3, 1, 2))
         return w.grad.permute(0, 2, 3, 1).reshape(co, -1)
 
-    T.conv3_weight_grad(dy3, y2, gw3, B)
+    gb1, gb2, gb3 = torch.full((32,), 0.25), torch.full((64,), 0.25), torch.full((64,), 0.25)
+    _reg(gb1, gb2, gb3)
+    T.conv3_weight_grad(dy3, y2, gw3, B, gb3)
     torch.testing.assert_close(gw3, ref(a2[:, :6, :14], d3[:, :4, :12], 64, 3, 64, 1) + 0.5, rtol=1e-3, atol=1e-3)
-    T.conv2_weight_grad(dy2, y1, gw2, B)
+    torch.testing.assert_close(gb3, d3.sum((0, 1, 2)) + 0.25, rtol=1e-3, atol=1e-3)
+    T.conv2_weight_grad(dy2, y1, gw2, B, gb2)
     torch.testing.assert_close(gw2, ref(a1[:, :15, :31], d2[:, :6, :14], 64, 4, 32, 2) + 0.5, rtol=1e-3, atol=1e-3)
-    T.conv1_weight_grad(dy1, x0, gw1, B)
+    torch.testing.assert_close(gb2, d2.sum((0, 1, 2)) + 0.25, rtol=1e-3, atol=1e-3)
+    T.conv1_weight_grad(dy1, x0, gw1, B, gb1)
     torch.testing.assert_close(gw1, ref(img, d1[:, :15, :31], 32, 2, 16, 1) + 0.5, rtol=1e-3, atol=1e-3)
+    torch.testing.assert_close(gb1, d1.sum((0, 1, 2)) + 0.25, rtol=1e-3, atol=1e-3)
 
 
 def test_stacked_tables_cover_every_weight_once():

@@ -117,9 +117,13 @@ def test_weight_grads(B):
         F.conv2d(x.permute(0, 3, 1, 2), w, stride=s).backward(d.permute(0, 3, 1, 2))
         return w.grad.permute(0, 2, 3, 1).reshape(co, -1)
 
-    T.conv3_weight_grad(dy3, y2, gw3, B)
+    gb1, gb2, gb3 = (torch.full((n,), 0.25, device=DEV) for n in (32, 64, 64))
+    T.conv3_weight_grad(dy3, y2, gw3, B, gb3)
     torch.testing.assert_close(gw3, ref(a2[:, :6, :14], d3[:, :4, :12], 64, 3, 64, 1) + 0.5, rtol=1e-2, atol=3e-2)
-    T.conv2_weight_grad(dy2, y1, gw2, B)
+    torch.testing.assert_close(gb3, d3.sum((0, 1, 2)) + 0.25, rtol=1e-3, atol=1e-2)
+    T.conv2_weight_grad(dy2, y1, gw2, B, gb2)
     torch.testing.assert_close(gw2, ref(a1[:, :15, :31], d2[:, :6, :14], 64, 4, 32, 2) + 0.5, rtol=1e-2, atol=3e-2)
-    T.conv1_weight_grad(dy1, x0, gw1, B)
+    torch.testing.assert_close(gb2, d2.sum((0, 1, 2)) + 0.25, rtol=1e-3, atol=1e-2)
+    T.conv1_weight_grad(dy1, x0, gw1, B, gb1)
     torch.testing.assert_close(gw1, ref(img, d1[:, :15, :31], 32, 2, 16, 1) + 0.5, rtol=1e-2, atol=3e-2)
+    torch.testing.assert_close(gb1, d1.sum((0, 1, 2)) + 0.25, rtol=1e-3, atol=1e-2)
