@@ -107,13 +107,6 @@ struct ShArgs {
   ShOut om;
 };
 
-// wait on an mbarrier phase for at most the usual bound, whatever the abort flag says
-__device__ __forceinline__ void mbar_wait_bounded(uint32_t bar, uint32_t parity) {
-  const uint64_t t0 = globaltimer();
-  while (!mbar_try(bar, parity))
-    if (globaltimer() - t0 > kWaitNs) return;
-}
-
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"

@@ -27,7 +27,11 @@
 // Every wait on an mbarrier is bounded by %globaltimer (2 s); on expiry the
 // kernel records an error code in a device flag, skips the remaining work,
 // releases its tensor memory and returns, so a fault in the pipeline shows
-// up as an error status on the host instead of a hung GPU.
+// up as an error status on the host instead of a hung GPU. Before leaving,
+// the producer waits (bounded) for the loads it issued that nobody consumed
+// and the MMA thread commits and waits (bounded) for its last MMAs, so no
+// copy lands in released shared memory and no MMA writes freed tensor
+// memory; the remaining risk is a copy or MMA that outlives those bounds.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -181,7 +185,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = bars + 2 * STAGES;
   uint64_t* acc_empty = bars + 2 * STAGES + C::kAcc;
   uint64_t* bres_full = bars + 2 * STAGES + 2 * C::kAcc;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres_full + 1);
+  uint64_t* drain = bres_full + 1;                      // the MMA thread's final commit
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   // output staging after the barrier block, 1024-aligned (swizzle atoms)
   uint8_t* stage_out = b_res + C::kResBytes + 1024;
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -197,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&acc_empty[b]), C::kEpiPerTile);     // one arrival per epilogue warp of the tile
     }
     mbar_init(smem_u32(bres_full), 1);
+    mbar_init(smem_u32(drain), 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -310,6 +316,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if (*abort) {
+        // loads may still be landing in stages nobody consumes: wait for them
+        // (bounded) before the CTA's shared memory goes away
+        for (int j = it > STAGES ? it - STAGES : 0; j < it; ++j)
+          mbar_wait_bounded(smem_u32(&bars[j % STAGES]), (j / STAGES) & 1);
+      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -319,6 +331,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (RB && static_cast<int>(blockIdx.x) < ntiles) {
         res_ok = mbar_wait(smem_u32(bres_full), 0, ep.err, 5, abort);
         fence_after();
+      }
+      // UMMA descriptors: the layout / LBO / SBO bits and every k step's start
+      // offset are fixed for the launch; per stage only the base address
+      // (the low 14-bit field, in 16-byte units) is added.
+      // K-major: +32 B per 16-element k step inside the 128 B swizzled row;
+      // MN-major: +2 k-groups (2 x 1024 B) per step; MN blocks BK*128 B apart.
+      // Mode 3 (32 B swizzle): A steps one 128-row slab per k step (8-row
+      // groups 256 B apart); B steps 16 positions (512 B) inside every
+      // 16-column slab, the slabs BK*32 B apart.
+      // Mode 4 (64 B swizzle): A k steps 0-1 lie in window box 0 and
+      // 2-3 in box 1 (+32 B per step inside a 64 B row, 8-row groups
+      // 512 B apart); B steps 16 positions (1024 B) inside every
+      // 32-column window box, the boxes BK*64 B apart.
+      const uint64_t a_proto = cc.a.mode == 3   ? smem_desc(0, 16, 256, kSw32)
+                               : cc.a.mode == 4 ? smem_desc(0, 16, 512, kSw64)
+                               : A_MN           ? smem_desc(0, BK * 128, 1024)
+                                                : smem_desc(0, 16, 1024);
+      const uint64_t b_proto = cc.b.mode == 3   ? smem_desc(0, BK * 32, 256, kSw32)
+                               : cc.b.mode == 4 ? smem_desc(0, BK * 64, 512, kSw64)
+                               : B_MN           ? smem_desc(0, BK * 128, 1024)
+                                                : smem_desc(0, 16, 1024);
+      uint32_t a_step[BK / 16], b_step[BK / 16];
+#pragma unroll
+      for (int j = 0; j < BK / 16; ++j) {
+        a_step[j] = (cc.a.mode == 3 ? j * (BM * 32) : cc.a.mode == 4 ? (j >> 1) * (BM * 64) + (j & 1) * 32
+                     : A_MN ? j * 2048 : j * 32) >> 4;
+        b_step[j] = (cc.b.mode == 3 ? j * 512 : cc.b.mode == 4 ? j * 1024 : B_MN ? j * 2048 : j * 32) >> 4;
       }
       for (int t = blockIdx.x; res_ok && t < ntiles && !*abort; t += gridDim.x, ++tc) {
         int m0, nb, kt0, nkt;
@@ -335,26 +374,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (ep.trace && blockIdx.x == 0 && it < kTraceN) ep.trace[kTraceN + it] = globaltimer();
           const uint32_t a_base = smem_u32(tiles + s * C::kStageBytes);
           const uint32_t b_base = RB ? smem_u32(b_res + (kt0 + i) * C::kBBytes) : a_base + C::kABytes;
+          const uint64_t da0 = a_proto + (a_base >> 4), db0 = b_proto + (b_base >> 4);
+          if (!(ep.dbg & 2)) {
 #pragma unroll
-          for (int j = 0; j < BK / 16; ++j) {
-            // K-major: +32 B per 16-element k step inside the 128 B swizzled row;
-            // MN-major: +2 k-groups (2 x 1024 B) per step; MN blocks BK*128 B apart.
-            // Mode 3 (32 B swizzle): A steps one 128-row slab per k step (8-row
-            // groups 256 B apart); B steps 16 positions (512 B) inside every
-            // 16-column slab, the slabs BK*32 B apart.
-            // Mode 4 (64 B swizzle): A k steps 0-1 lie in window box 0 and
-            // 2-3 in box 1 (+32 B per step inside a 64 B row, 8-row groups
-            // 512 B apart); B steps 16 positions (1024 B) inside every
-            // 32-column window box, the boxes BK*64 B apart.
-            const uint64_t da = cc.a.mode == 3   ? smem_desc(a_base + j * (BM * 32), 16, 256, kSw32)
-                                : cc.a.mode == 4 ? smem_desc(a_base + (j >> 1) * (BM * 64) + (j & 1) * 32, 16, 512, kSw64)
-                                : A_MN           ? smem_desc(a_base + j * 2048, BK * 128, 1024)
-                                                 : smem_desc(a_base + j * 32, 16, 1024);
-            const uint64_t db = cc.b.mode == 3   ? smem_desc(b_base + j * 512, BK * 32, 256, kSw32)
-                                : cc.b.mode == 4 ? smem_desc(b_base + j * 1024, BK * 64, 512, kSw64)
-                                : B_MN           ? smem_desc(b_base + j * 2048, BK * 128, 1024)
-                                                 : smem_desc(b_base + j * 32, 16, 1024);
-            if (!(ep.dbg & 2)) mma_bf16(dtm, da, db, C::kIdesc, (i > 0 || j > 0) ? 1u : 0u);
+            for (int j = 0; j < BK / 16; ++j)
+              mma_bf16(dtm, da0 + a_step[j], db0 + b_step[j], C::kIdesc, (i > 0 || j > 0) ? 1u : 0u);
           }
           mma_commit(smem_u32(&bars[STAGES + s]));      // frees the stage when these MMAs finish
           if (ep.trace && blockIdx.x == 0 && it < kTraceN) ep.trace[2 * kTraceN + it] = globaltimer();
@@ -362,6 +386,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         mma_commit(smem_u32(&acc_full[buf]));          // accumulator of this tile complete
       }
+      // every MMA issued by this thread has completed before the tensor memory is freed
+      mma_commit(smem_u32(drain));
+      mbar_wait_bounded(smem_u32(drain), 0);
     }
   } else {
     // ---- epilogue warps 2..9 (TMEM lane quadrant = warp % 4; `half` picks

@@ -116,6 +116,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
   }
 }
 
+// wait on an mbarrier phase for at most the usual bound, whatever the abort
+// flag says (the abort paths' drains of work still in flight)
+__device__ __forceinline__ void mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try(bar, parity))
+    if (globaltimer() - t0 > kWaitNs) return;
+}
+
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
