@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--env-device", choices=["cpu", "cuda"], default="cpu",
                     help="cpu: C++ env threads + pinned rows (the headline); cuda: the same env rules on the GPU")
+    ap.add_argument("--race", action="store_true",
+                    help="the race configuration (config 5: race track, geodesic potential, 2048 envs per GPU)")
     ap.add_argument("--json", default=None)
     ap.add_argument("--timing", action="store_true", help="also print each timed iteration's TIMING line to stderr")
     ap.add_argument("--no-phases", action="store_true",
@@ -103,7 +105,7 @@ def dist_env():
 def run_ours(args) -> None:
     import torch
     import surfb200  # noqa: F401
-    from surfb200.trainer.config import bench_config
+    from surfb200.trainer.config import bench_config, race_bench_config
     from surfb200.trainer.ppo import Trainer
     from surfb200.ops import _lib as L
 
@@ -114,7 +116,7 @@ def run_ours(args) -> None:
         from surfb200.parallel.dist import init_process_group, make_comm
         init_process_group()
         comm = make_comm(args.comm)
-    cfg = bench_config(args.envs)
+    cfg = race_bench_config(args.envs) if args.race else bench_config(args.envs)
     cfg.graphs = not args.no_graphs
     cfg.seed = 0
     cfg.timing = args.timing or not args.no_phases
@@ -171,10 +173,14 @@ def run_ours(args) -> None:
             "config": {"model": "nature-cnn-128x64+proprio256 vision PPO", "global_batch": cfg.envs * world,
                        "seq_len": cfg.n_steps, "parallelism": f"dp{world}", "envs_per_gpu": cfg.envs,
                        "act_every": cfg.act_every, "epochs": cfg.epochs, "minibatches": cfg.minibatches,
-                       "map": "procedural random field, 512 brushes, 16u SDF 1024x1024x256",
+                       "map": ("procedural race track (40 chained ramps, 4 gap jumps over teleport fail nets, "
+                               "finish curtain), 16u SDF and geodesic grid" if args.race else
+                               "procedural random field, 512 brushes, 16u SDF 1024x1024x256"),
                        "comm": args.comm if world > 1 else "none", "cuda_graphs": cfg.graphs,
                        "env_device": cfg.env_device,
-                       "reward": "coverage (revisit_pen 0.25) + count curiosity 0.25 (256u cell x 8 yaw x 8 speed)",
+                       "reward": ("race: potential on the geodesic distance to the finish, 15 s stall kill, + "
+                                  "count curiosity 0.25" if args.race else
+                                  "coverage (revisit_pen 0.25) + count curiosity 0.25 (256u cell x 8 yaw x 8 speed)"),
                        "differs_from_reference_arm": ["network: Nature CNN + proprio 256 vs the reference's own trunk",
                                                       "reward: curiosity 0.25 on top of coverage (the reference "
                                                       "pays curiosity only in race mode)"],
@@ -182,6 +188,7 @@ def run_ours(args) -> None:
             "clocks": clocks,
             "e2e": {"value": round(e2e, 1), "unit": "ticks/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
+            "goal_field_bake_ms": round(tr.field_bake_ms, 1) if tr.field_bake_ms is not None else None,
             "phases_ms_per_step": {k: round(v, 2) for k, v in phases.items()} or None,
             "last_iteration": {k: v for k, v in stats.items() if k != "timing"},
         }

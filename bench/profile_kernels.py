@@ -3,7 +3,7 @@
     python bench/profile_kernels.py --only march|conv1_fwd|conv2_dgrad|fc_wgrad|col2im|im2col|conv1_ifwd|
                                            conv1_iwgrad|conv2_ifwd|
                                            conv2_iwgrad|conv2_idgrad|conv3_ifwd|conv3_iwgrad|conv3_idgrad|sample|gae|
-                                           ppo_loss|reward|adam|p2p1|edt|geodesic|surfnz|framestack [--reps 2]
+                                           ppo_loss|reward|adam|p2p1|edt|geodesic|geodesic_race|surfnz|framestack [--reps 2]
 
 Each case builds its inputs (a few GB on the device at most, larger than L2
 where the kernel streams memory), warms up once, then launches the kernel
@@ -270,6 +270,23 @@ def main():
         info["ms"] = _time(lambda: surfmask.bake(tris, mins, 16.0, (nx, ny, nz), core=core, linear=False), 1)
         info["triangles"] = len(tris)
         info["voxels"] = nx * ny * nz
+    elif k == "geodesic_race":
+        # the race track's free-voxel grid at 16u (config 5), seeded at its finish zone
+        from surfb200.ops.geodesic import geodesic, seed_box
+        from surfb200.ops.vision import grid_dims, occupancy
+        from surfb200.sim import mapgen
+        from surfb200.sim.core import SimCore, default_config
+        m = mapgen.generate("race", 0)
+        core = SimCore.from_bytes(m.image, default_config(1), threads=4)
+        mn, mx = core.map_bounds()
+        mins, nx, ny, nz = grid_dims(mn, mx, 16.0)
+        occ = occupancy(core, mins, 16.0, (nx, ny, nz), slab=True, device=dev)
+        lo, hi = seed_box(m.zones["end"], mins, 16.0, (nx, ny, nz))
+        st = {}
+        info["ms"] = _time(lambda: geodesic(occ, 16.0, lo, hi, stats=st), args.reps)
+        info["voxels"] = nx * ny * nz
+        info["dims"] = [nx, ny, nz]
+        info["passes"] = st.get("passes")
     elif k == "geodesic":
         from surfb200.ops.geodesic import geodesic
         occ = torch.zeros(128, 256, 256, dtype=torch.uint8, device=dev)

@@ -39,8 +39,10 @@ def seed_box(zone, mins, cell: float, dims):
     return lo, hi
 
 
-def geodesic(occ: torch.Tensor, cell: float, lo, hi, max_passes: int = 100000) -> torch.Tensor:
-    """Distances (float [nz, ny, nx], +3e38 where unreachable) on the GPU."""
+def geodesic(occ: torch.Tensor, cell: float, lo, hi, max_passes: int = 100000,
+             stats: Optional[dict] = None) -> torch.Tensor:
+    """Distances (float [nz, ny, nx], +3e38 where unreachable) on the GPU.
+    ``stats`` (optional dict) receives the number of worklist passes."""
     _lib.require_cuda(occ, "geodesic")
     nz, ny, nx = occ.shape
     L = _lib.lib(VLIB)
@@ -60,13 +62,17 @@ def geodesic(occ: torch.Tensor, cell: float, lo, hi, max_passes: int = 100000) -
     if int(n_seed.item()) == 0:
         raise RuntimeError("goal zone contains no free voxel")
     cur = 0
+    passes = 0
     for _ in range(max_passes):
         changed.zero_()
         check(L.surf_geodesic_pass(ptr(dist), ptr(occ), ptr(flags), ptr(work), ptr(counts), cur, nx, ny, nz,
                                    float(cell), ptr(changed), s), "surf_geodesic_pass")
         cur = 1 - cur
+        passes += 1
         if not int(changed.item()):
             break
+    if stats is not None:
+        stats["passes"] = passes
     return dist
 
 

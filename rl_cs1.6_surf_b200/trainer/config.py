@@ -188,3 +188,15 @@ def bench_config(n_envs: int = 2048) -> TrainConfig:
         map="field", envs=n_envs, ep_ticks=6000, n_steps=128, act_every=3, epochs=4, minibatches=8,
         gamma=0.9995, gae=0.95, clip=0.2,
         reward=RewardSpec(mode="coverage", int_coef=0.25, int_cell=256.0, int_view=8, int_speed=8))
+
+
+def race_bench_config(n_envs: int = 2048) -> TrainConfig:
+    """The race benchmark (8-GPU config 5, per rank): the procedural linear
+    race track (40 chained ramps, 4 gap jumps over teleport fail nets, a
+    finish curtain), the GPU Bellman-Ford geodesic bake over the free voxels
+    at 16u, potential shaping on the geodesic distance to the finish with a
+    15 s stall kill, and the benchmark's network, PPO settings and curiosity."""
+    return TrainConfig(
+        map="race", envs=n_envs, ep_ticks=6000, spawn="pool", n_steps=128, act_every=3, epochs=4, minibatches=8,
+        gamma=0.9995, gae=0.95, clip=0.2, lidar_cell=16.0,
+        reward=RewardSpec(mode="race", int_coef=0.25, int_cell=256.0, int_view=8, int_speed=8, stall_secs=15.0))

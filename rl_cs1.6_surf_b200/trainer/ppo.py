@@ -154,6 +154,7 @@ class Trainer:
             raise ValueError(f"env_device must be cpu or cuda, got {cfg.env_device!r}")
         self.bounds = self.core.map_bounds()
         self.field = None
+        self.field_bake_ms = None          # host-timed goal-field bake (occupancy + geodesic), race only
         self.d0 = None
         if cfg.reward.mode == "race":
             from ..ops.geodesic import bake_goal_field, euclid_goal_field
@@ -164,8 +165,12 @@ class Trainer:
                 gmins, gx, gy, gz = grid_dims(mn, mx, gcell)
                 self.field = euclid_goal_field(end, gmins, gcell, (gx, gy, gz), device=self.device)
             else:
+                t_bake = time.perf_counter()
                 self.field = bake_goal_field(self.core, end, cell=gcell, device=self.device if self.gpu else "cpu",
                                              kill_aware=cfg.race_kill_aware)
+                if self.gpu:
+                    torch.cuda.synchronize(self.device)
+                self.field_bake_ms = 1e3 * (time.perf_counter() - t_bake)
             start = pool["origin"] if pool is not None else np.array([s[0] for s in self.core.spawns()])
             d_start = self.field.sample(start)
             ok = d_start < self.field.valid_max
