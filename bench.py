@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--env-device", choices=["cpu", "cuda"], default="cpu",
                     help="cpu: C++ env threads + pinned rows (the headline); cuda: the same env rules on the GPU")
+    ap.add_argument("--env-groups", type=int, default=None,
+                    help="rollout env groups alternating host stepping with GPU work (default: the config's)")
     ap.add_argument("--race", action="store_true",
                     help="the race configuration (config 5: race track, geodesic potential, 2048 envs per GPU)")
     ap.add_argument("--json", default=None)
@@ -121,6 +123,8 @@ def run_ours(args) -> None:
     cfg.seed = 0
     cfg.timing = args.timing or not args.no_phases
     cfg.env_device = args.env_device
+    if args.env_groups:
+        cfg.env_groups = args.env_groups
     tr = Trainer(cfg, rank=rank, world=world, comm=comm, verbose=(rank == 0))
     for _ in range(args.warmup):
         tr.train_iteration()
@@ -177,7 +181,7 @@ def run_ours(args) -> None:
                                "finish curtain), 16u SDF and geodesic grid" if args.race else
                                "procedural random field, 512 brushes, 16u SDF 1024x1024x256"),
                        "comm": args.comm if world > 1 else "none", "cuda_graphs": cfg.graphs,
-                       "env_device": cfg.env_device,
+                       "env_device": cfg.env_device, "env_groups": cfg.env_groups, "env_threads": tr.core.threads,
                        "reward": ("race: potential on the geodesic distance to the finish, 15 s stall kill, + "
                                   "count curiosity 0.25" if args.race else
                                   "coverage (revisit_pen 0.25) + count curiosity 0.25 (256u cell x 8 yaw x 8 speed)"),

@@ -27,6 +27,10 @@ enum Contents : int {
   kCurrent0 = -9, kCurrentDown = -14, kTranslucent = -15, kLadder = -16,
 };
 
+// pm_shared's liquid test (water, slime, lava, sky and the contents between
+// them): the contents for which CheckWater raises the water level
+SURF_HD inline bool contents_liquid(int c) { return c <= kWater && c > kTranslucent; }
+
 #pragma pack(push, 1)
 struct DLump { int32_t offset, length; };
 struct DHeader { int32_t version; DLump lumps[kNumLumps]; };

@@ -171,7 +171,23 @@ bool Map::load_memory(const uint8_t* data, size_t size, std::string* err) {
   for (int k = 0; k < 3; ++k) { world_mins[k] = models[0].mins[k]; world_maxs[k] = models[0].maxs[k]; }
   if (!parse_entities()) return false;
   build_grids();
+  find_liquids();
   return true;
+}
+
+// Every value point_contents can return is a hull-0 leaf's contents (a
+// current mapped to water) or a contents volume's: if none is a liquid, no
+// probe of CheckWater can raise the water level.
+void Map::find_liquids() {
+  any_liquid = false;
+  for (const DClipnode& n : hull0)
+    for (int s = 0; s < 2; ++s) {
+      int c = n.child[s];
+      if (c >= 0) continue;
+      if (c <= kCurrent0 && c >= kCurrentDown) c = kWater;
+      any_liquid |= contents_liquid(c);
+    }
+  for (const BrushEntity& v : volumes) any_liquid |= contents_liquid(v.contents);
 }
 
 namespace {
@@ -352,6 +368,7 @@ MapView Map::view() const {
   v.triggers = span_of(triggers);
   v.spawns = span_of(spawns);
   for (int k = 0; k < 3; ++k) { v.world_mins[k] = world_mins[k]; v.world_maxs[k] = world_maxs[k]; }
+  v.any_liquid = any_liquid;
   for (int h = 0; h < 4; ++h) {
     v.world_grid[h] = grid_meta[h];
     v.world_grid[h].cells = grid_cells[h].empty() ? nullptr : grid_cells[h].data();

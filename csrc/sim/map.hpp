@@ -125,6 +125,11 @@ struct MapView {
   Span<SpawnPoint> spawns;
   float world_mins[3] = {0, 0, 0}, world_maxs[3] = {0, 0, 0};
   HullGrid world_grid[4];             // start-node grids of the world model's hulls
+  // false when no point of the map can have liquid contents (no hull-0 leaf
+  // and no contents volume is water, slime, lava, sky or a current): the
+  // movement's water checks then skip their point-contents probes, whose
+  // result could not change anything
+  bool any_liquid = true;
 
   SURF_HD HullView hull(int model, int bsp_hull) const {
     HullView v;
@@ -167,6 +172,7 @@ class Map {
   std::vector<SpawnPoint> spawns;
 
   float world_mins[3] = {0, 0, 0}, world_maxs[3] = {0, 0, 0};
+  bool any_liquid = true;             // see MapView::any_liquid
 
   // Start-node grids of the world model's hulls 0 (point), 1 (standing) and
   // 3 (crouched), built at load; at most kGridCells cells each.
@@ -177,6 +183,7 @@ class Map {
  private:
   bool parse_entities();
   void build_grids();
+  void find_liquids();
 };
 
 }  // namespace surf

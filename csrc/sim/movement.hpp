@@ -432,13 +432,14 @@ struct Mover {
     fly_move();
   }
 
-  SURF_HD static bool liquid(int c) { return c <= kWater && c > kTranslucent; }
+  SURF_HD static bool liquid(int c) { return contents_liquid(c); }
 
   // CheckWater: sample feet, body centre and eyes for liquid contents.
   SURF_HD void check_water() {
     float p[3];
     waterlevel = 0;
     watertype = kEmpty;
+    if (!map.any_liquid) return;             // no probe could find a liquid (same result)
     p[0] = st->origin[0] + (player_mins(usehull, 0) + player_maxs(usehull, 0)) * 0.5f;
     p[1] = st->origin[1] + (player_mins(usehull, 1) + player_maxs(usehull, 1)) * 0.5f;
     p[2] = st->origin[2] + player_mins(usehull, 2) + 1;

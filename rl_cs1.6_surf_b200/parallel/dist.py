@@ -23,10 +23,60 @@ import torch
 import torch.distributed as dist
 
 
+def physical_cores(cpus) -> list:
+    """``cpus`` grouped by physical core (hyperthread siblings together),
+    from /sys topology; one group per CPU where it cannot be read."""
+    cpus = sorted(cpus)
+    key = {}
+    for c in cpus:
+        try:
+            base = f"/sys/devices/system/cpu/cpu{c}/topology/"
+            with open(base + "physical_package_id") as f:
+                pkg = int(f.read())
+            with open(base + "core_id") as f:
+                core = int(f.read())
+            key[c] = (pkg, core)
+        except (OSError, ValueError):
+            key[c] = ("cpu", c)
+    groups = {}
+    for c in cpus:
+        groups.setdefault(key[c], []).append(c)
+    return sorted(groups.values(), key=lambda g: g[0])
+
+
+def rank_cpu_share(cpus, local_rank: int, local_world: int) -> list:
+    """This local rank's disjoint share of ``cpus``: whole physical cores,
+    contiguous blocks, the remainder spread over the first ranks."""
+    cores = physical_cores(cpus)
+    if local_world <= 1 or len(cores) < local_world:
+        return sorted(cpus)
+    per, extra = divmod(len(cores), local_world)
+    start = local_rank * per + min(local_rank, extra)
+    mine = cores[start:start + per + (1 if local_rank < extra else 0)]
+    return sorted(c for g in mine for c in g)
+
+
+def pin_rank_cpus() -> Optional[list]:
+    """Pin this process (and the env threads it starts later) to its rank's
+    disjoint share of the node's CPUs, so the ranks' simulator pools do not
+    compete for cores (process CPU affinity only). Off with SURF_NO_PIN=1 or
+    with one rank per node. Returns the CPUs pinned to, or None."""
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", "1"))
+    if local_world <= 1 or os.environ.get("SURF_NO_PIN") == "1" or not hasattr(os, "sched_setaffinity"):
+        return None
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    share = rank_cpu_share(os.sched_getaffinity(0), local_rank, local_world)
+    os.sched_setaffinity(0, share)
+    os.environ["SURF_CPUS_PINNED"] = "1"          # default_threads(): the affinity is this rank's share
+    return share
+
+
 def init_process_group(backend: Optional[str] = None, timeout_s: float = 120.0) -> None:
-    """Join the job's process group (env:// rendezvous; 127.0.0.1 default)."""
+    """Join the job's process group (env:// rendezvous; 127.0.0.1 default)
+    and pin this rank to its share of the node's CPUs."""
     if dist.is_initialized():
         return
+    pin_rank_cpus()
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
     os.environ.setdefault("MASTER_PORT", "29533")
     if backend is None:

@@ -237,7 +237,8 @@ class TraceResult:
 
 def default_threads() -> int:
     """Env worker threads: this process's share of the CPUs it may use (the
-    node's ranks, LOCAL_WORLD_SIZE, split them evenly), capped at 64
+    node's ranks, LOCAL_WORLD_SIZE, split them evenly, unless the rank is
+    already pinned to its share), capped at 64
     (overridable via SURF_THREADS). The calling (Python/GPU-driving) thread is
     one of them: it steps the first chunk of envs itself, and the GPU work of
     the other env group was launched before the step."""
@@ -248,7 +249,8 @@ def default_threads() -> int:
         n = len(os.sched_getaffinity(0))
     except AttributeError:   # pragma: no cover
         n = os.cpu_count() or 4
-    local = max(1, int(os.environ.get("LOCAL_WORLD_SIZE", "1")))
+    # a rank pinned to its own CPU share (parallel.dist.pin_rank_cpus) uses all of it
+    local = 1 if os.environ.get("SURF_CPUS_PINNED") == "1" else max(1, int(os.environ.get("LOCAL_WORLD_SIZE", "1")))
     return max(1, min(64, n // local))
 
 

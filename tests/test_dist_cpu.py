@@ -43,3 +43,21 @@ def test_gloo_corrupt_replica_is_detected():
     assert len(reports) == 2, (reports, codes)
     for r, (ok, msg) in reports.items():
         assert ok and msg.startswith("detected"), f"rank {r}: {msg}"
+
+
+def test_rank_cpu_shares_are_disjoint_whole_cores(monkeypatch):
+    """Each local rank gets whole physical cores (hyperthread siblings
+    together), the shares are disjoint and cover every CPU."""
+    from surfb200.parallel import dist as D
+    # 16 logical CPUs = 8 cores x 2 siblings numbered i and i + 8
+    topo = {c: (0, c % 8) for c in range(16)}
+    monkeypatch.setattr(D, "physical_cores", lambda cpus: sorted(
+        [[c for c in sorted(cpus) if topo[c] == k] for k in sorted({topo[c] for c in cpus})], key=lambda g: g[0]))
+    for world in (1, 2, 3, 4, 8):
+        shares = [D.rank_cpu_share(range(16), r, world) for r in range(world)]
+        flat = sorted(c for s in shares for c in s)
+        assert flat == list(range(16))
+        for s in shares:
+            assert all((c + 8) % 16 in s for c in s)          # siblings stay together
+        if world == 8:
+            assert shares[0] == [0, 8] and shares[7] == [7, 15]
