@@ -6,16 +6,36 @@
 // the kernels below then read and write the peers' memory directly with
 // plain loads/stores over NVLink/NVSwitch. No TMA, no multicast.
 //
+// Gradients cross NVLink in bf16: every rank publishes a bf16 copy of its
+// fp32 gradient (the peers read it) and sums the W copies of its own shard
+// in fp32, in rank order.
+//
+// Buckets (overlap with the backward pass): a contiguous range of the
+// gradient that is final before the backward ends (the tower and FC weights,
+// whose gradients come before the convolutions') is reduced by three small
+// kernels launched on a side stream while the backward continues:
+//   publish  convert the bucket of my gradient to bf16;
+//   flag     release "bucket b published" to every peer;
+//   reduce   wait for every peer's flag, then sum my shard's part of the
+//            bucket from the W bf16 copies into my fp32 gradient, with
+//            per-block sums of squares kept for the clip.
+// None of them waits on another kernel of this GPU (only on peers' flags),
+// and the reduce blocks wait independently, so they need no co-residency.
+//
 // Gradient step: ONE cooperative kernel (co-residency guaranteed by the
 // cooperative launch attribute, so in-kernel grid barriers are safe; the
-// launch is graph-capturable):
-//   A  barrier-in: tell every peer "my gradient is final"; wait for all.
-//   B  reduce-scatter: rank r sums shard r of all W gradients (fixed rank
-//      order, fp32, several float4 groups per thread in flight) into its
-//      own gradient buffer; per-block sums of squares (fp64); each block
-//      then arrives on a counter and goes on (no grid-wide wait).
-//   C  the block that arrives last adds the block sums in block order and
-//      publishes the shard's sum of squares to every peer; every block
+// launch is graph-capturable), for the rest of the gradient:
+//   A  publish the bf16 copy of the ranges outside the buckets; the block
+//      that finishes last tells every peer "my gradient is final"; every
+//      block waits for all peers.
+//   B  reduce-scatter of those ranges: rank r sums shard r of the W bf16
+//      gradients (fixed rank order, fp32 accumulation, several 16-byte
+//      groups per thread in flight) into its own fp32 gradient buffer;
+//      per-block sums of squares (fp64); each block then arrives on a
+//      counter and goes on (no grid-wide wait).
+//   C  the block that arrives last adds the block sums in block order (and
+//      the buckets' block sums after them) and publishes the shard's sum of
+//      squares to every peer; every block
 //      waits for all W shard norms and forms the clip coefficient (same
 //      values, same order on every rank, so every rank clips identically).
 //   D  Adam on the owned shard (m, v local); the new bf16 parameters are
@@ -58,6 +78,7 @@ namespace {
 constexpr int kMaxW = 8;
 constexpr int kMaxBlocks = 1024;
 constexpr int kMaxMom = 256;
+constexpr int kMaxB = 2;            // overlapped gradient buckets
 
 // Sync block layout (uint64 words, one block per rank, zeroed at start).
 enum : int {
@@ -68,10 +89,12 @@ enum : int {
   kProf = 112,                       // phase timestamps of the last gradient step (block 0)
   kPartial = 128,                    // [kMaxBlocks] doubles
   kMomSlots = kPartial + kMaxBlocks, // [2][kMaxW][kMaxMom] doubles
-  kSyncWords = kMomSlots + 2 * kMaxW * kMaxMom,
+  kBFlags = kMomSlots + 2 * kMaxW * kMaxMom,   // [kMaxB][kMaxW] "bucket published" flags
+  kBPartial = kBFlags + kMaxB * kMaxW,         // [kMaxB][kMaxBlocks] doubles: bucket reduce block sums
+  kSyncWords = kBPartial + kMaxB * kMaxBlocks,
 };
 enum : int { kFReady = 0, kFNorm = 1, kFDone = 2, kFMom = 3, kFCntReady = 4, kFCntDone = 5 };
-enum : int { kBarGrad1 = 0, kBarGrad2 = 1, kBarCnt = 2 };
+enum : int { kBarGrad1 = 0, kBarGrad2 = 1, kBarCnt = 2, kBarGrad0 = 3 };
 
 __host__ __device__ constexpr int flag_word(int f, int rank) { return kFlags + f * kMaxW + rank; }
 
@@ -85,6 +108,12 @@ struct Plan {
   // gradient step
   int64_t n = 0, shard = 0;
   float* grad_peer[kMaxW] = {};
+  uint16_t* g16_peer[kMaxW] = {};           // every rank's bf16 copy of its gradient (what peers read)
+  int nb = 0;                               // overlapped buckets [b_lo, b_hi)
+  int64_t b_lo[kMaxB] = {}, b_hi[kMaxB] = {};
+  int nf = 1;                               // the rest: ranges [f_lo, f_hi), reduced by the step kernel
+  int64_t f_lo[kMaxB + 1] = {}, f_hi[kMaxB + 1] = {};
+  int bgrid = 296;                          // blocks of a bucket reduce
   float* p_peer[kMaxW] = {};
   uint16_t* p16_peer[kMaxW] = {};
   float* m = nullptr;
@@ -170,6 +199,18 @@ __device__ bool block_wait_all(const Plan& P, int f, uint64_t target, uint64_t c
   return ok != 0;
 }
 
+// Every thread t < world waits for word base + t of the local sync block.
+__device__ bool block_wait_words(const Plan& P, int base, uint64_t target, uint64_t code) {
+  __shared__ int okw;
+  if (threadIdx.x == 0) okw = ld_relaxed_sys_u64(P.sync + kErr) == 0ull;
+  __syncthreads();
+  if (okw && static_cast<int>(threadIdx.x) < P.world) {
+    if (!wait_flag(P.sync + base + threadIdx.x, target, P.sync, P.timeout_ns, code + threadIdx.x)) okw = 0;
+  }
+  __syncthreads();
+  return okw != 0;
+}
+
 __device__ __forceinline__ double block_sum(double s) {
   for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   __shared__ double red[32];
@@ -248,10 +289,114 @@ __device__ __forceinline__ void prof_mark(const Plan& P, int k) {
   if (blockIdx.x == 0 && threadIdx.x == 0) P.sync[kProf + k] = globaltimer();
 }
 
-__device__ __forceinline__ void add4(float4& a, const float4& b) { a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w; }
-__device__ __forceinline__ double sq4(const float4& a) {
-  return static_cast<double>(a.x) * a.x + static_cast<double>(a.y) * a.y + static_cast<double>(a.z) * a.z +
-         static_cast<double>(a.w) * a.w;
+// bf16 copy of gradient[lo, hi) (lo, hi multiples of 8) into this rank's published buffer
+__device__ void publish_range(const Plan& P, int64_t lo, int64_t hi, int64_t tid, int64_t stride) {
+  const float* g = P.grad_peer[P.rank];
+  uint16_t* o = P.g16_peer[P.rank];
+  for (int64_t j = lo / 8 + tid; j < hi / 8; j += stride) {
+    const float4 a = reinterpret_cast<const float4*>(g)[2 * j];
+    const float4 b = reinterpret_cast<const float4*>(g)[2 * j + 1];
+    reinterpret_cast<uint4*>(o)[j] = make_uint4(surfk::pack_bf16x2(a.x, a.y), surfk::pack_bf16x2(a.z, a.w),
+                                                surfk::pack_bf16x2(b.x, b.y), surfk::pack_bf16x2(b.z, b.w));
+  }
+}
+
+__device__ __forceinline__ void add_bf16x8(float* acc, const uint4& w) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    acc[2 * k] += __uint_as_float(u[k] << 16);
+    acc[2 * k + 1] += __uint_as_float(u[k] & 0xFFFF0000u);
+  }
+}
+
+// fp32 sum of the W gradients over [lo, hi) (multiples of 8), rank order
+// 0..W-1, into this rank's fp32 gradient: the peers' terms from their
+// published bf16 copies, this rank's own term in fp32 (each element is
+// reduced by its owner only, so the mix is the same wherever it is read);
+// returns the thread's sum of squares. kU 16-byte groups per peer in
+// flight per thread.
+template <int W, int kU>
+__device__ double reduce_range(const Plan& P, int64_t lo, int64_t hi, int64_t tid, int64_t stride) {
+  double ss = 0.0;
+  float* mine = P.grad_peer[P.rank];
+  const int64_t j_lo = lo / 8, j_hi = hi / 8;
+  for (int64_t j0 = j_lo + tid; j0 < j_hi; j0 += stride * kU) {
+    uint4 v[W][kU];
+    float4 own[2][kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t j = j0 + u * stride;
+      if (j < j_hi) {
+#pragma unroll
+        for (int q = 0; q < W; ++q)
+          if (q != P.rank) v[q][u] = reinterpret_cast<const uint4*>(P.g16_peer[q])[j];
+        own[0][u] = reinterpret_cast<const float4*>(mine)[2 * j];
+        own[1][u] = reinterpret_cast<const float4*>(mine)[2 * j + 1];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t j = j0 + u * stride;
+      if (j < j_hi) {
+        float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int q = 0; q < W; ++q) {
+          if (q == P.rank) {
+            a[0] += own[0][u].x; a[1] += own[0][u].y; a[2] += own[0][u].z; a[3] += own[0][u].w;
+            a[4] += own[1][u].x; a[5] += own[1][u].y; a[6] += own[1][u].z; a[7] += own[1][u].w;
+          } else {
+            add_bf16x8(a, v[q][u]);
+          }
+        }
+        reinterpret_cast<float4*>(mine)[2 * j] = make_float4(a[0], a[1], a[2], a[3]);
+        reinterpret_cast<float4*>(mine)[2 * j + 1] = make_float4(a[4], a[5], a[6], a[7]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ss += static_cast<double>(a[k]) * a[k];
+      }
+    }
+  }
+  return ss;
+}
+
+// ---- overlapped buckets ----------------------------------------------------------------------
+__global__ void __launch_bounds__(128) bucket_publish_kernel(Plan P, int b) {
+  if (ld_relaxed_sys_u64(P.sync + kErr) != 0ull) return;
+  publish_range(P, P.b_lo[b], P.b_hi[b], blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x,
+                static_cast<int64_t>(gridDim.x) * blockDim.x);
+}
+
+// runs after the publish kernel in stream order: its bf16 copy is complete
+__global__ void bucket_flag_kernel(Plan P, int b) {
+  if (ld_relaxed_sys_u64(P.sync + kErr) != 0ull) return;
+  const uint64_t target = P.sync[kSeqGrad] + 1;
+  fence_acq_rel_sys();
+  if (static_cast<int>(threadIdx.x) < P.world)
+    st_release_sys(P.sync_peer[threadIdx.x] + kBFlags + b * kMaxW + P.rank, target);
+}
+
+// small blocks and grid (kBucketThreads x Plan::bgrid): the bucket kernels
+// run beside the backward's kernels (one 320-thread CTA per SM) instead of
+// displacing them
+constexpr int kBucketThreads = 128;
+
+template <int W>
+__global__ void __launch_bounds__(kBucketThreads) bucket_reduce_kernel(Plan P, int b) {
+  constexpr int kU = W <= 2 ? 2 : 1;             // registers: <= 88 per thread at every W
+  double* part = reinterpret_cast<double*>(P.sync + kBPartial) + b * kMaxBlocks;
+  if (ld_relaxed_sys_u64(P.sync + kErr) != 0ull) return;
+  const uint64_t target = P.sync[kSeqGrad] + 1;
+  if (!block_wait_words(P, kBFlags + b * kMaxW, target, 0x800 + 0x10 * b)) return;
+  const int64_t s_lo = static_cast<int64_t>(P.rank) * P.shard;
+  const int64_t s_hi = s_lo + P.shard < P.n ? s_lo + P.shard : P.n;
+  const int64_t lo = s_lo > P.b_lo[b] ? s_lo : P.b_lo[b];
+  const int64_t hi = s_hi < P.b_hi[b] ? s_hi : P.b_hi[b];
+  double ss = 0.0;
+  if (hi > lo && !(P.dbg & 1))
+    ss = reduce_range<W, kU>(P, lo, hi, blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x,
+                             static_cast<int64_t>(gridDim.x) * blockDim.x);
+  const double bs = block_sum(ss);
+  if (threadIdx.x == 0) part[blockIdx.x] = bs;
 }
 
 // ---- gradient step ---------------------------------------------------------------------------
@@ -267,10 +412,14 @@ __global__ void __launch_bounds__(256) grad_step_kernel(Plan P) {
   if (ld_relaxed_sys_u64(sync + kErr) != 0ull) return;
   const uint64_t target = sync[kSeqGrad] + 1;
   const int par = static_cast<int>(target & 1);
+  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   prof_mark(P, 0);
-  // A: barrier-in (the release store orders the gradient, written by the
-  // earlier kernels of this stream, before the flag)
-  if (blockIdx.x == 0 && static_cast<int>(threadIdx.x) < P.world)
+  // A: publish the bf16 copy of the ranges outside the buckets; the last
+  // block to finish releases "ready" to every peer (system-scope release of
+  // every block's copy), then every block waits for all peers
+  for (int f = 0; f < P.nf; ++f) publish_range(P, P.f_lo[f], P.f_hi[f], tid, stride);
+  if (arrive_last(sync, kBarGrad0, true) && static_cast<int>(threadIdx.x) < P.world)
     st_release_sys(P.sync_peer[threadIdx.x] + flag_word(kFReady, P.rank), target);
   if (!block_wait_all(P, kFReady, target, 0x100)) return;
   prof_mark(P, 1);
@@ -278,42 +427,16 @@ __global__ void __launch_bounds__(256) grad_step_kernel(Plan P) {
   const int64_t lo = static_cast<int64_t>(P.rank) * P.shard;
   const int64_t hi = lo + P.shard < P.n ? lo + P.shard : P.n;
   const int64_t cnt = hi > lo ? hi - lo : 0;
-  // 4-element groups (the shard start is 32-byte aligned): one float4 per
-  // thread and array, so every warp-wide load or store (peer memory
-  // included) covers 512 contiguous bytes
+  // 4-element groups (the shard start is 32-byte aligned) for Adam below
   const int64_t n4 = cnt >> 2;
-  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   float* mine = P.grad_peer[P.rank];
-  // B: reduce-scatter of the owned shard (rank order 0..W-1 in every sum)
+  // B: reduce-scatter of the owned shard outside the buckets (rank order
+  // 0..W-1 in every sum, fp32 accumulation of the bf16 copies)
   double ss = 0.0;
-  for (int64_t j0 = tid; j0 < ((P.dbg & 1) ? 0 : n4); j0 += stride * kU) {
-    float4 v[W][kU];
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int64_t j = j0 + u * stride;
-      if (j < n4) {
-#pragma unroll
-        for (int q = 0; q < W; ++q) v[q][u] = *reinterpret_cast<const float4*>(P.grad_peer[q] + lo + 4 * j);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int64_t j = j0 + u * stride;
-      if (j < n4) {
-        float4 a = v[0][u];
-#pragma unroll
-        for (int q = 1; q < W; ++q) add4(a, v[q][u]);
-        *reinterpret_cast<float4*>(mine + lo + 4 * j) = a;
-        ss += sq4(a);
-      }
-    }
-  }
-  for (int64_t i = lo + 4 * n4 + tid; i < hi; i += stride) {
-    float a = P.grad_peer[0][i];
-    for (int q = 1; q < W; ++q) a += P.grad_peer[q][i];
-    mine[i] = a;
-    ss += static_cast<double>(a) * a;
+  for (int f = 0; f < P.nf && !(P.dbg & 1); ++f) {
+    const int64_t a = lo > P.f_lo[f] ? lo : P.f_lo[f];
+    const int64_t e = hi < P.f_hi[f] ? hi : P.f_hi[f];
+    if (e > a) ss += reduce_range<W, kU>(P, a, e, tid, stride);
   }
   const double bs = block_sum(ss);
   double* partial = reinterpret_cast<double*>(sync + kPartial);
@@ -327,6 +450,12 @@ __global__ void __launch_bounds__(256) grad_step_kernel(Plan P) {
     // thread t adds blocks t, t+256, ... then a fixed-shape tree
     double part = 0.0;
     for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) part += partial[b];
+    // the overlapped buckets' block sums, bucket by bucket (their kernels
+    // finished before this one: stream order)
+    for (int bk = 0; bk < P.nb; ++bk) {
+      const double* bp = reinterpret_cast<const double*>(sync + kBPartial) + bk * kMaxBlocks;
+      for (int b = threadIdx.x; b < P.bgrid; b += blockDim.x) part += bp[b];
+    }
     const double tot_b = block_sum(part);
     __shared__ double s_tot;
     if (threadIdx.x == 0) s_tot = tot_b;
@@ -370,9 +499,7 @@ __global__ void __launch_bounds__(256) grad_step_kernel(Plan P) {
     p4.w = adam1(g4.w, m4.w, v4.w, p4.w);
     return p4;
   };
-  auto pack2 = [](float a, float b) {
-    return static_cast<uint32_t>(surfk::f32_to_bf16(a)) | (static_cast<uint32_t>(surfk::f32_to_bf16(b)) << 16);
-  };
+  auto pack2 = [](float a, float b) { return surfk::pack_bf16x2(a, b); };
   for (int64_t j0 = tid; j0 < ((P.dbg & 2) ? 0 : n4); j0 += stride * kUA) {
     float4 g4[kUA], m4[kUA], v4[kUA], p4[kUA];
 #pragma unroll
@@ -499,6 +626,20 @@ __global__ void __launch_bounds__(256) counts_merge_kernel(Plan P) {
   for (int64_t i = 4 * nv + tid; i < P.cn; i += stride) d[i] = 0;
 }
 
+using BucketKernel = void (*)(Plan, int);
+BucketKernel bucket_kernel_for(int world) {
+  switch (world) {
+    case 1: return bucket_reduce_kernel<1>;
+    case 2: return bucket_reduce_kernel<2>;
+    case 3: return bucket_reduce_kernel<3>;
+    case 4: return bucket_reduce_kernel<4>;
+    case 5: return bucket_reduce_kernel<5>;
+    case 6: return bucket_reduce_kernel<6>;
+    case 7: return bucket_reduce_kernel<7>;
+    default: return bucket_reduce_kernel<8>;
+  }
+}
+
 using GradKernel = void (*)(Plan);
 GradKernel grad_kernel_for(int world) {
   switch (world) {
@@ -611,6 +752,11 @@ SURF_EXPORT void* surf_p2p_create(int rank, int world, void* const* sync_peers, 
     if (b >= 1 && b <= m) p->coop_grid = sms * b;
   }
   if (p->coop_grid > kMaxBlocks) p->coop_grid = kMaxBlocks;
+  p->bgrid = sms / 2 > 0 ? sms / 2 : 1;        // bucket kernels: a small footprint beside the backward
+  if (const char* e = std::getenv("SURF_P2P_BUCKET_BLOCKS")) {
+    const int b = std::atoi(e);
+    if (b >= 1 && b <= kMaxBlocks) p->bgrid = b;
+  }
   if (const char* e = std::getenv("SURF_P2P_DBG")) p->dbg = std::atoi(e);
   return p;
 }
@@ -626,8 +772,13 @@ SURF_EXPORT int surf_p2p_set_grad(void* plan, int64_t n, void* const* grad_peers
                                   void* const* p16_peers, float* m, float* v, float* hyper, int64_t push32_from) {
   Plan* P = static_cast<Plan*>(plan);
   if (push32_from < 0 || push32_from % 8) return static_cast<int>(cudaErrorInvalidValue);
+  if (n % 8) return static_cast<int>(cudaErrorInvalidValue);   // 16-byte bf16 groups
   P->n = n;
   P->push32_from = push32_from;
+  P->nb = 0;
+  P->nf = 1;
+  P->f_lo[0] = 0;
+  P->f_hi[0] = n;
   P->shard = surfk::ceil_div(surfk::ceil_div(n, P->world), 8) * 8;   // 32-byte aligned shard starts
   for (int q = 0; q < P->world; ++q) {
     P->grad_peer[q] = static_cast<float*>(grad_peers[q]);
@@ -647,6 +798,55 @@ SURF_EXPORT int surf_p2p_set_grad(void* plan, int64_t n, void* const* grad_peers
 
 SURF_EXPORT int64_t surf_p2p_shard(void* plan) { return static_cast<Plan*>(plan)->shard; }
 
+// Every rank's bf16 gradient copy (n elements each, 16-byte aligned): the
+// buffer the peers read. Required before the first step.
+SURF_EXPORT int surf_p2p_set_grad16(void* plan, void* const* g16_peers) {
+  Plan* P = static_cast<Plan*>(plan);
+  for (int q = 0; q < P->world; ++q) {
+    P->g16_peer[q] = static_cast<uint16_t*>(g16_peers[q]);
+    if (!g16_peers[q] || (reinterpret_cast<uintptr_t>(g16_peers[q]) & 15u))
+      return static_cast<int>(cudaErrorMisalignedAddress);
+  }
+  return 0;
+}
+
+// Overlapped buckets: nb (<= 2) sorted, disjoint ranges [lo, hi) of the
+// gradient, boundaries multiples of 8; the step kernel reduces the rest.
+// nb = 0: the step kernel reduces everything.
+SURF_EXPORT int surf_p2p_set_buckets(void* plan, int nb, const int64_t* lo, const int64_t* hi) {
+  Plan* P = static_cast<Plan*>(plan);
+  if (nb < 0 || nb > kMaxB || !P->n || (P->n & 7)) return static_cast<int>(cudaErrorInvalidValue);
+  int64_t prev = 0;
+  for (int b = 0; b < nb; ++b)
+    if (lo[b] < prev || hi[b] <= lo[b] || hi[b] > P->n || (lo[b] & 7) || (hi[b] & 7))
+      return static_cast<int>(cudaErrorInvalidValue);
+    else
+      prev = hi[b];
+  P->nb = nb;
+  P->nf = 0;
+  int64_t at = 0;
+  for (int b = 0; b < nb; ++b) {
+    P->b_lo[b] = lo[b];
+    P->b_hi[b] = hi[b];
+    if (lo[b] > at) { P->f_lo[P->nf] = at; P->f_hi[P->nf] = lo[b]; ++P->nf; }
+    at = hi[b];
+  }
+  if (at < P->n) { P->f_lo[P->nf] = at; P->f_hi[P->nf] = P->n; ++P->nf; }
+  return 0;
+}
+
+// Bucket b is final in this stream's order: publish its bf16 copy, release
+// it to the peers, and reduce my shard's part of it (three launches).
+SURF_EXPORT int surf_p2p_bucket(void* plan, int b, void* stream) {
+  const Plan& P = *static_cast<const Plan*>(plan);
+  if (b < 0 || b >= P.nb || !P.g16_peer[P.rank]) return static_cast<int>(cudaErrorInvalidValue);
+  auto s = static_cast<cudaStream_t>(stream);
+  bucket_publish_kernel<<<P.bgrid, 128, 0, s>>>(P, b);
+  bucket_flag_kernel<<<1, 32, 0, s>>>(P, b);
+  bucket_kernel_for(P.world)<<<P.bgrid, kBucketThreads, 0, s>>>(P, b);
+  SURF_RETURN_LAUNCH();
+}
+
 SURF_EXPORT int surf_p2p_set_counts(void* plan, int64_t n, int* counts, void* const* delta_peers) {
   Plan* P = static_cast<Plan*>(plan);
   P->cn = n;
@@ -660,7 +860,7 @@ SURF_EXPORT int surf_p2p_set_counts(void* plan, int64_t n, int* counts, void* co
 
 SURF_EXPORT int surf_p2p_grad_step(void* plan, void* stream) {
   const Plan& P = *static_cast<const Plan*>(plan);
-  if (!P.n) return static_cast<int>(cudaErrorInvalidValue);
+  if (!P.n || !P.g16_peer[P.rank]) return static_cast<int>(cudaErrorInvalidValue);
   return launch_coop(grad_kernel_for(P.world), P.coop_grid, static_cast<cudaStream_t>(stream), P);
 }
 

@@ -235,6 +235,19 @@ class PolicyNet:
         self.p("log_std").fill_(0.0)
         self.sync_bf16()
 
+    def overlap_range(self):
+        """[lo, hi) of the flat gradient that is final when ``backward_gpu``
+        calls its ``on_towers`` hook (the tower, FC and head weight matrices,
+        stored contiguously after the convolution weights), or None."""
+        if not self.cfg.vision:
+            return None
+        lo = self.offsets["fc.w"][0]
+        names = [n for n, _, _, _, b in self.specs if not b and not n.startswith("conv")]
+        if any(self.offsets[n][0] < lo for n in names) or any(
+                self.offsets[n][0] >= lo for n, *_ in self.specs if n.startswith("conv") and n.endswith(".w")):
+            return None
+        return lo, self.fp32_from
+
     def uses_shift_trunk(self) -> bool:
         from ..ops.conv_shift import Trunk
         return self.device.type == "cuda" and self.shift_conv and Trunk.supported(self.cfg)
@@ -419,9 +432,13 @@ def forward_gpu(net: "PolicyNet", ws: Workspace, scal16: torch.Tensor, img16: Op
     return ws.out[:B]
 
 
-def backward_gpu(net: "PolicyNet", ws: Workspace, scal16: torch.Tensor, B: Optional[int] = None) -> None:
+def backward_gpu(net: "PolicyNet", ws: Workspace, scal16: torch.Tensor, B: Optional[int] = None,
+                 on_towers=None) -> None:
     """Accumulate parameter gradients into net.grad from ws.dout16 (the
-    gradient of the loss w.r.t. the head output, bf16)."""
+    gradient of the loss w.r.t. the head output, bf16). ``on_towers`` is
+    called once the gradients of ``net.overlap_range()`` are final in stream
+    order (before the convolutions' backward) -- the data-parallel step
+    reduces that range on a side stream meanwhile."""
     from ..ops import gemm as G
     cfg = net.cfg
     B = ws.B if B is None else B
@@ -446,6 +463,8 @@ def backward_gpu(net: "PolicyNet", ws: Workspace, scal16: torch.Tensor, B: Optio
             feat = ws.y3[:B * 48].view(B, cfg.flat_conv)
             _wgrad(G, df, feat, net.g("fc.w"), B)
             G.colsum(df, net.g("fc.b"))
+            if on_towers is not None:
+                on_towers()
             # conv3's output gradient lands on its 8 x 16 input grid (row h*12 + w of the
             # dense feature -> h*16 + w), the padding staying zero
             dy3 = ws.dy3[:B * 128]
@@ -462,6 +481,8 @@ def backward_gpu(net: "PolicyNet", ws: Workspace, scal16: torch.Tensor, B: Optio
         feat = ws.y[-1][:last_rows].view(B, cfg.flat_conv)
         _wgrad(G, df, feat, net.g("fc.w"), B)
         G.colsum(df, net.g("fc.b"))
+        if on_towers is not None:
+            on_towers()
         dfeat = ws.dy[-1][:last_rows].view(B, cfg.flat_conv)
         G.gemm(df, w("fc.w"), b_mn=True, out=dfeat, act="relu_grad", aux=feat)
         from ..ops import conv as CV

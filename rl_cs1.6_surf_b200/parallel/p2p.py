@@ -7,10 +7,15 @@ curiosity-count increments and a 48 KB sync block); the handles travel once
 over the process group, after which no library collective runs on the hot
 path:
 
-* ``step``  — reduce-scatter of the gradient over peer loads, global-norm
-  clip, Adam on the owned shard, push of the updated shard to every peer
-  (one cooperative kernel with in-kernel grid barriers, graph-capturable;
-  replaces all-reduce + clip + Adam);
+* ``bucket`` — the gradient range that is final before the backward ends
+  (the tower and FC weights, ~93% of the parameters) is published in bf16
+  and reduce-scattered over peer loads on a side stream while the
+  convolutions' backward runs (``PolicyNet.overlap_range``);
+* ``step``  — reduce-scatter of the rest of the gradient (bf16 over NVLink,
+  fp32 sums), global-norm clip over both parts, Adam on the owned shard,
+  push of the updated shard to every peer (one cooperative kernel with
+  in-kernel grid barriers, graph-capturable; replaces all-reduce + clip +
+  Adam);
 * ``allreduce_moments`` — per-minibatch advantage moments (one block);
 * ``merge_counts`` — curiosity count increments summed into every rank's
   table, then cleared.
@@ -52,6 +57,9 @@ _lib.register(CLIB, {
     "surf_p2p_set_grad": (c_int, [c_void_p, c_int64, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p),
                                   ctypes.POINTER(c_void_p), c_void_p, c_void_p, c_void_p, c_int64]),
     "surf_p2p_shard": (c_int64, [c_void_p]),
+    "surf_p2p_set_grad16": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "surf_p2p_set_buckets": (c_int, [c_void_p, c_int, ctypes.POINTER(c_int64), ctypes.POINTER(c_int64)]),
+    "surf_p2p_bucket": (c_int, [c_void_p, c_int, c_void_p]),
     "surf_p2p_set_counts": (c_int, [c_void_p, c_int64, c_void_p, ctypes.POINTER(c_void_p)]),
     "surf_p2p_grad_step": (c_int, [c_void_p, c_void_p]),
     "surf_p2p_moments": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
@@ -104,6 +112,9 @@ class P2PComm(NcclComm):
         self.push32_from = 0
         self._opt = None
         self._counts = False
+        self.grad16 = None
+        self.nbuckets = 0
+        self._bucketed = set()
 
     # ---- set-up -------------------------------------------------------------------------
     def share(self, t: torch.Tensor) -> list:
@@ -142,6 +153,22 @@ class P2PComm(NcclComm):
         check(L.surf_p2p_set_grad(self.plan, net.numel, _ptr_array(g), _ptr_array(p), _ptr_array(p16), ptr(opt.m),
                                   ptr(opt.v), ptr(opt.hyper), self.push32_from), "surf_p2p_set_grad")
         self.shard = int(L.surf_p2p_shard(self.plan))
+        # the bf16 copy of the gradient that the peers read
+        self.grad16 = torch.zeros(net.numel, dtype=torch.bfloat16, device=self.device)
+        check(L.surf_p2p_set_grad16(self.plan, _ptr_array(self.share(self.grad16))), "surf_p2p_set_grad16")
+        # one overlapped bucket: the range whose gradient is final before the
+        # convolutions' backward (SURF_P2P_OVERLAP=0: none, everything in the step)
+        rng = net.overlap_range() if hasattr(net, "overlap_range") else None
+        if os.environ.get("SURF_P2P_OVERLAP", "1") == "0":
+            rng = None
+        flags = [None] * self.world
+        dist.all_gather_object(flags, rng)
+        if any(f != rng for f in flags):
+            raise P2PError("ranks disagree on the overlapped gradient bucket")
+        if rng is not None:
+            lo, hi = (c_int64 * 1)(rng[0]), (c_int64 * 1)(rng[1])
+            check(L.surf_p2p_set_buckets(self.plan, 1, lo, hi), "surf_p2p_set_buckets")
+            self.nbuckets = 1
         self._opt = opt
         use_counts = reward is not None and reward.spec.int_coef > 0 and torch.is_tensor(reward.counts)
         flags = [None] * self.world
@@ -166,9 +193,20 @@ class P2PComm(NcclComm):
             return super().allreduce_moments(moments)
         check(L.surf_p2p_moments(self.plan, ptr(moments), n, stream_ptr(moments.device)), "surf_p2p_moments")
 
+    def bucket(self, b: int = 0) -> None:
+        """Bucket b's gradient is final in the current stream's order: publish,
+        release and reduce it there (launch on a side stream to overlap)."""
+        check(_lib.lib(CLIB).surf_p2p_bucket(self.plan, int(b), stream_ptr(self.device)), "surf_p2p_bucket")
+        self._bucketed.add(int(b))
+
     def step(self, net, opt) -> None:
         if self._opt is None:
             raise P2PError("P2PComm.step before attach()")
+        # a bucket nobody launched during the backward is reduced here, in order
+        for b in range(self.nbuckets):
+            if b not in self._bucketed:
+                self.bucket(b)
+        self._bucketed.clear()
         check(_lib.lib(CLIB).surf_p2p_grad_step(self.plan, stream_ptr(net.flat.device)), "surf_p2p_grad_step")
 
     def merge_counts(self, reward) -> None:

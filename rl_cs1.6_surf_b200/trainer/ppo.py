@@ -680,11 +680,28 @@ class Trainer:
                    self.adv.view(-1), self.ret.view(-1), idx, self.mom_mb[m], self.heads, self.net.p("log_std"),
                    self.coef, float(mb * self.world), self.ws_upd.dout, self.net.g("log_std"), self.loss_stats)
         G.to_bf16(self.ws_upd.dout, self.ws_upd.dout16)
-        backward_gpu(self.net, self.ws_upd, self.scal_mb)
+        hook = None
+        if self.comm is not None and getattr(self.comm, "nbuckets", 0):
+            # the tower / FC gradient is reduced across ranks on a side stream
+            # while the convolutions' backward runs on this one
+            main, side = torch.cuda.current_stream(self.device), self._side_stream()
+
+            def hook():
+                side.wait_stream(main)
+                with torch.cuda.stream(side):
+                    self.comm.bucket(0)
+        backward_gpu(self.net, self.ws_upd, self.scal_mb, on_towers=hook)
+        if hook is not None:
+            torch.cuda.current_stream(self.device).wait_stream(self._side_stream())
         if self.comm is not None:
-            self.comm.step(self.net, self.opt)          # fused all-reduce + clip + Adam
+            self.comm.step(self.net, self.opt)          # fused reduce-scatter (rest) + clip + Adam + push
         else:
             self.opt.step()
+
+    def _side_stream(self):
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(self.device)
+        return self._side
 
     def _epoch_body(self) -> None:
         self._epoch_prologue()

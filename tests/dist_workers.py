@@ -160,9 +160,12 @@ def p2p_collectives(rank: int, world: int, port: int, q) -> None:
     def body():
         import torch
         import torch.distributed as dist
+        import ctypes
+
         import surfb200  # noqa: F401
+        from surfb200.ops import _lib
         from surfb200.parallel.dist import init_process_group
-        from surfb200.parallel.p2p import P2PComm
+        from surfb200.parallel.p2p import CLIB, P2PComm
         torch.cuda.set_device(rank)
         init_process_group("nccl", timeout_s=60)
         dev = torch.device("cuda", rank)
@@ -180,7 +183,7 @@ def p2p_collectives(rank: int, world: int, port: int, q) -> None:
         class Rew:
             pass
 
-        n = 1_000_003
+        n = 1_000_000                    # a multiple of 8: 16-byte bf16 groups
         gen = torch.Generator().manual_seed(0)
         net = Net()
         net.numel = n
@@ -204,12 +207,26 @@ def p2p_collectives(rank: int, world: int, port: int, q) -> None:
         p_ref = net.flat.clone()
         m_ref = torch.zeros(n, device=dev)
         v_ref = torch.zeros(n, device=dev)
+        owner = torch.arange(n, device=dev) // comm.shard
         graph = None
-        for step in range(1, 5):
+        L = _lib.lib(CLIB)
+        side = torch.cuda.Stream()
+        for step in range(1, 9):
+            if step == 5:
+                # from here on the range [200_000, 600_000) is an overlapped
+                # bucket, launched on a side stream like the trainer does
+                lo, hi = (ctypes.c_int64 * 1)(200_000), (ctypes.c_int64 * 1)(600_000)
+                assert L.surf_p2p_set_buckets(comm.plan, 1, lo, hi) == 0
+                comm.nbuckets = 1
+                graph = None
             g_local = torch.randn(n, generator=torch.Generator().manual_seed(100 * step + rank)).to(dev) * 0.01
             allg = [torch.empty_like(g_local) for _ in range(world)]
             dist.all_gather(allg, g_local)
-            gsum = torch.stack(allg).sum(0)
+            # the kernels' sum: rank order, fp32, each element's owner adds its
+            # own term in fp32 and the peers' through their bf16 copies
+            gsum = torch.zeros(n, device=dev)
+            for q in range(world):
+                gsum += torch.where(owner == q, allg[q], allg[q].to(torch.bfloat16).float())
             norm = float(gsum.double().norm())
             coef = min(1.0, max_norm / (norm + 1e-6))
             gc = gsum * coef
@@ -220,15 +237,25 @@ def p2p_collectives(rank: int, world: int, port: int, q) -> None:
 
             net.grad.copy_(g_local)
             torch.cuda.synchronize()
-            if step <= 2:
-                comm.step(net, opt)                       # eager launches
+
+            def fused_step():
+                if comm.nbuckets:
+                    main = torch.cuda.current_stream()
+                    side.wait_stream(main)
+                    with torch.cuda.stream(side):
+                        comm.bucket(0)
+                    main.wait_stream(side)
+                comm.step(net, opt)
+
+            if step in (1, 2, 5, 6):
+                fused_step()                               # eager launches
             else:
                 if graph is None:                          # the trainer replays the step inside CUDA graphs
                     s = torch.cuda.Stream()
                     s.wait_stream(torch.cuda.current_stream())
                     graph = torch.cuda.CUDAGraph()
                     with torch.cuda.graph(graph, stream=s):
-                        comm.step(net, opt)
+                        fused_step()
                     torch.cuda.synchronize()
                 graph.replay()
             torch.cuda.synchronize()

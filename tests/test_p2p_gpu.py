@@ -1,11 +1,13 @@
 """Peer-memory collectives (csrc/comm/p2p.cu).
 
-Single GPU: a one-rank plan must reproduce the fused clip + Adam kernel, and
+Single GPU: a one-rank plan must reproduce the fused clip + Adam kernel (its
+own gradient term is read in fp32), and
 a wait on a flag that no peer ever sets must run out after its short limit
 and report an error status while the context stays usable. Two or more GPUs:
-two NCCL ranks compare the fused reduce-scatter / clip / Adam / push step,
-the moments all-reduce and the count merge with plain torch (eager and
-inside a CUDA graph).
+two NCCL ranks compare the fused reduce-scatter / clip / Adam / push step
+(peer terms in bf16, without and with the overlapped bucket launched on a
+side stream), the moments all-reduce and the count merge with plain torch
+(eager and inside CUDA graphs).
 """
 import ctypes
 from ctypes import c_int64, c_void_p
@@ -34,8 +36,9 @@ def test_single_rank_step_matches_fused_adam():
     from surfb200.ops.rl import Adam
     L = _lib.lib(P.CLIB)
     dev = torch.device("cuda")
-    n = 300_007
+    n = 300_008                                   # gradients cross NVLink in 16-byte bf16 groups
     flat, grad, flat16, m, v = _buffers(n, dev)
+    g16 = torch.zeros(n, dtype=torch.bfloat16, device=dev)
     hyper = torch.tensor([1e-3, 0.9, 0.999, 1e-5, 0.5, 0.0], device=dev)
     sync = torch.zeros(int(L.surf_p2p_sync_words()), dtype=torch.int64, device=dev)
     plan = L.surf_p2p_create(0, 1, _arr([sync.data_ptr()]), 5.0)
@@ -43,6 +46,7 @@ def test_single_rank_step_matches_fused_adam():
     try:
         assert L.surf_p2p_set_grad(plan, n, _arr([grad.data_ptr()]), _arr([flat.data_ptr()]),
                                    _arr([flat16.data_ptr()]), m.data_ptr(), v.data_ptr(), hyper.data_ptr(), 0) == 0
+        assert L.surf_p2p_set_grad16(plan, _arr([g16.data_ptr()])) == 0
 
         class Net:
             pass
@@ -82,6 +86,8 @@ def test_wait_without_peer_times_out_with_status():
                                    _arr([flat.data_ptr(), peer[0].data_ptr()]),
                                    _arr([flat16.data_ptr(), peer[2].data_ptr()]), m.data_ptr(), v.data_ptr(),
                                    hyper.data_ptr(), 0) == 0
+        g16 = torch.zeros(2, n, dtype=torch.bfloat16, device=dev)
+        assert L.surf_p2p_set_grad16(plan, _arr([g16[0].data_ptr(), g16[1].data_ptr()])) == 0
         before = flat.clone()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
