@@ -6,7 +6,8 @@ eyes uniform in free space (>= 48u from geometry), yaw uniform, pitch uniform
 in [-70, +30] degrees; full-map range with per-ray early exit; near-linear /
 far-compressed depth code. Reports device-timed rays/s (CUDA events, inputs
 larger than L2), the per-ray step census, and the median depth error against
-exact point-hull traces of the simulator.
+exact point-hull traces of the simulator, at the trainer's 2000u range and at
+the full-map range (the headline).
 
     python bench/bench_march.py [--envs 2048] [--iters 20] [--json out.json]
 """
@@ -66,6 +67,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--max-steps", type=int, default=64)
     ap.add_argument("--near", type=float, default=2000.0)
+    ap.add_argument("--trainer-range", type=float, default=2000.0, help="the trainer's camera range (lidar_range)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--check-rays", type=int, default=20000)
     ap.add_argument("--json", default=None)
@@ -82,54 +84,67 @@ def main() -> None:
     torch.cuda.synchronize()
     bake_s = time.time() - tb
     diag = float(np.linalg.norm(np.array(dims) * cell))
-    cam = vision.DepthCamera(vol, args.width, args.height, range_units=diag, near_range=args.near,
-                             max_steps=args.max_steps, dtype=torch.bfloat16, layout=vision.LAYOUT_S2D4)
     # several pose sets, cycled, so consecutive renders do not reuse a warm L2 footprint
     sets = [free_space_poses(vol, args.envs, args.seed + 17 * i) for i in range(4)]
-    out = torch.empty((args.envs, cam.frame), dtype=torch.bfloat16, device="cuda")
-    for i in range(args.warmup):
-        cam.render(sets[i % 4], out=out)
-    torch.cuda.synchronize()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.iters)]
-    for i in range(args.iters):
-        ev[i][0].record()
-        cam.render(sets[i % 4], out=out)
-        ev[i][1].record()
-    torch.cuda.synchronize()
-    ms = sorted(a.elapsed_time(b) for a, b in ev)
-    med = ms[len(ms) // 2]
     rays = args.envs * args.width * args.height
-    steps = torch.empty((args.envs, args.height, args.width), dtype=torch.uint8, device="cuda")
-    cam.render(sets[0], out=out, steps=steps)
-    st = steps.float()
-    # accuracy: exact point-hull traces for a sample of rays of set 0
-    n_chk = min(args.check_rays, rays)
-    lin_cam = vision.DepthCamera(vol, args.width, args.height, range_units=diag, near_range=diag,
-                                 max_steps=args.max_steps)
-    dep = lin_cam.render(sets[0]).reshape(args.envs, args.height, args.width).cpu().numpy() * diag
     pose = sets[0].cpu().numpy()
     rng = np.random.default_rng(0)
+    n_chk = min(args.check_rays, rays)
     sel = rng.integers(0, rays, n_chk)
     e, r, c = sel // (args.width * args.height), (sel // args.width) % args.height, sel % args.width
-    col, row = lin_cam.offsets()
-    eye = pose[e, :3] + np.where(pose[e, 5:6] != 0, [0, 0, 12.0], [0, 0, 17.0])
-    yaw = np.radians(pose[e, 3]) + col[c]
-    pit = np.radians(pose[e, 4]) + row[r]
-    d = np.stack([np.cos(pit) * np.cos(yaw), np.cos(pit) * np.sin(yaw), np.sin(pit)], 1)
-    res = core.trace_batch(eye, eye + d * diag, hull=2)
-    exact = res[:, 0] * diag
-    hit = (res[:, 0] < 0.999) & (res[:, 7] == 0)
-    err = np.abs(dep[e, r, c] - exact)[hit]
+
+    def measure(range_units: float) -> dict:
+        cam = vision.DepthCamera(vol, args.width, args.height, range_units=range_units, near_range=args.near,
+                                 max_steps=args.max_steps, dtype=torch.bfloat16, layout=vision.LAYOUT_S2D4)
+        out = torch.empty((args.envs, cam.frame), dtype=torch.bfloat16, device="cuda")
+        for i in range(args.warmup):
+            cam.render(sets[i % 4], out=out)
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.iters)]
+        for i in range(args.iters):
+            ev[i][0].record()
+            cam.render(sets[i % 4], out=out)
+            ev[i][1].record()
+        torch.cuda.synchronize()
+        ms = sorted(a.elapsed_time(b) for a, b in ev)
+        med = ms[len(ms) // 2]
+        steps = torch.empty((args.envs, args.height, args.width), dtype=torch.uint8, device="cuda")
+        cam.render(sets[0], out=out, steps=steps)
+        st = steps.float()
+        # accuracy: exact point-hull traces of a sample of rays of set 0, hits within the range
+        lin_cam = vision.DepthCamera(vol, args.width, args.height, range_units=range_units, near_range=range_units,
+                                     max_steps=args.max_steps)
+        dep = lin_cam.render(sets[0]).reshape(args.envs, args.height, args.width).cpu().numpy() * range_units
+        col, row = lin_cam.offsets()
+        eye = pose[e, :3] + np.where(pose[e, 5:6] != 0, [0, 0, 12.0], [0, 0, 17.0])
+        yaw = np.radians(pose[e, 3]) + col[c]
+        pit = np.radians(pose[e, 4]) + row[r]
+        d = np.stack([np.cos(pit) * np.cos(yaw), np.cos(pit) * np.sin(yaw), np.sin(pit)], 1)
+        res = core.trace_batch(eye, eye + d * diag, hull=2)
+        exact = res[:, 0] * diag
+        hit = (res[:, 0] < 0.999) & (res[:, 7] == 0) & (exact < range_units)
+        err = np.abs(dep[e, r, c] - exact)[hit]
+        return {"range": range_units, "rays_per_s": rays / (med * 1e-3), "ms_per_render": med, "ms_min": ms[0],
+                "mean_steps": float(st.mean()), "p50_steps": float(st.median()),
+                "p99_steps": float(torch.quantile(st.flatten()[::97], 0.99)),
+                "exhausted_frac": float((st >= args.max_steps).float().mean()),
+                # SIMD efficiency of the 16 x 2 pixel warps: mean steps / longest ray's steps per warp
+                "warp_step_efficiency": _warp_efficiency(st, args.height, args.width),
+                "median_abs_err_units": float(np.median(err)) if err.size else None,
+                "checked_hits": int(hit.sum())}
+
+    # the trainer's range (TrainConfig.lidar_range) and the whole map (the headline)
+    per_range = [measure(args.trainer_range), measure(diag)]
+    full = per_range[-1]
     result = {
-        "metric": "sdf_rays_per_s", "value": rays / (med * 1e-3), "unit": "rays/s", "ms_per_render": med,
-        "ms_min": ms[0], "rays": rays, "envs": args.envs, "image": [args.height, args.width],
+        "metric": "sdf_rays_per_s", "value": full["rays_per_s"], "unit": "rays/s", "ms_per_render": full["ms_per_render"],
+        "ms_min": full["ms_min"], "rays": rays, "envs": args.envs, "image": [args.height, args.width],
         "grid": list(dims), "cell": cell, "sdf_bytes": int(vol.bricked.numel() * 2), "range": diag,
-        "max_steps": args.max_steps, "mean_steps": float(st.mean()), "p50_steps": float(st.median()),
-        "p99_steps": float(torch.quantile(st.flatten()[::97], 0.99)),
-        "exhausted_frac": float((st >= args.max_steps).float().mean()),
-        # SIMD efficiency of the 16 x 2 pixel warps: mean steps / longest ray's steps per warp
-        "warp_step_efficiency": _warp_efficiency(st, args.height, args.width),
-        "median_abs_err_units": float(np.median(err)) if err.size else None, "checked_hits": int(hit.sum()),
+        "max_steps": args.max_steps, "mean_steps": full["mean_steps"], "p50_steps": full["p50_steps"],
+        "p99_steps": full["p99_steps"], "exhausted_frac": full["exhausted_frac"],
+        "warp_step_efficiency": full["warp_step_efficiency"],
+        "median_abs_err_units": full["median_abs_err_units"], "checked_hits": full["checked_hits"],
+        "per_range": per_range,
         "bake_s": bake_s, "setup_s": time.time() - t0, "gpu": torch.cuda.get_device_name(),
     }
     print(json.dumps(result))
