@@ -209,10 +209,6 @@ __global__ void __launch_bounds__(kShThreads, 1)
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (KIND == kShFwd && ep.bias && threadIdx.x >= 64 && threadIdx.x < 64 + 128) {
-    const int i = threadIdx.x - 64;
-    bias_s[i] = i < a.N / a.nblk ? ep.bias[i] : 0.0f;
-  }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(C::kTmemCols));
@@ -221,6 +217,13 @@ __global__ void __launch_bounds__(kShThreads, 1)
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();          // the previous kernel's outputs (this kernel's inputs) are visible from here on
+  pdl_trigger();
+  if (KIND == kShFwd && ep.bias && threadIdx.x >= 64 && threadIdx.x < 64 + 128) {
+    const int i = threadIdx.x - 64;
+    bias_s[i] = i < a.N / a.nblk ? ep.bias[i] : 0.0f;
+  }
+  __syncthreads();
   // work units of this CTA: FWD tiles; WGRAD (n tile, k split) pairs
   const int nunits = KIND == kShFwd ? a.mt : a.nt * a.splits;
   auto unit_range = [&](int t, int* n0, int* k0, int* nk) {       // WGRAD: n tile and load-unit range of unit t
@@ -684,7 +687,7 @@ int sh_launch(const ShDesc& d, const Epilogue& ep, cudaStream_t s) {
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   const int units = KIND == kShFwd ? a.mt : a.nt * a.splits;
   const int grid = units < sms ? units : sms;
-  kern<<<grid, kShThreads, smem, s>>>(mp[0], mp[1], mp[2], mp[3], mres, a, ep, stages);
+  launch_pdl(kern, dim3(grid), dim3(kShThreads), smem, s, mp[0], mp[1], mp[2], mp[3], mres, a, ep, stages);
   SURF_RETURN_LAUNCH();
 }
 

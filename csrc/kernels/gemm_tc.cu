@@ -215,6 +215,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   fence_after();
   const uint32_t tmem = *tmem_slot;
   const int ntiles = sc.count();
+  pdl_wait();          // the previous kernel's outputs (this kernel's inputs) are visible from here on
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -609,7 +611,7 @@ int launch_cfg(const void* A, int64_t lda, const void* B, int64_t ldb, int M, in
   sc.group = 8;
   const int64_t ntiles = static_cast<int64_t>(sc.mt) * sc.nt * sc.splits;
   const int grid = static_cast<int>(ntiles < static_cast<int64_t>(sms) * resident ? ntiles : static_cast<int64_t>(sms) * resident);
-  kern<<<grid, kThreads, C::kSmem, s>>>(ta, tb, tc, use_tma_c, M, N, sc, ep, cc);
+  launch_pdl(kern, dim3(grid), dim3(kThreads), C::kSmem, s, ta, tb, tc, use_tma_c, M, N, sc, ep, cc);
   SURF_RETURN_LAUNCH();
 }
 

@@ -13,8 +13,10 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "surf_cuda.cuh"
 
@@ -341,7 +343,40 @@ __device__ __forceinline__ void store_chunk32(const Epilogue& ep, const float* v
   }
 }
 
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialization attribute may start while the previous kernel of its
+// stream drains; every thread calls pdl_wait() after its prologue (barrier
+// set-up, tensor-memory allocation) and before it reads any input, which
+// returns once the previous grid has completed and its writes are visible
+// (a no-op for a normal launch). pdl_trigger() lets this kernel's own
+// dependents start their prologues.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- host side ---------------------------------------------------------------
+// Launch with programmatic stream serialization (SURF_NO_PDL=1: plain launch).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("SURF_NO_PDL");
+    return !(e && e[0] == '1');
+  }();
+  return on;
+}
+
+template <typename... Exp, typename... Act>
+cudaError_t launch_pdl(void (*kernel)(Exp...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Act&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Act>(args)...);
+}
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
