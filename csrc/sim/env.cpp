@@ -34,6 +34,7 @@ EnvBatch::EnvBatch(std::shared_ptr<const Map> map, const EnvConfig& cfg, int thr
   const size_t n = static_cast<size_t>(cfg_.num_envs);
   st_.assign(n, PlayerState{});
   memo_.assign(n, StuckMemo{});
+  ground_.assign(n, GroundMemo{});
   last_yd_.assign(n, 0.f);
   last_pd_.assign(n, 0.f);
   rng_.assign(n, 0);
@@ -65,6 +66,7 @@ void EnvBatch::sync_core() {
   copy3(c.goal_max, goal_max_);
   c.st = st_.data();
   c.memo = memo_.data();
+  c.ground = ground_.data();
   c.last_yd = last_yd_.data();
   c.last_pd = last_pd_.data();
   c.rng = rng_.data();

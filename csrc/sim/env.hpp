@@ -88,6 +88,7 @@ class EnvBatch {
   float goal_min_[3] = {0, 0, 0}, goal_max_[3] = {0, 0, 0};
   std::vector<PlayerState> st_;
   std::vector<StuckMemo> memo_;
+  std::vector<GroundMemo> ground_;
   std::vector<float> last_yd_, last_pd_;
   std::vector<uint64_t> rng_;
   std::vector<uint64_t> push_used_;      // per env: bitset over triggers

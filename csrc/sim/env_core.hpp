@@ -128,6 +128,7 @@ struct EnvCore {
   // per-env state
   PlayerState* st = nullptr;
   StuckMemo* memo = nullptr;
+  GroundMemo* ground = nullptr;    // host: per-env categorize cache (null on the GPU)
   float* last_yd = nullptr;
   float* last_pd = nullptr;
   uint64_t* rng = nullptr;
@@ -353,7 +354,8 @@ struct EnvCore {
     envk::copy3(prev_org, s->origin);
     float prev_prog = s->progress;
     // View pitch never enters the movement tick (it aims the sensor only).
-    MoveResult mr = mover.tick(s, &memo[i], s->yaw, 0.0f, fmove, smove, buttons, cfg.phys.msec);
+    MoveResult mr = mover.tick(s, &memo[i], s->yaw, 0.0f, fmove, smove, buttons, cfg.phys.msec,
+                               ground ? &ground[i] : nullptr);
     s->tick++;
     bool fail = false, complete = false;
     if (goal_on) {

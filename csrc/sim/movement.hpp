@@ -44,6 +44,18 @@ static_assert(sizeof(PlayerState) == 108, "PlayerState layout");
 
 struct StuckMemo { int32_t index = 0; int32_t last_tick = 0; };   // CheckStuck bookkeeping
 
+// Host-side cache of one player's last CategorizePosition down-trace. The
+// trace is a pure function of the (static) map, the hull and the start point,
+// so a player whose origin did not change between two categorisations (the
+// end of one tick and the start of the next, while airborne) reuses it; the
+// key is the origin's bit pattern. Nothing needs resetting: a hit returns
+// exactly what the trace would.
+struct GroundMemo {
+  uint32_t key[3] = {0, 0, 0};
+  int32_t hull = -1;
+  Trace tr;
+};
+
 struct MoveResult { int waterlevel = 0; bool blocked = false; };
 
 // Host and device: holds the map view and the physics settings by value, so
@@ -55,7 +67,7 @@ class PlayerMove {
   PlayerMove(const Map& map, const Physics& phys) : map_(map.view()), ph_(phys) {}
   // yaw/pitch in GoldSrc convention (pitch + = down); fmove/smove in units.
   SURF_HD MoveResult tick(PlayerState* st, StuckMemo* memo, float yaw, float pitch, float fmove, float smove,
-                          int buttons, int msec) const;
+                          int buttons, int msec, GroundMemo* ground = nullptr) const;
 
  private:
   MapView map_;
@@ -184,6 +196,7 @@ struct Mover {
   const Physics& ph;
   PlayerState* st;
   StuckMemo* memo;
+  GroundMemo* ground = nullptr;       // host only (null: always trace)
   float frametime = 0, maxspeed = 0, pfriction = 1.0f;
   float angles[3] = {0, 0, 0};
   float forward[3], right[3], up[3];
@@ -460,6 +473,24 @@ struct Mover {
     }
   }
 
+  // The down-trace of categorize(), through the player's GroundMemo if any.
+  SURF_HD void ground_trace(const float* p, Trace* tr) {
+    if (!ground) {
+      trace(usehull, st->origin, p, tr);
+      return;
+    }
+    uint32_t key[3];
+    memcpy(key, st->origin, sizeof key);
+    if (ground->hull == usehull && key[0] == ground->key[0] && key[1] == ground->key[1] && key[2] == ground->key[2]) {
+      *tr = ground->tr;
+      return;
+    }
+    trace(usehull, st->origin, p, tr);
+    ground->hull = usehull;
+    memcpy(ground->key, key, sizeof key);
+    ground->tr = *tr;
+  }
+
   // CategorizePosition: grounded iff a 2u down-trace hits a floor (n_z >= 0.7)
   // and we are not moving up faster than 180 u/s; snap onto it.
   SURF_HD void categorize() {
@@ -470,7 +501,7 @@ struct Mover {
     p[1] = st->origin[1];
     p[2] = st->origin[2] - 2;
     if (st->velocity[2] > 180) { st->onground = -1; return; }
-    trace(usehull, st->origin, p, &tr);
+    ground_trace(p, &tr);
     st->onground = tr.normal[2] < 0.7f ? -1 : tr.ent;
     if (st->onground != -1 && waterlevel < 2 && !tr.startsolid && !tr.allsolid) copy3(st->origin, tr.endpos);
   }
@@ -751,9 +782,10 @@ struct Mover {
 }  // namespace mv
 
 SURF_HD inline MoveResult PlayerMove::tick(PlayerState* st, StuckMemo* memo, float yaw, float pitch, float fmove,
-                                           float smove, int buttons, int msec) const {
+                                           float smove, int buttons, int msec, GroundMemo* ground) const {
   using namespace mv;
   Mover c{map_, ph_, st, memo};
+  c.ground = ground;
   c.usehull = (ph_.enable_duck && st->ducked) ? 1 : 0;
   c.view_ofs = (ph_.enable_duck && st->ducked) ? kViewDuck : kViewStand;
   c.buttons = buttons;
