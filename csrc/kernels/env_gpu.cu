@@ -165,6 +165,7 @@ SURF_EXPORT void* surf_genv_create(const void* host_core, int core_bytes, int* e
   EnvCore& c = g->core;
   c = h;
   for (auto& gr : c.map.world_grid) gr.cells = nullptr;   // host arrays until uploaded below
+  c.ground = nullptr;                                      // the categorize cache is host-only
   int e = 0;
   e = e ? e : upload(&c.map.planes, h.map.planes, g);
   e = e ? e : upload(&c.map.clipnodes, h.map.clipnodes, g);

@@ -354,8 +354,12 @@ struct EnvCore {
     envk::copy3(prev_org, s->origin);
     float prev_prog = s->progress;
     // View pitch never enters the movement tick (it aims the sensor only).
-    MoveResult mr = mover.tick(s, &memo[i], s->yaw, 0.0f, fmove, smove, buttons, cfg.phys.msec,
-                               ground ? &ground[i] : nullptr);
+#if defined(__CUDA_ARCH__)
+    GroundMemo* gm = nullptr;                          // host-only cache
+#else
+    GroundMemo* gm = ground ? &ground[i] : nullptr;
+#endif
+    MoveResult mr = mover.tick(s, &memo[i], s->yaw, 0.0f, fmove, smove, buttons, cfg.phys.msec, gm);
     s->tick++;
     bool fail = false, complete = false;
     if (goal_on) {
