@@ -1,6 +1,8 @@
 // env.cpp — vectorized env. See env.hpp.
 #include "env.hpp"
 
+#include <algorithm>
+
 #include <cmath>
 #include <cstring>
 
@@ -222,12 +224,43 @@ void EnvBatch::step_k_range(int lo, int hi, const int32_t* actions, int action_s
   hi = hi > cfg_.num_envs ? cfg_.num_envs : hi;
   if (hi <= lo) return;
   auto lidar = [this](const PlayerState& s, float* o) { write_lidar(s, o); };
+  const int32_t* order = spatial_order(lo, hi);
   pool_->run(hi - lo, [&](int b, int e) {
-    for (int i = b + lo; i < e + lo; ++i) {
+    for (int j = b; j < e; ++j) {
+      const int i = order[j];
       const int32_t* a = &actions[static_cast<size_t>(i) * static_cast<size_t>(action_stride)];
       core_.step_k_one(i, a, yaw_slot, fail_slot, k, obs, term_obs, rec, term_rec, lidar);
     }
   });
+}
+
+const int32_t* EnvBatch::spatial_order(int lo, int hi) {
+  constexpr int kOrderEvery = 8;          // calls between re-sorts (players move ~100u per call)
+  constexpr float kCell = 256.f;          // Morton cell edge (units)
+  RangeOrder* r = nullptr;
+  for (RangeOrder& o : orders_)
+    if (o.lo == lo && o.hi == hi) r = &o;
+  if (!r) {
+    orders_.push_back(RangeOrder{lo, hi, kOrderEvery, {}});
+    r = &orders_.back();
+  }
+  if (r->age++ < kOrderEvery) return r->idx.data();
+  r->age = 1;
+  std::vector<std::pair<uint32_t, int32_t>> key(static_cast<size_t>(hi - lo));
+  for (int i = lo; i < hi; ++i) {
+    uint32_t c[2];
+    for (int a = 0; a < 2; ++a) {
+      const float f = (st_[static_cast<size_t>(i)].origin[a] - map_->world_mins[a]) / kCell;
+      c[a] = f > 0.f ? (f < 1023.f ? static_cast<uint32_t>(f) : 1023u) : 0u;   // NaN -> 0
+    }
+    uint32_t m = 0;
+    for (int bit = 0; bit < 10; ++bit) m |= ((c[0] >> bit) & 1u) << (2 * bit) | ((c[1] >> bit) & 1u) << (2 * bit + 1);
+    key[static_cast<size_t>(i - lo)] = {m, i};
+  }
+  std::sort(key.begin(), key.end());
+  r->idx.resize(key.size());
+  for (size_t j = 0; j < key.size(); ++j) r->idx[j] = key[j].second;
+  return r->idx.data();
 }
 
 // ---- single-player primitives ------------------------------------------------

@@ -73,6 +73,16 @@ class EnvBatch {
  private:
   void sync_core();
   void write_lidar(const PlayerState& s, float* o) const;
+  // The order step_k_range visits envs [lo, hi) in: Morton order of their
+  // x-y cells, rebuilt every kOrderEvery calls for that range. Neighbouring
+  // envs share clip-tree and start-grid cache lines; no env's result depends
+  // on the order (each env owns its state, memos and random stream).
+  const int32_t* spatial_order(int lo, int hi);
+  struct RangeOrder {
+    int lo = 0, hi = 0, age = 0;
+    std::vector<int32_t> idx;
+  };
+  std::vector<RangeOrder> orders_;
 
   std::shared_ptr<const Map> map_;
   EnvConfig cfg_;
