@@ -47,6 +47,8 @@ def parse():
                     help="cpu: C++ env threads + pinned rows (the headline); cuda: the same env rules on the GPU")
     ap.add_argument("--env-groups", type=int, default=None,
                     help="rollout env groups alternating host stepping with GPU work (default: the config's)")
+    ap.add_argument("--no-async-env", action="store_true",
+                    help="host env: step each group synchronously (no overlap of its launches with env stepping)")
     ap.add_argument("--race", action="store_true",
                     help="the race configuration (config 5: race track, geodesic potential, 2048 envs per GPU)")
     ap.add_argument("--json", default=None)
@@ -125,6 +127,8 @@ def run_ours(args) -> None:
     cfg.env_device = args.env_device
     if args.env_groups:
         cfg.env_groups = args.env_groups
+    if args.no_async_env:
+        cfg.async_env = False
     tr = Trainer(cfg, rank=rank, world=world, comm=comm, verbose=(rank == 0))
     for _ in range(args.warmup):
         tr.train_iteration()
@@ -181,7 +185,7 @@ def run_ours(args) -> None:
                                "finish curtain), 16u SDF and geodesic grid" if args.race else
                                "procedural random field, 512 brushes, 16u SDF 1024x1024x256"),
                        "comm": args.comm if world > 1 else "none", "cuda_graphs": cfg.graphs,
-                       "env_device": cfg.env_device, "env_groups": cfg.env_groups, "env_threads": tr.core.threads,
+                       "env_device": cfg.env_device, "env_groups": cfg.env_groups, "async_env": cfg.async_env, "env_threads": tr.core.threads,
                        "reward": ("race: potential on the geodesic distance to the finish, 15 s stall kill, + "
                                   "count curiosity 0.25" if args.race else
                                   "coverage (revisit_pen 0.25) + count curiosity 0.25 (256u cell x 8 yaw x 8 speed)"),

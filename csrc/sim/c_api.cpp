@@ -97,8 +97,19 @@ SURFSIM_API void surfsim_step_k_range(void* h, int32_t lo, int32_t hi, const int
   ENV(h)->step_k_range(lo, hi, actions, action_stride, yaw_slot, fail_slot, k, RowOut{obs, obs_stride},
                        RowOut{term_obs, term_obs_stride}, RowOut{rec, rec_stride}, RowOut{term_rec, term_rec_stride});
 }
+// step_k_range on the pool's workers; surfsim_step_wait joins it (see EnvBatch).
+SURFSIM_API void surfsim_step_k_range_async(void* h, int32_t lo, int32_t hi, const int32_t* actions,
+                                            int32_t action_stride, int32_t yaw_slot, int32_t fail_slot, int32_t k,
+                                            float* obs, int64_t obs_stride, float* term_obs, int64_t term_obs_stride,
+                                            float* rec, int64_t rec_stride, float* term_rec, int64_t term_rec_stride) {
+  ENV(h)->step_k_range_async(lo, hi, actions, action_stride, yaw_slot, fail_slot, k, RowOut{obs, obs_stride},
+                             RowOut{term_obs, term_obs_stride}, RowOut{rec, rec_stride},
+                             RowOut{term_rec, term_rec_stride});
+}
+SURFSIM_API void surfsim_step_wait(void* h) { ENV(h)->step_wait(); }
 SURFSIM_API PlayerState* surfsim_states_ptr(void* h) { return ENV(h)->states(); }
 SURFSIM_API void surfsim_get_states(void* h, PlayerState* out) {
+  ENV(h)->step_wait();
   std::memcpy(out, ENV(h)->states(), sizeof(PlayerState) * static_cast<size_t>(ENV(h)->num_envs()));
 }
 SURFSIM_API void surfsim_set_state(void* h, int32_t env, const PlayerState* s) { ENV(h)->set_state(env, *s); }

@@ -79,6 +79,7 @@ void EnvBatch::sync_core() {
 }
 
 int EnvBatch::set_waypoints(const float* xyz, int count) {
+  step_wait();
   if (!xyz || count < 2) return -1;
   wp_.assign(xyz, xyz + 3 * count);
   cum_.assign(static_cast<size_t>(count), 0.f);
@@ -124,6 +125,7 @@ int EnvBatch::set_waypoints(const float* xyz, int count) {
 }
 
 int EnvBatch::set_spawn_pool(const PlayerState* pool, int n) {
+  step_wait();
   if (!pool || n < 1) return -1;
   spawn_pool_.assign(pool, pool + n);
   sync_core();
@@ -131,6 +133,7 @@ int EnvBatch::set_spawn_pool(const PlayerState* pool, int n) {
 }
 
 void EnvBatch::set_goal_box(const float* mins, const float* maxs) {
+  step_wait();
   if (!mins || !maxs) {
     goal_on_ = false;
   } else {
@@ -142,12 +145,14 @@ void EnvBatch::set_goal_box(const float* mins, const float* maxs) {
 }
 
 void EnvBatch::force_fail(const uint8_t* mask) {
+  step_wait();
   if (!mask) return;
   for (int i = 0; i < cfg_.num_envs; ++i)
     if (mask[i]) pending_fail_[static_cast<size_t>(i)] = 1;
 }
 
 void EnvBatch::set_state(int env, const PlayerState& s) {
+  step_wait();
   if (env < 0 || env >= cfg_.num_envs) return;
   st_[static_cast<size_t>(env)] = s;
   PlayerState& d = st_[static_cast<size_t>(env)];
@@ -179,6 +184,7 @@ void EnvBatch::write_lidar(const PlayerState& s, float* o) const {
 }
 
 void EnvBatch::reset_all(uint64_t seed, float* obs) {
+  step_wait();
   for (int i = 0; i < cfg_.num_envs; ++i) {
     core_.seed_and_reset(i, seed);
     if (obs) {
@@ -191,6 +197,7 @@ void EnvBatch::reset_all(uint64_t seed, float* obs) {
 
 void EnvBatch::step(const int32_t* actions, float* obs, float* rewards, uint8_t* done, uint8_t* trunc,
                     float* terminal_obs) {
+  step_wait();
   auto lidar = [this](const PlayerState& s, float* o) { write_lidar(s, o); };
   pool_->run(cfg_.num_envs, [&](int b, int e) {
     for (int i = b; i < e; ++i) {
@@ -219,19 +226,35 @@ void EnvBatch::step_k(const int32_t* actions, int action_stride, int yaw_slot, i
 
 void EnvBatch::step_k_range(int lo, int hi, const int32_t* actions, int action_stride, int yaw_slot, int fail_slot,
                             int k, RowOut obs, RowOut term_obs, RowOut rec, RowOut term_rec) {
+  step_k_range_async(lo, hi, actions, action_stride, yaw_slot, fail_slot, k, obs, term_obs, rec, term_rec);
+  step_wait();
+}
+
+void EnvBatch::step_k_range_async(int lo, int hi, const int32_t* actions, int action_stride, int yaw_slot,
+                                  int fail_slot, int k, RowOut obs, RowOut term_obs, RowOut rec, RowOut term_rec) {
+  step_wait();                            // one job in flight at a time
   if (k < 1) k = 1;
   lo = lo < 0 ? 0 : lo;
   hi = hi > cfg_.num_envs ? cfg_.num_envs : hi;
   if (hi <= lo) return;
-  auto lidar = [this](const PlayerState& s, float* o) { write_lidar(s, o); };
   const int32_t* order = spatial_order(lo, hi);
-  pool_->run(hi - lo, [&](int b, int e) {
+  const EnvCore* core = &core_;
+  const EnvBatch* self = this;
+  pool_->run_async(hi - lo, [=](int b, int e) {
+    auto lidar = [self](const PlayerState& s, float* o) { self->write_lidar(s, o); };
     for (int j = b; j < e; ++j) {
       const int i = order[j];
       const int32_t* a = &actions[static_cast<size_t>(i) * static_cast<size_t>(action_stride)];
-      core_.step_k_one(i, a, yaw_slot, fail_slot, k, obs, term_obs, rec, term_rec, lidar);
+      core->step_k_one(i, a, yaw_slot, fail_slot, k, obs, term_obs, rec, term_rec, lidar);
     }
   });
+  in_flight_ = true;
+}
+
+void EnvBatch::step_wait() {
+  if (!in_flight_) return;
+  pool_->wait();
+  in_flight_ = false;
 }
 
 const int32_t* EnvBatch::spatial_order(int lo, int hi) {
@@ -323,6 +346,7 @@ void EnvBatch::pm_step_single(PlayerState* s, const int32_t action[6]) {
 }
 
 void EnvBatch::occupancy_grid(const float* mins, float cell, int nx, int ny, int nz, uint8_t* out) {
+  step_wait();
   pool_->run(nz, [&](int b, int e) {
     for (int iz = b; iz < e; ++iz)
       for (int iy = 0; iy < ny; ++iy)

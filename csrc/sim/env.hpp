@@ -27,6 +27,9 @@ namespace surf {
 class EnvBatch {
  public:
   EnvBatch(std::shared_ptr<const Map> map, const EnvConfig& cfg, int threads);
+  ~EnvBatch() { step_wait(); }            // no worker may outlive the arrays it steps
+  EnvBatch(const EnvBatch&) = delete;
+  EnvBatch& operator=(const EnvBatch&) = delete;
   int obs_dim() const { return obs_dim_; }
   int num_envs() const { return cfg_.num_envs; }
   const EnvConfig& config() const { return cfg_; }
@@ -52,6 +55,14 @@ class EnvBatch {
   // that two halves of the batch can alternate with the GPU work of the other.
   void step_k_range(int lo, int hi, const int32_t* actions, int action_stride, int yaw_slot, int fail_slot, int k,
                     RowOut obs, RowOut term_obs, RowOut rec, RowOut term_rec);
+  // step_k_range on the pool's workers: returns at once; step_wait() joins
+  // the work and returns when it is done. The action and row buffers must
+  // stay untouched (for the envs of the range) until then, and no other
+  // batch call may come in between except step_wait(). Every other entry
+  // point waits first.
+  void step_k_range_async(int lo, int hi, const int32_t* actions, int action_stride, int yaw_slot, int fail_slot,
+                          int k, RowOut obs, RowOut term_obs, RowOut rec, RowOut term_rec);
+  void step_wait();
 
   PlayerState* states() { return st_.data(); }
   void set_state(int env, const PlayerState& s);
@@ -83,6 +94,7 @@ class EnvBatch {
     std::vector<int32_t> idx;
   };
   std::vector<RangeOrder> orders_;
+  bool in_flight_ = false;               // a step_k_range_async job not yet waited for
 
   std::shared_ptr<const Map> map_;
   EnvConfig cfg_;

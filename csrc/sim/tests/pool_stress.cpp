@@ -1,7 +1,8 @@
 // pool_stress.cpp — the env batch's worker pool under a thread sanitizer.
 //
 // The same seed and actions are stepped through one env batch with 1 worker
-// thread and one with 4 (step_k with K = 3, episodes short enough that most
+// thread and one with 4 (step_k with K = 3; the 4-thread batch in two groups
+// through step_k_range_async / step_wait, episodes short enough that most
 // envs autoreset several times); every player state and every output row
 // must be identical. Built with -fsanitize=thread (tests/test_sanitizers.py),
 // any data race between the workers and the caller is reported and fails the
@@ -74,8 +75,17 @@ int main() {
       for (int j = 0; j < 6; ++j) act[static_cast<size_t>(i) * 8 + j] = static_cast<int32_t>(rng() % nvec[j]);
     one.step_k(act.data(), 8, -1, -1, 3, RowOut{o1.data(), 32}, RowOut{t1.data(), 32}, RowOut{r1.data(), kRecCols},
                RowOut{q1.data(), kTermCols});
-    four.step_k(act.data(), 8, -1, -1, 3, RowOut{o4.data(), 32}, RowOut{t4.data(), 32}, RowOut{r4.data(), kRecCols},
-                RowOut{q4.data(), kTermCols});
+    // the 4-thread batch in two groups through the asynchronous entry point,
+    // the caller reading the first group's rows while the second steps
+    four.step_k_range_async(0, 40, act.data(), 8, -1, -1, 3, RowOut{o4.data(), 32}, RowOut{t4.data(), 32},
+                            RowOut{r4.data(), kRecCols}, RowOut{q4.data(), kTermCols});
+    four.step_wait();
+    four.step_k_range_async(40, n, act.data(), 8, -1, -1, 3, RowOut{o4.data(), 32}, RowOut{t4.data(), 32},
+                            RowOut{r4.data(), kRecCols}, RowOut{q4.data(), kTermCols});
+    float first = 0;
+    for (int i = 0; i < 40; ++i) first += r4[static_cast<size_t>(i) * kRecCols];
+    four.step_wait();
+    if (first != first) ++bad;
     if (std::memcmp(one.states(), four.states(), sizeof(PlayerState) * n) != 0 || o1 != o4 || r1 != r4 || q1 != q4)
       ++bad;
   }

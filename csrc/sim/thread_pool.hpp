@@ -10,6 +10,11 @@
 // static per-thread chunks the slowest chunk set the pace -- 3 threads on
 // 1024 envs stepped 24% faster with claimed chunks. Items are independent, so
 // which thread runs which chunk changes no result.
+//
+// run_async() hands a job to the workers only and returns; wait() then makes
+// the caller claim the chunks still open and returns when all are done, so
+// the caller can do other work (launching the GPU's next graph) while the
+// workers step envs.
 #pragma once
 #include <atomic>
 #include <condition_variable>
@@ -43,17 +48,29 @@ class ThreadPool {
   // and the calling thread. Returns when every chunk has finished.
   void run(int n, const std::function<void(int, int)>& fn) {
     if (nthreads_ == 1 || n < 2 * nthreads_) { fn(0, n); return; }
-    {
-      std::lock_guard<std::mutex> g(mu_);
-      job_ = &fn;
-      n_ = n;
-      next_.store(0, std::memory_order_relaxed);
-      pending_.store(nthreads_ - 1, std::memory_order_relaxed);
-      ++generation_;
-    }
-    cv_.notify_all();
+    publish(&fn, n);
     work(fn, n);
     while (pending_.load(std::memory_order_acquire) != 0) std::this_thread::yield();
+  }
+
+  // Start fn over [0, n) on the workers (the pool keeps its own copy of fn)
+  // and return; wait() finishes it. One job at a time: run() and run_async()
+  // must not be called again before wait().
+  void run_async(int n, std::function<void(int, int)> fn) {
+    async_fn_ = std::move(fn);
+    async_n_ = n;
+    if (nthreads_ == 1 || n < 2 * nthreads_) return;      // wait() runs it on the caller
+    publish(&async_fn_, n);
+  }
+  void wait() {
+    if (!async_fn_) return;
+    if (nthreads_ == 1 || async_n_ < 2 * nthreads_) {
+      async_fn_(0, async_n_);
+    } else {
+      work(async_fn_, async_n_);
+      while (pending_.load(std::memory_order_acquire) != 0) std::this_thread::yield();
+    }
+    async_fn_ = nullptr;
   }
 
  private:
@@ -65,6 +82,17 @@ class ThreadPool {
       if (b >= n) break;
       fn(b, b + grain < n ? b + grain : n);
     }
+  }
+  void publish(const std::function<void(int, int)>* fn, int n) {
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      job_ = fn;
+      n_ = n;
+      next_.store(0, std::memory_order_relaxed);
+      pending_.store(nthreads_ - 1, std::memory_order_relaxed);
+      ++generation_;
+    }
+    cv_.notify_all();
   }
   void loop() {
     uint64_t seen = 0;
@@ -90,6 +118,8 @@ class ThreadPool {
   std::condition_variable cv_;
   uint64_t generation_ = 0;
   bool stop_ = false;
+  std::function<void(int, int)> async_fn_;
+  int async_n_ = 0;
   const std::function<void(int, int)>* job_ = nullptr;
   int n_ = 0;
   std::atomic<int> pending_{0};

@@ -180,6 +180,10 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
                                   c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64]),
         "surfsim_step_k_range": (None, [c_void_p, c_int32, c_int32, c_void_p, c_int32, c_int32, c_int32, c_int32,
                                         c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64]),
+        "surfsim_step_k_range_async": (None, [c_void_p, c_int32, c_int32, c_void_p, c_int32, c_int32, c_int32,
+                                              c_int32, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
+                                              c_void_p, c_int64]),
+        "surfsim_step_wait": (None, [c_void_p]),
         "surfsim_states_ptr": (c_void_p, [c_void_p]),
         "surfsim_get_states": (None, [c_void_p, c_void_p]),
         "surfsim_set_state": (None, [c_void_p, c_int32, c_void_p]),
@@ -345,6 +349,22 @@ class SimCore:
                                       c_void_p(obs[0] or None), int(obs[1]), c_void_p(term_obs[0] or None),
                                       int(term_obs[1]), c_void_p(rec[0] or None), int(rec[1]),
                                       c_void_p(term_rec[0] or None), int(term_rec[1]))
+
+    def step_k_range_async(self, lo: int, hi: int, actions_ptr: int, action_stride: int, k: int, *,
+                           yaw_slot: int = -1, fail_slot: int = -1, obs: tuple = (0, 0), term_obs: tuple = (0, 0),
+                           rec: tuple = (0, 0), term_rec: tuple = (0, 0)) -> None:
+        """``step_k_range`` on the simulator's worker threads: returns at once,
+        ``step_wait`` joins the work (the calling thread steps envs too) and
+        returns when it is done. Until then the action rows and output rows of
+        envs [lo, hi) belong to the simulator; every other call waits first."""
+        self.lib.surfsim_step_k_range_async(self._h, int(lo), int(hi), c_void_p(actions_ptr), int(action_stride),
+                                            int(yaw_slot), int(fail_slot), int(k),
+                                            c_void_p(obs[0] or None), int(obs[1]), c_void_p(term_obs[0] or None),
+                                            int(term_obs[1]), c_void_p(rec[0] or None), int(rec[1]),
+                                            c_void_p(term_rec[0] or None), int(term_rec[1]))
+
+    def step_wait(self) -> None:
+        self.lib.surfsim_step_wait(self._h)
 
     def step_k_numpy(self, actions: np.ndarray, k: int, yaw: Optional[np.ndarray] = None,
                      fail: Optional[np.ndarray] = None):

@@ -296,6 +296,7 @@ class Trainer:
             self.stk_grp = [torch.zeros((step, self.img_w), dtype=torch.bfloat16, device=dev) for _ in range(G)] \
                 if self.stacker is not None else None
             self.grp_events = [torch.cuda.Event() for _ in range(G)]
+            self._host_bound = False          # set after each host-env rollout (picks the loop)
             self.ws_upd = Workspace(self.net, self.mb)
             self.perm = torch.zeros(T * N, dtype=torch.int64, device=dev)
             if self.pooled:
@@ -516,14 +517,15 @@ class Trainer:
                 self._group_body(g, t)
         self.grp_events[g].record()
 
-    def _env_step_group(self, g: int) -> None:
+    def _env_step_group(self, g: int, wait: bool = True) -> None:
         lo, hi = self.groups[g]
         h = self.hrec
         base, stride = h.data_ptr(), H_COLS
-        self.core.step_k_range(lo, hi, self.act_pin.data_ptr(), 8, self.K,
-                               yaw_slot=6 if self.layout.continuous_yaw else -1, fail_slot=7,
-                               obs=(base + 4 * C_OBS, stride), term_obs=(base + 4 * C_TOBS, stride),
-                               rec=(base + 4 * C_REC, stride), term_rec=(base + 4 * C_TREC, stride))
+        step = self.core.step_k_range if wait else self.core.step_k_range_async
+        step(lo, hi, self.act_pin.data_ptr(), 8, self.K,
+             yaw_slot=6 if self.layout.continuous_yaw else -1, fail_slot=7,
+             obs=(base + 4 * C_OBS, stride), term_obs=(base + 4 * C_TOBS, stride),
+             rec=(base + 4 * C_REC, stride), term_rec=(base + 4 * C_TREC, stride))
 
     def _env_body(self, g: int, t: int) -> None:
         """GPU env: K ticks of group g's envs with decision t-1's action rows,
@@ -595,17 +597,88 @@ class Trainer:
             return
         for g in range(G):
             self._run_group(g, 0)
+        # The overlapped loop only pays when the host is the bottleneck (it
+        # costs launch latency when env workers share cores with this thread
+        # while the GPU is the slower side): choose it from the previous
+        # rollout's split between waiting for the GPU and stepping envs.
+        if G > 1 and self.cfg.async_env and self._host_bound:
+            wait_s, env_s = self._rollout_host_async()
+        else:
+            wait_s, env_s = self._rollout_host_sync()
+        self._host_bound = wait_s < 0.05 * env_s
+
+    def _rollout_host_sync(self) -> tuple:
+        """One group at a time: wait for its GPU work, step its envs (this
+        thread and the workers), launch its next decision. Returns the seconds
+        spent waiting for the GPU and stepping envs."""
+        T, G = self.T, len(self.groups)
+        tm = self.timer
+        wait_s = env_s = 0.0
         for t in range(T):
             for g in range(G):
+                t0 = time.perf_counter()
                 with tm.phase("wait_gpu"):
                     self.grp_events[g].synchronize()
+                t1 = time.perf_counter()
                 with tm.phase("env"):
                     self._env_step_group(g)
+                t2 = time.perf_counter()
+                wait_s += t1 - t0
+                env_s += t2 - t1
                 if self.cfg.ep_ticks:
                     self._bootstrap_truncations(g, t)
                 self._run_group(g, t + 1)
             self._observe_respawn(t)
             self.global_step += self.N * self.K * self.world
+        return wait_s, env_s
+
+    def _rollout_host_async(self) -> tuple:
+        """The host-env rollout with the next group's env step started on the
+        simulator's workers before this thread launches the finished group's
+        GPU work (truncation bootstrap, graph replay), so those launches
+        overlap env stepping instead of following it -- when the next group's
+        GPU work is already done (the host is the bottleneck); otherwise the
+        launches go first so the GPU stays fed, as in the synchronous loop.
+        Groups own disjoint rows of the action and record buffers; the respawn
+        reservoir reads every env's state, so with it on the first group of a
+        decision starts after the observation."""
+        T, G = self.T, len(self.groups)
+        tm = self.timer
+        seq = [(t, g) for t in range(T) for g in range(G)]
+        started = -1                       # index in seq of the env step in flight
+        wait_s = env_s = 0.0
+
+        def start(i: int) -> None:
+            nonlocal started, wait_s, env_s
+            g2 = seq[i][1]
+            t0 = time.perf_counter()
+            with tm.phase("wait_gpu"):
+                self.grp_events[g2].synchronize()
+            t1 = time.perf_counter()
+            self._env_step_group(g2, wait=False)
+            wait_s += t1 - t0
+            env_s += time.perf_counter() - t1
+            started = i
+
+        start(0)
+        for i, (t, g) in enumerate(seq):
+            t0 = time.perf_counter()
+            with tm.phase("env"):
+                self.core.step_wait()
+            env_s += time.perf_counter() - t0
+            last = g == G - 1
+            if (i + 1 < len(seq) and not (last and self.respawn is not None)
+                    and self.grp_events[seq[i + 1][1]].query()):
+                start(i + 1)
+            if self.cfg.ep_ticks:
+                self._bootstrap_truncations(g, t)
+            self._run_group(g, t + 1)
+            if last:
+                self._observe_respawn(t)
+                self.global_step += self.N * self.K * self.world
+            if i + 1 < len(seq) and started != i + 1:
+                start(i + 1)
+        return wait_s, env_s
 
     def _rollout_device(self) -> None:
         """The rollout with the env on the GPU: every step is device work, so

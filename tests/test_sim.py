@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 from surfb200.sim import mapgen
-from surfb200.sim.core import (NVEC, REC, STATE_DTYPE, EnvConfig, Physics, PlayerState, SimCore, default_config,
+from surfb200.sim.core import (NVEC, REC, REC_COLS, STATE_DTYPE, EnvConfig, Physics, PlayerState, SimCore, default_config,
                                validate_actions)
 from surfb200.sim.parity import RefCore, reference_available
 
@@ -158,6 +158,40 @@ def test_step_k_equals_sequential_steps(field_map):
         np.testing.assert_array_equal(obs_k, o)
         np.testing.assert_array_equal(rec[:, REC["ended"]] > 0, ended)
         np.testing.assert_allclose(rec[:, REC["reward"]], rsum, rtol=0, atol=1e-6)
+
+
+def test_async_group_steps_match_sync(field_map):
+    """Two env groups stepped with step_k_range_async / step_wait (the
+    rollout's overlap of one group's stepping with the other's launches) give
+    the same states and rows as synchronous step_k_range calls."""
+    m, path = field_map
+    n, K = 96, 3
+    cfg = default_config(n, max_episode_ticks=120, spawn_mode=2)
+    a = SimCore(str(path), cfg, threads=3)
+    b = SimCore(str(path), cfg, threads=3)
+    for c in (a, b):
+        c.set_spawn_pool(m.spawn_pool)
+        c.set_teleport_fail(True)
+        c.reset(9)
+    rows = [np.zeros((n, 8), np.int32) for _ in range(2)]
+    outs = [(np.zeros((n, c.obs_dim), np.float32), np.zeros((n, REC_COLS), np.float32)) for c in (a, b)]
+    rng = np.random.default_rng(4)
+    groups = [(0, 40), (40, n)]
+    for _ in range(30):
+        act = random_actions(rng, n)
+        for r in rows:
+            r[:, :6] = act
+        for (lo, hi) in groups:
+            for c, r, (obs, rec), run in ((a, rows[0], outs[0], "async"), (b, rows[1], outs[1], "sync")):
+                kw = dict(obs=(obs.ctypes.data, c.obs_dim), rec=(rec.ctypes.data, REC_COLS))
+                if run == "async":
+                    c.step_k_range_async(lo, hi, r.ctypes.data, 8, K, **kw)
+                else:
+                    c.step_k_range(lo, hi, r.ctypes.data, 8, K, **kw)
+        a.step_wait()
+        assert a.states_view.tobytes() == b.states_view.tobytes()
+        np.testing.assert_array_equal(outs[0][0], outs[1][0])
+        np.testing.assert_array_equal(outs[0][1], outs[1][1])
 
 
 def test_continuous_yaw(field_map):

@@ -36,6 +36,27 @@ def test_vision_ppo_iterations(graphs, cont):
     assert int(a[:, 2].min()) >= 0 and int(a[:, 2].max()) <= 2
 
 
+def test_async_host_rollout_matches_sync():
+    """The overlapped host-env rollout (next group's env step started before
+    this group's launches) fills the rollout buffers bit for bit like the
+    one-group-at-a-time loop: same seed, same config, one rollout each."""
+    def run(async_loop: bool):
+        cfg = TrainConfig(map="field", envs=256, n_steps=12, act_every=3, epochs=1, minibatches=2, ep_ticks=20,
+                          env_groups=2, reward=RewardSpec(mode="coverage", int_coef=0.25, int_view=8, int_speed=8))
+        cfg.async_env = async_loop
+        tr = Trainer(cfg, verbose=False)
+        tr._host_bound = async_loop               # take the overlapped loop from the first rollout on
+        tr.rollout_gpu()
+        torch.cuda.synchronize()
+        out = [t.clone() for t in (tr.b_act, tr.b_rew, tr.b_done, tr.b_img)] + [tr.hrec.clone()]
+        assert tr.global_step == 256 * 12 * 3
+        tr.release_graphs()
+        return out
+
+    for a, b in zip(run(True), run(False)):
+        assert torch.equal(a, b)
+
+
 @pytest.mark.parametrize("stack,mask", [(5, False), (3, True), (1, True)])
 def test_frame_stack_and_surface_mask_training(stack, mask):
     """Rollout composition == update gather (same decision, same bytes), the
