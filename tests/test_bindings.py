@@ -13,7 +13,8 @@ PKG = ROOT / "rl_cs1.6_surf_b200"
 
 def _modules():
     import importlib
-    for name in ("ops.vision", "ops.gemm", "ops.rl", "ops.geodesic", "ops.conv", "ops.framestack", "ops.surfmask",
+    for name in ("ops.vision", "ops.gemm", "ops.rl", "ops.geodesic", "ops.conv", "ops.conv_shift", "ops.framestack",
+                 "ops.surfmask",
                  "rewards.spec", "parallel.p2p", "models.policy", "trainer.ppo"):
         importlib.import_module("surfb200." + name)
 
