@@ -59,29 +59,60 @@ def parse():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """SM clock, power and throttle-reason sampling of this rank's GPU during
+    the timed region, every 100 ms: in-process NVML reads (the library
+    nvidia-smi reports from; read-only queries), or nvidia-smi itself where
+    the NVML binding is missing. An nvidia-smi process per sample costs
+    0.2-0.5 s of CPU each, taken from the rank's CPU share that the host
+    env steps on."""
+
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, index: int):
         self.index = index
-        self.samples = []
+        self.samples = []                  # (sm_mhz, sm_max_mhz, set of active reason names)
         self._stop = threading.Event()
         self._t = None
 
+    def _nvml_reader(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.index)
+            bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+            mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+
+            def read():
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                return (float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)), mx,
+                        {k for k, b in bits.items() if r & b})
+            read()
+            return read
+        except Exception:
+            return None
+
+    def _smi_read(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits"],
+                             capture_output=True, text=True, timeout=5).stdout.strip()
+        s = [x.strip() for x in out.split(",")]
+        num = lambda x: float(x) if x.replace(".", "").isdigit() else None
+        return (num(s[1]), num(s[2]), {self.REASONS[i] for i in range(4) if s[4 + i].lower() == "active"})
+
     def start(self):
         def run():
-            q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_power_cap")
+            read = self._nvml_reader() or self._smi_read
             while not self._stop.is_set():
                 try:
-                    out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits"], capture_output=True, text=True,
-                                         timeout=5).stdout.strip()
-                    if out:
-                        self.samples.append([x.strip() for x in out.split(",")])
+                    self.samples.append(read())
                 except Exception:
                     pass
-                self._stop.wait(0.2)
+                self._stop.wait(0.1)
         self._t = threading.Thread(target=run, daemon=True)
         self._t.start()
 
@@ -91,10 +122,9 @@ class ClockSampler:
             self._t.join(timeout=6)
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = sorted(float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit())
-        mx = max(float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit())
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[4 + i].strip().lower() == "active"})
+        sm = sorted(s[0] for s in self.samples if s[0] is not None)
+        mx = max((s[1] for s in self.samples if s[1] is not None), default=None)
+        reasons = sorted(set().union(*(s[2] for s in self.samples)))
         return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
                 "samples": len(self.samples)}
 

@@ -108,7 +108,7 @@ def write_bench_map(directory: Path, kind: str = "field", seed: int = 0) -> Path
 
 
 def run_reference_bench(args, clock_sampler) -> None:
-    """``clock_sampler(gpu_index)`` is bench.py's nvidia-smi sampler (start / stop -> dict)."""
+    """``clock_sampler(gpu_index)`` is bench.py's clock sampler (start / stop -> dict)."""
     rank, world, local = _dist_env()
     if not (REF / "python" / "train_fast.py").exists() or not (REF / "build" / "libsurfcore.so").exists():
         if rank == 0:
