@@ -191,9 +191,16 @@ def run_ours(args) -> None:
     launches = L.launch_count() - launches0
     # per-phase ms per timed iteration, max over ranks (every rank reports the same fixed key list)
     phases = {k: phase_sum.get(k, 0.0) / args.steps for k in PHASE_KEYS} if phase_sum else {}
+    per_rank = None
     if comm is not None:
         ms = comm.max_scalar(ms)
         wall = comm.max_scalar(wall)
+        if phases:
+            # every rank's rollout / env / update, to show which side sets the pace
+            import torch.distributed as dist
+            got = [None] * world
+            dist.all_gather_object(got, {k: round(phases[k], 1) for k in ("rollout", "env", "update")})
+            per_rank = {k: [g[k] for g in got] for k in ("rollout", "env", "update")}
         phases = {k: comm.max_scalar(v) for k, v in phases.items()}
     ticks_per_iter = cfg.envs * cfg.n_steps * cfg.act_every * world
     value = ticks_per_iter * args.steps / (ms / 1e3)
@@ -228,6 +235,7 @@ def run_ours(args) -> None:
             "gpu_launches": launches,
             "goal_field_bake_ms": round(tr.field_bake_ms, 1) if tr.field_bake_ms is not None else None,
             "phases_ms_per_step": {k: round(v, 2) for k, v in phases.items()} or None,
+            "phases_ms_per_rank": per_rank,
             "last_iteration": {k: v for k, v in stats.items() if k != "timing"},
         }
         line = json.dumps(out)
