@@ -86,7 +86,7 @@ def for_volume(core, volume, device=None) -> Tuple[torch.Tensor, torch.Tensor]:
 
 def surfnz_reference(tris: np.ndarray, mins, cell: float, dims, keep: Optional[np.ndarray] = None) -> np.ndarray:
     """CPU oracle of the claim rule -> int8 [nz, ny, nx] (``keep``: optional
-    per-triangle mask, e.g. the internal-face filter's verdicts)."""
+    per-triangle mask, e.g. the internal-face filter's decisions)."""
     nx, ny, nz = (int(d) for d in dims)
     key = np.zeros((nz, ny, nx), np.uint64)
     tris = np.asarray(tris, np.float32).astype(np.float64).reshape(-1, 3, 3)
