@@ -501,7 +501,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
-          if (lane == 0) tma_store_2d(&tma_c, smem_u32(tile), n0 + c0, m0 + quad * 32);
+          // a remapped output column (cmap): 32-column chunks never straddle a segment
+          const int oc = ep.cmap_in ? ((n0 + c0) / ep.cmap_in) * ep.cmap_out + (n0 + c0) % ep.cmap_in : n0 + c0;
+          if (lane == 0) tma_store_2d(&tma_c, smem_u32(tile), oc, m0 + quad * 32);
           ++stage_ctr;
         }
       } else {
@@ -582,10 +584,12 @@ int launch_cfg(const void* A, int64_t lda, const void* B, int64_t ldb, int M, in
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof tc);
   const int esize = ep.c_dtype == 1 ? 2 : 4;
-  int use_tma_c = ep.c && ep.c_mode == kStore && !ep.ct && !cc.o.on && !ep.cmap_in &&
+  // (a column remap keeps the TMA store when every chunk is whole: N % 32 == 0)
+  const int c_cols = ep.cmap_in ? (N / ep.cmap_in) * ep.cmap_out + N % ep.cmap_in : N;
+  int use_tma_c = ep.c && ep.c_mode == kStore && !ep.ct && !cc.o.on && (!ep.cmap_in || N % 32 == 0) &&
                   ((reinterpret_cast<uintptr_t>(ep.c) & 15) == 0) && ((ep.ldc * esize) % 16 == 0);
   if (use_tma_c)
-    use_tma_c = make_map(&tc, ep.c, N, M, ep.ldc, 32, 32, ep.c_dtype != 1,
+    use_tma_c = make_map(&tc, ep.c, c_cols, M, ep.ldc, 32, 32, ep.c_dtype != 1,
                          ep.c_dtype == 1 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)
                     ? 1
                     : 0;

@@ -77,6 +77,29 @@ def test_split_k_atomic_weight_gradient(splits):
     close(dW, dY.float().t() @ X.float(), 1e-2)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_column_remap_onto_padded_grid(dtype):
+    """cmap = (n_in, n_out): dense column n lands at (n // n_in) * n_out +
+    n % n_in of a wider row (the FC input gradient written onto the trunk's
+    zero-padded grid); the padding columns stay untouched, the saved
+    activation of the derivative epilogue stays dense."""
+    torch.manual_seed(3)
+    M, N, K = 1000, 3072, 512
+    A, B = operands(M, N, K, False, True)
+    aux = rand(M, N)
+    out = torch.full((M, 8192), 7.0, dtype=dtype, device="cuda")
+    G.gemm(A, B, b_mn=True, out=out, act="relu_grad", aux=aux, cmap=(768, 1024))
+    torch.cuda.synchronize()
+    G.check_error_flag("cuda")
+    ref = G.gemm_reference(A, B, b_mn=True, act="relu_grad", aux=aux)
+    cols = torch.arange(N, device="cuda")
+    dst = (cols // 768) * 1024 + cols % 768
+    close(out[:, dst], ref)
+    pad = torch.ones(8192, dtype=torch.bool, device="cuda")
+    pad[dst] = False
+    assert bool((out[:, pad] == 7.0).all())
+
+
 def test_narrow_mn_operand():
     """Weight gradient of a 32-channel layer: an MN-major operand narrower than the 64-wide box."""
     col, dy = rand(8192, 64), rand(8192, 32)
