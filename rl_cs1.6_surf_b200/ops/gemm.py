@@ -46,6 +46,7 @@ _SIG = {
                                  c_void_p, c_void_p]),
     "surf_f32_to_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_void_p]),
     "surf_adam_norm": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
+    "surf_adam_acc_size": (c_int, []),
     "surf_adam_update": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
                                  c_void_p]),
 }

@@ -278,6 +278,9 @@ def ppo_loss_reference(logits_value, value_col: int, act, old_logp, adv, ret, la
 
 
 # ---- optimizer ------------------------------------------------------------------------------
+ADAM_ACC = 2 + 296                 # fp64 slots of surf_adam_norm's accumulator (surf_adam_acc_size)
+
+
 class Adam:
     """Fused clip + Adam over a PolicyNet's flat buffers (GPU), or torch's Adam
     + clip_grad_norm_ over the same flat tensor (CPU)."""
@@ -288,7 +291,11 @@ class Adam:
         self.m = torch.zeros_like(net.flat)
         self.v = torch.zeros_like(net.flat)
         self.hyper = torch.tensor([lr, betas[0], betas[1], eps, max_norm, 0.0], dtype=torch.float32, device=dev)
-        self.acc = torch.zeros(1, dtype=torch.float64, device=dev)
+        # squared norm, arrival counter and per-block partials of surf_adam_norm
+        # (zero once; every launch leaves the counter at zero)
+        self.acc = torch.zeros(ADAM_ACC, dtype=torch.float64, device=dev)
+        if self.acc.is_cuda and _lib.lib(NLIB).surf_adam_acc_size() != ADAM_ACC:
+            raise RuntimeError("libsurf_nn's Adam accumulator size differs from ADAM_ACC: rebuild the extensions")
         self.max_norm = max_norm
 
     @property
@@ -303,7 +310,6 @@ class Adam:
         if net.flat.is_cuda:
             L = _lib.lib(NLIB)
             s = stream_ptr(net.flat.device)
-            self.acc.zero_()
             check(L.surf_adam_norm(ptr(net.grad), net.numel, ptr(self.acc), ptr(self.hyper), s), "surf_adam_norm")
             check(L.surf_adam_update(ptr(net.flat), ptr(net.grad), ptr(self.m), ptr(self.v), ptr(net.flat16),
                                      net.numel, ptr(self.acc), ptr(self.hyper), s), "surf_adam_update")
