@@ -77,8 +77,7 @@ def main():
         def step():
             out = forward_gpu(net, ws, scal, img)
             R.ppo_loss(out, layout.value_col, act, old, adv, ret, idx, mom, heads, net.p("log_std"), coef, float(B),
-                       ws.dout, net.g("log_std"), stats)
-            G.to_bf16(ws.dout, ws.dout16)
+                       ws.dout16, net.g("log_std"), stats)
             backward_gpu(net, ws, scal)
             opt.step()
 

@@ -125,8 +125,7 @@ def main():
     def step():
         out = forward_gpu(net, ws, scal, img)
         R.ppo_loss(out, layout.value_col, act, old_logp, adv, ret, idx, mom, heads, net.p("log_std"), coef, float(B),
-                   ws.dout, net.g("log_std"), stats)
-        G.to_bf16(ws.dout, ws.dout16)
+                   ws.dout16, net.g("log_std"), stats)
         backward_gpu(net, ws, scal)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -190,9 +189,7 @@ def verify(net, ws, layout, heads, scal, img, adv, ret, coef, loss_tol: float = 
     net.grad.zero_()
     out = forward_gpu(net, ws, scal, img)
     R.ppo_loss(out, layout.value_col, act, old_logp, adv, ret, idx, mom, heads, net.p("log_std"), coef, float(B),
-               ws.dout, net.g("log_std"), stats)
-    from surfb200.ops import gemm as G
-    G.to_bf16(ws.dout, ws.dout16)
+               ws.dout16, net.g("log_std"), stats)
     backward_gpu(net, ws, scal)
     torch.cuda.synchronize()
     check_error_flag(dev)

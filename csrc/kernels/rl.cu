@@ -266,13 +266,18 @@ struct LossArgs {
   int* err;             // device error flag (may be null)
 };
 
+// gradient store: fp32, or bf16 (the backward GEMMs' operand; rounded as
+// a separate fp32 -> bf16 conversion would round it)
+__device__ __forceinline__ void st_grad(float* p, float v) { *p = v; }
+__device__ __forceinline__ void st_grad(uint16_t* p, float v) { *p = surfk::f32_to_bf16(v); }
+
 // stats[0..5]: policy loss, value loss, entropy, approx_kl, clip fraction, samples (sums)
-template <typename T>
+template <typename T, typename G>
 __global__ void ppo_loss_kernel(const T* logits, int64_t ld_logits, const float* value, int64_t ld_value,
                                 const int32_t* act, int64_t ld_act, const float* old_logp, const float* adv,
                                 const float* ret, const int64_t* idx, const double* moments, HeadSpec hs,
-                                const float* log_std, LossArgs la, int n, float* dlogits, int64_t ld_dlogits,
-                                float* dvalue, int64_t ld_dvalue, float* dlog_std, float* stats) {
+                                const float* log_std, LossArgs la, int n, G* dlogits, int64_t ld_dlogits,
+                                G* dvalue, int64_t ld_dvalue, float* dlog_std, float* stats) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   float pg = 0, vl = 0, ent = 0, kl = 0, clipped = 0, dls = 0;
@@ -281,8 +286,8 @@ __global__ void ppo_loss_kernel(const T* logits, int64_t ld_logits, const float*
   const bool bad = warp < n && (src < 0 || src >= la.n_src);
   if (bad && lane == 0) surfk::report_error(la.err, surfk::kErrLossIndex);
   if (bad) {                        // no gradient from a row that cannot be read
-    for (int c = lane; c < hs.width; c += 32) dlogits[warp * ld_dlogits + c] = 0.0f;
-    if (lane == 0) dvalue[warp * ld_dvalue] = 0.0f;
+    for (int c = lane; c < hs.width; c += 32) st_grad(dlogits + warp * ld_dlogits + c, 0.0f);
+    if (lane == 0) st_grad(dvalue + warp * ld_dvalue, 0.0f);
   }
   if (warp < n && !bad) {
     const T* row = logits + warp * ld_logits;
@@ -343,15 +348,15 @@ __global__ void ppo_loss_kernel(const T* logits, int64_t ld_logits, const float*
       const float Hh = -warp_sum(lane < sz ? p * lp : 0.0f);
       if (lane < sz) {
         const float onehot = (lane == a[hs.slot[h]]) ? 1.0f : 0.0f;
-        dlogits[warp * ld_dlogits + hs.offset[h] + lane] = g_logp * (onehot - p) + ce * p * (lp + Hh);
+        st_grad(dlogits + warp * ld_dlogits + hs.offset[h] + lane, g_logp * (onehot - p) + ce * p * (lp + Hh));
       }
     }
     if (hs.cont && lane == 0) {
       // d logp/d mu = za/sigma ; d logp/d log_std = za^2 - 1 ; dH/d log_std = 1
-      dlogits[warp * ld_dlogits + hs.cont_col] = g_logp * za * expf(-ls);
+      st_grad(dlogits + warp * ld_dlogits + hs.cont_col, g_logp * za * expf(-ls));
       dls = g_logp * (za * za - 1.0f) - ce;
     }
-    if (lane == 0) dvalue[warp * ld_dvalue] = vf_coef * dv / la.count;
+    if (lane == 0) st_grad(dvalue + warp * ld_dvalue, vf_coef * dv / la.count);
   }
   // block reduction of the statistics, one atomic per block and field
   __shared__ float red[8][8];
@@ -441,27 +446,31 @@ SURF_EXPORT int surf_adv_moments(const float* adv, const int64_t* perm, int64_t 
   SURF_RETURN_LAUNCH();
 }
 
+// dout_bf16: dlogits / dvalue are bf16 (the backward's operand) instead of fp32.
 SURF_EXPORT int surf_ppo_loss(const void* logits, int logits_bf16, int64_t ld_logits, const float* value,
                               int64_t ld_value, const int32_t* act, int64_t ld_act, const float* old_logp,
                               const float* adv, const float* ret, const int64_t* idx, const double* moments,
                               const int* sizes, int n_heads, const int* slots, int cont, const float* log_std,
                               const float* coef, float count, int norm_adv, int n,
-                              float* dlogits, int64_t ld_dlogits, float* dvalue, int64_t ld_dvalue, float* dlog_std,
-                              float* stats, int64_t n_src, int* err, void* stream) {
+                              void* dlogits, int64_t ld_dlogits, void* dvalue, int64_t ld_dvalue, int dout_bf16,
+                              float* dlog_std, float* stats, int64_t n_src, int* err, void* stream) {
   const int neutral[6] = {-1, -1, -1, -1, -1, -1};
   HeadSpec hs = make_spec(sizes, n_heads, slots, cont, neutral);
   LossArgs la{coef, count, norm_adv, n_src, err};
   const int threads = 256, blocks = static_cast<int>(surfk::ceil_div(static_cast<int64_t>(n) * 32, threads));
   auto s = static_cast<cudaStream_t>(stream);
-  if (logits_bf16)
-    ppo_loss_kernel<uint16_t><<<blocks, threads, 0, s>>>(static_cast<const uint16_t*>(logits), ld_logits, value,
-                                                         ld_value, act, ld_act, old_logp, adv, ret, idx, moments, hs,
-                                                         log_std, la, n, dlogits, ld_dlogits, dvalue, ld_dvalue,
-                                                         dlog_std, stats);
-  else
-    ppo_loss_kernel<float><<<blocks, threads, 0, s>>>(static_cast<const float*>(logits), ld_logits, value, ld_value,
-                                                      act, ld_act, old_logp, adv, ret, idx, moments, hs, log_std, la,
-                                                      n, dlogits, ld_dlogits, dvalue, ld_dvalue, dlog_std, stats);
+  auto run = [&](auto* dl, auto* dv) {
+    if (logits_bf16)
+      ppo_loss_kernel<<<blocks, threads, 0, s>>>(static_cast<const uint16_t*>(logits), ld_logits, value, ld_value,
+                                                  act, ld_act, old_logp, adv, ret, idx, moments, hs, log_std, la, n,
+                                                  dl, ld_dlogits, dv, ld_dvalue, dlog_std, stats);
+    else
+      ppo_loss_kernel<<<blocks, threads, 0, s>>>(static_cast<const float*>(logits), ld_logits, value, ld_value,
+                                                  act, ld_act, old_logp, adv, ret, idx, moments, hs, log_std, la, n,
+                                                  dl, ld_dlogits, dv, ld_dvalue, dlog_std, stats);
+  };
+  if (dout_bf16) run(static_cast<uint16_t*>(dlogits), static_cast<uint16_t*>(dvalue));
+  else run(static_cast<float*>(dlogits), static_cast<float*>(dvalue));
   SURF_RETURN_LAUNCH();
 }
 

@@ -369,7 +369,6 @@ class Workspace:
             self.h = [torch.empty(batch, w, dtype=bf, device=dev) for w in cfg.mlp]
         self.dh = [torch.empty_like(t) for t in self.h]
         self.out = torch.empty(batch, cfg.out_pad, dtype=torch.float32, device=dev)
-        self.dout = torch.zeros(batch, cfg.out_pad, dtype=torch.float32, device=dev)
         self.dout16 = torch.zeros(batch, cfg.out_pad, dtype=bf, device=dev)
 
 

@@ -37,8 +37,8 @@ _lib.register(RLIB, {
     "surf_adv_moments": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p]),
     "surf_ppo_loss": (c_int, [c_void_p, c_int, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p,
                               c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
-                              c_float, c_int, c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p,
-                              c_int64, c_void_p, c_void_p]),
+                              c_float, c_int, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p,
+                              c_void_p, c_int64, c_void_p, c_void_p]),
 })
 
 LOG_SQRT_2PI = 0.9189385332046727
@@ -241,14 +241,19 @@ def ppo_loss(out: torch.Tensor, value_col: int, act: torch.Tensor, old_logp, adv
              norm_adv: bool = True, n: Optional[int] = None) -> None:
     """Fused PPO loss + gradient. ``out`` [B, >=value_col+1] head output (fp32);
     rollout tensors are indexed through ``idx`` (int64 [B]) when given.
-    Writes dout [B, ...] (logit gradients + value gradient column), adds the
-    log-std gradient into ``dlog_std`` and loss sums into ``stats`` (6 floats)."""
+    Writes dout [B, ...] (logit gradients + value gradient column; fp32, or
+    bf16 -- the backward GEMMs' operand, rounded as a conversion would),
+    adds the log-std gradient into ``dlog_std`` and loss sums into ``stats``
+    (6 floats)."""
     B = out.shape[0] if n is None else n
+    if dout.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("dout must be float32 or bfloat16")
     check(_lib.lib(RLIB).surf_ppo_loss(
         ptr(out), 0, out.stride(0), ptr(out[:, value_col:]), out.stride(0), ptr(act), act.stride(0), ptr(old_logp),
         ptr(adv), ptr(ret), ptr(idx), ptr(moments), heads.host_ptr(heads.sizes), heads.n_heads,
         heads.host_ptr(heads.slots), heads.cont, ptr(log_std), ptr(coef), float(count), 1 if norm_adv else 0, B,
-        ptr(dout), dout.stride(0), ptr(dout[:, value_col:]), dout.stride(0), ptr(dlog_std), ptr(stats),
+        ptr(dout), dout.stride(0), ptr(dout[:, value_col:]), dout.stride(0), 1 if dout.dtype == torch.bfloat16 else 0,
+        ptr(dlog_std), ptr(stats),
         min(act.shape[0], old_logp.numel(), adv.numel(), ret.numel()), ptr(_error_flag(out.device)),
         stream_ptr(out.device)), "surf_ppo_loss")
 

@@ -751,8 +751,7 @@ class Trainer:
         out = forward_gpu(self.net, self.ws_upd, self.scal_mb, self.img_mb if self.cfg.vision else None)
         R.ppo_loss(out, self.layout.value_col, self.b_act.view(T * N, 8), self.b_logp.view(-1),
                    self.adv.view(-1), self.ret.view(-1), idx, self.mom_mb[m], self.heads, self.net.p("log_std"),
-                   self.coef, float(mb * self.world), self.ws_upd.dout, self.net.g("log_std"), self.loss_stats)
-        G.to_bf16(self.ws_upd.dout, self.ws_upd.dout16)
+                   self.coef, float(mb * self.world), self.ws_upd.dout16, self.net.g("log_std"), self.loss_stats)
         hook = None
         if self.comm is not None and getattr(self.comm, "nbuckets", 0):
             # the tower / FC gradient is reduced across ranks on a side stream

@@ -150,6 +150,12 @@ def test_ppo_loss_gradient_matches_autograd(layout, norm_adv):
     assert float(stats[5]) == B
     cos = torch.nn.functional.cosine_similarity(dout.flatten(), x.grad.flatten(), dim=0)
     assert float(cos) > 0.9999
+    # the bf16 gradient (the backward GEMMs' operand) is the fp32 one rounded
+    dout16 = torch.zeros(B, vc + 1, dtype=torch.bfloat16, device=DEV)
+    R.ppo_loss(out, vc, act, old_logp, adv, ret, idx, moments, heads, log_std, coef, float(B), dout16,
+               torch.zeros(1, device=DEV), torch.zeros(6, device=DEV), norm_adv=norm_adv)
+    torch.cuda.synchronize()
+    assert torch.equal(dout16, dout.to(torch.bfloat16))
 
 
 # ---- GAE and moments -----------------------------------------------------------------------
