@@ -49,6 +49,8 @@ def parse():
                     help="rollout env groups alternating host stepping with GPU work (default: the config's)")
     ap.add_argument("--no-async-env", action="store_true",
                     help="host env: step each group synchronously (no overlap of its launches with env stepping)")
+    ap.add_argument("--no-render-order", action="store_true",
+                    help="host env: render each group in env index order instead of the env step's spatial order")
     ap.add_argument("--race", action="store_true",
                     help="the race configuration (config 5: race track, geodesic potential, 2048 envs per GPU)")
     ap.add_argument("--json", default=None)
@@ -159,6 +161,8 @@ def run_ours(args) -> None:
         cfg.env_groups = args.env_groups
     if args.no_async_env:
         cfg.async_env = False
+    if args.no_render_order:
+        cfg.render_order = False
     tr = Trainer(cfg, rank=rank, world=world, comm=comm, verbose=(rank == 0))
     for _ in range(args.warmup):
         tr.train_iteration()
@@ -222,7 +226,7 @@ def run_ours(args) -> None:
                                "finish curtain), 16u SDF and geodesic grid" if args.race else
                                "procedural random field, 512 brushes, 16u SDF 1024x1024x256"),
                        "comm": args.comm if world > 1 else "none", "cuda_graphs": cfg.graphs,
-                       "env_device": cfg.env_device, "env_groups": cfg.env_groups, "async_env": cfg.async_env, "env_threads": tr.core.threads,
+                       "env_device": cfg.env_device, "env_groups": cfg.env_groups, "async_env": cfg.async_env, "render_order": cfg.render_order, "env_threads": tr.core.threads,
                        "reward": ("race: potential on the geodesic distance to the finish, 15 s stall kill, + "
                                   "count curiosity 0.25" if args.race else
                                   "coverage (revisit_pen 0.25) + count curiosity 0.25 (256u cell x 8 yaw x 8 speed)"),

@@ -45,6 +45,7 @@ struct MarchParams {
   int flags;              // bit 2: 64-bit voxel addressing even for small grids (timing comparisons)
   int idx32;              // the bricked grid has < 2^31 elements: 32-bit voxel addressing
   uint8_t* steps;         // optional per-ray step census [n_env, H, W]
+  const int32_t* env_order;  // optional: the env each run of blocks renders (a permutation of [0, n_env))
 };
 
 enum Layout : int { kNHW = 0, kS2D4 = 1 };
@@ -63,8 +64,12 @@ template <int kPinhole, typename OutT, int kLayout, bool kSurfNz>
 __global__ void __launch_bounds__(128) march_kernel(MarchParams p) {
   const int tiles_w = (p.W + 15) >> 4;
   const int tiles = tiles_w * ((p.H + 7) >> 3);
-  const int n = blockIdx.x / tiles;
-  const int tile = blockIdx.x - n * tiles;
+  const int nb = blockIdx.x / tiles;
+  const int tile = blockIdx.x - nb * tiles;
+  // with env_order, consecutive envs of the launch are spatial neighbours
+  // (the host env's Morton order): their rays share SDF bricks in L2
+  const int n = p.env_order ? __ldg(p.env_order + nb) : nb;
+  if (n < 0) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = (tile % tiles_w) * 16 + (lane & 15);
   const int r = (tile / tiles_w) * 8 + warp * 2 + (lane >> 4);
@@ -196,11 +201,13 @@ __global__ void brick_kernel(const T* src, __half* dst, BrickGrid g) {
 // 0 float32, 1 bfloat16. layout: 0 NHW, 1 space-to-depth 4x4 (H, W % 4 == 0).
 // flags bit 0: the grid has >= 1 free boundary layer (enables the
 // outside-the-grid shortcut, which leaves every output unchanged).
+// env_order (optional, int32 [n_env], a permutation): the order the envs are
+// rendered in; every env's output is the same in any order.
 SURF_EXPORT int surf_march(const float* pose, int64_t pose_stride, int n_env, int H, int W, const void* sdf_bricked,
                            int nx, int ny, int nz, float mnx, float mny, float mnz, float cell, const float* col_off,
                            const float* row_off, float range, float near_range, int max_steps, int camera,
                            void* out, int64_t out_stride, int out_dtype, int layout, const int8_t* surf_nz,
-                           uint8_t* steps, int flags, void* stream) {
+                           uint8_t* steps, int flags, const int32_t* env_order, void* stream) {
   MarchParams p;
   p.pose = pose;
   p.pose_stride = pose_stride;
@@ -221,6 +228,7 @@ SURF_EXPORT int surf_march(const float* pose, int64_t pose_stride, int n_env, in
   p.out_stride = out_stride;
   p.surf_nz = surf_nz;
   p.steps = steps;
+  p.env_order = env_order;
   p.exit_outside = flags & 1;
   p.flags = flags;
   p.idx32 = p.grid.size() < (int64_t(1) << 31) && !(flags & 4);

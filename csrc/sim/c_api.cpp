@@ -107,6 +107,11 @@ SURFSIM_API void surfsim_step_k_range_async(void* h, int32_t lo, int32_t hi, con
                              RowOut{term_rec, term_rec_stride});
 }
 SURFSIM_API void surfsim_step_wait(void* h) { ENV(h)->step_wait(); }
+// The visiting order of the last step of [lo, hi) (offsets from lo; see EnvBatch::env_order).
+SURFSIM_API void surfsim_env_order(void* h, int32_t lo, int32_t hi, int32_t* out) {
+  if (lo < 0 || hi > ENV(h)->num_envs() || hi <= lo || !out) return;
+  ENV(h)->env_order(lo, hi, out);
+}
 SURFSIM_API PlayerState* surfsim_states_ptr(void* h) { return ENV(h)->states(); }
 SURFSIM_API void surfsim_get_states(void* h, PlayerState* out) {
   ENV(h)->step_wait();

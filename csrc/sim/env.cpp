@@ -257,6 +257,16 @@ void EnvBatch::step_wait() {
   in_flight_ = false;
 }
 
+void EnvBatch::env_order(int lo, int hi, int32_t* out) const {
+  for (const RangeOrder& o : orders_) {
+    if (o.lo == lo && o.hi == hi && static_cast<int>(o.idx.size()) == hi - lo) {
+      for (int j = 0; j < hi - lo; ++j) out[j] = o.idx[static_cast<size_t>(j)] - lo;
+      return;
+    }
+  }
+  for (int j = 0; j < hi - lo; ++j) out[j] = j;
+}
+
 const int32_t* EnvBatch::spatial_order(int lo, int hi) {
   constexpr int kOrderEvery = 8;          // calls between re-sorts (players move ~100u per call)
   constexpr float kCell = 256.f;          // Morton cell edge (units)

@@ -63,6 +63,11 @@ class EnvBatch {
   void step_k_range_async(int lo, int hi, const int32_t* actions, int action_stride, int yaw_slot, int fail_slot,
                           int k, RowOut obs, RowOut term_obs, RowOut rec, RowOut term_rec);
   void step_wait();
+  // The order the last step of [lo, hi) visited its envs (Morton order of
+  // their x-y cells), as offsets from lo: out[j] = env - lo. The identity
+  // before that range's first step. Also the order a camera should render
+  // them in (neighbours share cached map data there too).
+  void env_order(int lo, int hi, int32_t* out) const;
 
   PlayerState* states() { return st_.data(); }
   void set_state(int env, const PlayerState& s);

@@ -23,7 +23,7 @@ _D = c_double
 _SIGS = {
     "libsurf_vision.so": {
         "surf_march": (_I, [_V, _L, _I, _I, _I, _V, _I, _I, _I, _F, _F, _F, _F, _V, _V, _F, _F, _I, _I, _V, _L, _I,
-                            _I, _V, _V, _I, _V]),
+                            _I, _V, _V, _I, _V, _V]),
         "surf_brick_size": (_L, [_I, _I, _I]),
         "surf_brick_sdf": (_I, [_V, _I, _V, _I, _I, _I, _V]),
         "surf_brick_i8": (_I, [_V, _V, _I, _I, _I, _V]),

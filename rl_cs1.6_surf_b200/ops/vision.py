@@ -210,11 +210,18 @@ class DepthCamera:
         return self.H * self.W * self.channels
 
     def render(self, pose: torch.Tensor, out: Optional[torch.Tensor] = None, steps: Optional[torch.Tensor] = None,
-               stream: Optional[int] = None) -> torch.Tensor:
+               stream: Optional[int] = None, env_order: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Depth images of every pose row into ``out`` rows. ``env_order``
+        (int32 [n], a permutation of the rows) is the order the kernel renders
+        them in -- spatial neighbours in a row share cached SDF bricks; the
+        images are the same in any order."""
         require_cuda(pose, "DepthCamera.render")
         if pose.dtype != torch.float32 or pose.stride(-1) != 1 or pose.shape[-1] < 6:
             raise ValueError("pose must be float32 rows (x, y, z, yaw, pitch, ducked, ...) with unit column stride")
         n = pose.shape[0]
+        if env_order is not None and (env_order.dtype != torch.int32 or env_order.numel() != n
+                                      or not env_order.is_contiguous()):
+            raise ValueError("env_order must be a contiguous int32 permutation of the pose rows")
         if out is None:
             out = torch.empty((n, self.frame), dtype=self.dtype, device=pose.device)
         if out.dtype not in (torch.float32, torch.bfloat16) or out.stride(-1) != 1 or out.shape[-1] < self.frame:
@@ -225,7 +232,8 @@ class DepthCamera:
             float(v.mins[0]), float(v.mins[1]), float(v.mins[2]), float(v.cell), ptr(self.col_off),
             ptr(self.row_off), self.range, self.near, self.max_steps, 1 if self.pinhole else 0, ptr(out),
             out.stride(0), 1 if out.dtype == torch.bfloat16 else 0, self.layout, ptr(self.surf_nz), ptr(steps),
-            (1 if self.vol.padded else 0) | MARCH_DIAG_FLAGS, stream if stream is not None else stream_ptr(pose.device)),
+            (1 if self.vol.padded else 0) | MARCH_DIAG_FLAGS, ptr(env_order),
+            stream if stream is not None else stream_ptr(pose.device)),
             "surf_march")
         return out
 

@@ -184,6 +184,7 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
                                               c_int32, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
                                               c_void_p, c_int64]),
         "surfsim_step_wait": (None, [c_void_p]),
+        "surfsim_env_order": (None, [c_void_p, c_int32, c_int32, c_void_p]),
         "surfsim_states_ptr": (c_void_p, [c_void_p]),
         "surfsim_get_states": (None, [c_void_p, c_void_p]),
         "surfsim_set_state": (None, [c_void_p, c_int32, c_void_p]),
@@ -365,6 +366,11 @@ class SimCore:
 
     def step_wait(self) -> None:
         self.lib.surfsim_step_wait(self._h)
+
+    def env_order(self, lo: int, hi: int, out_ptr: int) -> None:
+        """Write the order the last step of envs [lo, hi) visited them in
+        (int32 offsets from lo, a permutation) to the address ``out_ptr``."""
+        self.lib.surfsim_env_order(self._h, int(lo), int(hi), c_void_p(out_ptr))
 
     def step_k_numpy(self, actions: np.ndarray, k: int, yaw: Optional[np.ndarray] = None,
                      fail: Optional[np.ndarray] = None):

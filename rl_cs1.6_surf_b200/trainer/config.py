@@ -117,6 +117,7 @@ class TrainConfig:
     graphs: bool = True
     env_groups: int = 2                # rollout: env groups alternating host stepping with GPU work
     async_env: bool = True             # host env: start the next group's step before this group's launches
+    render_order: bool = True          # host env: render each group in the env step's spatial order
     env_device: str = "cpu"            # cpu: C++ thread pool + pinned rows; cuda: the same env rules on the GPU
     comm: str = "p2p"                  # p2p (fused NVLink kernels) | nccl (library baseline)
     threads: Optional[int] = None

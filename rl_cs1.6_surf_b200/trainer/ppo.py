@@ -283,6 +283,12 @@ class Trainer:
             G = cfg.env_groups if (cfg.env_groups > 1 and N % cfg.env_groups == 0 and N // cfg.env_groups >= 64) else 1
             step = N // G
             self.groups = [(g * step, (g + 1) * step) for g in range(G)]
+            # the order each group's depth images are rendered in: the host
+            # env's spatial visiting order of the group (neighbouring cameras
+            # share cached SDF bricks), identity until the first step
+            self.order_pin = torch.cat([torch.arange(hi - lo, dtype=torch.int32) for lo, hi in self.groups])
+            self.order_pin = self.order_pin.pin_memory()
+            self.order_dev = self.order_pin.to(dev)
             self.ws_grp = [Workspace(self.net, step) for _ in range(G)]
             if self.genv is not None:
                 if self.stacker is not None:
@@ -430,6 +436,7 @@ class Trainer:
         T = self.T
         if self.genv is None:
             self.hdev[lo:hi].copy_(self.hrec[lo:hi], non_blocking=True)
+            self.order_dev[lo:hi].copy_(self.order_pin[lo:hi], non_blocking=True)
         elif t > 0 and env:               # the env steps on the GPU with the previous decision's actions
             self._env_body(g, t)
         if t > 0:
@@ -444,7 +451,8 @@ class Trainer:
         img = None
         if self.cfg.vision:
             img = self.b_img[self.pro + t, lo:hi]
-            self.camera.render(self.hdev[lo:hi, C_REC:C_REC + 6], out=img)
+            self.camera.render(self.hdev[lo:hi, C_REC:C_REC + 6], out=img,
+                               env_order=self.order_dev[lo:hi] if self.genv is None and self.cfg.render_order else None)
             if self.stacker is not None:
                 done = self.b_done[t - 1, lo:hi] if t > 0 else None      # t == 0 continues the last tail
                 img = self.stacker.rollout(self.b_img, self.pro + t, lo, hi, done, self.age_cur, self.b_age[t, lo:hi],
@@ -526,6 +534,7 @@ class Trainer:
              yaw_slot=6 if self.layout.continuous_yaw else -1, fail_slot=7,
              obs=(base + 4 * C_OBS, stride), term_obs=(base + 4 * C_TOBS, stride),
              rec=(base + 4 * C_REC, stride), term_rec=(base + 4 * C_TREC, stride))
+        self.core.env_order(lo, hi, self.order_pin.data_ptr() + 4 * lo)
 
     def _env_body(self, g: int, t: int) -> None:
         """GPU env: K ticks of group g's envs with decision t-1's action rows,

@@ -194,6 +194,26 @@ def test_async_group_steps_match_sync(field_map):
         np.testing.assert_array_equal(outs[0][1], outs[1][1])
 
 
+def test_env_order_is_a_permutation(field_map):
+    """The visiting order the host env exports for a range (the render order
+    of its depth images): the identity before the range's first step, a
+    permutation of the range's offsets after it."""
+    m, path = field_map
+    n = 96
+    core = SimCore(str(path), default_config(n, spawn_mode=2), threads=2)
+    core.set_spawn_pool(m.spawn_pool)
+    core.reset(3)
+    out = np.full(n, -1, np.int32)
+    core.env_order(16, 80, out[16:].ctypes.data)
+    np.testing.assert_array_equal(out[16:80], np.arange(64))
+    rows = np.zeros((n, 8), np.int32)
+    rows[:, :6] = random_actions(np.random.default_rng(1), n)
+    core.step_k_range(16, 80, rows.ctypes.data, 8, 3)
+    core.env_order(16, 80, out[16:].ctypes.data)
+    assert sorted(out[16:80].tolist()) == list(range(64))
+    assert (out[:16] == -1).all() and (out[80:] == -1).all()
+
+
 def test_continuous_yaw(field_map):
     m, path = field_map
     core = SimCore(str(path), default_config(4, spawn_mode=2, yaw_jitter_deg=0.0), threads=1)

@@ -90,6 +90,22 @@ def test_layouts_and_dtypes(field):
     torch.testing.assert_close(one[0], base[3])
 
 
+def test_render_order_changes_nothing(field):
+    """env_order (the host env's spatial order) only changes which env a run
+    of blocks renders: every image is bit-identical to the plain launch."""
+    m, core = field
+    vol = vision.SdfVolume.build(core, cell=32.0)
+    pose = torch.as_tensor(poses_from_pool(m, 64, 2), device="cuda")
+    cam = vision.DepthCamera(vol, 128, 64, layout=vision.LAYOUT_S2D4, dtype=torch.bfloat16)
+    base = cam.render(pose)
+    order = torch.randperm(64, device="cuda").to(torch.int32)
+    got = cam.render(pose, env_order=order)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), base.view(torch.int16))
+    with pytest.raises(ValueError):
+        cam.render(pose, env_order=order[:10])
+
+
 def test_depth_accuracy_vs_exact_traces(field):
     """Median error vs exact point-hull traces stays within a voxel (16u)."""
     m, core = field
