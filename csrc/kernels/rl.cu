@@ -23,6 +23,7 @@
 // numbers: as easy as 1, 2, 3", SC 2011), keyed by (seed, stream) and counted
 // by (env, decision), so a decision's actions do not depend on the launch.
 #include <cstdint>
+#include <type_traits>
 
 #include "surf_cuda.cuh"
 
@@ -271,42 +272,64 @@ struct LossArgs {
 __device__ __forceinline__ void st_grad(float* p, float v) { *p = v; }
 __device__ __forceinline__ void st_grad(uint16_t* p, float v) { *p = surfk::f32_to_bf16(v); }
 
+// Reductions over a group of GW lanes (the group's lanes are contiguous).
+template <int GW>
+__device__ __forceinline__ float group_max(float v) {
+  for (int o = GW / 2; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o, GW));
+  return v;
+}
+template <int GW>
+__device__ __forceinline__ float group_sum(float v) {
+  for (int o = GW / 2; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o, GW);
+  return v;
+}
+
 // stats[0..5]: policy loss, value loss, entropy, approx_kl, clip fraction, samples (sums)
-template <typename T, typename G>
+// RW rows per warp, one group of GW = 32 / RW lanes each (RW = 2 when every
+// head has at most 16 categories: half the instructions per row). Every lane
+// runs every shuffle; rows past n or with an unreadable index compute on row
+// 0 / source 0 and write zeros (bad) or nothing (past n).
+template <typename T, typename G, int RW>
 __global__ void ppo_loss_kernel(const T* logits, int64_t ld_logits, const float* value, int64_t ld_value,
                                 const int32_t* act, int64_t ld_act, const float* old_logp, const float* adv,
                                 const float* ret, const int64_t* idx, const double* moments, HeadSpec hs,
                                 const float* log_std, LossArgs la, int n, G* dlogits, int64_t ld_dlogits,
                                 G* dvalue, int64_t ld_dvalue, float* dlog_std, float* stats) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  constexpr int GW = 32 / RW;
   const int lane = threadIdx.x & 31;
+  const int gl = lane % GW;                                   // lane within the row's group
+  const int r = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * RW + lane / GW;
+  const bool in = r < n;
   float pg = 0, vl = 0, ent = 0, kl = 0, clipped = 0, dls = 0;
   const float clip = la.coef[0], vf_coef = la.coef[1], ent_coef = la.coef[2];
-  const int64_t src = warp < n ? (idx ? idx[warp] : warp) : 0;
-  const bool bad = warp < n && (src < 0 || src >= la.n_src);
-  if (bad && lane == 0) surfk::report_error(la.err, surfk::kErrLossIndex);
+  int64_t src = in ? (idx ? idx[r] : r) : 0;
+  const bool bad = in && (src < 0 || src >= la.n_src);
+  if (bad && gl == 0) surfk::report_error(la.err, surfk::kErrLossIndex);
   if (bad) {                        // no gradient from a row that cannot be read
-    for (int c = lane; c < hs.width; c += 32) st_grad(dlogits + warp * ld_dlogits + c, 0.0f);
-    if (lane == 0) st_grad(dvalue + warp * ld_dvalue, 0.0f);
+    for (int c = gl; c < hs.width; c += GW) st_grad(dlogits + r * ld_dlogits + c, 0.0f);
+    if (gl == 0) st_grad(dvalue + r * ld_dvalue, 0.0f);
   }
-  if (warp < n && !bad) {
-    const T* row = logits + warp * ld_logits;
+  const bool live = in && !bad;
+  if (!live) src = 0;
+  const int rr = in ? r : 0;
+  {
+    const T* row = logits + rr * ld_logits;
     const int32_t* a = act + src * ld_act;
     // pass 1: log-prob and entropy of every head
     float logp = 0.0f, H = 0.0f;
     float lse_h[kMaxHeads];
     for (int h = 0; h < hs.n_heads; ++h) {
       const int sz = hs.size[h];
-      const float z = lane < sz ? ld<T>(row + hs.offset[h] + lane) : -INFINITY;
-      const float m = warp_max(z);
-      const float e = lane < sz ? expf(z - m) : 0.0f;
-      const float sum = warp_sum(e);
+      const float z = gl < sz ? ld<T>(row + hs.offset[h] + gl) : -INFINITY;
+      const float m = group_max<GW>(z);
+      const float e = gl < sz ? expf(z - m) : 0.0f;
+      const float sum = group_sum<GW>(e);
       const float lse = m + logf(sum);
       lse_h[h] = lse;
       const float lp = z - lse;
       const float p = e / sum;
-      H += -warp_sum(lane < sz ? p * lp : 0.0f);
-      logp += __shfl_sync(0xffffffffu, lp, a[hs.slot[h]]);
+      H += -group_sum<GW>(gl < sz ? p * lp : 0.0f);
+      logp += __shfl_sync(0xffffffffu, lp, a[hs.slot[h]], GW);
     }
     float mu = 0.0f, ls = 0.0f, za = 0.0f;
     if (hs.cont) {
@@ -323,58 +346,57 @@ __global__ void ppo_loss_kernel(const T* logits, int64_t ld_logits, const float*
       A = static_cast<float>((A - mean) / (sqrt(var > 0 ? var : 0.0) + 1e-8));
     }
     const float diff = logp - old_logp[src];
-    const float r = expf(diff);
+    const float ratio = expf(diff);
     const float lo = 1.0f - clip, hi = 1.0f + clip;
-    const float rc = fminf(fmaxf(r, lo), hi);
-    const float s1 = -A * r, s2 = -A * rc;
+    const float rc = fminf(fmaxf(ratio, lo), hi);
+    const float s1 = -A * ratio, s2 = -A * rc;
     pg = fmaxf(s1, s2);
     // d(policy loss)/d(logp): the unclipped branch is the active one
-    const float g_logp = (s1 >= s2) ? -A * r / la.count : 0.0f;
-    const float v = value[warp * ld_value];
+    const float g_logp = (s1 >= s2) ? -A * ratio / la.count : 0.0f;
+    const float v = value[rr * ld_value];
     const float dv = v - ret[src];
     vl = 0.5f * dv * dv;
     ent = H;
     kl = -diff;
-    clipped = fabsf(r - 1.0f) > clip ? 1.0f : 0.0f;
+    clipped = fabsf(ratio - 1.0f) > clip ? 1.0f : 0.0f;
     // gradients w.r.t. the logits of each head:
     //   policy  g_logp * (onehot - p)
     //   entropy -ent_coef/B * dH/dz = ent_coef/B * p * (log p + H_head)
     const float ce = ent_coef / la.count;
     for (int h = 0; h < hs.n_heads; ++h) {
       const int sz = hs.size[h];
-      const float z = lane < sz ? ld<T>(row + hs.offset[h] + lane) : 0.0f;
+      const float z = gl < sz ? ld<T>(row + hs.offset[h] + gl) : 0.0f;
       const float lp = z - lse_h[h];
-      const float p = lane < sz ? expf(lp) : 0.0f;
-      const float Hh = -warp_sum(lane < sz ? p * lp : 0.0f);
-      if (lane < sz) {
-        const float onehot = (lane == a[hs.slot[h]]) ? 1.0f : 0.0f;
-        st_grad(dlogits + warp * ld_dlogits + hs.offset[h] + lane, g_logp * (onehot - p) + ce * p * (lp + Hh));
+      const float p = gl < sz ? expf(lp) : 0.0f;
+      const float Hh = -group_sum<GW>(gl < sz ? p * lp : 0.0f);
+      if (live && gl < sz) {
+        const float onehot = (gl == a[hs.slot[h]]) ? 1.0f : 0.0f;
+        st_grad(dlogits + r * ld_dlogits + hs.offset[h] + gl, g_logp * (onehot - p) + ce * p * (lp + Hh));
       }
     }
-    if (hs.cont && lane == 0) {
+    if (hs.cont && gl == 0) {
       // d logp/d mu = za/sigma ; d logp/d log_std = za^2 - 1 ; dH/d log_std = 1
-      st_grad(dlogits + warp * ld_dlogits + hs.cont_col, g_logp * za * expf(-ls));
+      if (live) st_grad(dlogits + r * ld_dlogits + hs.cont_col, g_logp * za * expf(-ls));
       dls = g_logp * (za * za - 1.0f) - ce;
     }
-    if (lane == 0) st_grad(dvalue + warp * ld_dvalue, vf_coef * dv / la.count);
+    if (live && gl == 0) st_grad(dvalue + r * ld_dvalue, vf_coef * dv / la.count);
   }
   // block reduction of the statistics, one atomic per block and field
-  __shared__ float red[8][8];
-  const int wib = threadIdx.x >> 5;
-  if (lane == 0) {
-    const bool live = warp < n && !bad;
-    red[wib][0] = live ? pg : 0.f;
-    red[wib][1] = live ? vl : 0.f;
-    red[wib][2] = live ? ent : 0.f;
-    red[wib][3] = live ? kl : 0.f;
-    red[wib][4] = live ? clipped : 0.f;
-    red[wib][5] = live ? 1.f : 0.f;
-    red[wib][6] = live ? dls : 0.f;
+  __shared__ float red[16][8];
+  const int grp = threadIdx.x / GW;                           // < 8 * RW
+  if (gl == 0) {
+    red[grp][0] = live ? pg : 0.f;
+    red[grp][1] = live ? vl : 0.f;
+    red[grp][2] = live ? ent : 0.f;
+    red[grp][3] = live ? kl : 0.f;
+    red[grp][4] = live ? clipped : 0.f;
+    red[grp][5] = live ? 1.f : 0.f;
+    red[grp][6] = live ? dls : 0.f;
   }
   __syncthreads();
   if (threadIdx.x < 7) {
     float acc = 0.f;
-    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) acc += red[w][threadIdx.x];
+    for (int w = 0; w < static_cast<int>(blockDim.x / GW); ++w) acc += red[w][threadIdx.x];
     if (threadIdx.x < 6) atomicAdd(stats + threadIdx.x, acc);
     else if (hs.cont) atomicAdd(dlog_std, acc);
   }
@@ -457,17 +479,35 @@ SURF_EXPORT int surf_ppo_loss(const void* logits, int logits_bf16, int64_t ld_lo
   const int neutral[6] = {-1, -1, -1, -1, -1, -1};
   HeadSpec hs = make_spec(sizes, n_heads, slots, cont, neutral);
   LossArgs la{coef, count, norm_adv, n_src, err};
-  const int threads = 256, blocks = static_cast<int>(surfk::ceil_div(static_cast<int64_t>(n) * 32, threads));
+  bool narrow = true;                      // every head fits a 16-lane group: two rows per warp
+  for (int h = 0; h < n_heads; ++h) narrow = narrow && sizes[h] <= 16;
+  const int rw = narrow ? 2 : 1;
+  const int threads = 256;
+  const int blocks = static_cast<int>(surfk::ceil_div(surfk::ceil_div(static_cast<int64_t>(n), rw) * 32, threads));
   auto s = static_cast<cudaStream_t>(stream);
   auto run = [&](auto* dl, auto* dv) {
-    if (logits_bf16)
-      ppo_loss_kernel<<<blocks, threads, 0, s>>>(static_cast<const uint16_t*>(logits), ld_logits, value, ld_value,
-                                                  act, ld_act, old_logp, adv, ret, idx, moments, hs, log_std, la, n,
-                                                  dl, ld_dlogits, dv, ld_dvalue, dlog_std, stats);
-    else
-      ppo_loss_kernel<<<blocks, threads, 0, s>>>(static_cast<const float*>(logits), ld_logits, value, ld_value,
-                                                  act, ld_act, old_logp, adv, ret, idx, moments, hs, log_std, la, n,
-                                                  dl, ld_dlogits, dv, ld_dvalue, dlog_std, stats);
+    using DL = std::remove_pointer_t<decltype(dl)>;
+    if (logits_bf16) {
+      auto* lg = static_cast<const uint16_t*>(logits);
+      if (narrow)
+        ppo_loss_kernel<uint16_t, DL, 2><<<blocks, threads, 0, s>>>(lg, ld_logits, value, ld_value, act, ld_act, old_logp,
+                                                                    adv, ret, idx, moments, hs, log_std, la, n, dl,
+                                                                    ld_dlogits, dv, ld_dvalue, dlog_std, stats);
+      else
+        ppo_loss_kernel<uint16_t, DL, 1><<<blocks, threads, 0, s>>>(lg, ld_logits, value, ld_value, act, ld_act, old_logp,
+                                                                    adv, ret, idx, moments, hs, log_std, la, n, dl,
+                                                                    ld_dlogits, dv, ld_dvalue, dlog_std, stats);
+    } else {
+      auto* lg = static_cast<const float*>(logits);
+      if (narrow)
+        ppo_loss_kernel<float, DL, 2><<<blocks, threads, 0, s>>>(lg, ld_logits, value, ld_value, act, ld_act, old_logp,
+                                                                 adv, ret, idx, moments, hs, log_std, la, n, dl,
+                                                                 ld_dlogits, dv, ld_dvalue, dlog_std, stats);
+      else
+        ppo_loss_kernel<float, DL, 1><<<blocks, threads, 0, s>>>(lg, ld_logits, value, ld_value, act, ld_act, old_logp,
+                                                                 adv, ret, idx, moments, hs, log_std, la, n, dl,
+                                                                 ld_dlogits, dv, ld_dvalue, dlog_std, stats);
+    }
   };
   if (dout_bf16) run(static_cast<uint16_t*>(dlogits), static_cast<uint16_t*>(dvalue));
   else run(static_cast<float*>(dlogits), static_cast<float*>(dvalue));
