@@ -684,7 +684,12 @@ int sh_launch(const ShDesc& d, const Epilogue& ep, cudaStream_t s) {
   if (stages < 2) return static_cast<int>(cudaErrorInvalidValue);
   const size_t smem = 1024 + static_cast<size_t>(stages) * a.stage_bytes + res_bytes + stg_total + 1024;
   auto kern = shconv_kernel<BN, KIND, KS>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  // the largest dynamic size any call of this instantiation asks for, set
+  // once: several layers share an instantiation with different stage counts,
+  // and a graph node captured with a larger size must not meet an attribute
+  // lowered by a later call
+  static const cudaError_t attr = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+  if (attr != cudaSuccess) return static_cast<int>(attr);
   const int units = KIND == kShFwd ? a.mt : a.nt * a.splits;
   const int grid = units < sms ? units : sms;
   launch_pdl(kern, dim3(grid), dim3(kShThreads), smem, s, mp[0], mp[1], mp[2], mp[3], mres, a, ep, stages);

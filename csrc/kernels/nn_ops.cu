@@ -190,6 +190,26 @@ __global__ void gather_kernel(const uint8_t* src, int64_t src_stride, const int6
   }
 }
 
+// One warp per destination row, 16-byte vectors (rows, strides and bases
+// 16-byte aligned): the index is read once per row and there is no
+// per-element division; several vectors per lane are in flight.
+__global__ void __launch_bounds__(256) gather16_kernel(const uint8_t* src, int64_t src_stride, const int64_t* idx,
+                                                       int64_t offset, int64_t n, int row_bytes, uint8_t* dst,
+                                                       int64_t dst_stride, int64_t src_rows, int* err) {
+  const int lane = threadIdx.x & 31;
+  const int vecs = row_bytes >> 4;
+  const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t r = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; r < n; r += warps) {
+    const int64_t s = idx[r] + offset;
+    const bool ok = s >= 0 && s < src_rows;
+    if (!ok && lane == 0) surfk::report_error(err, surfk::kErrGatherIndex);
+    const uint4* sp = reinterpret_cast<const uint4*>(src + (ok ? s : 0) * src_stride);
+    uint4* dp = reinterpret_cast<uint4*>(dst + r * dst_stride);
+#pragma unroll 4
+    for (int c = lane; c < vecs; c += 32) dp[c] = ok ? __ldcs(sp + c) : make_uint4(0, 0, 0, 0);
+  }
+}
+
 __global__ void f32_to_bf16_kernel(const float* x, int64_t ldx, uint16_t* y, int64_t ldy, int64_t rows, int cols) {
   const int64_t total = rows * cols;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -400,6 +420,15 @@ SURF_EXPORT int surf_gather_rows(const void* src, int64_t src_stride_bytes, cons
                                  int64_t n, int row_bytes, void* dst, int64_t dst_stride_bytes, int64_t src_rows,
                                  int* err, void* stream) {
   if (row_bytes & 3) return static_cast<int>(cudaErrorInvalidValue);
+  if (!((row_bytes | src_stride_bytes | dst_stride_bytes | reinterpret_cast<uintptr_t>(src) |
+         reinterpret_cast<uintptr_t>(dst)) & 15) && row_bytes >= 512) {
+    const int64_t blocks = surfk::ceil_div(n, 8);               // 8 rows (warps) per block
+    gather16_kernel<<<static_cast<unsigned>(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0,
+                      static_cast<cudaStream_t>(stream)>>>(static_cast<const uint8_t*>(src), src_stride_bytes, idx,
+                                                           offset, n, row_bytes, static_cast<uint8_t*>(dst),
+                                                           dst_stride_bytes, src_rows, err);
+    SURF_RETURN_LAUNCH();
+  }
   gather_kernel<<<blocks_for(n * (row_bytes / 4), 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint8_t*>(src), src_stride_bytes, idx, offset, n, row_bytes, static_cast<uint8_t*>(dst),
       dst_stride_bytes, src_rows, err);

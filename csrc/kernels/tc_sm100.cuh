@@ -358,11 +358,15 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---- host side ---------------------------------------------------------------
-// Launch with programmatic stream serialization (SURF_NO_PDL=1: plain launch).
+// Launch with programmatic stream serialization (SURF_NO_PDL=1: plain
+// launch). Under a profiler's injection library (Nsight Compute sets
+// CUDA_INJECTION64_PATH) the launches are plain too: a programmatic launch
+// inside a captured graph failed to launch under ncu's kernel serialization.
 inline bool pdl_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("SURF_NO_PDL");
-    return !(e && e[0] == '1');
+    const char* inj = std::getenv("CUDA_INJECTION64_PATH");
+    return !(e && e[0] == '1') && !(inj && inj[0]);
   }();
   return on;
 }

@@ -140,3 +140,10 @@ def test_colsum_and_gather():
     dst = torch.empty(123, 16, device="cuda")
     G.gather_rows(src, idx, dst, offset=50)
     torch.testing.assert_close(dst, src[idx + 50])
+    # image-sized rows (16 KB): the 16-byte vector path, bit-exact
+    img = rand(3000, 8192)
+    idx = torch.randint(0, 2900, (777,), device="cuda")
+    got = torch.empty(777, 8192, dtype=torch.bfloat16, device="cuda")
+    G.gather_rows(img, idx, got, offset=7)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), img[idx + 7].view(torch.int16))
