@@ -274,6 +274,57 @@ SURF_HD inline void trace_player(const MapView& m, int usehull, const float star
   }
 }
 
+namespace detail {
+// Whether the expanded hull of `model` holds the player box (usehull) at p:
+// the startsolid of clip_model(model, ent_origin, usehull, p, p). A segment of
+// zero length never straddles a plane (both ends give the same plane_side),
+// so the descent visits one child per node down to a single leaf, and only a
+// solid leaf makes it start solid. Same offsets, start node and node tests
+// as clip_model, so the answer is the same bit for bit (p must not be NaN:
+// a NaN side takes clip_model's split branch).
+SURF_HD inline bool model_point_solid(const MapView& m, int model, const float ent_origin[3], int usehull,
+                                      const float p[3]) {
+  HullView h = m.hull(model, bsp_hull_of_usehull(usehull));
+  float a[3];
+  for (int k = 0; k < 3; ++k) {
+    const float off = h.clip_mins[k] - player_mins(usehull, k) + ent_origin[k];
+    a[k] = p[k] - off;
+  }
+  const int32_t g = h.grid.point_start(a);        // segment_start(a, a) picks the same node
+  int num = g != HullGrid::kNone ? g : h.first;
+  if (num >= 0 && h.first >= h.last) return false;   // empty tree: in the open
+  while (num >= 0) {
+    const Clipnode& node = h.nodes[num];
+    num = plane_side(h.planes[node.plane], a) >= 0.f ? node.child[0] : node.child[1];
+  }
+  return num == kSolid;
+}
+}  // namespace detail
+
+// trace_player(m, usehull, p, p).startsolid without the sweep: the world or any
+// solid brush entity whose padded bounds hold p puts p in solid (a model that
+// starts solid reports fraction 0, which no later model can undercut). This is
+// the engine's PM_TestPlayerPosition question (stuck checks, unduck headroom),
+// asked once or twice per tick, so it skips the segment set-up and the
+// descent's continuation stack.
+SURF_HD inline bool player_point_solid(const MapView& m, int usehull, const float p[3]) {
+  if (p[0] != p[0] || p[1] != p[1] || p[2] != p[2]) {
+    Trace tr;
+    trace_player(m, usehull, p, p, &tr);
+    return tr.startsolid;
+  }
+  if (detail::model_point_solid(m, 0, m.models[0].origin, usehull, p)) return true;
+  const float pad = 40.f;                 // trace_player's broad-phase margin
+  for (int i = 0; i < m.solids.size(); ++i) {
+    const BrushEntity& s = m.solids[i];
+    if (p[0] - pad > s.absmax[0] || p[0] + pad < s.absmin[0] || p[1] - pad > s.absmax[1] ||
+        p[1] + pad < s.absmin[1] || p[2] - pad > s.absmax[2] || p[2] + pad < s.absmin[2])
+      continue;
+    if (detail::model_point_solid(m, s.model, s.origin, usehull, p)) return true;
+  }
+  return false;
+}
+
 SURF_HD inline int point_contents(const MapView& m, const float p[3]) {
   HullView h0 = m.hull(0, 0);
   const int32_t g = h0.grid.point_start(p);

@@ -207,11 +207,7 @@ struct Mover {
   bool blocked_solid = false;
 
   SURF_HD void trace(int hull, const float* a, const float* b, Trace* tr) const { trace_player(map, hull, a, b, tr); }
-  SURF_HD bool position_free(const float* p) const {
-    Trace tr;
-    trace(usehull, p, p, &tr);
-    return !tr.startsolid;
-  }
+  SURF_HD bool position_free(const float* p) const { return !player_point_solid(map, usehull, p); }
 
   // CheckVelocity: NaN scrub and per-axis clamp to sv_maxvelocity.
   SURF_HD void check_velocity() {
@@ -692,15 +688,12 @@ struct Mover {
   }
 
   SURF_HD void unduck() {
-    Trace tr;
     float np[3];
     copy3(np, st->origin);
     if (st->onground != -1) np[2] = static_cast<float>(np[2] + 18.0);
-    trace(usehull, np, np, &tr);
-    if (tr.startsolid) return;
+    if (player_point_solid(map, usehull, np)) return;
     usehull = 0;
-    trace(0, np, np, &tr);
-    if (tr.startsolid) { usehull = 1; return; }       // no headroom: stay ducked
+    if (player_point_solid(map, 0, np)) { usehull = 1; return; }   // no headroom: stay ducked
     st->ducked = 0;
     st->induck = 0;
     view_ofs = kViewStand;

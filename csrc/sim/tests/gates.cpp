@@ -17,6 +17,8 @@
 //   E  start-node grids: random traces and point contents starting at a grid
 //      cell's node equal the root-started ones bit for bit (no reference
 //      counterpart: the grids are this build's)
+//   F  point-in-solid: player_point_solid equals the zero-length trace's
+//      startsolid (this build's shortcut of PM_TestPlayerPosition)
 // Exit status 0 when every gate passes; one line per check on stdout.
 #include <chrono>
 #include <cmath>
@@ -258,6 +260,38 @@ int main() {
     }
     check(mismatch == 0, "E grid-started traces / contents == root-started", mismatch, 0);
     check(from_grid > n / 4, "E grid starts most short traces below the root", from_grid, n / 4);
+  }
+  // ---- F: the point-in-solid test (stuck checks, unduck headroom) answers as
+  // the zero-length trace's startsolid, with and without grids, at random
+  // points and at trace end points (boxes resting against a surface)
+  {
+    const MapView with = map->view();
+    MapView without = with;
+    for (auto& g : without.world_grid) g = HullGrid();
+    std::mt19937 rng(13);
+    std::uniform_real_distribution<float> ux(with.world_mins[0] - 40, with.world_maxs[0] + 40),
+        uy(with.world_mins[1] - 40, with.world_maxs[1] + 40), uz(with.world_mins[2] - 40, with.world_maxs[2] + 40);
+    std::uniform_real_distribution<float> step(-200.f, 200.f);
+    int mismatch = 0, solid = 0;
+    const int n = 200000;
+    for (int i = 0; i < n; ++i) {
+      const int usehull = i % 3;
+      float p[3] = {ux(rng), uy(rng), uz(rng)};
+      if (i % 2) {                        // the end of a sweep: resting against whatever it hit
+        const float b[3] = {p[0] + step(rng), p[1] + step(rng), p[2] + step(rng)};
+        Trace t;
+        trace_player(with, usehull, p, b, &t);
+        for (int k = 0; k < 3; ++k) p[k] = t.endpos[k];
+      }
+      Trace tw, to;
+      trace_player(with, usehull, p, p, &tw);
+      trace_player(without, usehull, p, p, &to);
+      const bool fw = player_point_solid(with, usehull, p), fo = player_point_solid(without, usehull, p);
+      mismatch += (fw != tw.startsolid) + (fo != to.startsolid);
+      solid += fw;
+    }
+    check(mismatch == 0, "F point-in-solid == zero-length trace startsolid", mismatch, 0);
+    check(solid > n / 20 && solid < n - n / 20, "F both answers occur", solid, n / 2);
   }
   std::printf("%s: %d failed\n", g_fail ? "FAILED" : "OK", g_fail);
   return g_fail ? 1 : 0;
