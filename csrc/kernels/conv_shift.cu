@@ -685,10 +685,10 @@ int sh_launch(const ShDesc& d, const Epilogue& ep, cudaStream_t s) {
   const size_t smem = 1024 + static_cast<size_t>(stages) * a.stage_bytes + res_bytes + stg_total + 1024;
   auto kern = shconv_kernel<BN, KIND, KS>;
   // the largest dynamic size any call of this instantiation asks for, set
-  // once: several layers share an instantiation with different stage counts,
-  // and a graph node captured with a larger size must not meet an attribute
-  // lowered by a later call
-  static const cudaError_t attr = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+  // once per device: several layers share an instantiation with different
+  // stage counts, and a graph node captured with a larger size must not meet
+  // an attribute lowered by a later call
+  const cudaError_t attr = smem_limit_once<shconv_kernel<BN, KIND, KS>>(232448);
   if (attr != cudaSuccess) return static_cast<int>(attr);
   const int units = KIND == kShFwd ? a.mt : a.nt * a.splits;
   const int grid = units < sms ? units : sms;

@@ -593,10 +593,11 @@ int launch_cfg(const void* A, int64_t lda, const void* B, int64_t ldb, int M, in
                          ep.c_dtype == 1 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)
                     ? 1
                     : 0;
+  const cudaError_t attr = smem_limit_once<gemm_kernel<BN, A_MN, B_MN, STAGES, RB>>(static_cast<int>(C::kSmem));
+  if (attr != cudaSuccess) return static_cast<int>(attr);
   static int resident = 0;          // CTAs per SM for this instantiation
   static int sms = 0;
   if (!resident) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmem));
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, kThreads, C::kSmem);
     int dev = 0;
     cudaGetDevice(&dev);

@@ -12,6 +12,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
@@ -369,6 +370,23 @@ inline bool pdl_enabled() {
     return !(e && e[0] == '1') && !(inj && inj[0]);
   }();
   return on;
+}
+
+// Raise kernel Kern's dynamic shared-memory limit to `bytes` once per device.
+// The attribute belongs to the kernel in the current device's context, so a
+// process that drives several GPUs sets it on each of them; after the first
+// call on a device this is a device query and an atomic load.
+template <auto Kern>
+cudaError_t smem_limit_once(int bytes) {
+  static std::atomic<uint64_t> done{0};    // bit d: set on device d (0..63)
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev >= 0 && dev < 64 ? uint64_t{1} << dev : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
 }
 
 template <typename... Exp, typename... Act>
