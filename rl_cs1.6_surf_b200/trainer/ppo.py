@@ -578,8 +578,15 @@ class Trainer:
         trunc = lo + np.flatnonzero(h[lo:hi, C_REC + 12] != 0)
         if len(trunc) == 0:
             return
-        idx = torch.as_tensor(trunc, device=self.device)
-        rows = self.hrec[torch.as_tensor(trunc)].to(self.device, non_blocking=True)      # [M, 64]
+        # the indices and the group's pinned rows go up as asynchronous copies
+        # (a fancy-indexed host gather would be pageable memory, which blocks
+        # the host) and the truncated rows are picked on the device. hrec[lo:hi] is not
+        # rewritten before this stream's next group launch has completed
+        # (the env steps the group again only after that decision's actions).
+        grp = torch.empty((hi - lo, self.hrec.shape[1]), dtype=self.hrec.dtype, device=self.device)
+        grp.copy_(self.hrec[lo:hi], non_blocking=True)
+        idx = torch.from_numpy(trunc).pin_memory().to(self.device, non_blocking=True)
+        rows = grp.index_select(0, idx - lo)                                              # [M, 64]
         M = len(trunc)
         scal = torch.zeros((M, 16), dtype=torch.bfloat16, device=self.device)
         self._features(rows[:, C_TOBS:C_TOBS + 15].contiguous(), scal)

@@ -134,3 +134,37 @@ def test_pooled_update_stride_and_ez(graphs):
     assert torch.all(tr.b_act[flags][:, 0] < 15)
     assert np.all(tr.core.states_view["pitch"] == np.float32(-10.0))        # fixed gaze held
     tr.release_graphs()
+
+
+def test_host_truncation_bootstrap_values():
+    """The host-env truncation bootstrap stages gamma * V(terminal state) for
+    exactly the truncated envs of the group, the same values as a forward
+    pass on the truncated rows gathered on the host."""
+    from surfb200.models.policy import Workspace, forward_gpu
+    from surfb200.trainer.ppo import C_OBS, C_REC, C_TOBS, C_TREC
+    cfg = TrainConfig(map="field", envs=256, n_steps=4, act_every=3, epochs=1, minibatches=2, ep_ticks=60,
+                      graphs=False, reward=RewardSpec(mode="coverage"))
+    tr = Trainer(cfg, verbose=False)
+    tr.reset()
+    torch.cuda.synchronize()
+    h = tr.hrec.numpy()
+    lo, hi = tr.groups[1]
+    trunc = np.array([lo + 3, lo + 40, hi - 1])
+    h[trunc, C_TOBS:C_TOBS + 15] = h[trunc, C_OBS:C_OBS + 15]        # terminal obs / pose of a live state
+    h[trunc, C_TREC:C_TREC + 6] = h[trunc, C_REC:C_REC + 6]
+    h[trunc, C_TREC + 2] += 50.0
+    h[trunc, C_REC + 12] = 1.0
+    tr.reward.boot.zero_()
+    tr._bootstrap_truncations(1, 0)
+    got = tr.reward.boot.clone()
+    rows = torch.from_numpy(h[trunc]).cuda()
+    scal = torch.zeros((len(trunc), 16), dtype=torch.bfloat16, device="cuda")
+    tr._features(rows[:, C_TOBS:C_TOBS + 15].contiguous(), scal)
+    img = tr.camera.render(rows[:, C_TREC:C_TREC + 6].contiguous())
+    out = forward_gpu(tr.net, Workspace(tr.net, len(trunc)), scal, img, B=len(trunc))
+    want = cfg.gamma * out[:, tr.layout.value_col].float()
+    torch.testing.assert_close(got[torch.from_numpy(trunc).cuda()].float(), want, rtol=1e-3, atol=1e-4)
+    mask = torch.ones(len(got), dtype=torch.bool, device="cuda")
+    mask[torch.from_numpy(trunc).cuda()] = False
+    assert float(got[mask].abs().max()) == 0.0
+    assert float(want.abs().max()) > 0.0
